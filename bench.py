@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark: Q4_K decode GEMV sweep on B200 (the reference's headline path).
+
+Workload (the BASELINE config "Q4_K decode GEMV sweep"): Q4_K weights of shapes
+(K -> N) 4096->4096, 4096->12288, 12288->4096 and 2048->151936, activations
+f32 N(0,1) at batch 1, 2, 4 and 8. One step = one pass over all 16
+(shape, batch) GEMVs, batch-major, so no matrix is re-read before the ~241 MB
+of the other matrices have streamed through L2 (126 MB). Each step also uses
+its own copy of every matrix (copies rotated so each set exceeds 4x L2), so
+every launch reads its weights from HBM.
+
+value     = algorithmic bytes of all GEMVs (weights once + activations + outputs)
+            / device time of the K timed steps (CUDA events on the launch stream,
+            max over ranks), GB/s.
+e2e       = the same metric through the public host-buffer C ABI call
+            (strata_cuda_gemv: pinned host copy in, kernel, result copied out,
+            bounded wait), timed on the host clock.
+roofline  = that kernel against the measured HBM copy bandwidth.
+cpu_baseline = the CPU oracle (the C restatement of ops::gemv, all host
+            threads, row-parallel) on the same sweep.
+
+`--impl reference` times only the reference path on the CPU (the oracle port;
+the Rust reference cannot be built on this image) and prints its own line.
+Multi-GPU (torchrun): output rows of every matrix are sharded across ranks and
+the per-rank outputs are all-gathered over NCCL each step (strong scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "strata-rs_b200"
+sys.path.insert(0, str(PKG))
+
+from synth import Q4K_SWEEP, SWEEP_BATCHES, Q4_K, activations, quant_matrix  # noqa: E402
+
+METRIC = "Q4_K GEMV GB/s (% of HBM peak); MoE layer tokens/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+
+
+def gemv_bytes(k: int, n: int, b: int) -> int:
+    return n * (k // 256) * 144 + b * k * 4 + b * n * 4
+
+
+def sweep_bytes(shapes, batches) -> int:
+    return sum(gemv_bytes(k, n, b) for b in batches for (k, n) in shapes)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 100 ms while running."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(device), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU (oracle port)
+
+class CpuSweep:
+    """The CPU restatement of ops::gemv (oracle/, the checker, used here only as
+    the CPU baseline) over the sweep, or a row sample of it sized to a time budget.
+    Every (shape, batch) is one ops::gemv per activation column, as the
+    reference's batch-1 trait does; rows are split across `threads` pthreads."""
+
+    def __init__(self, shapes, batches, threads: int):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle
+        self.oracle = oracle
+        self.shapes, self.batches, self.threads = shapes, batches, threads
+        self.mats = {(k, n): quant_matrix(k + n, Q4_K, n, k) for (k, n) in shapes}
+        self.xs = {b: activations(900 + b, b, max(k for k, _ in shapes)) for b in batches}
+        k0, n0 = max(shapes, key=lambda s: s[0] * s[1])
+        probe = max(threads * 16, 256)
+        oracle.gemv_rows(Q4_K, self.mats[(k0, n0)], n0, k0, self.xs[1][0, :k0], 0, probe, threads)
+        t = time.perf_counter()
+        oracle.gemv_rows(Q4_K, self.mats[(k0, n0)], n0, k0, self.xs[1][0, :k0], 0, probe, threads)
+        self.elem_rate = probe * k0 / max(time.perf_counter() - t, 1e-6)
+
+    def run(self, budget_s: float):
+        total_elems = sum(n * k * b for b in self.batches for (k, n) in self.shapes)
+        frac = min(1.0, budget_s * self.elem_rate / total_elems)
+        nbytes = 0
+        t = time.perf_counter()
+        for b in self.batches:
+            for (k, n) in self.shapes:
+                rows = max(1, int(n * frac))
+                for j in range(b):
+                    self.oracle.gemv_rows(Q4_K, self.mats[(k, n)], n, k, self.xs[b][j, :k], 0, rows, self.threads)
+                nbytes += rows * (k // 256) * 144 + b * k * 4 + b * rows * 4
+        dt = time.perf_counter() - t
+        desc = (f"Q4_K sweep ({len(self.shapes)} shapes x batches {self.batches}), first {frac:.2%} of each "
+                f"matrix's rows per step, one ops::gemv per activation column, {self.threads} threads")
+        return nbytes / dt / 1e9, desc, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    shapes, batches = Q4K_SWEEP, SWEEP_BATCHES
+    cpu = CpuSweep(shapes, batches, threads)
+    per_step = max(0.02, 120.0 / max(1, args.steps + args.warmup))
+    vals = []
+    desc = ""
+    for i in range(args.warmup + args.steps):
+        v, desc, _ = cpu.run(per_step)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    total = sweep_bytes(shapes, batches)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / (value * 1e9) * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (f64 accumulate)", "data": "synthetic",
+        "config": {"workload": "Q4_K decode GEMV sweep (K->N 4096->4096, 4096->12288, 12288->4096, 2048->151936; "
+                               "batch 1,2,4,8)", "path": "reference CPU path (oracle port of ops::gemv)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU
+
+def run_gpu(args):
+    import torch
+    import strata_cuda as sc
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    shapes, batches = Q4K_SWEEP, SWEEP_BATCHES
+    ctx = sc.Context(local)
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    stream = torch.cuda.Stream()
+
+    # this rank's row shard of every matrix, uploaded `copies` times
+    weights, shard = {}, {}
+    for (k, n) in shapes:
+        r0, r1 = n * rank // world, n * (rank + 1) // world
+        full = quant_matrix(k + n, Q4_K, n, k)
+        rb = (k // 256) * 144
+        part = full[r0 * rb:r1 * rb]
+        copies = max(1, -(-4 * l2 // max(part.nbytes, 1)))
+        weights[(k, n)] = [ctx.upload(part, Q4_K, r1 - r0, k) for _ in range(copies)]
+        shard[(k, n)] = (r0, r1)
+    rot = max(len(v) for v in weights.values())
+    xs = {b: torch.from_numpy(activations(900 + b, b, max(k for k, _ in shapes))).cuda() for b in batches}
+    xk = {(b, k): xs[b][:, :k].contiguous() for b in batches for (k, _) in shapes}
+    ys = {(k, n, b): torch.empty(b, shard[(k, n)][1] - shard[(k, n)][0], device="cuda")
+          for (k, n) in shapes for b in batches}
+    gathered = {(k, n, b): torch.empty(world, b, (n + world - 1) // world, device="cuda")
+                for (k, n) in shapes for b in batches} if world > 1 else None
+
+    def enqueue(step_idx: int, s: int):
+        for b in batches:
+            for (k, n) in shapes:
+                w = weights[(k, n)][step_idx % len(weights[(k, n)])]
+                ctx.gemv_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, s)
+
+    graphs = []
+    with torch.cuda.stream(stream):
+        enqueue(0, stream.cuda_stream)  # warm the kernels before capture
+    stream.synchronize()
+    for i in range(rot):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            enqueue(i, stream.cuda_stream)
+        graphs.append(g)
+    launches_per_step = len(batches) * len(shapes)
+
+    def allgather():
+        for (k, n) in shapes:
+            for b in batches:
+                y = ys[(k, n, b)]
+                pad = gathered[(k, n, b)]
+                chunk = pad.shape[2]
+                src = torch.zeros(b, chunk, device="cuda") if y.shape[1] != chunk else y
+                if y.shape[1] != chunk:
+                    src[:, :y.shape[1]] = y
+                dist.all_gather_into_tensor(pad.view(-1), src.reshape(-1))
+
+    def step(i):
+        graphs[i % rot].replay()
+        if world > 1:
+            allgather()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    t_clock0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    # keep the same load on for >= 1.5 s so the clock record covers it
+    with torch.cuda.stream(stream):
+        i = 0
+        while time.perf_counter() - t_clock0 < 1.5:
+            for _ in range(50):
+                step(i)
+                i += 1
+            stream.synchronize()
+    clk = clocks.stop()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    torch.cuda.synchronize()
+
+    total = sweep_bytes(shapes, batches)
+    value = total * args.steps / (ms / 1e3) / 1e9
+    hbm, peak_kind = peaks()
+
+    # per-case device time: each case as its own graph over its rotated copies
+    cases = []
+    if not args.quick:
+        for b in batches:
+            for (k, n) in shapes:
+                ws = weights[(k, n)]
+                reps = max(1, 64 // len(ws))
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for _ in range(reps):
+                        for w in ws:
+                            ctx.gemv_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, stream.cuda_stream)
+                with torch.cuda.stream(stream):
+                    g.replay()
+                    a0 = torch.cuda.Event(enable_timing=True)
+                    a1 = torch.cuda.Event(enable_timing=True)
+                    a0.record(stream)
+                    for _ in range(5):
+                        g.replay()
+                    a1.record(stream)
+                a1.synchronize()
+                us = a0.elapsed_time(a1) * 1e3 / (5 * reps * len(ws))
+                r0, r1 = shard[(k, n)]
+                gb = gemv_bytes(k, r1 - r0, b) / (us * 1e-6) / 1e9
+                cases.append({"k": k, "n": n, "batch": b, "us": round(us, 2), "gbs": round(gb, 1),
+                              "frac_hbm": round(gb / hbm, 3)})
+                del g
+
+    # end to end through the host-buffer C ABI (pinned host input, result read back)
+    e2e = None
+    if not args.no_e2e and world == 1:
+        hx = {b: torch.from_numpy(activations(900 + b, b, max(k for k, _ in shapes))).pin_memory().numpy()
+              for b in batches}
+        hxk = {(b, k): np.ascontiguousarray(hx[b][:, :k]) for b in batches for (k, _) in shapes}
+        hy = {(k, n, b): np.empty((b, n), np.float32) for (k, n) in shapes for b in batches}
+        lib = sc.lib()
+        import ctypes as C
+
+        def host_step(i):
+            for b in batches:
+                for (k, n) in shapes:
+                    w = weights[(k, n)][i % len(weights[(k, n)])]
+                    x, y = hxk[(b, k)], hy[(k, n, b)]
+                    rc = lib.strata_cuda_gemv(ctx.h, w.handle, x.ctypes.data_as(C.POINTER(C.c_float)),
+                                              y.ctypes.data_as(C.POINTER(C.c_float)), b)
+                    if rc:
+                        ctx.check(rc)
+        for i in range(3):
+            host_step(i)
+        n_e2e = max(10, min(args.steps, 200))
+        t = time.perf_counter()
+        for i in range(n_e2e):
+            host_step(i)
+        dt = time.perf_counter() - t
+        h2d = sum(b * k * 4 for b in batches for (k, _) in shapes)
+        d2h = sum(b * n * 4 for b in batches for (_, n) in shapes)
+        e2e = {"value": round(total * n_e2e / dt / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": n_e2e, "timer": "host perf_counter"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        v, desc, dt = CpuSweep(shapes, batches, threads).run(10.0)
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (Q4_K weights, fp32 accumulate)",
+            "data": "synthetic (seeded PCG64; BASELINE config distributions)",
+            "config": {"workload": "Q4_K decode GEMV sweep: K->N 4096->4096, 4096->12288, 12288->4096, "
+                                   "2048->151936 at batch 1,2,4,8 (16 GEMVs per step, batch-major)",
+                       "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 "
+                             "per matrix), no matrix re-read within 241 MB of traffic",
+                       "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "launch": "CUDA graph per step"},
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(value / hbm, 3), "traffic": None,
+                         "note": f"Q4_K GEMV kernel over the timed sweep; peak = {peak_kind} copy bandwidth"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "cases": cases,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+    del graphs
+    for ws in weights.values():
+        for w in ws:
+            w.free()
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="strata", choices=["strata", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="skip the per-case table")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

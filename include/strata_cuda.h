@@ -1,0 +1,133 @@
+/*
+ * strata_cuda.h — C ABI of the B200 quantized-matmul backend for strata-rs.
+ *
+ * This is the boundary a `strata-backend-cuda` crate binds (`extern "C"`):
+ * plain pointers and sizes, no torch or CUDA types in any signature. Every
+ * function returns a status (STRATA_OK = 0); the message of the last failure
+ * on a context is strata_cuda_last_error(ctx).
+ *
+ * Reference interface being replaced (paths relative to the strata-rs repo):
+ *   trait ComputeBackend ............. crates/strata-core/src/backend.rs:20-51
+ *   ComputeBackend::gemv ............. crates/strata-core/src/backend.rs:25
+ *   ComputeBackend::expert_gemv ...... crates/strata-core/src/backend.rs:28-35
+ *   QuantTensor (rows = OUT) ......... crates/strata-core/src/backend.rs:114-154
+ *   ExpertView ([E][IN][OUT]) ........ crates/strata-core/src/weights.rs:11-34
+ *   dequantize_row ................... crates/strata-gguf/src/dequant.rs:45-61
+ *   MoeLayer::route / combine ........ crates/strata-core/src/moe.rs:48-144
+ *   Error::Backend { message } ....... crates/strata-core/src/error.rs:31-32
+ *
+ * Threading: a context may be shared between threads (the trait is
+ * Send + Sync); calls on one context are serialised by an internal mutex.
+ * Host-buffer calls are synchronous: results are in the output buffer when
+ * the call returns, as the trait requires. The *_dev variants take device
+ * pointers and only enqueue work on the given stream (NULL = the context's
+ * own stream).
+ */
+#ifndef STRATA_CUDA_H
+#define STRATA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define STRATA_CUDA_ABI_VERSION 1
+
+/* Status codes. STRATA_ERR_UNSUPPORTED_QUANT and STRATA_ERR_TRUNCATED are the
+ * two strata_gguf::Error variants dequantize_row returns
+ * (crates/strata-gguf/src/dequant.rs:50-55, :102-105); everything else maps
+ * to strata_core::Error::Backend. */
+enum {
+    STRATA_OK = 0,
+    STRATA_ERR_INVALID = 1,           /* bad argument, shape or handle */
+    STRATA_ERR_UNSUPPORTED_QUANT = 2, /* quant type not on this path */
+    STRATA_ERR_TRUNCATED = 3,         /* byte slice shorter than the shape needs */
+    STRATA_ERR_CUDA = 4,              /* a CUDA runtime call failed */
+    STRATA_ERR_OOM = 5,               /* device allocation failed */
+    STRATA_ERR_TIMEOUT = 6,           /* a bounded wait on the device expired */
+    STRATA_ERR_NCCL = 7,              /* a collective failed */
+    STRATA_ERR_BUDGET = 8             /* the weight budget would be exceeded */
+};
+
+/* Strata ggml type ids accepted here (crates/strata-gguf/src/quant.rs:15-43). */
+enum {
+    STRATA_QUANT_F32 = 0,
+    STRATA_QUANT_F16 = 1,
+    STRATA_QUANT_Q8_0 = 8,
+    STRATA_QUANT_Q4_K = 12,
+    STRATA_QUANT_Q5_K = 13,
+    STRATA_QUANT_Q6_K = 14,
+    STRATA_QUANT_BF16 = 30
+};
+
+typedef struct strata_ctx strata_ctx;       /* one device, one stream */
+typedef struct strata_weight strata_weight; /* a tensor resident in HBM */
+
+/* ---------------------------------------------------------------- context */
+
+int strata_cuda_abi_version(void);
+
+/* ComputeBackend::name (backend.rs:22): always "cuda". */
+const char *strata_cuda_name(void);
+
+/* Creates a context on `device` (its own non-blocking stream, pinned staging). */
+int strata_cuda_create(int device, strata_ctx **out);
+int strata_cuda_destroy(strata_ctx *ctx);
+
+/* Message of the last failure on ctx ("" if none). Valid until the next call. */
+const char *strata_cuda_last_error(const strata_ctx *ctx);
+
+/* Caps the HBM bytes weights may occupy (0 = no cap). The CLI's
+ * --gpu-weights-mib (crates/strata-cli/src/main.rs:116-118) maps here. */
+int strata_cuda_set_weight_budget(strata_ctx *ctx, uint64_t bytes);
+int strata_cuda_resident_bytes(const strata_ctx *ctx, uint64_t *out);
+
+/* Bound, in milliseconds, on every host wait for device work (default 60000).
+ * An expired wait returns STRATA_ERR_TIMEOUT and leaves the context usable. */
+int strata_cuda_set_wait_timeout_ms(strata_ctx *ctx, uint32_t ms);
+
+/* Waits (bounded) for all work enqueued on the context's stream. */
+int strata_cuda_synchronize(strata_ctx *ctx);
+
+/* The context's stream as an opaque cudaStream_t. */
+int strata_cuda_stream(const strata_ctx *ctx, void **stream_out);
+
+/* ---------------------------------------------------------------- weights */
+
+/* Copies a tensor's bytes to HBM unchanged (the strata-gguf payload slice,
+ * GgufFile::tensor_data, crates/strata-gguf/src/reader.rs:425-445).
+ *   dense   (QuantTensor): n_expert = 0, rows = OUT, cols = IN
+ *   experts (ExpertView):  n_expert = E, rows = IN,  cols = OUT
+ * Each row is quantized along `cols`. `len` must cover
+ * max(1, n_expert) * rows * byte_size(cols); cols must be a whole number of
+ * blocks (else STRATA_ERR_TRUNCATED, as dequantize_row). */
+int strata_cuda_upload(strata_ctx *ctx, const uint8_t *bytes, size_t len, uint32_t quant,
+                       int64_t n_expert, int64_t rows, int64_t cols, strata_weight **out);
+int strata_cuda_free_weight(strata_weight *w);
+
+/* Dequantizes rows [row0, row0 + nrows) of expert `expert` (0 for dense)
+ * into out_host (nrows * cols f32). Bit-exact with dequantize_row. */
+int strata_cuda_dequant(strata_ctx *ctx, const strata_weight *w, int64_t expert, int64_t row0,
+                        int64_t nrows, float *out_host);
+
+/* ------------------------------------------------------------ decode GEMV */
+
+/* ComputeBackend::gemv (backend.rs:25) over `batch` (1..8) activation rows:
+ * x is batch x cols f32, y is batch x rows f32 (row-major). */
+int strata_cuda_gemv(strata_ctx *ctx, const strata_weight *w, const float *x, float *y, int batch);
+int strata_cuda_gemv_dev(strata_ctx *ctx, const strata_weight *w, const float *x_dev, float *y_dev,
+                         int batch, void *stream);
+
+/* ComputeBackend::expert_gemv (backend.rs:28-35) for expert e:
+ * x is batch x rows(IN), y is batch x cols(OUT). */
+int strata_cuda_expert_gemv(strata_ctx *ctx, const strata_weight *w, int64_t e, const float *x,
+                            float *y, int batch);
+int strata_cuda_expert_gemv_dev(strata_ctx *ctx, const strata_weight *w, int64_t e,
+                                const float *x_dev, float *y_dev, int batch, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* STRATA_CUDA_H */

@@ -1,0 +1,392 @@
+// runtime.cu — contexts, resident weights and the C ABI of strata_cuda.h.
+//
+// The host side of the backend: it owns the CUDA stream, the pinned staging
+// used by the synchronous (trait-shaped) entry points, the device workspace,
+// and the weights uploaded byte-for-byte. Kernels live in the other .cu files.
+#include "runtime.cuh"
+
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+
+using namespace strata;
+
+namespace strata {
+
+int fail(strata_ctx* ctx, int code, const char* fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        ctx->last_error = buf;
+    }
+    return code;
+}
+
+int cuda_fail(strata_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, e == cudaErrorMemoryAllocation ? STRATA_ERR_OOM : STRATA_ERR_CUDA, "%s: %s (%s)", what,
+                cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int64_t quant_row_bytes(uint32_t quant, int64_t cols) {
+    int be = block_elems(quant), bb = block_bytes(quant);
+    if (be == 0) return -1;
+    return ((cols + be - 1) / be) * bb;
+}
+
+int ensure_device(strata_ctx* ctx, DevBuf& b, size_t bytes, const char* what) {
+    if (b.bytes >= bytes && b.ptr) return STRATA_OK;
+    if (b.ptr) {
+        // the old buffer may still be read by queued work
+        int rc = wait_stream(ctx, ctx->stream);
+        if (rc) return rc;
+        cudaFree(b.ptr);
+        b.ptr = nullptr;
+        b.bytes = 0;
+    }
+    size_t want = bytes < 4096 ? 4096 : bytes;
+    cudaError_t e = cudaMalloc(&b.ptr, want);
+    if (e != cudaSuccess) {
+        b.ptr = nullptr;
+        return cuda_fail(ctx, e, what);
+    }
+    b.bytes = want;
+    return STRATA_OK;
+}
+
+int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what) {
+    if (b.bytes >= bytes && b.ptr) return STRATA_OK;
+    if (b.ptr) {
+        int rc = wait_stream(ctx, ctx->stream);
+        if (rc) return rc;
+        cudaFreeHost(b.ptr);
+        b.ptr = nullptr;
+        b.bytes = 0;
+    }
+    size_t want = bytes < 4096 ? 4096 : bytes;
+    cudaError_t e = cudaMallocHost(&b.ptr, want);
+    if (e != cudaSuccess) {
+        b.ptr = nullptr;
+        return cuda_fail(ctx, e, what);
+    }
+    b.bytes = want;
+    return STRATA_OK;
+}
+
+// Bounded wait: poll an event recorded on `s` until it completes or the
+// context's timeout expires (the device work keeps running in that case; the
+// context stays usable and the caller gets STRATA_ERR_TIMEOUT).
+int wait_stream(strata_ctx* ctx, cudaStream_t s) {
+    cudaError_t e = cudaEventRecord(ctx->done, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventRecord");
+    auto t0 = std::chrono::steady_clock::now();
+    int spins = 0;
+    for (;;) {
+        e = cudaEventQuery(ctx->done);
+        if (e == cudaSuccess) return STRATA_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "device work");
+        auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if ((uint64_t)ms > ctx->wait_timeout_ms)
+            return fail(ctx, STRATA_ERR_TIMEOUT, "device work did not finish within %u ms", ctx->wait_timeout_ms);
+        if (++spins > 64) std::this_thread::yield();
+    }
+}
+
+cudaStream_t pick_stream(strata_ctx* ctx, void* stream) {
+    return stream ? reinterpret_cast<cudaStream_t>(stream) : ctx->stream;
+}
+
+int check_launch(strata_ctx* ctx, const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+    return STRATA_OK;
+}
+
+int check_weight(strata_ctx* ctx, const strata_weight* w, bool expert) {
+    if (!w || w->magic != kWeightMagic) return fail(ctx, STRATA_ERR_INVALID, "invalid weight handle");
+    if (w->ctx != ctx) return fail(ctx, STRATA_ERR_INVALID, "weight belongs to another context");
+    if (expert && w->n_expert == 0) return fail(ctx, STRATA_ERR_INVALID, "expert call on a dense tensor");
+    if (!expert && w->n_expert != 0) return fail(ctx, STRATA_ERR_INVALID, "dense call on an expert tensor");
+    return STRATA_OK;
+}
+
+}  // namespace strata
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" {
+
+int strata_cuda_abi_version(void) { return STRATA_CUDA_ABI_VERSION; }
+
+const char* strata_cuda_name(void) { return "cuda"; }
+
+int strata_cuda_create(int device, strata_ctx** out) {
+    if (!out) return STRATA_ERR_INVALID;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return STRATA_ERR_CUDA;
+    if (device < 0 || device >= n) return STRATA_ERR_INVALID;
+    if (cudaSetDevice(device) != cudaSuccess) return STRATA_ERR_CUDA;
+    strata_ctx* ctx = new strata_ctx();
+    ctx->device = device;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+        delete ctx;
+        return STRATA_ERR_CUDA;
+    }
+    ctx->sm_count = prop.multiProcessorCount;
+    ctx->l2_bytes = prop.l2CacheSize;
+    ctx->cc_major = prop.major;
+    ctx->cc_minor = prop.minor;
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess) {
+        delete ctx;
+        return STRATA_ERR_CUDA;
+    }
+    *out = ctx;
+    return STRATA_OK;
+}
+
+int strata_cuda_destroy(strata_ctx* ctx) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    cudaSetDevice(ctx->device);
+    int rc = wait_stream(ctx, ctx->stream);
+    comm_release(ctx);
+    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work})
+        if (b->ptr) cudaFree(b->ptr);
+    for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host})
+        if (b->ptr) cudaFreeHost(b->ptr);
+    cudaEventDestroy(ctx->done);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return rc;
+}
+
+const char* strata_cuda_last_error(const strata_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+int strata_cuda_set_weight_budget(strata_ctx* ctx, uint64_t bytes) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    ctx->budget_bytes = bytes;
+    return STRATA_OK;
+}
+
+int strata_cuda_resident_bytes(const strata_ctx* ctx, uint64_t* out) {
+    if (!ctx || !out) return STRATA_ERR_INVALID;
+    *out = ctx->resident_bytes;
+    return STRATA_OK;
+}
+
+int strata_cuda_set_wait_timeout_ms(strata_ctx* ctx, uint32_t ms) {
+    if (!ctx || ms == 0) return STRATA_ERR_INVALID;
+    ctx->wait_timeout_ms = ms;
+    return STRATA_OK;
+}
+
+int strata_cuda_synchronize(strata_ctx* ctx) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    cudaSetDevice(ctx->device);
+    return wait_stream(ctx, ctx->stream);
+}
+
+int strata_cuda_stream(const strata_ctx* ctx, void** out) {
+    if (!ctx || !out) return STRATA_ERR_INVALID;
+    *out = reinterpret_cast<void*>(ctx->stream);
+    return STRATA_OK;
+}
+
+int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32_t quant, int64_t n_expert,
+                       int64_t rows, int64_t cols, strata_weight** out) {
+    if (!ctx || !out) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    *out = nullptr;
+    int be = block_elems(quant);
+    if (be == 0) return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "quant type id %u is not on the CUDA path", quant);
+    if (n_expert < 0 || rows < 0 || cols <= 0 || (!bytes && len > 0))
+        return fail(ctx, STRATA_ERR_INVALID, "bad shape n_expert=%lld rows=%lld cols=%lld", (long long)n_expert,
+                    (long long)rows, (long long)cols);
+    if (cols % be != 0)
+        return fail(ctx, STRATA_ERR_TRUNCATED, "cols=%lld is not a whole number of %d-element blocks",
+                    (long long)cols, be);
+    int64_t rb = quant_row_bytes(quant, cols);
+    int64_t mats = n_expert > 0 ? n_expert : 1;
+    int64_t need = mats * rows * rb;
+    if ((int64_t)len < need)
+        return fail(ctx, STRATA_ERR_TRUNCATED, "tensor needs %lld bytes, got %zu", (long long)need, len);
+    if (ctx->budget_bytes && ctx->resident_bytes + (uint64_t)need > ctx->budget_bytes)
+        return fail(ctx, STRATA_ERR_BUDGET, "upload of %lld bytes exceeds the weight budget (%llu resident of %llu)",
+                    (long long)need, (unsigned long long)ctx->resident_bytes,
+                    (unsigned long long)ctx->budget_bytes);
+    cudaSetDevice(ctx->device);
+    strata_weight* w = new strata_weight();
+    w->ctx = ctx;
+    w->quant = quant;
+    w->n_expert = n_expert;
+    w->rows = rows;
+    w->cols = cols;
+    w->row_bytes = rb;
+    w->bytes = (size_t)need;
+    if (need > 0) {
+        cudaError_t e = cudaMalloc(&w->dev, (size_t)need);
+        if (e != cudaSuccess) {
+            delete w;
+            return cuda_fail(ctx, e, "cudaMalloc(weights)");
+        }
+        e = cudaMemcpy(w->dev, bytes, (size_t)need, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(w->dev);
+            delete w;
+            return cuda_fail(ctx, e, "cudaMemcpy(weights)");
+        }
+    }
+    ctx->resident_bytes += (uint64_t)need;
+    *out = w;
+    return STRATA_OK;
+}
+
+int strata_cuda_free_weight(strata_weight* w) {
+    if (!w || w->magic != kWeightMagic) return STRATA_ERR_INVALID;
+    strata_ctx* ctx = w->ctx;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    cudaSetDevice(ctx->device);
+    int rc = wait_stream(ctx, ctx->stream);
+    if (w->dev) cudaFree(w->dev);
+    ctx->resident_bytes -= (uint64_t)w->bytes;
+    w->magic = 0;
+    delete w;
+    return rc;
+}
+
+int strata_cuda_dequant(strata_ctx* ctx, const strata_weight* w, int64_t expert, int64_t row0, int64_t nrows,
+                        float* out_host) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    if (!w || w->magic != kWeightMagic || w->ctx != ctx) return fail(ctx, STRATA_ERR_INVALID, "invalid weight handle");
+    int64_t mats = w->n_expert > 0 ? w->n_expert : 1;
+    if (expert < 0 || expert >= mats || row0 < 0 || nrows < 0 || row0 + nrows > w->rows || (!out_host && nrows))
+        return fail(ctx, STRATA_ERR_INVALID, "dequant range out of bounds");
+    if (nrows == 0) return STRATA_OK;
+    cudaSetDevice(ctx->device);
+    size_t nbytes = (size_t)(nrows * w->cols) * sizeof(float);
+    int rc = ensure_device(ctx, ctx->y_dev, nbytes, "cudaMalloc(dequant out)");
+    if (!rc) rc = ensure_pinned(ctx, ctx->y_host, nbytes, "cudaMallocHost(dequant out)");
+    if (rc) return rc;
+    const uint8_t* base = w->dev + (expert * w->rows + row0) * w->row_bytes;
+    if (launch_dequant(w->quant, base, w->row_bytes, w->cols, nrows, (float*)ctx->y_dev.ptr, ctx->stream))
+        return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no dequant kernel for quant %u", w->quant);
+    if ((rc = check_launch(ctx, "dequant kernel"))) return rc;
+    cudaError_t e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, nbytes, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
+    if ((rc = wait_stream(ctx, ctx->stream))) return rc;
+    memcpy(out_host, ctx->y_host.ptr, nbytes);
+    return STRATA_OK;
+}
+
+// ---- decode GEMV
+
+static int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
+                        cudaStream_t s) {
+    if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
+    if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
+        return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
+    GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch, ctx->sm_count};
+    if (launch_gemv(w->quant, a, s))
+        return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no gemv kernel for quant %u", w->quant);
+    return check_launch(ctx, "gemv kernel");
+}
+
+int strata_cuda_gemv_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
+                         void* stream) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = check_weight(ctx, w, false);
+    if (rc) return rc;
+    cudaSetDevice(ctx->device);
+    return gemv_enqueue(ctx, w, x_dev, y_dev, batch, pick_stream(ctx, stream));
+}
+
+int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int batch) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = check_weight(ctx, w, false);
+    if (rc) return rc;
+    if (!x || !y) return fail(ctx, STRATA_ERR_INVALID, "null x or y");
+    if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
+    cudaSetDevice(ctx->device);
+    size_t xb = (size_t)batch * (size_t)w->cols * sizeof(float);
+    size_t yb = (size_t)batch * (size_t)w->rows * sizeof(float);
+    if ((rc = ensure_device(ctx, ctx->x_dev, xb, "cudaMalloc(x)"))) return rc;
+    if ((rc = ensure_device(ctx, ctx->y_dev, yb, "cudaMalloc(y)"))) return rc;
+    if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
+    if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
+    memcpy(ctx->x_host.ptr, x, xb);
+    cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
+    if ((rc = gemv_enqueue(ctx, w, (const float*)ctx->x_dev.ptr, (float*)ctx->y_dev.ptr, batch, ctx->stream)))
+        return rc;
+    e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
+    if ((rc = wait_stream(ctx, ctx->stream))) return rc;
+    memcpy(y, ctx->y_host.ptr, yb);
+    return STRATA_OK;
+}
+
+// ---- expert GEMV
+
+static int expert_enqueue(strata_ctx* ctx, const strata_weight* w, int64_t e, const float* x_dev, float* y_dev,
+                          int batch, cudaStream_t s) {
+    if (e < 0 || e >= w->n_expert) return fail(ctx, STRATA_ERR_INVALID, "expert %lld out of range", (long long)e);
+    if (batch < 1 || batch > 64) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..64", batch);
+    int64_t wf = expert_gemv_work_floats(w->rows, w->cols, ctx->sm_count);
+    int rc = ensure_device(ctx, ctx->work, (size_t)wf * sizeof(float), "cudaMalloc(workspace)");
+    if (rc) return rc;
+    ExpertGemvArgs a{w->dev + e * w->rows * w->row_bytes, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch,
+                     ctx->sm_count};
+    int k = launch_expert_gemv_ws(w->quant, a, (float*)ctx->work.ptr, wf, s);
+    if (k) return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no expert gemv kernel for quant %u (%d)", w->quant, k);
+    return check_launch(ctx, "expert gemv kernel");
+}
+
+int strata_cuda_expert_gemv_dev(strata_ctx* ctx, const strata_weight* w, int64_t e, const float* x_dev,
+                                float* y_dev, int batch, void* stream) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = check_weight(ctx, w, true);
+    if (rc) return rc;
+    cudaSetDevice(ctx->device);
+    return expert_enqueue(ctx, w, e, x_dev, y_dev, batch, pick_stream(ctx, stream));
+}
+
+int strata_cuda_expert_gemv(strata_ctx* ctx, const strata_weight* w, int64_t e, const float* x, float* y,
+                            int batch) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = check_weight(ctx, w, true);
+    if (rc) return rc;
+    if (!x || !y) return fail(ctx, STRATA_ERR_INVALID, "null x or y");
+    if (batch < 1 || batch > 64) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..64", batch);
+    cudaSetDevice(ctx->device);
+    size_t xb = (size_t)batch * (size_t)w->rows * sizeof(float);
+    size_t yb = (size_t)batch * (size_t)w->cols * sizeof(float);
+    if ((rc = ensure_device(ctx, ctx->x_dev, xb, "cudaMalloc(x)"))) return rc;
+    if ((rc = ensure_device(ctx, ctx->y_dev, yb, "cudaMalloc(y)"))) return rc;
+    if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
+    if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
+    memcpy(ctx->x_host.ptr, x, xb);
+    cudaError_t err = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
+    if (err != cudaSuccess) return cuda_fail(ctx, err, "cudaMemcpyAsync(H2D)");
+    if ((rc = expert_enqueue(ctx, w, e, (const float*)ctx->x_dev.ptr, (float*)ctx->y_dev.ptr, batch, ctx->stream)))
+        return rc;
+    err = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
+    if (err != cudaSuccess) return cuda_fail(ctx, err, "cudaMemcpyAsync(D2H)");
+    if ((rc = wait_stream(ctx, ctx->stream))) return rc;
+    memcpy(y, ctx->y_host.ptr, yb);
+    return STRATA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// runtime.cuh — the host-side state behind the opaque handles of strata_cuda.h.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/strata_cuda.h"
+#include "kernels.cuh"
+#include "quant.cuh"
+
+namespace strata {
+
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+struct PinnedBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct CommState;  // comm.cu
+
+}  // namespace strata
+
+struct strata_ctx {
+    int device = 0;
+    int sm_count = 0;
+    int l2_bytes = 0;
+    int cc_major = 0, cc_minor = 0;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;
+    std::mutex mu;
+    std::string last_error;
+    uint64_t budget_bytes = 0;
+    uint64_t resident_bytes = 0;
+    uint32_t wait_timeout_ms = 60000;
+    strata::DevBuf x_dev, y_dev, work;
+    strata::PinnedBuf x_host, y_host;
+    strata::CommState* comm = nullptr;
+};
+
+constexpr uint32_t kWeightMagic = 0x57545253u;  // "SRTW"
+
+struct strata_weight {
+    uint32_t magic = kWeightMagic;
+    strata_ctx* ctx = nullptr;
+    uint32_t quant = 0;
+    int64_t n_expert = 0, rows = 0, cols = 0, row_bytes = 0;
+    uint8_t* dev = nullptr;
+    size_t bytes = 0;
+};
+
+namespace strata {
+
+int fail(strata_ctx* ctx, int code, const char* fmt, ...);
+int cuda_fail(strata_ctx* ctx, cudaError_t e, const char* what);
+int64_t quant_row_bytes(uint32_t quant, int64_t cols);
+int ensure_device(strata_ctx* ctx, DevBuf& b, size_t bytes, const char* what);
+int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what);
+int wait_stream(strata_ctx* ctx, cudaStream_t s);
+cudaStream_t pick_stream(strata_ctx* ctx, void* stream);
+int check_launch(strata_ctx* ctx, const char* what);
+int check_weight(strata_ctx* ctx, const strata_weight* w, bool expert);
+
+// expert.cu
+int64_t expert_gemv_work_floats(int64_t IN, int64_t OUT, int sm_count);
+int launch_expert_gemv_ws(uint32_t quant, const ExpertGemvArgs& a, float* work, int64_t work_floats,
+                          cudaStream_t s);
+
+// comm.cu
+void comm_release(strata_ctx* ctx);
+
+}  // namespace strata

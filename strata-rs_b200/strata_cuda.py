@@ -1,0 +1,248 @@
+"""Python binding of libstrata_cuda.so (the C ABI in include/strata_cuda.h).
+
+This is the host-side mirror of strata-core's ComputeBackend seam
+(crates/strata-core/src/backend.rs:20-51) for Python callers, tests and the
+benchmark: `CudaBackend.gemv` / `expert_gemv` take the same arguments and
+meaning as the trait methods (a QuantTensor or ExpertView, host f32 slices,
+an unused scratch), and failures raise `BackendError` carrying the status
+code, as `strata_core::Error::Backend` would.
+
+There is no fallback: if the shared library is missing or no CUDA device is
+present, construction raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("STRATA_CUDA_LIB", HERE / "libstrata_cuda.so"))
+
+# status codes (include/strata_cuda.h)
+OK, ERR_INVALID, ERR_UNSUPPORTED_QUANT, ERR_TRUNCATED, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_NCCL, ERR_BUDGET = range(9)
+
+# Strata ggml type ids (crates/strata-gguf/src/quant.rs:15-43)
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176),
+         Q6_K: (256, 210)}
+NAMES = {F32: "F32", F16: "F16", BF16: "BF16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+
+
+def byte_size(quant: int, n: int) -> int:
+    """QuantType::byte_size (crates/strata-gguf/src/quant.rs:178-180)."""
+    bs, ts = BLOCK[quant]
+    return -(-n // bs) * ts
+
+
+class BackendError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libstrata_cuda.so once; raises if it is not built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(f"{LIB_PATH} is not built (run strata-rs_b200/build.py)")
+        L = C.CDLL(str(LIB_PATH))
+        vp, i32, i64, u32, u64, sz = C.c_void_p, C.c_int, C.c_int64, C.c_uint32, C.c_uint64, C.c_size_t
+        fp = C.POINTER(C.c_float)
+        sig = {
+            "strata_cuda_abi_version": (i32, []),
+            "strata_cuda_name": (C.c_char_p, []),
+            "strata_cuda_create": (i32, [i32, C.POINTER(vp)]),
+            "strata_cuda_destroy": (i32, [vp]),
+            "strata_cuda_last_error": (C.c_char_p, [vp]),
+            "strata_cuda_set_weight_budget": (i32, [vp, u64]),
+            "strata_cuda_resident_bytes": (i32, [vp, C.POINTER(u64)]),
+            "strata_cuda_set_wait_timeout_ms": (i32, [vp, u32]),
+            "strata_cuda_synchronize": (i32, [vp]),
+            "strata_cuda_stream": (i32, [vp, C.POINTER(vp)]),
+            "strata_cuda_upload": (i32, [vp, vp, sz, u32, i64, i64, i64, C.POINTER(vp)]),
+            "strata_cuda_free_weight": (i32, [vp]),
+            "strata_cuda_dequant": (i32, [vp, vp, i64, i64, i64, fp]),
+            "strata_cuda_gemv": (i32, [vp, vp, fp, fp, i32]),
+            "strata_cuda_gemv_dev": (i32, [vp, vp, vp, vp, i32, vp]),
+            "strata_cuda_expert_gemv": (i32, [vp, vp, i64, fp, fp, i32]),
+            "strata_cuda_expert_gemv_dev": (i32, [vp, vp, i64, vp, vp, i32, vp]),
+        }
+        for name, (res, args) in sig.items():
+            if not hasattr(L, name):
+                continue
+            f = getattr(L, name)
+            f.restype, f.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+@dataclass
+class QuantTensor:
+    """strata_core::backend::QuantTensor (backend.rs:114-154): rows = OUT, cols = IN."""
+    name: str
+    quant: int
+    rows: int
+    cols: int
+    data: np.ndarray  # uint8
+
+    def row_bytes(self) -> int:
+        return byte_size(self.quant, self.cols)
+
+
+@dataclass
+class ExpertView:
+    """strata_core::weights::ExpertView (weights.rs:11-34): [n_expert][rows = IN][cols = OUT]."""
+    name: str
+    quant: int
+    n_expert: int
+    rows: int
+    cols: int
+    data: np.ndarray  # uint8
+
+
+class Weight:
+    """A tensor resident in HBM (uploaded byte-for-byte)."""
+
+    def __init__(self, ctx: "Context", handle: C.c_void_p, quant: int, n_expert: int, rows: int, cols: int):
+        self.ctx, self.handle, self.quant = ctx, handle, quant
+        self.n_expert, self.rows, self.cols = n_expert, rows, cols
+
+    def free(self):
+        if self.handle:
+            lib().strata_cuda_free_weight(self.handle)
+            self.handle = None
+
+
+class Context:
+    """One device + stream (strata_cuda_create)."""
+
+    def __init__(self, device: int = 0):
+        L = lib()
+        h = C.c_void_p()
+        rc = L.strata_cuda_create(device, C.byref(h))
+        if rc != OK:
+            raise BackendError(rc, f"strata_cuda_create(device={device}) failed")
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            lib().strata_cuda_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def check(self, rc: int):
+        if rc != OK:
+            raise BackendError(rc, lib().strata_cuda_last_error(self.h).decode())
+
+    @property
+    def stream(self) -> int:
+        s = C.c_void_p()
+        self.check(lib().strata_cuda_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def synchronize(self):
+        self.check(lib().strata_cuda_synchronize(self.h))
+
+    def set_weight_budget(self, nbytes: int):
+        self.check(lib().strata_cuda_set_weight_budget(self.h, nbytes))
+
+    def set_wait_timeout_ms(self, ms: int):
+        self.check(lib().strata_cuda_set_wait_timeout_ms(self.h, ms))
+
+    def resident_bytes(self) -> int:
+        v = C.c_uint64()
+        self.check(lib().strata_cuda_resident_bytes(self.h, C.byref(v)))
+        return v.value
+
+    def upload(self, data: np.ndarray, quant: int, rows: int, cols: int, n_expert: int = 0) -> Weight:
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        h = C.c_void_p()
+        self.check(lib().strata_cuda_upload(self.h, data.ctypes.data, data.nbytes, quant, n_expert, rows, cols,
+                                            C.byref(h)))
+        return Weight(self, h, quant, n_expert, rows, cols)
+
+    def dequant(self, w: Weight, row0: int = 0, nrows: int | None = None, expert: int = 0) -> np.ndarray:
+        nrows = w.rows - row0 if nrows is None else nrows
+        out = np.empty((nrows, w.cols), np.float32)
+        self.check(lib().strata_cuda_dequant(self.h, w.handle, expert, row0, nrows, _fptr(out)))
+        return out
+
+    def gemv(self, w: Weight, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        batch = 1 if x.ndim == 1 else x.shape[0]
+        y = np.empty((batch, w.rows), np.float32)
+        self.check(lib().strata_cuda_gemv(self.h, w.handle, _fptr(x), _fptr(y), batch))
+        return y[0] if x.ndim == 1 else y
+
+    def expert_gemv(self, w: Weight, e: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        batch = 1 if x.ndim == 1 else x.shape[0]
+        y = np.empty((batch, w.cols), np.float32)
+        self.check(lib().strata_cuda_expert_gemv(self.h, w.handle, e, _fptr(x), _fptr(y), batch))
+        return y[0] if x.ndim == 1 else y
+
+    # device-pointer variants (int addresses, e.g. torch.Tensor.data_ptr())
+    def gemv_dev(self, w: Weight, x_ptr: int, y_ptr: int, batch: int, stream: int = 0):
+        self.check(lib().strata_cuda_gemv_dev(self.h, w.handle, x_ptr, y_ptr, batch, stream or None))
+
+    def expert_gemv_dev(self, w: Weight, e: int, x_ptr: int, y_ptr: int, batch: int, stream: int = 0):
+        self.check(lib().strata_cuda_expert_gemv_dev(self.h, w.handle, e, x_ptr, y_ptr, batch, stream or None))
+
+
+class CudaBackend:
+    """strata-core's ComputeBackend over the CUDA path (name() == "cuda").
+
+    Weights are uploaded on first use and cached by (data address, length),
+    like the wgpu backend's name-keyed cache (crates/strata-backend-wgpu/src/gpu.rs:271,287).
+    """
+
+    def __init__(self, device: int = 0):
+        self.ctx = Context(device)
+        self._cache: dict[tuple[int, int, int], Weight] = {}
+
+    def name(self) -> str:
+        return lib().strata_cuda_name().decode()
+
+    def _resident(self, data: np.ndarray, quant: int, rows: int, cols: int, n_expert: int) -> Weight:
+        key = (data.ctypes.data, data.nbytes, n_expert)
+        w = self._cache.get(key)
+        if w is None:
+            w = self.ctx.upload(data, quant, rows, cols, n_expert)
+            self._cache[key] = w
+        return w
+
+    def gemv(self, w: QuantTensor, x: np.ndarray, y: np.ndarray, scratch=None) -> None:
+        if x.shape[-1] != w.cols or y.shape[-1] != w.rows:
+            raise BackendError(ERR_INVALID, f"gemv {w.name}: x/y do not match {w.rows}x{w.cols}")
+        dw = self._resident(w.data, w.quant, w.rows, w.cols, 0)
+        y[...] = self.ctx.gemv(dw, x)
+
+    def expert_gemv(self, w: ExpertView, e: int, x: np.ndarray, y: np.ndarray, scratch=None) -> None:
+        if x.shape[-1] != w.rows or y.shape[-1] != w.cols:
+            raise BackendError(ERR_INVALID, f"expert_gemv {w.name}: x/y do not match {w.rows}x{w.cols}")
+        dw = self._resident(w.data, w.quant, w.rows, w.cols, w.n_expert)
+        y[...] = self.ctx.expert_gemv(dw, e, x)
+
+    def close(self):
+        for w in self._cache.values():
+            w.free()
+        self._cache.clear()
+        self.ctx.close()

@@ -1,0 +1,167 @@
+"""Pins the CPU oracle (oracle/liboracle.so) before anything is compared with it.
+
+* The reference's own known-answer tests (tests/golden/reference_kats.json).
+* A second, vectorised numpy restatement of every block format, bit for bit
+  (the reference pins Q4_K and Q5_K by no test of its own).
+* The scalar codecs the `half` crate provides (f16 -> f32 over all 65,536
+  patterns; bf16 round-to-nearest-even against numpy).
+* Routing invariants of MoeLayer::route (crates/strata-core/src/moe.rs:48-92).
+"""
+import numpy as np
+import pytest
+
+import oracle
+import numpy_dequant
+from golden import reference_cases as rc
+from synth import bf16_bits, quant_blocks, rng, Q4_K, Q5_K, Q6_K, Q8_0
+
+
+@pytest.mark.parametrize("case", rc.KATS["dequant"], ids=lambda c: c["name"])
+def test_reference_dequant_known_answers(case):
+    out = oracle.dequantize_row(case["quant"], rc.dequant_case(case), case["n"])
+    for idx, want in case["expect"]:
+        assert out[idx] == np.float32(want)
+
+
+@pytest.mark.parametrize("quant,n", [tuple(c) for c in rc.KATS["finite_lcg"]["cases"]])
+def test_reference_every_type_finite_on_lcg_bytes(quant, n):
+    nbytes = int(oracle.lib().orc_byte_size(quant, n))
+    block = rc.lcg_block(quant, nbytes, rc.KATS["finite_lcg"])
+    out = oracle.dequantize_row(quant, block, n)
+    assert np.all(np.isfinite(out))
+
+
+@pytest.mark.parametrize("case", rc.KATS["gemv"], ids=lambda c: c["name"])
+def test_reference_gemv_known_answers(case):
+    q, w, rows, cols, x = rc.gemv_case(case)
+    y = oracle.gemv(q, w, rows, cols, x)
+    deq = oracle.dequantize(q, w, rows, cols).astype(np.float64)
+    expect = deq @ x.astype(np.float64)
+    if case.get("exact"):
+        assert y[0] == np.float32(deq[0, 0] * 1.0 - 2.0)
+    else:
+        assert np.max(np.abs(y.astype(np.float64) - expect)) < case["abs_tol"]
+
+
+def test_reference_q8_0_gemv_value():
+    # ops_tests.rs:55-58: expect = sum_j ((j % 7 - 3) * 0.5) * x[j] in f64
+    case = rc.KATS["gemv"][0]
+    q, w, rows, cols, x = rc.gemv_case(case)
+    y = oracle.gemv(q, w, rows, cols, x)
+    expect = sum(float((j % 7) - 3) * 0.5 * float(x[j]) for j in range(32))
+    assert abs(float(y[0]) - expect) < 1e-4
+
+
+@pytest.mark.parametrize("quant", [Q8_0, Q4_K, Q5_K, Q6_K])
+def test_oracle_matches_independent_numpy_restatement(quant):
+    g = rng(100 + quant)
+    blocks = quant_blocks(g, quant, 512)
+    # also cover extreme scales: subnormal, max and negative fp16 d / dmin
+    extremes = np.array([0x0001, 0x03FF, 0x7BFF, 0xFBFF, 0x8001, 0x3C00], np.uint16).view(np.uint8)
+    off = 208 if quant == Q6_K else 0
+    for i in range(6):
+        blocks[i, off:off + 2] = extremes[2 * i:2 * i + 2]
+        if quant in (Q4_K, Q5_K):
+            blocks[i, 2:4] = extremes[2 * ((i + 1) % 6):2 * ((i + 1) % 6) + 2]
+    bs = 32 if quant == Q8_0 else 256
+    got = oracle.dequantize_row(quant, blocks.reshape(-1), blocks.shape[0] * bs)
+    want = numpy_dequant.DEQUANT[quant](blocks)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_q4_k_hand_derived_answer():
+    # d = 0.5, dmin = 0.25; scale byte 0 = 3 (sc0), byte 4 = 2 (m0); q[0] = 0x5A
+    # element 0 = 0.5*3*0xA - 0.25*2 = 14.5 ; element 32 uses sub-block 1 (sc1 = 0)
+    b = np.zeros(144, np.uint8)
+    b[0:2] = rc.f16_bytes(0.5)
+    b[2:4] = rc.f16_bytes(0.25)
+    b[4] = 3
+    b[8] = 2
+    b[16] = 0x5A
+    out = oracle.dequantize_row(Q4_K, b, 256)
+    assert out[0] == np.float32(14.5)
+    assert out[32] == np.float32(0.0)  # d*0*5 - dmin*0 (m1 = byte 5 & 63 = 0)
+    # sub-block 4 takes its scale from the high bits: sc4 = (q[8]&15) | (q[0]>>6)<<4
+    b[4] = 0xC3  # sc0 = 3, top bits 3 -> sc4 high part 3<<4 = 48
+    b[12] = 0x01  # q[8] low nibble 1 -> sc4 = 49
+    b[16 + 64] = 0x02  # chunk 2 (sub-block 4) element 128 -> q = 2
+    out = oracle.dequantize_row(Q4_K, b, 256)
+    assert out[128] == np.float32(0.5 * 49 * 2)
+
+
+def test_q5_k_hand_derived_answer():
+    # the qh bit 1 << (2c + hi) adds 16 (dequant.rs:290-295)
+    b = np.zeros(176, np.uint8)
+    b[0:2] = rc.f16_bytes(1.0)
+    b[4] = 1      # sc0 = 1
+    b[5] = 1      # sc1 = 1
+    b[16] = 0b11  # qh[0]: bit0 -> element 0 (+16), bit1 -> element 32 (+16)
+    b[48] = 0x21  # ql[0]: low 1, high 2
+    out = oracle.dequantize_row(Q5_K, b, 256)
+    assert out[0] == np.float32(17.0)
+    assert out[32] == np.float32(18.0)
+
+
+def test_f16_to_f32_all_patterns():
+    L = oracle.lib()
+    bits = np.arange(65536, dtype=np.uint32)
+    got = np.array([L.orc_f16_to_f32(int(h)) for h in bits], np.float32)
+    want = bits.astype(np.uint16).view(np.float16).astype(np.float32)
+    finite = np.isfinite(want)
+    assert np.array_equal(got[finite].view(np.uint32), want[finite].view(np.uint32))
+    assert np.array_equal(np.isinf(got), np.isinf(want))
+    nan = np.isnan(want)
+    # NaN: payload kept, quiet bit set (half 2.7.1)
+    g = got[nan].view(np.uint32)
+    h = bits[nan]
+    assert np.array_equal(g, ((h & 0x8000) << 16) | 0x7FC00000 | ((h & 0x3FF) << 13))
+
+
+def test_bf16_round_matches_numpy_rne():
+    L = oracle.lib()
+    g = rng(7)
+    x = np.concatenate([g.standard_normal(20000).astype(np.float32),
+                        (g.integers(0, 2**32, 20000, dtype=np.uint64).astype(np.uint32) & 0x7F7FFFFF).view(np.float32)])
+    # exact ties: low half = 0x8000 with even and odd high halves
+    ties = (np.arange(0x3F80, 0x3F90, dtype=np.uint32) << 16 | 0x8000).view(np.float32)
+    x = np.concatenate([x, ties])
+    got = np.array([L.orc_f32_to_bf16_bits(float(v)) for v in x], np.uint16)
+    assert np.array_equal(got, bf16_bits(x))
+
+
+def test_route_top_k_order_and_renorm():
+    g = rng(3)
+    logits = g.standard_normal((16, 256)).astype(np.float32)
+    ids, w = oracle.route_logits(logits, 8)
+    for t in range(16):
+        assert np.all(np.diff(ids[t]) > 0), "ids come back in ascending order"
+        lg = logits[t].astype(np.float32)
+        p = np.exp((lg - lg.max()).astype(np.float32)).astype(np.float32)
+        top = np.argsort(-p, kind="stable")[:8]
+        assert set(top.tolist()) == set(ids[t].tolist())
+        assert abs(float(w[t].astype(np.float64).sum()) - 1.0) < 1e-6
+
+
+def test_route_ties_go_to_the_lower_index():
+    logits = np.zeros((1, 16), np.float32)
+    ids, w = oracle.route_logits(logits, 4)
+    assert ids[0].tolist() == [0, 1, 2, 3]
+    assert np.all(w[0] == np.float32(0.25))
+
+
+def test_dequantize_row_truncation_errors():
+    L = oracle.lib()
+    out = np.empty(256, np.float32)
+    b = np.zeros(143, np.uint8)
+    assert L.orc_dequantize_row(Q4_K, b.ctypes.data, b.nbytes, oracle._fp(out), 256) == oracle.ERR_TRUNCATED
+    b = np.zeros(144, np.uint8)
+    assert L.orc_dequantize_row(Q4_K, b.ctypes.data, b.nbytes, oracle._fp(out), 200) == oracle.ERR_TRUNCATED
+    assert L.orc_dequantize_row(99, b.ctypes.data, b.nbytes, oracle._fp(out), 256) == oracle.ERR_UNSUPPORTED
+
+
+def test_threaded_gemv_equals_single_thread():
+    w = quant_blocks(rng(11), Q4_K, 64 * 8).reshape(-1)
+    x = rng(12).standard_normal((2, 2048)).astype(np.float32)
+    a = oracle.gemv(Q4_K, w, 64, 2048, x, threads=1)
+    b = oracle.gemv(Q4_K, w, 64, 2048, x, threads=4)
+    assert np.array_equal(a, b)
