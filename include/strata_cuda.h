@@ -88,6 +88,13 @@ int strata_cuda_resident_bytes(const strata_ctx *ctx, uint64_t *out);
  * An expired wait returns STRATA_ERR_TIMEOUT and leaves the context usable. */
 int strata_cuda_set_wait_timeout_ms(strata_ctx *ctx, uint32_t ms);
 
+/* Which kernels serve the decode GEMV: AUTO picks the tensor-core kernel for
+ * Q4_K / Q5_K and the CUDA-core kernels otherwise; the others force one family
+ * (TENSOR_CORES fails with STRATA_ERR_UNSUPPORTED_QUANT where it has no kernel).
+ * Both families meet the same tolerance; the switch exists for diagnosis. */
+enum { STRATA_GEMV_AUTO = 0, STRATA_GEMV_CUDA_CORES = 1, STRATA_GEMV_TENSOR_CORES = 2 };
+int strata_cuda_set_gemv_path(strata_ctx *ctx, int path);
+
 /* Waits (bounded) for all work enqueued on the context's stream. */
 int strata_cuda_synchronize(strata_ctx *ctx);
 
@@ -115,7 +122,11 @@ int strata_cuda_dequant(strata_ctx *ctx, const strata_weight *w, int64_t expert,
 /* ------------------------------------------------------------ decode GEMV */
 
 /* ComputeBackend::gemv (backend.rs:25) over `batch` (1..8) activation rows:
- * x is batch x cols f32, y is batch x rows f32 (row-major). */
+ * x is batch x cols f32, y is batch x rows f32 (row-major). The _dev variant
+ * needs x 16-byte aligned; its first call may size the context's workspace
+ * (a device allocation), so make one call before capturing it in a graph.
+ * The workspace is per context: _dev calls of one context on different
+ * streams must not overlap. */
 int strata_cuda_gemv(strata_ctx *ctx, const strata_weight *w, const float *x, float *y, int batch);
 int strata_cuda_gemv_dev(strata_ctx *ctx, const strata_weight *w, const float *x_dev, float *y_dev,
                          int batch, void *stream);

@@ -4,10 +4,27 @@
 // rounding per operation (__fmul_rn / __fsub_rn / __fadd_rn cannot be fused
 // into an FMA), so the output is bit-identical to strata-gguf's
 // dequantize_row (crates/strata-gguf/src/dequant.rs:45-61).
+//
+// Non-finite scales: the reference runs on x86-64, whose SSE/AVX arithmetic
+// returns the (quietened) NaN operand when one input is NaN, the first
+// operand's when both are, and the negative "indefinite" NaN 0xFFC00000 for
+// an invalid operation on non-NaN inputs (inf * 0, inf - inf). CUDA returns a
+// canonical NaN instead, so each operation below re-derives the x86 result
+// whenever its CUDA result is NaN.
 #include "quant.cuh"
 #include "kernels.cuh"
 
 namespace strata {
+
+__device__ __forceinline__ float x86_nan(float r, float a, float b) {
+    if (!isnan(r)) return r;
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(0xFFC00000u);
+}
+__device__ __forceinline__ float mul_x86(float a, float b) { return x86_nan(__fmul_rn(a, b), a, b); }
+__device__ __forceinline__ float sub_x86(float a, float b) { return x86_nan(__fsub_rn(a, b), a, b); }
+__device__ __forceinline__ float add_x86(float a, float b) { return x86_nan(__fadd_rn(a, b), a, b); }
 
 __device__ __forceinline__ uint32_t rd16(const uint8_t* b) { return (uint32_t)b[0] | ((uint32_t)b[1] << 8); }
 
@@ -24,7 +41,7 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* b, int j) {
     } else if constexpr (Q == kQ8_0) {
         // dequant.rs:123-128: (qs[j] as i8) as f32 * d
         float d = f16_bits_to_f32_exact(rd16(b));
-        return __fmul_rn((float)(int8_t)b[2 + j], d);
+        return mul_x86((float)(int8_t)b[2 + j], d);
     } else if constexpr (Q == kQ4_K) {
         // dequant.rs:247-270: chunk c of 64, low nibbles then high nibbles
         float d = f16_bits_to_f32_exact(rd16(b));
@@ -34,8 +51,8 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* b, int j) {
         scale_min_k4(2 * c + hi, b + 4, sc, m);
         uint32_t byte = b[16 + 32 * c + (l & 31)];
         uint32_t q = hi ? (byte >> 4) : (byte & 0xFu);
-        float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(mn, (float)m);
-        return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+        float d1 = mul_x86(d, (float)sc), m1 = mul_x86(mn, (float)m);
+        return sub_x86(mul_x86(d1, (float)q), m1);
     } else if constexpr (Q == kQ5_K) {
         // dequant.rs:272-302: + 16 when the qh bit (u1 / u2 = 1 << (2c + hi)) is set
         float d = f16_bits_to_f32_exact(rd16(b));
@@ -46,8 +63,8 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* b, int j) {
         uint32_t byte = b[48 + 32 * c + ll];
         uint32_t q = hi ? (byte >> 4) : (byte & 0xFu);
         float h = (b[16 + ll] & (1u << (2 * c + hi))) ? 16.0f : 0.0f;
-        float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(mn, (float)m);
-        return __fsub_rn(__fmul_rn(d1, __fadd_rn((float)q, h)), m1);
+        float d1 = mul_x86(d, (float)sc), m1 = mul_x86(mn, (float)m);
+        return sub_x86(mul_x86(d1, add_x86((float)q, h)), m1);
     } else if constexpr (Q == kQ6_K) {
         // dequant.rs:208-234: halves of 128; quarter g = l / 32 selects
         // (ql lo / ql+32 lo / ql hi / ql+32 hi) and qh bits 2g..2g+1; u8 scales
@@ -60,7 +77,7 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* b, int j) {
         uint32_t nib = (g >= 2) ? (qlb >> 4) : (qlb & 0xFu);
         int q = (int)(nib | (((qh[l] >> (2 * g)) & 3u) << 4)) - 32;
         float s = (float)sc[(l >> 4) + 2 * g];
-        return __fmul_rn(__fmul_rn(d, s), (float)q);
+        return mul_x86(mul_x86(d, s), (float)q);
     } else {
         return 0.0f;
     }

@@ -156,7 +156,7 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     cudaSetDevice(ctx->device);
     int rc = wait_stream(ctx, ctx->stream);
     comm_release(ctx);
-    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work})
+    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag})
         if (b->ptr) cudaFree(b->ptr);
     for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host})
         if (b->ptr) cudaFreeHost(b->ptr);
@@ -184,6 +184,13 @@ int strata_cuda_resident_bytes(const strata_ctx* ctx, uint64_t* out) {
 int strata_cuda_set_wait_timeout_ms(strata_ctx* ctx, uint32_t ms) {
     if (!ctx || ms == 0) return STRATA_ERR_INVALID;
     ctx->wait_timeout_ms = ms;
+    return STRATA_OK;
+}
+
+int strata_cuda_set_gemv_path(strata_ctx* ctx, int path) {
+    if (!ctx || path < STRATA_GEMV_AUTO || path > STRATA_GEMV_TENSOR_CORES) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    ctx->gemv_path = path;
     return STRATA_OK;
 }
 
@@ -295,6 +302,15 @@ static int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
         return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
     GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch, ctx->sm_count};
+    if (ctx->gemv_path != STRATA_GEMV_CUDA_CORES && gemv_mma_supported(w->quant, a)) {
+        int64_t need = gemv_mma_work_bytes(w->cols, batch);
+        int rc = ensure_device(ctx, ctx->xfrag, (size_t)(need > (4 << 20) ? need : (4 << 20)), "cudaMalloc(x limbs)");
+        if (rc) return rc;
+        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, s);
+        return check_launch(ctx, "tensor-core gemv kernel");
+    }
+    if (ctx->gemv_path == STRATA_GEMV_TENSOR_CORES)
+        return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no tensor-core gemv for quant %u", w->quant);
     if (launch_gemv(w->quant, a, s))
         return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no gemv kernel for quant %u", w->quant);
     return check_launch(ctx, "gemv kernel");

@@ -37,7 +37,8 @@ struct strata_ctx {
     uint64_t budget_bytes = 0;
     uint64_t resident_bytes = 0;
     uint32_t wait_timeout_ms = 60000;
-    strata::DevBuf x_dev, y_dev, work;
+    int gemv_path = 0;  // STRATA_GEMV_AUTO / _CUDA_CORES / _TENSOR_CORES
+    strata::DevBuf x_dev, y_dev, work, xfrag;
     strata::PinnedBuf x_host, y_host;
     strata::CommState* comm = nullptr;
 };
@@ -69,6 +70,11 @@ int check_weight(strata_ctx* ctx, const strata_weight* w, bool expert);
 int64_t expert_gemv_work_floats(int64_t IN, int64_t OUT, int sm_count);
 int launch_expert_gemv_ws(uint32_t quant, const ExpertGemvArgs& a, float* work, int64_t work_floats,
                           cudaStream_t s);
+
+// gemv_mma.cu
+int64_t gemv_mma_work_bytes(int64_t K, int batch);
+bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, cudaStream_t s);
 
 // comm.cu
 void comm_release(strata_ctx* ctx);

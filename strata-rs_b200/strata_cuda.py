@@ -66,6 +66,7 @@ def lib() -> C.CDLL:
             "strata_cuda_resident_bytes": (i32, [vp, C.POINTER(u64)]),
             "strata_cuda_set_wait_timeout_ms": (i32, [vp, u32]),
             "strata_cuda_synchronize": (i32, [vp]),
+            "strata_cuda_set_gemv_path": (i32, [vp, i32]),
             "strata_cuda_stream": (i32, [vp, C.POINTER(vp)]),
             "strata_cuda_upload": (i32, [vp, vp, sz, u32, i64, i64, i64, C.POINTER(vp)]),
             "strata_cuda_free_weight": (i32, [vp]),
@@ -157,6 +158,11 @@ class Context:
         s = C.c_void_p()
         self.check(lib().strata_cuda_stream(self.h, C.byref(s)))
         return s.value or 0
+
+    GEMV_AUTO, GEMV_CUDA_CORES, GEMV_TENSOR_CORES = 0, 1, 2
+
+    def set_gemv_path(self, path: int):
+        self.check(lib().strata_cuda_set_gemv_path(self.h, path))
 
     def synchronize(self):
         self.check(lib().strata_cuda_synchronize(self.h))

@@ -227,3 +227,50 @@ def test_bounded_wait_times_out_and_recovers():
     assert rel_err(c.gemv(w, xs), oracle.gemv(Q4_K, data, n, k, xs, threads=8)) < TOL
     w.free()
     c.close()
+
+
+# ---- the two decode kernel families (tensor-core and CUDA-core) on the same inputs
+
+@pytest.mark.parametrize("path", [sc.Context.GEMV_CUDA_CORES, sc.Context.GEMV_TENSOR_CORES])
+@pytest.mark.parametrize("quant", [Q4_K, Q5_K])
+@pytest.mark.parametrize("batch", [1, 2, 4, 5, 8])
+@pytest.mark.parametrize("rows,cols", [(203, 2048), (1000, 256), (64, 12288)])
+def test_gemv_both_paths(quant, batch, rows, cols, path, threads):
+    c = sc.Context(0)
+    c.set_gemv_path(path)
+    data = quant_matrix(2000 + quant + cols, quant, rows, cols)
+    x = activations(2001 + batch, batch, cols)
+    w = c.upload(data, quant, rows, cols)
+    got = c.gemv(w, x)
+    want = oracle.gemv(quant, data, rows, cols, x, threads=threads)
+    assert rel_err(got, want) < TOL
+    w.free()
+    c.close()
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1e-6, 1.0, 1e4, 1e30])
+def test_gemv_activation_magnitudes(ctx, scale, threads):
+    """fp16 activation limbs carry a per-(column, block) power-of-two scale:
+    tiny, huge, zero and mixed-magnitude activations stay within tolerance."""
+    rows, cols = 96, 4096
+    data = quant_matrix(2100, Q4_K, rows, cols)
+    x = activations(2101, 3, cols) * np.float32(scale)
+    x[1, :512] = 0.0                                   # an all-zero block
+    x[2, ::7] *= np.float32(1e-3)                      # mixed magnitudes in one block
+    w = ctx.upload(data, Q4_K, rows, cols)
+    got = ctx.gemv(w, x.astype(np.float32))
+    want = oracle.gemv(Q4_K, data, rows, cols, x.astype(np.float32), threads=threads)
+    for b in range(3):
+        assert rel_err(got[b], want[b]) < TOL, (scale, b)
+    w.free()
+
+
+def test_tensor_core_path_rejects_other_types():
+    c = sc.Context(0)
+    c.set_gemv_path(sc.Context.GEMV_TENSOR_CORES)
+    w = c.upload(quant_matrix(2200, Q6_K, 8, 256), Q6_K, 8, 256)
+    with pytest.raises(sc.BackendError) as e:
+        c.gemv(w, np.zeros(256, np.float32))
+    assert e.value.code == sc.ERR_UNSUPPORTED_QUANT
+    w.free()
+    c.close()
