@@ -11,19 +11,25 @@
 //   16 q for a high nibble) and one HFMA2 with per-sub-block constants turns
 //   that into sc*q, exactly (the fused multiply-add rounds once, and the
 //   result is a small integer).
-// * MMA rows 0..7 are 8 weight rows; rows 8..15 carry the same rows' 6-bit
-//   mins m_j, so D[8+r] = sum_k m_j(k) x_k comes out of the same instruction.
+// * An MMA covers 16 weight rows x 16 weights. The min term
+//   sum_j m_j * (sum of x over sub-block j) is one more MMA per block whose 16
+//   K slots are the block's 8 sub-blocks (and 8 zeros): A holds the rows'
+//   6-bit mins, B the per-sub-block activation sums (as fp16 limbs).
 // * B operand (fp16): each activation column is split into two fp16 limbs,
 //   x*s = hi + lo * 2^-11 (22 significant bits), with a power-of-two scale s
 //   per (column, block) chosen from the block's max |x|, so fp16 can neither
 //   overflow nor lose the small entries. Columns are (batch, limb) pairs.
-// * D (fp32) accumulates one 256-weight block (16 mma.sync m16n8k16), then is
-//   folded into fp32 accumulators with d / dmin / s. The products are exact
-//   and the sums are fp32, which is what the 1e-3 tolerance needs.
+// * D (fp32) accumulates one 256-weight block (16 mma.sync m16n8k16, plus the
+//   min MMA), then is folded into fp32 accumulators with d / dmin / s. The
+//   products are exact and the sums are fp32, which is what the 1e-3
+//   tolerance needs.
 //
-// Work split: a CTA owns 8*G rows; its warps split the K blocks; partial sums
-// meet in shared memory. A prologue kernel writes the activation limbs in the
-// order the B fragments are read (one 8-byte load per lane per mma).
+// Work split: row tiles of 16 rows; a producer warp streams each tile into
+// shared memory with bulk copies while 8 consumer warps split its K blocks
+// (see the kernel). A prologue kernel writes the activation limbs in
+// the order the B fragments are read (one 8-byte load per lane per mma); the
+// GEMV is launched as its programmatic dependent, so it starts streaming
+// weights while the prologue runs and waits only before reading the limbs.
 #include <cuda_fp16.h>
 
 #include "kernels.cuh"
@@ -47,15 +53,38 @@ __device__ __forceinline__ void mma16816(float d[4], uint32_t a0, uint32_t a1, u
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// d = (a & b) | c in one LOP3
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// d = A*B (accumulator input zero)
+__device__ __forceinline__ void mma16816_z(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    const float z = 0.0f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
 // ---------------------------------------------------------------- prologue
 //
-// XF layout: [blk][s = sub-block 0..7][i = word 0..7][n = column 0..ncols)
-// of uint2 {b0, b1}, where for e = 256 blk + 32 s + 4 i
-//   b0 = half2(v[e], v[e+2]), b1 = half2(v[e+1], v[e+3]),
+// XF layout: [blk][t = 0..3][i = word 0..7][n = column 0..2*batch) of
+// uint4 {b0(2t), b1(2t), b0(2t+1), b1(2t+1)}: the B fragments of the low- and
+// high-nibble MMAs of word i, where for sub-block s and e = 256 blk + 32 s + 4 i
+//   b0(s) = half2(v[e], v[e+2]), b1(s) = half2(v[e+1], v[e+3]),
 // v = limb (n & 1) of batch row (n >> 1) of x, scaled by XS^-1.
 // XS layout: [batch][blk] float: the power of two that undoes the scaling.
+// XQ layout: [blk][t = 0..3][n][2] __half: the sums of v over sub-blocks 2t
+// and 2t+1, limb (n & 1) of batch (n >> 1) -- the B operand of the min MMA.
 __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int batch, uint2* __restrict__ XF,
-                                    float* __restrict__ XS) {
+                                    float* __restrict__ XS, __half* __restrict__ XQ) {
+    // XF is addressed here in uint2 halves of the uint4 entries
+    asm volatile("griddepcontrol.launch_dependents;");
     const int nblk = (int)(K / 256);
     const int lane = threadIdx.x & 31;
     const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -72,8 +101,8 @@ __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int 
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
     // scale so that max |x| * s lies in [0.5, 1): s = 2^(126 - exp(max))
     int e = (int)((__float_as_uint(mx) >> 23) & 0xFF);
-    if (e == 0 || e == 0xFF) e = 127;       // zero / denormal / non-finite: no scaling
-    int se = 253 - e;                        // biased exponent of s
+    if (e == 0 || e == 0xFF) e = 127;  // zero, denormal or non-finite maximum: s = 1/2
+    int se = 253 - e;                  // biased exponent of s
     se = se < 1 ? 1 : (se > 254 ? 254 : se);
     const float s = __uint_as_float((uint32_t)se << 23);
     const float inv = __uint_as_float((uint32_t)(254 - se) << 23);
@@ -87,6 +116,16 @@ __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int 
     }
     const int ncols = 2 * batch;
     const int s_blk = lane >> 2;
+    float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+    if ((lane & 3) == 0) {
+        const __half shi = __float2half_rn(sum);
+        const __half slo = __float2half_rn((sum - __half2float(shi)) * 2048.0f);
+        __half* q = XQ + (((int64_t)blk * 4 + (s_blk >> 1)) * ncols + 2 * b) * 2 + (s_blk & 1);
+        q[0] = shi;
+        q[2] = slo;
+    }
 #pragma unroll
     for (int w = 0; w < 2; ++w) {
         const int i = 2 * (lane & 3) + w;
@@ -96,35 +135,59 @@ __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int 
         fh.y = h2u(__halves2half2(hi[o + 1], hi[o + 3]));
         fl.x = h2u(__halves2half2(lo[o + 0], lo[o + 2]));
         fl.y = h2u(__halves2half2(lo[o + 1], lo[o + 3]));
-        uint2* dst = XF + (((int64_t)blk * 8 + s_blk) * 8 + i) * ncols + 2 * b;
+        // entry (blk, t = s/2, i, n) is 2 uint2; sub-block parity picks the half
+        uint2* dst = XF + ((((int64_t)blk * 4 + (s_blk >> 1)) * 8 + i) * ncols + 2 * b) * 2 + (s_blk & 1);
         dst[0] = fh;
-        dst[1] = fl;
+        dst[2] = fl;
     }
 }
 
 // ---------------------------------------------------------------- main kernel
 
-struct BlockRegs {
-    uint4 hd;      // d, dmin, scales[12]
-    uint4 qa, qb;  // this lane's 32 quant bytes (chunk t of the block)
-    uint4 ha, hb;  // Q5_K: the block's 32 qh bytes
-};
-
-template <uint32_t Q>
-__device__ __forceinline__ void load_block(const uint8_t* __restrict__ blk, int t, BlockRegs& r) {
-    r.hd = __ldg(reinterpret_cast<const uint4*>(blk));
-    if constexpr (Q == kQ4_K) {
-        const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * t);
-        r.qa = __ldg(q);
-        r.qb = __ldg(q + 1);
-    } else {
-        const uint4* q = reinterpret_cast<const uint4*>(blk + 48 + 32 * t);
-        r.qa = __ldg(q);
-        r.qb = __ldg(q + 1);
-        const uint4* h = reinterpret_cast<const uint4*>(blk + 16);
-        r.ha = __ldg(h);
-        r.hb = __ldg(h + 1);
+// mbarrier / bulk-copy helpers (shared-memory addresses as 32-bit offsets)
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait on a phase parity: false (and *err set) if the phase has not
+// completed within about a second (a stage's copies take microseconds).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+    uint64_t t0 = 0;
+    for (long long i = 0; i < kSpinLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 255) == 0) {
+            const uint64_t now = global_ns();
+            if (i == 0) t0 = now;
+            else if (now - t0 > 1000000000ull) break;
+        }
     }
+    if (err) atomicExch(err, 1);
+    return false;
+}
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
 __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int i) {
@@ -134,194 +197,335 @@ __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int 
     }
 }
 
-template <uint32_t Q, int G, int NT>
-__global__ void __launch_bounds__(kMmaWarps * 32)
-gemv_kq_mma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int nblk,
-                   const uint2* __restrict__ XF, const float* __restrict__ XS, int batch,
-                   float* __restrict__ Y) {
-    constexpr int BB = block_bytes(Q);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int ncols = 2 * batch;
-    const int64_t row0 = (int64_t)blockIdx.x * (8 * G);
-    const int kb0 = warp * nblk / kMmaWarps, kb1 = (warp + 1) * nblk / kMmaWarps;
+constexpr int kStages = 3;     // smem ring depth
+constexpr int kConsumers = 4;  // consumer warps per CTA
+constexpr int kBpw = 2;        // K blocks per consumer warp per stage
+constexpr int kChunk = kConsumers * kBpw;  // K blocks per stage
+constexpr int kTileRows = 16;
 
-    const uint8_t* rowp[G];
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi) {
-        int64_t row = row0 + 8 * gi + g;
-        row = row < N ? row : N - 1;
-        rowp[gi] = W + row * row_bytes;
-    }
-    // per-lane constants: PRMT selector for bytes 2(t&1), 2(t&1)+1 under 0x64
-    const uint32_t sel = (4u << 12) | ((uint32_t)(2 * (t & 1) + 1) << 8) | (4u << 4) | (uint32_t)(2 * (t & 1));
+// One (16-row tile, K block) work item of a consumer warp: rows g and g+8 of
+// the tile, block kb (its bytes in shared memory at `blk0` / `blk1`), folded
+// into acc. NB is the batch; its 2*NB (batch, limb) columns fill
+// NT = ceil(2*NB / 8) n8 tiles. `xfl` / `xql` point at this lane's fragment
+// column of block 0. The 16 sc*q MMAs alternate between two accumulator chains.
+template <uint32_t Q, int NB>
+__device__ __forceinline__ void mma_block(const uint8_t* blk0, const uint8_t* blk1, const uint4* const (&xfl)[(2 * NB + 7) / 8],
+                                          const uint32_t* const (&xql)[(2 * NB + 7) / 8], const float* __restrict__ XS,
+                                          int kb, int nblk, int t, uint32_t sel, float (&acc)[(2 * NB + 7) / 8][4]) {
+    constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
+    constexpr int CH = 1;  // accumulator chains per nibble half
+    constexpr int QOFF = (Q == kQ4_K) ? 16 : 48;
     const __half2 k1024 = __float2half2_rn(1024.0f);
     const __half2 kneg1024 = __float2half2_rn(-1024.0f);
     const __half2 k1_16 = __float2half2_rn(0.0625f);
     const __half2 kneg64 = __float2half2_rn(-64.0f);
+    const uint8_t* blk[2] = {blk0, blk1};
+    float d_acc[NT][2 * CH][4], d_min[NT][4];
+    // masks kept in registers so each nibble extraction is one LOP3
+    const uint32_t kLoMask = 0x000F000Fu, kHiMask = 0x00F000F0u, kMagic = 0x64006400u;
 
-    float acc[G][NT][2];
+    // per row (r = 0: row g, r = 1: row g + 8): quant bytes, scale constants and mins
+    uint4 qa[2], qb[2], ha[2], hb[2];
+    __half2 sAB[2], cA[2], sB16[2], cB[2];
+    uint32_t mAB[2];
+    float dd[2], dm[2];
 #pragma unroll
-    for (int gi = 0; gi < G; ++gi)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[gi][nt][0] = acc[gi][nt][1] = 0.0f;
-
-    BlockRegs cur[G], nxt[G];
-    if (kb0 < kb1) {
-#pragma unroll
-        for (int gi = 0; gi < G; ++gi) load_block<Q>(rowp[gi] + (int64_t)kb0 * BB, t, cur[gi]);
+    for (int r = 0; r < 2; ++r) {
+        const uint4 hd = *reinterpret_cast<const uint4*>(blk[r]);
+        qa[r] = *reinterpret_cast<const uint4*>(blk[r] + QOFF + 32 * t);
+        qb[r] = *reinterpret_cast<const uint4*>(blk[r] + QOFF + 32 * t + 16);
+        if constexpr (Q == kQ5_K) {
+            ha[r] = *reinterpret_cast<const uint4*>(blk[r] + 16);
+            hb[r] = *reinterpret_cast<const uint4*>(blk[r] + 32);
+        }
+        dd[r] = f16_bits_to_f32(hd.x & 0xFFFFu);
+        dm[r] = f16_bits_to_f32(hd.x >> 16);
+        uint32_t sl, sh, ml, mh;
+        scales_k4_packed(hd.y, hd.z, hd.w, sl, sh, ml, mh);
+        const uint32_t sw = t < 2 ? sl : sh, mw = t < 2 ? ml : mh;
+        sAB[r] = __hsub2(u2h(__byte_perm(sw, 0x00006464u, sel)), k1024);
+        mAB[r] = h2u(__hsub2(u2h(__byte_perm(mw, 0x00006464u, sel)), k1024));
+        cA[r] = __hmul2(__low2half2(sAB[r]), kneg1024);
+        sB16[r] = __hmul2(__high2half2(sAB[r]), k1_16);
+        cB[r] = __hmul2(__high2half2(sAB[r]), kneg64);
     }
-    for (int kb = kb0; kb < kb1; ++kb) {
-        if (kb + 1 < kb1) {
+    // min MMA: K slots 2t, 2t+1 = sub-blocks 2t, 2t+1 (A: this lane's mins; B: sub-block sums)
 #pragma unroll
-            for (int gi = 0; gi < G; ++gi) load_block<Q>(rowp[gi] + (int64_t)(kb + 1) * BB, t, nxt[gi]);
-        }
-        // activation fragments of this block: sub-blocks 2t (low) and 2t+1 (high), words 0..7
-        const uint2* xf = XF + (int64_t)kb * 64 * ncols;
-        float d_acc[G][NT][4];
-#pragma unroll
-        for (int gi = 0; gi < G; ++gi)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) d_acc[gi][nt][c] = 0.0f;
-
-        // per-row, per-lane scale constants
-        __half2 sAA[G], cA[G], sB16[G], cB[G], mAA[G], mBB[G];
-        float dd[G], dm[G];
-#pragma unroll
-        for (int gi = 0; gi < G; ++gi) {
-            const uint4 hd = cur[gi].hd;
-            dd[gi] = f16_bits_to_f32(hd.x & 0xFFFFu);
-            dm[gi] = f16_bits_to_f32(hd.x >> 16);
-            uint32_t sl, sh, ml, mh;
-            scales_k4_packed(hd.y, hd.z, hd.w, sl, sh, ml, mh);
-            const uint32_t sw = t < 2 ? sl : sh, mw = t < 2 ? ml : mh;
-            const __half2 sAB = __hsub2(u2h(__byte_perm(sw, 0x00006464u, sel)), k1024);
-            const __half2 mAB = __hsub2(u2h(__byte_perm(mw, 0x00006464u, sel)), k1024);
-            sAA[gi] = __low2half2(sAB);
-            const __half2 sBB = __high2half2(sAB);
-            cA[gi] = __hmul2(sAA[gi], kneg1024);
-            sB16[gi] = __hmul2(sBB, k1_16);
-            cB[gi] = __hmul2(sBB, kneg64);
-            mAA[gi] = __low2half2(mAB);
-            mBB[gi] = __high2half2(mAB);
-        }
+    for (int nt = 0; nt < NT; ++nt) mma16816_z(d_min[nt], mAB[0], mAB[1], 0u, 0u, __ldg(xql[nt] + kb * (4 * NC)), 0u);
 
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            uint2 blo[NT], bhi[NT];
+    for (int i = 0; i < 8; ++i) {
+        uint4 bf[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int n = 8 * nt + g;
-                if (n < ncols) {
-                    blo[nt] = __ldg(xf + ((2 * t) * 8 + i) * ncols + n);
-                    bhi[nt] = __ldg(xf + ((2 * t + 1) * 8 + i) * ncols + n);
-                } else {
-                    blo[nt] = make_uint2(0u, 0u);
-                    bhi[nt] = make_uint2(0u, 0u);
-                }
+        for (int nt = 0; nt < NT; ++nt) bf[nt] = __ldg(xfl[nt] + (kb * 32 + i) * NC);
+        uint32_t a_lo0[2], a_lo1[2], a_hi0[2], a_hi1[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint32_t w = word_of(qa[r], qb[r], i);
+            const uint32_t w8 = w >> 8;
+            uint32_t lo0 = and_or(w, kLoMask, kMagic);
+            uint32_t lo1 = and_or(w8, kLoMask, kMagic);
+            uint32_t hi0 = and_or(w, kHiMask, kMagic);
+            uint32_t hi1 = and_or(w8, kHiMask, kMagic);
+            if constexpr (Q == kQ5_K) {
+                // qh byte l holds the 5th bit of element l of every sub-block:
+                // bit 2t for this lane's low sub-block, bit 2t+1 for the high one.
+                const uint32_t h = word_of(ha[r], hb[r], i) >> (2 * t);
+                lo0 = and_or(h << 4, 0x00100010u, lo0);
+                lo1 = and_or(h >> 4, 0x00100010u, lo1);
+                hi0 = and_or(h << 7, 0x01000100u, hi0);
+                hi1 = and_or(h >> 1, 0x01000100u, hi1);
             }
-#pragma unroll
-            for (int gi = 0; gi < G; ++gi) {
-                const uint32_t w = word_of(cur[gi].qa, cur[gi].qb, i);
-                const uint32_t w8 = w >> 8;
-                uint32_t lo0 = (w & 0x000F000Fu) | 0x64006400u;
-                uint32_t lo1 = (w8 & 0x000F000Fu) | 0x64006400u;
-                uint32_t hi0 = (w & 0x00F000F0u) | 0x64006400u;
-                uint32_t hi1 = (w8 & 0x00F000F0u) | 0x64006400u;
-                if constexpr (Q == kQ5_K) {
-                    // qh byte l holds the 5th bit of element l of every sub-block:
-                    // bit 2t for this lane's low sub-block, bit 2t+1 for the high one.
-                    const uint32_t h = word_of(cur[gi].ha, cur[gi].hb, i) >> (2 * t);
-                    lo0 |= (h << 4) & 0x00100010u;
-                    lo1 |= (h >> 4) & 0x00100010u;
-                    hi0 |= (h << 7) & 0x01000100u;
-                    hi1 |= (h >> 1) & 0x01000100u;
-                }
-                const uint32_t a_lo0 = h2u(__hfma2(u2h(lo0), sAA[gi], cA[gi]));
-                const uint32_t a_lo1 = h2u(__hfma2(u2h(lo1), sAA[gi], cA[gi]));
-                const uint32_t a_hi0 = h2u(__hfma2(u2h(hi0), sB16[gi], cB[gi]));
-                const uint32_t a_hi1 = h2u(__hfma2(u2h(hi1), sB16[gi], cB[gi]));
-                const uint32_t mA = h2u(mAA[gi]), mB = h2u(mBB[gi]);
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    mma16816(d_acc[gi][nt], a_lo0, mA, a_lo1, mA, blo[nt].x, blo[nt].y);
-                    mma16816(d_acc[gi][nt], a_hi0, mB, a_hi1, mB, bhi[nt].x, bhi[nt].y);
-                }
-            }
+            a_lo0[r] = h2u(__hfma2(u2h(lo0), __low2half2(sAB[r]), cA[r]));
+            a_lo1[r] = h2u(__hfma2(u2h(lo1), __low2half2(sAB[r]), cA[r]));
+            a_hi0[r] = h2u(__hfma2(u2h(hi0), sB16[r], cB[r]));
+            a_hi1[r] = h2u(__hfma2(u2h(hi1), sB16[r], cB[r]));
         }
-        // fold this block: columns 2t (limb 0) and 2t+1 (limb 1) of batch 4 nt + t
+        const int ch = (CH == 1) ? 0 : 2 * (i & 1);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const int b = 4 * nt + t;
-            const float xs = b < batch ? __ldg(XS + (int64_t)b * nblk + kb) : 0.0f;
-#pragma unroll
-            for (int gi = 0; gi < G; ++gi) {
-                const float ds = dd[gi] * xs, ms = dm[gi] * xs;
-                acc[gi][nt][0] = fmaf(ds, d_acc[gi][nt][0], fmaf(-ms, d_acc[gi][nt][2], acc[gi][nt][0]));
-                acc[gi][nt][1] = fmaf(ds, d_acc[gi][nt][1], fmaf(-ms, d_acc[gi][nt][3], acc[gi][nt][1]));
+            if (i < CH) {  // first mma of each chain starts from zero
+                mma16816_z(d_acc[nt][ch], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[nt].x, bf[nt].y);
+                mma16816_z(d_acc[nt][ch + 1], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[nt].z, bf[nt].w);
+            } else {
+                mma16816(d_acc[nt][ch], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[nt].x, bf[nt].y);
+                mma16816(d_acc[nt][ch + 1], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[nt].z, bf[nt].w);
             }
         }
-#pragma unroll
-        for (int gi = 0; gi < G; ++gi) cur[gi] = nxt[gi];
     }
-
-    // combine the warps' partial sums
-    __shared__ float red[kMmaWarps][G][NT][32];
+    // fold this block: D columns 2t (limb 0) and 2t+1 (limb 1) of batch 4 nt + t;
+    // D rows g (c = 0, 1) and g + 8 (c = 2, 3). Columns past the batch hold
+    // garbage (their lanes loaded a clamped column) and are never stored.
 #pragma unroll
-    for (int gi = 0; gi < G; ++gi)
+    for (int nt = 0; nt < NT; ++nt) {
+        const int b = min(4 * nt + t, NB - 1);
+        const float xs = __ldg(XS + b * nblk + kb);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) red[warp][gi][nt][lane] = fmaf(acc[gi][nt][1], 1.0f / 2048.0f, acc[gi][nt][0]);
-    __syncthreads();
-    if (warp < G * NT) {
-        const int gi = warp / NT, nt = warp % NT;
-        float v = 0.0f;
+        for (int c = 0; c < 4; ++c) {
+            const int r = c >> 1;
+            float v = d_acc[nt][0][c];
 #pragma unroll
-        for (int w = 0; w < kMmaWarps; ++w) v += red[w][gi][nt][lane];
-        const int b = 4 * nt + t;
-        const int64_t row = row0 + 8 * gi + g;
-        if (b < batch && row < N) Y[(int64_t)b * N + row] = v;
+            for (int ch = 1; ch < 2 * CH; ++ch) v += d_acc[nt][ch][c];
+            acc[nt][c] = fmaf(dd[r] * xs, v, fmaf(-dm[r] * xs, d_min[nt][c], acc[nt][c]));
+        }
     }
 }
 
-template <uint32_t Q, int G, int NT>
-void launch_mma(const GemvArgs& a, uint2* xf, float* xs, cudaStream_t s) {
+// Persistent, warp-specialised kernel. CTA c takes 16-row tiles c, c + grid,
+// ...; each tile is cut into stages of kChunk K blocks. The last warp (the
+// producer) copies every stage into a kStages-deep shared-memory ring with one
+// bulk copy per row (a row's blocks are contiguous bytes), completing on the
+// slot's `full` mbarrier; consumer warp w computes blocks kBpw*w .. kBpw*w +
+// kBpw - 1 of each stage and releases the slot through its `empty` mbarrier. Consumers keep their
+// partial sums across a tile's stages and combine them in shared memory when
+// the tile ends. Every wait is bounded; a timeout sets *err and the CTA stops.
+template <uint32_t Q, int NB>
+__global__ void __launch_bounds__((kConsumers + 1) * 32, 3)
+gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
+                   const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
+                   float* __restrict__ Y, int* __restrict__ err) {
+    constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
+    constexpr int BB = block_bytes(Q);
+    // smem stride of one row of a stage: its kChunk blocks plus 16 bytes, so
+    // that the 8 rows a 128-bit fragment read touches start 4 banks apart
+    // (kChunk * BB is a multiple of 128 bytes, which would put them all on
+    // the same banks)
+    constexpr int ROWB = kChunk * BB + 16;
+    constexpr int STAGE = kTileRows * ROWB;
+    extern __shared__ __align__(128) uint8_t ring[];  // kStages * STAGE
+    __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
+    __shared__ float red[2][kConsumers][NT][2][32];
+    __shared__ int abort_flag;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ntiles = (N + kTileRows - 1) / kTileRows;
+    const int nchunks = (nblk + kChunk - 1) / kChunk;
+    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int nstages = my_tiles * nchunks;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(smem_u32(&full_bar[i]), 1);
+            mbar_init(smem_u32(&empty_bar[i]), kConsumers);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kConsumers) {
+        // ---------------- producer: the weights do not depend on the prologue
+        // (abort decisions are made warp-uniform: the loop has __syncwarp)
+        for (int j = 0; j < nstages; ++j) {
+            const int slot = j % kStages;
+            bool ok = true;
+            if (j >= kStages) ok = mbar_wait(smem_u32(&empty_bar[slot]), ((j / kStages) - 1) & 1, err);
+            ok = __all_sync(0xFFFFFFFFu, ok) && __shfl_sync(0xFFFFFFFFu, *(volatile int*)&abort_flag, 0) == 0;
+            if (!ok) {
+                abort_flag = 1;
+                break;
+            }
+            const int tile = blockIdx.x + (j / nchunks) * gridDim.x;
+            const int c0 = (j % nchunks) * kChunk;
+            const int nb = min(kChunk, nblk - c0);
+            const uint32_t bytes = (uint32_t)(nb * BB);
+            const uint32_t fb = smem_u32(&full_bar[slot]);
+            if (lane == 0) mbar_expect_tx(fb, bytes * kTileRows);
+            __syncwarp();
+            if (lane < kTileRows) {
+                int row = tile * kTileRows + lane;
+                row = row < N ? row : N - 1;
+                const uint8_t* src = W + (int64_t)row * row_bytes + (int64_t)c0 * BB;
+                bulk_g2s(smem_u32(ring + slot * STAGE + lane * ROWB), src, bytes, fb);
+            }
+        }
+        // drain: wait (bounded) for the copies still in flight before exiting
+        for (int j = max(0, nstages - kStages); j < nstages; ++j)
+            mbar_wait(smem_u32(&full_bar[j % kStages]), (j / kStages) & 1, nullptr);
+        return;
+    }
+
+    // ---------------- consumers
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t sel = (4u << 12) | ((uint32_t)(2 * (t & 1) + 1) << 8) | (4u << 4) | (uint32_t)(2 * (t & 1));
+    // lane (g, t) feeds B column 8 nt + g; past the batch it reads the last
+    // column instead (a valid address; those D columns are never stored)
+    const uint4* xfl[NT];
+    const uint32_t* xql[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int n = min(8 * nt + g, NC - 1);
+        xfl[nt] = reinterpret_cast<const uint4*>(XF) + (8 * t) * NC + n;
+        xql[nt] = reinterpret_cast<const uint32_t*>(XQ) + t * NC + n;
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+
+    // the activation limbs come from the preceding kernel in the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // After an expired wait a consumer skips its waits and math but keeps
+    // walking the same stages, so every consumer still reaches every
+    // tile-end barrier (nothing can be left waiting there).
+    bool live = true;
+    for (int j = 0; j < nstages; ++j) {
+        const int slot = j % kStages;
+        if (live) {
+            bool ok = mbar_wait(smem_u32(&full_bar[slot]), (j / kStages) & 1, err);
+            live = __all_sync(0xFFFFFFFFu, ok) && __shfl_sync(0xFFFFFFFFu, *(volatile int*)&abort_flag, 0) == 0;
+            if (!live) abort_flag = 1;
+        }
+        const int tile = blockIdx.x + (j / nchunks) * gridDim.x;
+        const int chunk = j % nchunks;
+        if (live) {
+#pragma unroll
+            for (int u = 0; u < kBpw; ++u) {
+                const int kb = chunk * kChunk + warp * kBpw + u;
+                if (kb < nblk) {
+                    const uint8_t* st = ring + slot * STAGE + (warp * kBpw + u) * BB;
+                    mma_block<Q, NB>(st + g * ROWB, st + (g + 8) * ROWB, xfl, xql, XS, kb, nblk, t, sel, acc);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
+        if (chunk == nchunks - 1) {
+            // tile done: lane (g, t) holds rows g, g + 8 x columns (2t, 2t+1) of
+            // each n8 tile. The scratch alternates between two sets, so the
+            // next tile's writes cannot race this tile's reads and one barrier
+            // per tile suffices.
+            const int set = (j / nchunks) & 1;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                red[set][warp][nt][0][lane] = fmaf(acc[nt][1], 1.0f / 2048.0f, acc[nt][0]);
+                red[set][warp][nt][1][lane] = fmaf(acc[nt][3], 1.0f / 2048.0f, acc[nt][2]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+            if (warp < 2 * NT) {
+                const int nt = warp >> 1, r = warp & 1;
+                float v = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kConsumers; ++w) v += red[set][w][nt][r][lane];
+                const int b = 4 * nt + t;
+                const int row = tile * kTileRows + 8 * r + g;
+                if (b < NB && row < N) Y[b * N + row] = v;
+            }
+        }
+    }
+}
+
+template <uint32_t Q, int NB>
+void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
     const int nblk = (int)(a.K / 256);
-    const int64_t grid = (a.N + 8 * G - 1) / (8 * G);
-    gemv_kq_mma_kernel<Q, G, NT><<<(unsigned)grid, kMmaWarps * 32, 0, s>>>(a.W, a.row_bytes, a.N, nblk, xf, xs,
-                                                                          a.batch, a.Y);
+    const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
+    const int smem = kStages * kTileRows * (kChunk * block_bytes(Q) + 16);
+    static int per_sm = 0;  // resident CTAs per SM, per instantiation
+    if (per_sm == 0) {
+        cudaFuncSetAttribute(gemv_kq_tma_kernel<Q, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_tma_kernel<Q, NB>, (kConsumers + 1) * 32, smem);
+        if (per_sm < 1) per_sm = 1;
+    }
+    int64_t grid = (int64_t)a.sm_count * per_sm;
+    if (grid > ntiles) grid = ntiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((kConsumers + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err);
+}
+
+template <uint32_t Q>
+void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
+    switch (a.batch) {
+    case 1: launch_tma<Q, 1>(a, xf, xs, xq, err, s); break;
+    case 2: launch_tma<Q, 2>(a, xf, xs, xq, err, s); break;
+    case 3: launch_tma<Q, 3>(a, xf, xs, xq, err, s); break;
+    case 4: launch_tma<Q, 4>(a, xf, xs, xq, err, s); break;
+    case 5: launch_tma<Q, 5>(a, xf, xs, xq, err, s); break;
+    case 6: launch_tma<Q, 6>(a, xf, xs, xq, err, s); break;
+    case 7: launch_tma<Q, 7>(a, xf, xs, xq, err, s); break;
+    default: launch_tma<Q, 8>(a, xf, xs, xq, err, s); break;
+    }
 }
 
 }  // namespace
 
+// workspace: XF (nblk*64*2B uint2), XS (B*nblk float), XQ (nblk*4*2B half2)
 int64_t gemv_mma_work_bytes(int64_t K, int batch) {
     const int64_t nblk = K / 256;
-    return nblk * 64 * 2 * batch * (int64_t)sizeof(uint2) + (int64_t)batch * nblk * 4 + 256;
+    return nblk * 64 * 2 * batch * 8 + (int64_t)batch * nblk * 4 + nblk * 4 * 2 * batch * 4 + 512;
 }
 
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a) {
     return (quant == kQ4_K || quant == kQ5_K) && a.K % 256 == 0 && a.batch >= 1 && a.batch <= 8 &&
+           a.N < (1ll << 31) && a.N * a.batch < (1ll << 31) && a.K < (1ll << 26) &&
            (a.row_bytes % 16) == 0 && ((uintptr_t)a.W % 16) == 0 && ((uintptr_t)a.X % 16) == 0;
 }
 
 // x limbs into `work` (gemv_mma_work_bytes), then the tensor-core GEMV.
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, cudaStream_t s) {
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s) {
     const int nblk = (int)(a.K / 256);
-    uint2* xf = reinterpret_cast<uint2*>(work);
-    float* xs = reinterpret_cast<float*>(reinterpret_cast<char*>(work) + (int64_t)nblk * 64 * 2 * a.batch * 8);
+    char* base = reinterpret_cast<char*>(work);
+    uint2* xf = reinterpret_cast<uint2*>(base);
+    const int64_t xf_bytes = (int64_t)nblk * 64 * 2 * a.batch * 8;
+    float* xs = reinterpret_cast<float*>(base + xf_bytes);
+    const int64_t xs_bytes = ((int64_t)a.batch * nblk * 4 + 255) / 256 * 256;
+    __half* xq = reinterpret_cast<__half*>(base + xf_bytes + xs_bytes);
     const int64_t warps = (int64_t)nblk * a.batch;
-    prep_x_limbs_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a.X, a.K, a.batch, xf, xs);
-    const bool two = a.batch > 4;
-    // rows per CTA: 16 when there are enough rows to fill the GPU twice over
-    const bool wide = a.N >= (int64_t)a.sm_count * 16 * 2;
-    if (quant == kQ4_K) {
-        if (two) wide ? launch_mma<kQ4_K, 2, 2>(a, xf, xs, s) : launch_mma<kQ4_K, 1, 2>(a, xf, xs, s);
-        else wide ? launch_mma<kQ4_K, 2, 1>(a, xf, xs, s) : launch_mma<kQ4_K, 1, 1>(a, xf, xs, s);
-    } else {
-        if (two) wide ? launch_mma<kQ5_K, 2, 2>(a, xf, xs, s) : launch_mma<kQ5_K, 1, 2>(a, xf, xs, s);
-        else wide ? launch_mma<kQ5_K, 2, 1>(a, xf, xs, s) : launch_mma<kQ5_K, 1, 1>(a, xf, xs, s);
-    }
+    prep_x_limbs_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a.X, a.K, a.batch, xf, xs, xq);
+    if (quant == kQ4_K) dispatch_mma<kQ4_K>(a, xf, xs, xq, err, s);
+    else dispatch_mma<kQ5_K>(a, xf, xs, xq, err, s);
     return 0;
 }
 

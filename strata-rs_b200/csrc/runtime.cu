@@ -80,6 +80,14 @@ int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what)
 // Bounded wait: poll an event recorded on `s` until it completes or the
 // context's timeout expires (the device work keeps running in that case; the
 // context stays usable and the caller gets STRATA_ERR_TIMEOUT).
+int check_device_error(strata_ctx* ctx) {
+    if (ctx->err_host && *(volatile int*)ctx->err_host) {
+        *(volatile int*)ctx->err_host = 0;
+        return fail(ctx, STRATA_ERR_TIMEOUT, "a kernel's bounded wait on shared-memory copies expired");
+    }
+    return STRATA_OK;
+}
+
 int wait_stream(strata_ctx* ctx, cudaStream_t s) {
     cudaError_t e = cudaEventRecord(ctx->done, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventRecord");
@@ -87,7 +95,7 @@ int wait_stream(strata_ctx* ctx, cudaStream_t s) {
     int spins = 0;
     for (;;) {
         e = cudaEventQuery(ctx->done);
-        if (e == cudaSuccess) return STRATA_OK;
+        if (e == cudaSuccess) return check_device_error(ctx);
         if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "device work");
         auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
         if ((uint64_t)ms > ctx->wait_timeout_ms)
@@ -143,10 +151,13 @@ int strata_cuda_create(int device, strata_ctx** out) {
     ctx->cc_major = prop.major;
     ctx->cc_minor = prop.minor;
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess) {
+        cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaHostAlloc((void**)&ctx->err_host, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer((void**)&ctx->err_dev, ctx->err_host, 0) != cudaSuccess) {
         delete ctx;
         return STRATA_ERR_CUDA;
     }
+    *ctx->err_host = 0;
     *out = ctx;
     return STRATA_OK;
 }
@@ -162,6 +173,7 @@ int strata_cuda_destroy(strata_ctx* ctx) {
         if (b->ptr) cudaFreeHost(b->ptr);
     cudaEventDestroy(ctx->done);
     cudaStreamDestroy(ctx->stream);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
     return rc;
 }
@@ -306,7 +318,7 @@ static int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_
         int64_t need = gemv_mma_work_bytes(w->cols, batch);
         int rc = ensure_device(ctx, ctx->xfrag, (size_t)(need > (4 << 20) ? need : (4 << 20)), "cudaMalloc(x limbs)");
         if (rc) return rc;
-        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, s);
+        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, s);
         return check_launch(ctx, "tensor-core gemv kernel");
     }
     if (ctx->gemv_path == STRATA_GEMV_TENSOR_CORES)

@@ -41,6 +41,8 @@ struct strata_ctx {
     strata::DevBuf x_dev, y_dev, work, xfrag;
     strata::PinnedBuf x_host, y_host;
     strata::CommState* comm = nullptr;
+    int* err_host = nullptr;  // host-mapped word kernels set when a bounded wait expires
+    int* err_dev = nullptr;
 };
 
 constexpr uint32_t kWeightMagic = 0x57545253u;  // "SRTW"
@@ -74,7 +76,8 @@ int launch_expert_gemv_ws(uint32_t quant, const ExpertGemvArgs& a, float* work, 
 // gemv_mma.cu
 int64_t gemv_mma_work_bytes(int64_t K, int batch);
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, cudaStream_t s);
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
+int check_device_error(strata_ctx* ctx);
 
 // comm.cu
 void comm_release(strata_ctx* ctx);
