@@ -30,7 +30,11 @@
 // the order the B fragments are read (one 8-byte load per lane per mma); the
 // GEMV is launched as its programmatic dependent, so it starts streaming
 // weights while the prologue runs and waits only before reading the limbs.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
+
+#include <cstring>
 
 #include "kernels.cuh"
 #include "quant.cuh"
@@ -73,11 +77,14 @@ __device__ __forceinline__ void mma16816_z(float d[4], uint32_t a0, uint32_t a1,
 
 // ---------------------------------------------------------------- prologue
 //
-// XF layout: [blk][t = 0..3][i = word 0..7][n = column 0..2*batch) of
+// XF layout: [blk][i = word 0..7][n = column 0..2*batch)][t = 0..3] of
 // uint4 {b0(2t), b1(2t), b0(2t+1), b1(2t+1)}: the B fragments of the low- and
-// high-nibble MMAs of word i, where for sub-block s and e = 256 blk + 32 s + 4 i
+// high-nibble MMAs of word i for lane t, where for sub-block s and
+// e = 256 blk + 32 s + 4 i
 //   b0(s) = half2(v[e], v[e+2]), b1(s) = half2(v[e+1], v[e+3]),
-// v = limb (n & 1) of batch row (n >> 1) of x, scaled by XS^-1.
+// v = limb (n & 1) of batch row (n >> 1) of x, scaled by XS^-1. With t
+// innermost, the 8 lanes of a quarter-warp (two columns x four t) read one
+// contiguous 128-byte line per load.
 // XS layout: [batch][blk] float: the power of two that undoes the scaling.
 // XQ layout: [blk][t = 0..3][n][2] __half: the sums of v over sub-blocks 2t
 // and 2t+1, limb (n & 1) of batch (n >> 1) -- the B operand of the min MMA.
@@ -135,10 +142,10 @@ __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int 
         fh.y = h2u(__halves2half2(hi[o + 1], hi[o + 3]));
         fl.x = h2u(__halves2half2(lo[o + 0], lo[o + 2]));
         fl.y = h2u(__halves2half2(lo[o + 1], lo[o + 3]));
-        // entry (blk, t = s/2, i, n) is 2 uint2; sub-block parity picks the half
-        uint2* dst = XF + ((((int64_t)blk * 4 + (s_blk >> 1)) * 8 + i) * ncols + 2 * b) * 2 + (s_blk & 1);
-        dst[0] = fh;
-        dst[2] = fl;
+        // entry (blk, i, n, t = s/2) is 2 uint2; sub-block parity picks the half
+        uint2* dst = XF + ((((int64_t)blk * 8 + i) * ncols + 2 * b) * 4 + (s_blk >> 1)) * 2 + (s_blk & 1);
+        dst[0] = fh;   // column 2b   (limb 0)
+        dst[8] = fl;   // column 2b+1 (limb 1): the next column, 4 uint4 = 8 uint2 on
     }
 }
 
@@ -197,7 +204,16 @@ __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int 
     }
 }
 
-constexpr int kStages = 3;     // smem ring depth
+// 3-D tensor-map load into this CTA's shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+constexpr int kStages = 2;     // smem ring depth
 constexpr int kConsumers = 4;  // consumer warps per CTA
 constexpr int kBpw = 2;        // K blocks per consumer warp per stage
 constexpr int kChunk = kConsumers * kBpw;  // K blocks per stage
@@ -208,107 +224,122 @@ constexpr int kTileRows = 16;
 // into acc. NB is the batch; its 2*NB (batch, limb) columns fill
 // NT = ceil(2*NB / 8) n8 tiles. `xfl` / `xql` point at this lane's fragment
 // column of block 0. The 16 sc*q MMAs alternate between two accumulator chains.
-template <uint32_t Q, int NB>
-__device__ __forceinline__ void mma_block(const uint8_t* blk0, const uint8_t* blk1, const uint4* const (&xfl)[(2 * NB + 7) / 8],
-                                          const uint32_t* const (&xql)[(2 * NB + 7) / 8], const float* __restrict__ XS,
-                                          int kb, int nblk, int t, uint32_t sel, float (&acc)[(2 * NB + 7) / 8][4]) {
+template <uint32_t Q, int NB, int U, bool SW>
+__device__ __forceinline__ void mma_blocks(const uint8_t* stage, const uint32_t (&rowoff)[U][2], const int (&kbs)[U],
+                                           const uint4* const (&xfl)[(2 * NB + 7) / 8],
+                                           const uint32_t* const (&xql)[(2 * NB + 7) / 8],
+                                           const float* __restrict__ XS, int nblk, int t, uint32_t sel,
+                                           float (&acc)[(2 * NB + 7) / 8][4]) {
     constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
-    constexpr int CH = 1;  // accumulator chains per nibble half
     constexpr int QOFF = (Q == kQ4_K) ? 16 : 48;
     const __half2 k1024 = __float2half2_rn(1024.0f);
     const __half2 kneg1024 = __float2half2_rn(-1024.0f);
     const __half2 k1_16 = __float2half2_rn(0.0625f);
     const __half2 kneg64 = __float2half2_rn(-64.0f);
-    const uint8_t* blk[2] = {blk0, blk1};
-    float d_acc[NT][2 * CH][4], d_min[NT][4];
     // masks kept in registers so each nibble extraction is one LOP3
     const uint32_t kLoMask = 0x000F000Fu, kHiMask = 0x00F000F0u, kMagic = 0x64006400u;
+    float d_acc[U][NT][2][4], d_min[U][NT][4];
 
-    // per row (r = 0: row g, r = 1: row g + 8): quant bytes, scale constants and mins
-    uint4 qa[2], qb[2], ha[2], hb[2];
-    __half2 sAB[2], cA[2], sB16[2], cB[2];
-    uint32_t mAB[2];
-    float dd[2], dm[2];
+    // per block u and row r (0: row g, 1: row g + 8): quant bytes, scale constants and mins
+    uint4 qa[U][2], qb[U][2], ha[U][2], hb[U][2];
+    __half2 sAB[U][2], cA[U][2], sB16[U][2], cB[U][2];
+    uint32_t mAB[U][2];
+    float dd[U][2], dm[U][2];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const uint4 hd = *reinterpret_cast<const uint4*>(blk[r]);
-        qa[r] = *reinterpret_cast<const uint4*>(blk[r] + QOFF + 32 * t);
-        qb[r] = *reinterpret_cast<const uint4*>(blk[r] + QOFF + 32 * t + 16);
-        if constexpr (Q == kQ5_K) {
-            ha[r] = *reinterpret_cast<const uint4*>(blk[r] + 16);
-            hb[r] = *reinterpret_cast<const uint4*>(blk[r] + 32);
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            // a 16-byte unit at logical offset o of the stage; with the 128-byte
+            // swizzle the unit index inside each 128-byte line is XORed with the
+            // line index mod 8
+            auto ld = [&](uint32_t o) {
+                if constexpr (SW) o ^= (o >> 3) & 0x70u;
+                return *reinterpret_cast<const uint4*>(stage + o);
+            };
+            const uint32_t o = rowoff[u][r];
+            const uint4 hd = ld(o);
+            qa[u][r] = ld(o + QOFF + 32 * t);
+            qb[u][r] = ld(o + QOFF + 32 * t + 16);
+            if constexpr (Q == kQ5_K) {
+                ha[u][r] = ld(o + 16);
+                hb[u][r] = ld(o + 32);
+            }
+            dd[u][r] = f16_bits_to_f32(hd.x & 0xFFFFu);
+            dm[u][r] = f16_bits_to_f32(hd.x >> 16);
+            uint32_t sl, sh, ml, mh;
+            scales_k4_packed(hd.y, hd.z, hd.w, sl, sh, ml, mh);
+            const uint32_t sw = t < 2 ? sl : sh, mw = t < 2 ? ml : mh;
+            sAB[u][r] = __hsub2(u2h(__byte_perm(sw, 0x00006464u, sel)), k1024);
+            mAB[u][r] = h2u(__hsub2(u2h(__byte_perm(mw, 0x00006464u, sel)), k1024));
+            cA[u][r] = __hmul2(__low2half2(sAB[u][r]), kneg1024);
+            sB16[u][r] = __hmul2(__high2half2(sAB[u][r]), k1_16);
+            cB[u][r] = __hmul2(__high2half2(sAB[u][r]), kneg64);
         }
-        dd[r] = f16_bits_to_f32(hd.x & 0xFFFFu);
-        dm[r] = f16_bits_to_f32(hd.x >> 16);
-        uint32_t sl, sh, ml, mh;
-        scales_k4_packed(hd.y, hd.z, hd.w, sl, sh, ml, mh);
-        const uint32_t sw = t < 2 ? sl : sh, mw = t < 2 ? ml : mh;
-        sAB[r] = __hsub2(u2h(__byte_perm(sw, 0x00006464u, sel)), k1024);
-        mAB[r] = h2u(__hsub2(u2h(__byte_perm(mw, 0x00006464u, sel)), k1024));
-        cA[r] = __hmul2(__low2half2(sAB[r]), kneg1024);
-        sB16[r] = __hmul2(__high2half2(sAB[r]), k1_16);
-        cB[r] = __hmul2(__high2half2(sAB[r]), kneg64);
-    }
     // min MMA: K slots 2t, 2t+1 = sub-blocks 2t, 2t+1 (A: this lane's mins; B: sub-block sums)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) mma16816_z(d_min[nt], mAB[0], mAB[1], 0u, 0u, __ldg(xql[nt] + kb * (4 * NC)), 0u);
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            mma16816_z(d_min[u][nt], mAB[u][0], mAB[u][1], 0u, 0u, __ldg(xql[nt] + kbs[u] * (4 * NC)), 0u);
 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        uint4 bf[NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) bf[nt] = __ldg(xfl[nt] + (kb * 32 + i) * NC);
-        uint32_t a_lo0[2], a_lo1[2], a_hi0[2], a_hi1[2];
+        for (int u = 0; u < U; ++u) {
+            uint4 bf[NT];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const uint32_t w = word_of(qa[r], qb[r], i);
-            const uint32_t w8 = w >> 8;
-            uint32_t lo0 = and_or(w, kLoMask, kMagic);
-            uint32_t lo1 = and_or(w8, kLoMask, kMagic);
-            uint32_t hi0 = and_or(w, kHiMask, kMagic);
-            uint32_t hi1 = and_or(w8, kHiMask, kMagic);
-            if constexpr (Q == kQ5_K) {
-                // qh byte l holds the 5th bit of element l of every sub-block:
-                // bit 2t for this lane's low sub-block, bit 2t+1 for the high one.
-                const uint32_t h = word_of(ha[r], hb[r], i) >> (2 * t);
-                lo0 = and_or(h << 4, 0x00100010u, lo0);
-                lo1 = and_or(h >> 4, 0x00100010u, lo1);
-                hi0 = and_or(h << 7, 0x01000100u, hi0);
-                hi1 = and_or(h >> 1, 0x01000100u, hi1);
+            for (int nt = 0; nt < NT; ++nt) bf[nt] = __ldg(xfl[nt] + (kbs[u] * 8 + i) * NC * 4);
+            uint32_t a_lo0[2], a_lo1[2], a_hi0[2], a_hi1[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint32_t w = word_of(qa[u][r], qb[u][r], i);
+                const uint32_t w8 = w >> 8;
+                uint32_t lo0 = and_or(w, kLoMask, kMagic);
+                uint32_t lo1 = and_or(w8, kLoMask, kMagic);
+                uint32_t hi0 = and_or(w, kHiMask, kMagic);
+                uint32_t hi1 = and_or(w8, kHiMask, kMagic);
+                if constexpr (Q == kQ5_K) {
+                    // qh byte l holds the 5th bit of element l of every sub-block:
+                    // bit 2t for this lane's low sub-block, bit 2t+1 for the high one.
+                    const uint32_t h = word_of(ha[u][r], hb[u][r], i) >> (2 * t);
+                    lo0 = and_or(h << 4, 0x00100010u, lo0);
+                    lo1 = and_or(h >> 4, 0x00100010u, lo1);
+                    hi0 = and_or(h << 7, 0x01000100u, hi0);
+                    hi1 = and_or(h >> 1, 0x01000100u, hi1);
+                }
+                a_lo0[r] = h2u(__hfma2(u2h(lo0), __low2half2(sAB[u][r]), cA[u][r]));
+                a_lo1[r] = h2u(__hfma2(u2h(lo1), __low2half2(sAB[u][r]), cA[u][r]));
+                a_hi0[r] = h2u(__hfma2(u2h(hi0), sB16[u][r], cB[u][r]));
+                a_hi1[r] = h2u(__hfma2(u2h(hi1), sB16[u][r], cB[u][r]));
             }
-            a_lo0[r] = h2u(__hfma2(u2h(lo0), __low2half2(sAB[r]), cA[r]));
-            a_lo1[r] = h2u(__hfma2(u2h(lo1), __low2half2(sAB[r]), cA[r]));
-            a_hi0[r] = h2u(__hfma2(u2h(hi0), sB16[r], cB[r]));
-            a_hi1[r] = h2u(__hfma2(u2h(hi1), sB16[r], cB[r]));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                if (i == 0) {  // each chain starts from zero
+                    mma16816_z(d_acc[u][nt][0], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[nt].x, bf[nt].y);
+                    mma16816_z(d_acc[u][nt][1], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[nt].z, bf[nt].w);
+                } else {
+                    mma16816(d_acc[u][nt][0], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[nt].x, bf[nt].y);
+                    mma16816(d_acc[u][nt][1], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[nt].z, bf[nt].w);
+                }
+            }
         }
-        const int ch = (CH == 1) ? 0 : 2 * (i & 1);
+    }
+    // fold: D columns 2t (limb 0) and 2t+1 (limb 1) of batch 4 nt + t; D rows
+    // g (c = 0, 1) and g + 8 (c = 2, 3). Columns past the batch hold garbage
+    // (their lanes loaded a clamped column) and are never stored.
+#pragma unroll
+    for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            if (i < CH) {  // first mma of each chain starts from zero
-                mma16816_z(d_acc[nt][ch], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[nt].x, bf[nt].y);
-                mma16816_z(d_acc[nt][ch + 1], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[nt].z, bf[nt].w);
-            } else {
-                mma16816(d_acc[nt][ch], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[nt].x, bf[nt].y);
-                mma16816(d_acc[nt][ch + 1], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[nt].z, bf[nt].w);
+            const int b = min(4 * nt + t, NB - 1);
+            const float xs = __ldg(XS + b * nblk + kbs[u]);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int r = c >> 1;
+                const float v = d_acc[u][nt][0][c] + d_acc[u][nt][1][c];
+                acc[nt][c] = fmaf(dd[u][r] * xs, v, fmaf(-dm[u][r] * xs, d_min[u][nt][c], acc[nt][c]));
             }
         }
-    }
-    // fold this block: D columns 2t (limb 0) and 2t+1 (limb 1) of batch 4 nt + t;
-    // D rows g (c = 0, 1) and g + 8 (c = 2, 3). Columns past the batch hold
-    // garbage (their lanes loaded a clamped column) and are never stored.
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const int b = min(4 * nt + t, NB - 1);
-        const float xs = __ldg(XS + b * nblk + kb);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int r = c >> 1;
-            float v = d_acc[nt][0][c];
-#pragma unroll
-            for (int ch = 1; ch < 2 * CH; ++ch) v += d_acc[nt][ch][c];
-            acc[nt][c] = fmaf(dd[r] * xs, v, fmaf(-dm[r] * xs, d_min[nt][c], acc[nt][c]));
-        }
-    }
 }
 
 // Persistent, warp-specialised kernel. CTA c takes 16-row tiles c, c + grid,
@@ -319,20 +350,23 @@ __device__ __forceinline__ void mma_block(const uint8_t* blk0, const uint8_t* bl
 // kBpw - 1 of each stage and releases the slot through its `empty` mbarrier. Consumers keep their
 // partial sums across a tile's stages and combine them in shared memory when
 // the tile ends. Every wait is bounded; a timeout sets *err and the CTA stops.
-template <uint32_t Q, int NB>
+template <uint32_t Q, int NB, bool TM>
 __global__ void __launch_bounds__((kConsumers + 1) * 32, 3)
 gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
-                   float* __restrict__ Y, int* __restrict__ err) {
+                   float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap) {
     constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
     constexpr int BB = block_bytes(Q);
-    // smem stride of one row of a stage: its kChunk blocks plus 16 bytes, so
-    // that the 8 rows a 128-bit fragment read touches start 4 banks apart
-    // (kChunk * BB is a multiple of 128 bytes, which would put them all on
-    // the same banks)
-    constexpr int ROWB = kChunk * BB + 16;
+    // smem stride of one row of a stage. TM (one tensor-map copy per stage):
+    // the rows are dense and 128-byte swizzled, which puts consecutive rows'
+    // units on different banks. Otherwise (one bulk copy per row): each row is
+    // padded by 16 bytes so that the 8 rows a 128-bit fragment read touches
+    // start 4 banks apart (kChunk * BB is a multiple of 128 bytes).
+    constexpr int ROWB = TM ? kChunk * BB : kChunk * BB + 16;
     constexpr int STAGE = kTileRows * ROWB;
-    extern __shared__ __align__(128) uint8_t ring[];  // kStages * STAGE
+    constexpr int LINES = kChunk * BB / 128;  // 128-byte lines per row of a stage (TM)
+    extern __shared__ __align__(1024) uint8_t ring_raw[];  // kStages * STAGE (+ 1 KB for alignment)
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ring_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ float red[2][kConsumers][NT][2][32];
     __shared__ int abort_flag;
@@ -370,13 +404,22 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
             const int nb = min(kChunk, nblk - c0);
             const uint32_t bytes = (uint32_t)(nb * BB);
             const uint32_t fb = smem_u32(&full_bar[slot]);
-            if (lane == 0) mbar_expect_tx(fb, bytes * kTileRows);
-            __syncwarp();
-            if (lane < kTileRows) {
-                int row = tile * kTileRows + lane;
-                row = row < N ? row : N - 1;
-                const uint8_t* src = W + (int64_t)row * row_bytes + (int64_t)c0 * BB;
-                bulk_g2s(smem_u32(ring + slot * STAGE + lane * ROWB), src, bytes, fb);
+            if constexpr (TM) {
+                // the whole 16-row x kChunk-block box (rows past N are zero-filled)
+                if (lane == 0) {
+                    mbar_expect_tx(fb, (uint32_t)STAGE);
+                    tma_load_3d(smem_u32(ring + slot * STAGE), &tmap, 0, (c0 / kChunk) * LINES, tile * kTileRows, fb);
+                }
+                __syncwarp();
+            } else {
+                if (lane == 0) mbar_expect_tx(fb, bytes * kTileRows);
+                __syncwarp();
+                if (lane < kTileRows) {
+                    int row = tile * kTileRows + lane;
+                    row = row < N ? row : N - 1;
+                    const uint8_t* src = W + (int64_t)row * row_bytes + (int64_t)c0 * BB;
+                    bulk_g2s(smem_u32(ring + slot * STAGE + lane * ROWB), src, bytes, fb);
+                }
             }
         }
         // drain: wait (bounded) for the copies still in flight before exiting
@@ -395,7 +438,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         const int n = min(8 * nt + g, NC - 1);
-        xfl[nt] = reinterpret_cast<const uint4*>(XF) + (8 * t) * NC + n;
+        xfl[nt] = reinterpret_cast<const uint4*>(XF) + n * 4 + t;
         xql[nt] = reinterpret_cast<const uint32_t*>(XQ) + t * NC + n;
     }
     float acc[NT][4];
@@ -420,14 +463,26 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
         }
         const int tile = blockIdx.x + (j / nchunks) * gridDim.x;
         const int chunk = j % nchunks;
-        if (live) {
+        const int kb0 = chunk * kChunk + warp * kBpw;
+        if (live && kb0 + kBpw <= nblk) {
+            // the warp's kBpw blocks, interleaved for instruction-level parallelism
+            uint32_t rowoff[kBpw][2];
+            int kbs[kBpw];
 #pragma unroll
             for (int u = 0; u < kBpw; ++u) {
-                const int kb = chunk * kChunk + warp * kBpw + u;
-                if (kb < nblk) {
-                    const uint8_t* st = ring + slot * STAGE + (warp * kBpw + u) * BB;
-                    mma_block<Q, NB>(st + g * ROWB, st + (g + 8) * ROWB, xfl, xql, XS, kb, nblk, t, sel, acc);
-                }
+                const uint32_t ub = (uint32_t)((warp * kBpw + u) * BB);
+                rowoff[u][0] = g * ROWB + ub;
+                rowoff[u][1] = (g + 8) * ROWB + ub;
+                kbs[u] = kb0 + u;
+            }
+            mma_blocks<Q, NB, kBpw, TM>(ring + slot * STAGE, rowoff, kbs, xfl, xql, XS, nblk, t, sel, acc);
+        } else if (live) {
+            // a ragged last chunk: the blocks that exist, one at a time
+            for (int kb = kb0; kb < nblk && kb < kb0 + kBpw; ++kb) {
+                const uint32_t ub = (uint32_t)((kb - chunk * kChunk) * BB);
+                const uint32_t rowoff[1][2] = {{g * ROWB + ub, (g + 8) * ROWB + ub}};
+                const int kbs[1] = {kb};
+                mma_blocks<Q, NB, 1, TM>(ring + slot * STAGE, rowoff, kbs, xfl, xql, XS, nblk, t, sel, acc);
             }
         }
         __syncwarp();
@@ -459,17 +514,21 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     }
 }
 
-template <uint32_t Q, int NB>
+template <uint32_t Q, int NB, bool TM>
 void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
     const int nblk = (int)(a.K / 256);
     const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
-    const int smem = kStages * kTileRows * (kChunk * block_bytes(Q) + 16);
+    const int smem = kStages * kTileRows * (kChunk * block_bytes(Q) + (TM ? 0 : 16)) + 1024;
     static int per_sm = 0;  // resident CTAs per SM, per instantiation
     if (per_sm == 0) {
-        cudaFuncSetAttribute(gemv_kq_tma_kernel<Q, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_tma_kernel<Q, NB>, (kConsumers + 1) * 32, smem);
+        cudaFuncSetAttribute(gemv_kq_tma_kernel<Q, NB, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_tma_kernel<Q, NB, TM>, (kConsumers + 1) * 32,
+                                                      smem);
         if (per_sm < 1) per_sm = 1;
     }
+    CUtensorMap map;
+    if (TM) map = *reinterpret_cast<const CUtensorMap*>(a.tmap);
+    else memset(&map, 0, sizeof(map));
     int64_t grid = (int64_t)a.sm_count * per_sm;
     if (grid > ntiles) grid = ntiles;
     cudaLaunchConfig_t cfg = {};
@@ -482,24 +541,53 @@ void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __hal
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err);
+    cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err,
+                       map);
 }
 
-template <uint32_t Q>
+template <uint32_t Q, bool TM>
 void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
     switch (a.batch) {
-    case 1: launch_tma<Q, 1>(a, xf, xs, xq, err, s); break;
-    case 2: launch_tma<Q, 2>(a, xf, xs, xq, err, s); break;
-    case 3: launch_tma<Q, 3>(a, xf, xs, xq, err, s); break;
-    case 4: launch_tma<Q, 4>(a, xf, xs, xq, err, s); break;
-    case 5: launch_tma<Q, 5>(a, xf, xs, xq, err, s); break;
-    case 6: launch_tma<Q, 6>(a, xf, xs, xq, err, s); break;
-    case 7: launch_tma<Q, 7>(a, xf, xs, xq, err, s); break;
-    default: launch_tma<Q, 8>(a, xf, xs, xq, err, s); break;
+    case 1: launch_tma<Q, 1, TM>(a, xf, xs, xq, err, s); break;
+    case 2: launch_tma<Q, 2, TM>(a, xf, xs, xq, err, s); break;
+    case 3: launch_tma<Q, 3, TM>(a, xf, xs, xq, err, s); break;
+    case 4: launch_tma<Q, 4, TM>(a, xf, xs, xq, err, s); break;
+    case 5: launch_tma<Q, 5, TM>(a, xf, xs, xq, err, s); break;
+    case 6: launch_tma<Q, 6, TM>(a, xf, xs, xq, err, s); break;
+    case 7: launch_tma<Q, 7, TM>(a, xf, xs, xq, err, s); break;
+    default: launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s); break;
     }
 }
 
 }  // namespace
+
+// The 3-D view of a Q4_K / Q5_K matrix the tensor-core GEMV copies from:
+// [8-byte units x 16][128-byte lines x row_bytes/128][rows], box
+// [16][kChunk*BB/128][16] with 128-byte swizzle. Needs whole 8-block chunks
+// per row (K a multiple of 2048). Returns false when not applicable.
+bool encode_gemv_tmap(uint32_t quant, const void* base, int64_t rows, int64_t row_bytes, void* out128) {
+    if (quant != kQ4_K && quant != kQ5_K) return false;
+    const int bb = block_bytes(quant);
+    if (rows <= 0 || row_bytes % ((int64_t)kChunk * bb) != 0 || ((uintptr_t)base % 16) != 0) return false;
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return false;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dims[3] = {16, (cuuint64_t)(row_bytes / 128), (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {128, (cuuint64_t)row_bytes};
+    const cuuint32_t box[3] = {16, (cuuint32_t)(kChunk * bb / 128), (cuuint32_t)kTileRows};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = encode(reinterpret_cast<CUtensorMap*>(out128), CU_TENSOR_MAP_DATA_TYPE_UINT64, 3,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
 
 // workspace: XF (nblk*64*2B uint2), XS (B*nblk float), XQ (nblk*4*2B half2)
 int64_t gemv_mma_work_bytes(int64_t K, int batch) {
@@ -524,8 +612,9 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     __half* xq = reinterpret_cast<__half*>(base + xf_bytes + xs_bytes);
     const int64_t warps = (int64_t)nblk * a.batch;
     prep_x_limbs_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a.X, a.K, a.batch, xf, xs, xq);
-    if (quant == kQ4_K) dispatch_mma<kQ4_K>(a, xf, xs, xq, err, s);
-    else dispatch_mma<kQ5_K>(a, xf, xs, xq, err, s);
+    const bool tm = a.tmap != nullptr;
+    if (quant == kQ4_K) tm ? dispatch_mma<kQ4_K, true>(a, xf, xs, xq, err, s) : dispatch_mma<kQ4_K, false>(a, xf, xs, xq, err, s);
+    else tm ? dispatch_mma<kQ5_K, true>(a, xf, xs, xq, err, s) : dispatch_mma<kQ5_K, false>(a, xf, xs, xq, err, s);
     return 0;
 }
 

@@ -15,6 +15,7 @@ struct GemvArgs {
     float* Y;
     int batch;
     int sm_count;
+    const void* tmap = nullptr;  // CUtensorMap of W for the tensor-core GEMV, or null
 };
 
 int launch_dequant(uint32_t quant, const uint8_t* w, int64_t row_bytes, int64_t cols, int64_t nrows,

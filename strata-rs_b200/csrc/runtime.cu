@@ -263,6 +263,8 @@ int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32
             return cuda_fail(ctx, e, "cudaMemcpy(weights)");
         }
     }
+    if (n_expert == 0 && need > 0)
+        w->has_tmap = encode_gemv_tmap(quant, w->dev, rows, rb, w->tmap);
     ctx->resident_bytes += (uint64_t)need;
     *out = w;
     return STRATA_OK;
@@ -313,7 +315,8 @@ static int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_
     if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
         return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
-    GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch, ctx->sm_count};
+    GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch, ctx->sm_count,
+               w->has_tmap ? w->tmap : nullptr};
     if (ctx->gemv_path != STRATA_GEMV_CUDA_CORES && gemv_mma_supported(w->quant, a)) {
         int64_t need = gemv_mma_work_bytes(w->cols, batch);
         int rc = ensure_device(ctx, ctx->xfrag, (size_t)(need > (4 << 20) ? need : (4 << 20)), "cudaMalloc(x limbs)");

@@ -54,6 +54,8 @@ struct strata_weight {
     int64_t n_expert = 0, rows = 0, cols = 0, row_bytes = 0;
     uint8_t* dev = nullptr;
     size_t bytes = 0;
+    alignas(64) unsigned char tmap[128];  // tensor map of a dense Q4_K / Q5_K matrix for the GEMV
+    bool has_tmap = false;
 };
 
 namespace strata {
@@ -77,6 +79,7 @@ int launch_expert_gemv_ws(uint32_t quant, const ExpertGemvArgs& a, float* work, 
 int64_t gemv_mma_work_bytes(int64_t K, int batch);
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
 int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
+bool encode_gemv_tmap(uint32_t quant, const void* base, int64_t rows, int64_t row_bytes, void* out128);
 int check_device_error(strata_ctx* ctx);
 
 // comm.cu
