@@ -56,6 +56,18 @@ def sweep_bytes(shapes, batches) -> int:
     return sum(gemv_bytes(k, n, b) for b in batches for (k, n) in shapes)
 
 
+def profiled_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary
+    (profiles/gemv_q4k_sweep_dram.md), or None when it is absent."""
+    p = ROOT / "profiles" / "gemv_q4k_sweep_dram.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":")[1])
+    return None
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -230,7 +242,8 @@ def run_gpu(args):
         with torch.cuda.graph(g, stream=stream):
             enqueue(i, stream.cuda_stream)
         graphs.append(g)
-    launches_per_step = len(batches) * len(shapes)
+    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel
+    launches_per_step = 2 * len(batches) * len(shapes)
 
     def allgather():
         for (k, n) in shapes:
@@ -364,8 +377,11 @@ def run_gpu(args):
                        "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
                        "launch": "CUDA graph per step"},
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(value / hbm, 3), "traffic": None,
-                         "note": f"Q4_K GEMV kernel over the timed sweep; peak = {peak_kind} copy bandwidth"},
+                         "frac": round(value / hbm, 3), "traffic": profiled_traffic(),
+                         "algorithmic_bytes_per_launch": total // (len(batches) * len(shapes)),
+                         "note": f"Q4_K GEMV over the timed sweep (16 GEMVs per step, each a prologue + "
+                                 f"GEMV launch); peak = {peak_kind} copy bandwidth; traffic = DRAM bytes per "
+                                 f"GEMV launch from profiles/gemv_q4k_sweep_dram.md"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
             "cases": cases,
@@ -384,6 +400,32 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_profile_case(args):
+    """One GEMV case (K,N,B) launched warmup + steps times on one weight copy:
+    the small, single-kernel workload the ncu captures under profiles/ use."""
+    import torch
+    import strata_cuda as sc
+    k, n, b = (int(v) for v in args.profile_case.split(","))
+    ctx = sc.Context(0)
+    w = ctx.upload(quant_matrix(k + n, Q4_K, n, k), Q4_K, n, k)
+    x = torch.from_numpy(activations(900 + b, b, k)).cuda()
+    y = torch.empty(b, n, device="cuda")
+    s = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        ctx.gemv_dev(w, x.data_ptr(), y.data_ptr(), b, s.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        ctx.gemv_dev(w, x.data_ptr(), y.data_ptr(), b, s.cuda_stream)
+    e1.record(s)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / max(1, args.steps)
+    print(json.dumps({"profile_case": [k, n, b], "us_per_gemv": round(us, 2),
+                      "note": "same weights every launch (L2-warm): a profiling workload, not a bench value"}))
+    w.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -393,10 +435,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the per-case table")
+    ap.add_argument("--profile-case", default=None, metavar="K,N,B",
+                    help="launch one Q4_K GEMV case repeatedly (for ncu captures) instead of the bench")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)
