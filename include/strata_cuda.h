@@ -48,7 +48,8 @@ enum {
     STRATA_ERR_OOM = 5,               /* device allocation failed */
     STRATA_ERR_TIMEOUT = 6,           /* a bounded wait on the device expired */
     STRATA_ERR_NCCL = 7,              /* a collective failed */
-    STRATA_ERR_BUDGET = 8             /* the weight budget would be exceeded */
+    STRATA_ERR_BUDGET = 8,            /* the weight budget would be exceeded */
+    STRATA_ERR_SCRATCH_LIMIT = 9      /* too large for strata_cuda_gemv_noalloc's fixed scratch */
 };
 
 /* Strata ggml type ids accepted here (crates/strata-gguf/src/quant.rs:15-43). */
@@ -137,6 +138,32 @@ int strata_cuda_expert_gemv(strata_ctx *ctx, const strata_weight *w, int64_t e, 
                             float *y, int batch);
 int strata_cuda_expert_gemv_dev(strata_ctx *ctx, const strata_weight *w, int64_t e,
                                 const float *x_dev, float *y_dev, int batch, void *stream);
+
+/* ------------------------------------------------- decode GEMV, no allocation */
+
+/* No counterpart in the reference: an addition for callers that must not
+ * allocate device memory -- code running while a stream is being captured into
+ * a CUDA graph (where a cudaMalloc would break the capture), engines whose
+ * device memory all comes from their own pre-sized pool, or hosts where
+ * another runtime owns the allocator. It needs no context.
+ *
+ * The same tensor-core decode GEMV as strata_cuda_gemv_dev: y = W x for a
+ * Q4_K or Q5_K matrix already in device memory in strata-gguf's byte layout
+ * (w_dev, 16-byte aligned; rows = OUT, cols = IN, a multiple of 256), x
+ * batch x cols f32 and y batch x rows f32 on the device, work enqueued on
+ * `stream` (NULL = the legacy default stream). Its scratch is a 320 KiB
+ * static device array inside this library, so it allocates nothing; the
+ * limit is cols * batch <= 65,536 (e.g. K = 8192 at batch 8), beyond which it
+ * returns STRATA_ERR_SCRATCH_LIMIT without launching.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current), so make one call on each device before capturing a stream.
+ * Every call shares the one array: calls that can overlap on the GPU (other
+ * streams, other threads) race on it and must be serialised by the caller.
+ * The scratch keeps the last call's contents; each call rewrites all of it
+ * that it reads. Returns without synchronising. */
+int strata_cuda_gemv_noalloc(const uint8_t *w_dev, uint32_t quant, int64_t rows, int64_t cols,
+                             const float *x_dev, float *y_dev, int batch, void *stream);
 
 #ifdef __cplusplus
 }

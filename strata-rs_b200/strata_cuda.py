@@ -23,7 +23,8 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("STRATA_CUDA_LIB", HERE / "libstrata_cuda.so"))
 
 # status codes (include/strata_cuda.h)
-OK, ERR_INVALID, ERR_UNSUPPORTED_QUANT, ERR_TRUNCATED, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_NCCL, ERR_BUDGET = range(9)
+(OK, ERR_INVALID, ERR_UNSUPPORTED_QUANT, ERR_TRUNCATED, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_NCCL, ERR_BUDGET,
+ ERR_SCRATCH_LIMIT) = range(10)
 
 # Strata ggml type ids (crates/strata-gguf/src/quant.rs:15-43)
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
@@ -75,6 +76,7 @@ def lib() -> C.CDLL:
             "strata_cuda_gemv_dev": (i32, [vp, vp, vp, vp, i32, vp]),
             "strata_cuda_expert_gemv": (i32, [vp, vp, i64, fp, fp, i32]),
             "strata_cuda_expert_gemv_dev": (i32, [vp, vp, i64, vp, vp, i32, vp]),
+            "strata_cuda_gemv_noalloc": (i32, [vp, u32, i64, i64, vp, vp, i32, vp]),
         }
         for name, (res, args) in sig.items():
             if not hasattr(L, name):
