@@ -139,6 +139,32 @@ int strata_cuda_expert_gemv(strata_ctx *ctx, const strata_weight *w, int64_t e, 
 int strata_cuda_expert_gemv_dev(strata_ctx *ctx, const strata_weight *w, int64_t e,
                                 const float *x_dev, float *y_dev, int batch, void *stream);
 
+/* ------------------------------------------------------------ prefill GEMM */
+
+/* The prompt-prefill form of ComputeBackend::gemv: the reference runs one
+ * gemv per prompt token (crates/strata-core/src/generate.rs:116-118, through
+ * ops::gemv, crates/strata-core/src/ops.rs:14-28); this computes all m tokens
+ * at once on the tensor cores. y (m x rows f32) = x (m x cols) W^T for a dense
+ * Q4_K, Q5_K or Q6_K tensor whose cols is a multiple of 256 and whose row size
+ * in bytes is a multiple of 16. Activations are staged as bf16: the _bf16
+ * entry points take bf16 bit patterns, the _f32 ones round f32 to bf16
+ * (nearest even) on the device first; outputs match gemv on the bf16-rounded
+ * activations within relative error 1e-2. Other quant types return
+ * STRATA_ERR_UNSUPPORTED_QUANT (use strata_cuda_gemv per token). The _dev
+ * variants need x 16-byte aligned and may size the context's workspace on
+ * their first call for a shape; workspace rules as for strata_cuda_gemv_dev. */
+int strata_cuda_gemm_bf16(strata_ctx *ctx, const strata_weight *w, const uint16_t *x, float *y, int64_t m);
+int strata_cuda_gemm_bf16_dev(strata_ctx *ctx, const strata_weight *w, const uint16_t *x_dev,
+                              float *y_dev, int64_t m, void *stream);
+int strata_cuda_gemm_f32(strata_ctx *ctx, const strata_weight *w, const float *x, float *y, int64_t m);
+int strata_cuda_gemm_f32_dev(strata_ctx *ctx, const strata_weight *w, const float *x_dev, float *y_dev,
+                             int64_t m, void *stream);
+
+/* Weight staging of the GEMM: 2 (default) = bf16 hi + bf16 residual, the
+ * precision the 1e-2 bound needs; 1 = a single bf16 copy, about half the
+ * tensor work but outside that bound (kept for measurement only). */
+int strata_cuda_set_gemm_terms(strata_ctx *ctx, int terms);
+
 /* ------------------------------------------------- decode GEMV, no allocation */
 
 /* No counterpart in the reference: an addition for callers that must not

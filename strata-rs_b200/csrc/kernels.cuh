@@ -34,4 +34,25 @@ struct ExpertGemvArgs {
     int sm_count;
 };
 
+// Prefill GEMM: Y[m][n] = sum_k X[m][k] * W[n][k]; X is M x K bf16 bits,
+// Y is M x N f32, both row-major; W is N rows of `row_bytes` (Q4_K/Q5_K/Q6_K).
+struct GemmArgs {
+    const uint8_t* W;
+    int64_t row_bytes;
+    int64_t N, K;
+    const uint16_t* X;
+    float* Y;
+    int64_t M;
+    int terms;       // 2: weights staged as bf16 hi + lo (the parity path); 1: hi only
+    int sm_count;
+    int* err;        // set to 1 by a kernel whose bounded wait expired
+    float* work;     // split-K partials, gemm_tc_work_floats() floats (null when that is 0)
+};
+
+bool gemm_tc_supported(uint32_t quant, const GemmArgs& a);
+int gemm_tc_splits(const GemmArgs& a);
+int64_t gemm_tc_work_floats(const GemmArgs& a);
+int launch_gemm_tc(uint32_t quant, const GemmArgs& a, cudaStream_t s);
+void launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, int sm_count, cudaStream_t s);
+
 }  // namespace strata

@@ -167,7 +167,7 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     cudaSetDevice(ctx->device);
     int rc = wait_stream(ctx, ctx->stream);
     comm_release(ctx);
-    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag})
+    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag, &ctx->gemm_work, &ctx->x_bf16})
         if (b->ptr) cudaFree(b->ptr);
     for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host})
         if (b->ptr) cudaFreeHost(b->ptr);
@@ -203,6 +203,13 @@ int strata_cuda_set_gemv_path(strata_ctx* ctx, int path) {
     if (!ctx || path < STRATA_GEMV_AUTO || path > STRATA_GEMV_TENSOR_CORES) return STRATA_ERR_INVALID;
     std::lock_guard<std::mutex> g(ctx->mu);
     ctx->gemv_path = path;
+    return STRATA_OK;
+}
+
+int strata_cuda_set_gemm_terms(strata_ctx* ctx, int terms) {
+    if (!ctx || terms < 1 || terms > 2) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    ctx->gemm_terms = terms;
     return STRATA_OK;
 }
 
@@ -365,6 +372,109 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     if ((rc = wait_stream(ctx, ctx->stream))) return rc;
     memcpy(y, ctx->y_host.ptr, yb);
     return STRATA_OK;
+}
+
+// ---- prefill GEMM
+
+static int gemm_enqueue(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev, int64_t m,
+                        cudaStream_t s) {
+    if (m < 1 || m >= (1ll << 31)) return fail(ctx, STRATA_ERR_INVALID, "m %lld outside 1..2^31-1", (long long)m);
+    if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 15))
+        return fail(ctx, STRATA_ERR_INVALID, "x and y must be 16-byte aligned");
+    GemmArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, m, ctx->gemm_terms, ctx->sm_count,
+               ctx->err_dev, nullptr};
+    if (!gemm_tc_supported(w->quant, a)) {
+        if (w->quant != kQ4_K && w->quant != kQ5_K && w->quant != kQ6_K)
+            return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no prefill gemm for quant %u", w->quant);
+        return fail(ctx, STRATA_ERR_INVALID, "prefill gemm needs cols %% 256 == 0 and 16-byte rows (cols %lld)",
+                    (long long)w->cols);
+    }
+    const int64_t wf = gemm_tc_work_floats(a);
+    if (wf > 0) {
+        int rc = ensure_device(ctx, ctx->gemm_work, (size_t)wf * sizeof(float), "cudaMalloc(gemm split-K)");
+        if (rc) return rc;
+        a.work = (float*)ctx->gemm_work.ptr;
+    }
+    int k = launch_gemm_tc(w->quant, a, s);
+    if (k) return fail(ctx, STRATA_ERR_CUDA, "prefill gemm launch setup failed (%d)", k);
+    return check_launch(ctx, "prefill gemm kernel");
+}
+
+static int gemm_check(strata_ctx* ctx, const strata_weight* w, const void* x, const void* y) {
+    int rc = check_weight(ctx, w, false);
+    if (rc) return rc;
+    if (!x || !y) return fail(ctx, STRATA_ERR_INVALID, "null x or y");
+    return STRATA_OK;
+}
+
+int strata_cuda_gemm_bf16_dev(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev,
+                              int64_t m, void* stream) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = gemm_check(ctx, w, x_dev, y_dev);
+    if (rc) return rc;
+    cudaSetDevice(ctx->device);
+    return gemm_enqueue(ctx, w, x_dev, y_dev, m, pick_stream(ctx, stream));
+}
+
+int strata_cuda_gemm_f32_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int64_t m,
+                             void* stream) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = gemm_check(ctx, w, x_dev, y_dev);
+    if (rc) return rc;
+    if (m < 1 || m >= (1ll << 31)) return fail(ctx, STRATA_ERR_INVALID, "m %lld outside 1..2^31-1", (long long)m);
+    cudaSetDevice(ctx->device);
+    const int64_t n = m * w->cols;
+    if ((rc = ensure_device(ctx, ctx->x_bf16, (size_t)n * 2, "cudaMalloc(x bf16)"))) return rc;
+    cudaStream_t s = pick_stream(ctx, stream);
+    launch_f32_to_bf16(x_dev, (uint16_t*)ctx->x_bf16.ptr, n, ctx->sm_count, s);
+    if ((rc = check_launch(ctx, "bf16 rounding kernel"))) return rc;
+    return gemm_enqueue(ctx, w, (const uint16_t*)ctx->x_bf16.ptr, y_dev, m, s);
+}
+
+// Host-buffer GEMM: pinned staging, H2D, optional f32 -> bf16 rounding, GEMM, D2H, bounded wait.
+static int gemm_host(strata_ctx* ctx, const strata_weight* w, const void* x, size_t x_elem, float* y, int64_t m) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = gemm_check(ctx, w, x, y);
+    if (rc) return rc;
+    if (m < 1 || m >= (1ll << 31)) return fail(ctx, STRATA_ERR_INVALID, "m %lld outside 1..2^31-1", (long long)m);
+    cudaSetDevice(ctx->device);
+    const size_t xb = (size_t)m * (size_t)w->cols * x_elem;
+    const size_t yb = (size_t)m * (size_t)w->rows * sizeof(float);
+    if ((rc = ensure_device(ctx, ctx->x_dev, xb, "cudaMalloc(x)"))) return rc;
+    if ((rc = ensure_device(ctx, ctx->y_dev, yb, "cudaMalloc(y)"))) return rc;
+    if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
+    if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
+    const uint16_t* xg = (const uint16_t*)ctx->x_dev.ptr;
+    if (x_elem == 4) {
+        const size_t nb = (size_t)m * (size_t)w->cols * 2;
+        if ((rc = ensure_device(ctx, ctx->x_bf16, nb, "cudaMalloc(x bf16)"))) return rc;
+        xg = (const uint16_t*)ctx->x_bf16.ptr;
+    }
+    memcpy(ctx->x_host.ptr, x, xb);
+    cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
+    if (x_elem == 4) {
+        launch_f32_to_bf16((const float*)ctx->x_dev.ptr, (uint16_t*)ctx->x_bf16.ptr, m * w->cols, ctx->sm_count,
+                           ctx->stream);
+        if ((rc = check_launch(ctx, "bf16 rounding kernel"))) return rc;
+    }
+    if ((rc = gemm_enqueue(ctx, w, xg, (float*)ctx->y_dev.ptr, m, ctx->stream))) return rc;
+    e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
+    if ((rc = wait_stream(ctx, ctx->stream))) return rc;
+    memcpy(y, ctx->y_host.ptr, yb);
+    return STRATA_OK;
+}
+
+int strata_cuda_gemm_bf16(strata_ctx* ctx, const strata_weight* w, const uint16_t* x, float* y, int64_t m) {
+    return gemm_host(ctx, w, x, 2, y, m);
+}
+
+int strata_cuda_gemm_f32(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int64_t m) {
+    return gemm_host(ctx, w, x, 4, y, m);
 }
 
 // ---- expert GEMV

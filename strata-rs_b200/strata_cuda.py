@@ -77,6 +77,11 @@ def lib() -> C.CDLL:
             "strata_cuda_expert_gemv": (i32, [vp, vp, i64, fp, fp, i32]),
             "strata_cuda_expert_gemv_dev": (i32, [vp, vp, i64, vp, vp, i32, vp]),
             "strata_cuda_gemv_noalloc": (i32, [vp, u32, i64, i64, vp, vp, i32, vp]),
+            "strata_cuda_gemm_bf16": (i32, [vp, vp, vp, fp, i64]),
+            "strata_cuda_gemm_bf16_dev": (i32, [vp, vp, vp, vp, i64, vp]),
+            "strata_cuda_gemm_f32": (i32, [vp, vp, fp, fp, i64]),
+            "strata_cuda_gemm_f32_dev": (i32, [vp, vp, vp, vp, i64, vp]),
+            "strata_cuda_set_gemm_terms": (i32, [vp, i32]),
         }
         for name, (res, args) in sig.items():
             if not hasattr(L, name):
@@ -207,7 +212,32 @@ class Context:
         self.check(lib().strata_cuda_expert_gemv(self.h, w.handle, e, _fptr(x), _fptr(y), batch))
         return y[0] if x.ndim == 1 else y
 
+    def gemm_bf16(self, w: Weight, x_bits: np.ndarray) -> np.ndarray:
+        """Prefill GEMM: x_bits is m x cols bf16 bit patterns (uint16); returns m x rows f32."""
+        x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+        m = x_bits.shape[0]
+        y = np.empty((m, w.rows), np.float32)
+        self.check(lib().strata_cuda_gemm_bf16(self.h, w.handle, x_bits.ctypes.data, _fptr(y), m))
+        return y
+
+    def gemm_f32(self, w: Weight, x: np.ndarray) -> np.ndarray:
+        """Prefill GEMM on f32 activations (rounded to bf16 on the device)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        m = x.shape[0]
+        y = np.empty((m, w.rows), np.float32)
+        self.check(lib().strata_cuda_gemm_f32(self.h, w.handle, _fptr(x), _fptr(y), m))
+        return y
+
+    def set_gemm_terms(self, terms: int):
+        self.check(lib().strata_cuda_set_gemm_terms(self.h, terms))
+
     # device-pointer variants (int addresses, e.g. torch.Tensor.data_ptr())
+    def gemm_bf16_dev(self, w: Weight, x_ptr: int, y_ptr: int, m: int, stream: int = 0):
+        self.check(lib().strata_cuda_gemm_bf16_dev(self.h, w.handle, x_ptr, y_ptr, m, stream or None))
+
+    def gemm_f32_dev(self, w: Weight, x_ptr: int, y_ptr: int, m: int, stream: int = 0):
+        self.check(lib().strata_cuda_gemm_f32_dev(self.h, w.handle, x_ptr, y_ptr, m, stream or None))
+
     def gemv_dev(self, w: Weight, x_ptr: int, y_ptr: int, batch: int, stream: int = 0):
         self.check(lib().strata_cuda_gemv_dev(self.h, w.handle, x_ptr, y_ptr, batch, stream or None))
 
