@@ -14,9 +14,12 @@
 //   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16
 //               (A = dequantized weights, B = X, D in TMEM) and commits each
 //               stage's release to an mbarrier;
-//   warps 2..5  one weight row per thread: dequantize each K step into bf16 in
-//               the same SW128 layout, then read the accumulator back with
-//               tcgen05.ld and store Y.
+//   warps 2..9  two threads per weight row, each dequantizing half of every K
+//               step into bf16 in the same SW128 layout (two such warps per
+//               scheduler hide each other's latency), then read the
+//               accumulators back with tcgen05.ld and store Y.
+// X and W have separate rings (up to 4 and 3 stages as shared memory allows):
+// the X copy of a step is issued several MMA steps ahead of its use.
 // Precision: a single bf16 copy of a K-quant weight keeps 8 of its up to 17
 // significant bits, which misses the 1e-2 bound of the parity metric
 // (max |y - ref| / max(|ref|, 1e-3 |ref|inf)) by two orders of magnitude.
@@ -41,9 +44,9 @@ namespace {
 
 constexpr int kRowsTile = 128;  // UMMA M
 constexpr int kKStep = 64;      // bf16 elements per 128-byte swizzled row
-constexpr int kStagesG = 2;     // K-step ring depth
 constexpr int kRawSlots = 2;    // raw super-block ring depth
-constexpr int kThreadsG = 6 * 32;
+constexpr int kDequantWarps = 8;
+constexpr int kThreadsG = (2 + kDequantWarps) * 32;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ uint64_t now_ns() {
@@ -199,68 +202,62 @@ __device__ __forceinline__ void load_sb(const uint8_t* b, SbState<Q>& s) {
     }
 }
 
-// Dequantize K step kk (elements 64 kk .. 64 kk + 63) of this thread's
-// super-block into row r of the stage's A tile(s).
+// Dequantize half h of K step kk -- elements 64 kk + 32 h .. + 31, the 16-byte
+// units 4h .. 4h + 3 -- of this thread's super-block into row r of the
+// stage's A tile(s). h is warp-uniform.
 template <uint32_t Q, int TERMS>
-__device__ __forceinline__ void dequant_step(const uint8_t* b, const SbState<Q>& s, int kk, int r,
+__device__ __forceinline__ void dequant_half(const uint8_t* b, const SbState<Q>& s, int kk, int h, int r,
                                              uint8_t* tile) {
     if constexpr (Q == kQ4_K || Q == kQ5_K) {
-        // sub-blocks 2kk (low nibbles, units 0-3) and 2kk+1 (high nibbles, units 4-7)
-        const int j0 = 2 * kk, j1 = 2 * kk + 1;
-        const uint32_t sc0 = ((j0 < 4 ? s.sc_lo : s.sc_hi) >> (8 * (j0 & 3))) & 0xFFu;
-        const uint32_t sc1 = ((j1 < 4 ? s.sc_lo : s.sc_hi) >> (8 * (j1 & 3))) & 0xFFu;
-        const uint32_t mn0 = ((j0 < 4 ? s.m_lo : s.m_hi) >> (8 * (j0 & 3))) & 0xFFu;
-        const uint32_t mn1 = ((j1 < 4 ? s.m_lo : s.m_hi) >> (8 * (j1 & 3))) & 0xFFu;
-        const float dA = s.d * (float)sc0, nA = -(s.dmin * (float)mn0);
-        const float dB = s.d * (float)sc1, nB = -(s.dmin * (float)mn1);
+        // sub-block j = 2kk + h: low nibbles of qs[32kk..] for h = 0, high nibbles for h = 1
+        const int j = 2 * kk + h;
+        const uint32_t scb = ((j < 4 ? s.sc_lo : s.sc_hi) >> (8 * (j & 3))) & 0xFFu;
+        const uint32_t mnb = ((j < 4 ? s.m_lo : s.m_hi) >> (8 * (j & 3))) & 0xFFu;
+        const float dA = s.d * (float)scb, nA = -(s.dmin * (float)mnb);
+        const float2 sc2 = make_float2(dA, dA), mn2 = make_float2(nA, nA);
         const uint8_t* qs = b + ((Q == kQ4_K) ? 16 : 48) + 32 * kk;
         const uint4 qa = *reinterpret_cast<const uint4*>(qs);
         const uint4 qb = *reinterpret_cast<const uint4*>(qs + 16);
         const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const int nsh = 4 * h;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const bool second = u >= 4;
-            const float2 sc2 = second ? make_float2(dB, dB) : make_float2(dA, dA);
-            const float2 mn2 = second ? make_float2(nB, nB) : make_float2(nA, nA);
+        for (int u = 0; u < 4; ++u) {
             uint32_t hi[4], lo[4];
 #pragma unroll
             for (int wi = 0; wi < 2; ++wi) {
-                const int i = 2 * (u & 3) + wi;
-                uint32_t v = second ? ((qw[i] >> 4) & 0x0F0F0F0Fu) : (qw[i] & 0x0F0F0F0Fu);
-                if constexpr (Q == kQ5_K) v |= ((s.qh[i] >> (second ? j1 : j0)) & 0x01010101u) << 4;
+                const int i = 2 * u + wi;
+                uint32_t v = (qw[i] >> nsh) & 0x0F0F0F0Fu;
+                if constexpr (Q == kQ5_K) v |= ((s.qh[i] >> j) & 0x01010101u) << 4;
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
                     const float2 w = __ffma2_rn(sc2, byte_pair_f(v, 2 * p), mn2);
                     split_pair<TERMS>(w, hi[2 * wi + p], lo[2 * wi + p]);
                 }
             }
-            store_unit<TERMS>(tile, sw128_unit(r, u), hi, lo);
+            store_unit<TERMS>(tile, sw128_unit(r, 4 * h + u), hi, lo);
         }
     } else {
-        // Q6_K: half H = kk / 2 (ql 64 B, qh 32 B); quarters g0 = 2 (kk & 1), g0 + 1
-        const int H = kk >> 1, g0 = 2 * (kk & 1);
-        uint32_t ql[16], qh[8];
-        ld_words<16>(b + 64 * H, ql);
+        // Q6_K: half H = kk / 2 of the block; quarter g = 2 (kk & 1) + h of that half:
+        // ql bytes 64H + 32 (g & 1) + l (low nibble for g < 2, high for g >= 2),
+        // qh bytes 128 + 32H + l (bits 2g, 2g + 1), u8 scale 8H + 2g + l / 16
+        const int H = kk >> 1, g = 2 * (kk & 1) + h;
+        uint32_t ql[8], qh[8];
+        ld_words<8>(b + 64 * H + 32 * (g & 1), ql);
         ld_words<8>(b + 128 + 32 * H, qh);
+        const uint64_t sc64 = H ? (((uint64_t)s.sc[3] << 32) | s.sc[2]) : (((uint64_t)s.sc[1] << 32) | s.sc[0]);
+        const int nsh = 4 * (g >> 1), hsh = 2 * g;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int g = g0 + (u >> 2);
-            // scale byte 8H + 2g + (u&3)/2: word 2H + (that >> 2) (selected, not indexed,
-            // so the scale words stay in registers), byte (2g + (u&3)/2) & 3
-            const int within = 2 * g + ((u & 3) >> 1);  // compile-time after unrolling, up to g0
-            const uint32_t w_lo = (within >> 2) ? s.sc[1] : s.sc[0];
-            const uint32_t w_hi = (within >> 2) ? s.sc[3] : s.sc[2];
+        for (int u = 0; u < 4; ++u) {
             // the reference reads Q6_K scales as u8 (crates/strata-gguf/src/dequant.rs:208-234)
-            const uint32_t scv = ((H ? w_hi : w_lo) >> (8 * (within & 3))) & 0xFFu;
+            const uint32_t scv = (uint32_t)(sc64 >> (8 * (2 * g + (u >> 1)))) & 0xFFu;
             const float ds = s.d * (float)scv;
             const float2 ds2 = make_float2(ds, ds);
             uint32_t hi[4], lo[4];
 #pragma unroll
             for (int wi = 0; wi < 2; ++wi) {
-                const int i = 2 * (u & 3) + wi;
-                const uint32_t src = ql[i + 8 * (g & 1)];
-                uint32_t v = (g >= 2) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
-                v |= ((qh[i] >> (2 * g)) & 0x03030303u) << 4;
+                const int i = 2 * u + wi;
+                uint32_t v = (ql[i] >> nsh) & 0x0F0F0F0Fu;
+                v |= ((qh[i] >> hsh) & 0x03030303u) << 4;
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
                     const float2 q = __fadd2_rn(byte_pair_f(v, 2 * p), make_float2(-32.0f, -32.0f));
@@ -268,7 +265,7 @@ __device__ __forceinline__ void dequant_step(const uint8_t* b, const SbState<Q>&
                     split_pair<TERMS>(w, hi[2 * wi + p], lo[2 * wi + p]);
                 }
             }
-            store_unit<TERMS>(tile, sw128_unit(r, u), hi, lo);
+            store_unit<TERMS>(tile, sw128_unit(r, 4 * h + u), hi, lo);
         }
     }
 }
@@ -282,27 +279,44 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 
+// Ring depths: X (activation) stages, W (dequantized weight) stages. Deeper
+// rings where shared memory allows; TN = 256 with two terms takes 2 W + 3 X.
+template <uint32_t Q, int TN, int TERMS>
+struct GemmCfg {
+    static constexpr int kBW = raw_box_bytes<Q>();
+    static constexpr int kRawSlot = kRowsTile * kBW;
+    static constexpr int kWTile = kRowsTile * 128;
+    static constexpr int kWStage = TERMS * kWTile;
+    static constexpr int kXStage = TN * 128;
+    static constexpr int bytes(int ws, int xs) { return ws * kWStage + xs * kXStage + kRawSlots * kRawSlot + 1024; }
+    static constexpr int kBudget = 227 * 1024 - 256;  // opt-in maximum less the static barriers
+    static constexpr int kWS = bytes(3, 4) <= kBudget ? 3 : 2;
+    static constexpr int kXS = bytes(kWS, 4) <= kBudget ? 4 : bytes(kWS, 3) <= kBudget ? 3 : 2;
+    static constexpr int kSmem = bytes(kWS, kXS);
+    static_assert(kSmem <= kBudget, "GEMM tile does not fit shared memory");
+    static_assert(kRawSlot % 1024 == 0 && kWStage % 1024 == 0 && kXStage % 1024 == 0,
+                  "tiles must stay 1024-byte aligned");
+};
+
 template <uint32_t Q, int TN, int TERMS>
 __global__ void __launch_bounds__(kThreadsG, 1)
 gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, int M,
                   int N, int nblk, float* __restrict__ Y, int64_t split_stride, int* __restrict__ err) {
-    constexpr int BW = raw_box_bytes<Q>();
-    constexpr int RAW_SLOT = kRowsTile * BW;  // a multiple of 1024
-    constexpr int WTILE = kRowsTile * 128;    // one bf16 [128][64] tile
-    constexpr int XTILE = TN * 128;           // X [TN][64]
-    constexpr int STAGE = TERMS * WTILE + XTILE;
+    using C = GemmCfg<Q, TN, TERMS>;
+    constexpr int BW = C::kBW, RAW_SLOT = C::kRawSlot, WTILE = C::kWTile;
+    constexpr int WS = C::kWS, XS = C::kXS;
     // one TN-column f32 accumulator per weight term: the small lo products get
     // their own, so only the hi products round against the large running sums
     constexpr int TMEM_COLS = TN * TERMS <= 32 ? 32 : TN * TERMS <= 64 ? 64 : TN * TERMS <= 128 ? 128
                             : TN * TERMS <= 256 ? 256 : 512;
     static_assert(TN * TERMS <= 512, "accumulators exceed TMEM");
-    static_assert(RAW_SLOT % 1024 == 0 && STAGE % 1024 == 0, "tiles must stay 1024-byte aligned");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = sm;                  // kStagesG * STAGE
-    uint8_t* raw = sm + kStagesG * STAGE;  // kRawSlots * RAW_SLOT
+    uint8_t* wst = sm;                             // WS x [TERMS][128][64] bf16
+    uint8_t* xst = wst + WS * C::kWStage;          // XS x [TN][64] bf16
+    uint8_t* raw = xst + XS * C::kXStage;          // kRawSlots x [128][BW] bytes
     __shared__ __align__(8) uint64_t raw_full[kRawSlots], raw_empty[kRawSlots];
-    __shared__ __align__(8) uint64_t x_full[kStagesG], w_full[kStagesG], st_empty[kStagesG], acc_full;
+    __shared__ __align__(8) uint64_t x_full[XS], x_empty[XS], w_full[WS], w_empty[WS], acc_full;
     __shared__ uint32_t tmem_base;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -318,17 +332,20 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRawSlots; ++i) {
             bar_init(smem_addr(&raw_full[i]), 1);
-            bar_init(smem_addr(&raw_empty[i]), 4);
+            bar_init(smem_addr(&raw_empty[i]), kDequantWarps);
         }
-        for (int i = 0; i < kStagesG; ++i) {
+        for (int i = 0; i < XS; ++i) {
             bar_init(smem_addr(&x_full[i]), 1);
-            bar_init(smem_addr(&w_full[i]), 4);
-            bar_init(smem_addr(&st_empty[i]), 1);
+            bar_init(smem_addr(&x_empty[i]), 1);
+        }
+        for (int i = 0; i < WS; ++i) {
+            bar_init(smem_addr(&w_full[i]), kDequantWarps);
+            bar_init(smem_addr(&w_empty[i]), 1);
         }
         bar_init(smem_addr(&acc_full), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {  // TMEM accumulator: 128 lanes x TMEM_COLS f32 columns
+    if (warp == 1) {  // TMEM accumulators: 128 lanes x TMEM_COLS f32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
                      "r"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -339,7 +356,8 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     const uint32_t tmem_d = tmem_base;
 
     if (warp == 0) {
-        // ---------------- producer; every wait is warp-uniform, lane 0 issues
+        // ---------------- producer; every wait is warp-uniform, lane 0 issues.
+        // Raw super-blocks run ahead of the X steps by up to kRawSlots blocks.
         int j = 0, n_raw = 0;
         bool live = true;
         for (int t = 0; t < nsb && live; ++t) {
@@ -356,23 +374,22 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
             }
             ++n_raw;
             for (int kk = 0; kk < 4; ++kk) {
-                const int s = j % kStagesG;
-                if (j >= kStagesG)
-                    live = __all_sync(0xFFFFFFFFu,
-                                      bar_wait(smem_addr(&st_empty[s]), ((j / kStagesG) - 1) & 1, err));
+                const int s = j % XS;
+                if (j >= XS)
+                    live = __all_sync(0xFFFFFFFFu, bar_wait(smem_addr(&x_empty[s]), ((j / XS) - 1) & 1, err));
                 if (!live) break;
                 if (lane == 0) {
                     const uint32_t fb = smem_addr(&x_full[s]);
-                    bar_expect_tx(fb, XTILE);
-                    tma_2d(smem_addr(stages + s * STAGE + TERMS * WTILE), &xmap, (sb * 4 + kk) * kKStep, tok0, fb);
+                    bar_expect_tx(fb, C::kXStage);
+                    tma_2d(smem_addr(xst + s * C::kXStage), &xmap, (sb * 4 + kk) * kKStep, tok0, fb);
                 }
                 ++j;
             }
         }
         // drain: the last phase of every barrier a copy was issued on has
         // completed (immediate when the consumers already waited on it)
-        for (int s = 0; s < kStagesG; ++s) {
-            const int uses = j > s ? (j - s + kStagesG - 1) / kStagesG : 0;
+        for (int s = 0; s < XS; ++s) {
+            const int uses = j > s ? (j - s + XS - 1) / XS : 0;
             if (uses) bar_wait(smem_addr(&x_full[s]), (uses - 1) & 1, err);
         }
         for (int rs = 0; rs < kRawSlots; ++rs) {
@@ -383,20 +400,20 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
         // ---------------- MMA issuer
         constexpr uint32_t idesc = idesc_bf16(kRowsTile, TN);
         for (int j = 0; j < nsteps; ++j) {
-            const int s = j % kStagesG;
-            const uint32_t par = (j / kStagesG) & 1;
-            const bool ok = bar_wait(smem_addr(&x_full[s]), par, err) && bar_wait(smem_addr(&w_full[s]), par, err);
+            const int xs = j % XS, ws = j % WS;
+            const bool ok = bar_wait(smem_addr(&x_full[xs]), (j / XS) & 1, err) &&
+                            bar_wait(smem_addr(&w_full[ws]), (j / WS) & 1, err);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (lane == 0) {
-                const uint32_t st = smem_addr(stages + s * STAGE);
-                const uint32_t xs = st + TERMS * WTILE;
+                const uint32_t wa = smem_addr(wst + ws * C::kWStage);
+                const uint32_t xa = smem_addr(xst + xs * C::kXStage);
 #pragma unroll
                 for (int k16 = 0; k16 < kKStep / 16; ++k16) {
 #pragma unroll
                     for (int term = 0; term < TERMS; ++term) {
-                        const uint64_t da = sw128_desc(st + term * WTILE + 32 * k16);
-                        const uint64_t db = sw128_desc(xs + 32 * k16);
+                        const uint64_t da = sw128_desc(wa + term * WTILE + 32 * k16);
+                        const uint64_t db = sw128_desc(xa + 32 * k16);
                         const uint32_t acc = (j > 0 || k16 > 0) ? 1u : 0u;
                         asm volatile(
                             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -406,9 +423,12 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
                             : "memory");
                     }
                 }
-                // the stage is free once these MMAs have read it
+                // both stages are free once these MMAs have read them
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 smem_addr(&st_empty[s]))
+                                 smem_addr(&x_empty[xs]))
+                             : "memory");
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 smem_addr(&w_empty[ws]))
                              : "memory");
             }
             __syncwarp();
@@ -420,8 +440,11 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
                          : "memory");
         __syncwarp();
     } else {
-        // ---------------- dequantizers (one weight row per thread), then the epilogue
-        const int r = threadIdx.x - 64;  // 0..127
+        // ---------------- dequantizers: thread (h, r) converts half h of each K
+        // step of weight row r (warps 2-5: h = 0, warps 6-9: h = 1, so every
+        // scheduler runs two of them); then the epilogue
+        const int idx = threadIdx.x - 64;
+        const int r = idx & (kRowsTile - 1), h = idx >> 7;
         int j = 0;
         bool live = true;
         for (int t = 0; t < nsb && live; ++t) {
@@ -434,12 +457,12 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
             load_sb<Q>(blk, st);
 #pragma unroll 1
             for (int kk = 0; kk < 4; ++kk, ++j) {
-                const int s = j % kStagesG;
-                if (j >= kStagesG) {
-                    live = __all_sync(0xFFFFFFFFu, bar_wait(smem_addr(&st_empty[s]), ((j / kStagesG) - 1) & 1, err));
+                const int s = j % WS;
+                if (j >= WS) {
+                    live = __all_sync(0xFFFFFFFFu, bar_wait(smem_addr(&w_empty[s]), ((j / WS) - 1) & 1, err));
                     if (!live) break;
                 }
-                dequant_step<Q, TERMS>(blk, st, kk, r, stages + s * STAGE);
+                dequant_half<Q, TERMS>(blk, st, kk, h, r, wst + s * C::kWStage);
                 // make the generic-proxy stores visible to the tensor core, then publish
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
@@ -448,13 +471,14 @@ gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
             __syncwarp();
             if (live && lane == 0) bar_arrive(smem_addr(&raw_empty[rs]));
         }
-        // epilogue: TMEM lane 32 (warp % 4) + lane holds weight row row0 + that lane
+        // epilogue: TMEM lane 32 (warp % 4) + lane holds weight row row0 + that
+        // lane; half h stores token columns [h TN / 2, (h + 1) TN / 2)
         const bool ready = bar_wait(smem_addr(&acc_full), 0, err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int lane_base = 32 * (warp & 3);
         const int row = row0 + lane_base + lane;
 #pragma unroll 1
-        for (int c = 0; c < TN; c += 16) {
+        for (int c = h * (TN / 2); c < (h + 1) * (TN / 2); c += 16) {
             uint32_t v[16], vl[16];
             const uint32_t taddr = tmem_d + ((uint32_t)lane_base << 16) + (uint32_t)c;
             tmem_ld16(taddr, v);
@@ -523,11 +547,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 
 int pick_tn(int64_t M) { return M <= 64 ? 64 : M <= 128 ? 128 : 256; }
 
-template <uint32_t Q>
-constexpr int smem_bytes(int TN, int TERMS) {
-    return kStagesG * (TERMS * kRowsTile * 128 + TN * 128) + kRawSlots * kRowsTile * raw_box_bytes<Q>() + 1024;
-}
-
 template <uint32_t Q, int TN, int TERMS>
 int launch_gemm_t(const GemmArgs& a, int splits, cudaStream_t s) {
     constexpr int BW = raw_box_bytes<Q>();
@@ -554,7 +573,7 @@ int launch_gemm_t(const GemmArgs& a, int splits, cudaStream_t s) {
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return -5;
     }
-    constexpr int smem = smem_bytes<Q>(TN, TERMS);
+    constexpr int smem = GemmCfg<Q, TN, TERMS>::kSmem;
     static bool configured[64] = {};  // the attribute is per device
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -6;
