@@ -165,6 +165,49 @@ int strata_cuda_gemm_f32_dev(strata_ctx *ctx, const strata_weight *w, const floa
  * tensor work but outside that bound (kept for measurement only). */
 int strata_cuda_set_gemm_terms(strata_ctx *ctx, int terms);
 
+/* ---------------------------------------------------------------- MoE layer */
+
+/* One MoE layer resident on the device: the weights of strata_core::moe::MoeLayer
+ * (crates/strata-core/src/moe.rs:22-35) as uploaded handles. Expert tensors
+ * are uploaded with n_expert = the number of experts this context holds:
+ * all of them on one GPU, the slice [expert_begin, expert_end) under expert
+ * parallelism (ids stay global). The shared expert is optional (NULL
+ * gate_shexp) and runs only where with_shared is set. */
+typedef struct strata_moe strata_moe;
+typedef struct {
+    const strata_weight *router;          /* [n_expert rows][n_embd]; may be NULL when logits are given */
+    const strata_weight *gate_exps;       /* experts [held][n_embd][n_ff] */
+    const strata_weight *up_exps;         /* experts [held][n_embd][n_ff] */
+    const strata_weight *down_exps;       /* experts [held][n_ff][n_embd] */
+    const strata_weight *gate_shexp;      /* [n_ff_shexp][n_embd] or NULL */
+    const strata_weight *up_shexp;        /* [n_ff_shexp][n_embd] */
+    const strata_weight *down_shexp;      /* [n_embd][n_ff_shexp] */
+    const strata_weight *gate_inp_shexp;  /* [1][n_embd] */
+    int64_t n_embd, n_expert, top_k, n_ff, n_ff_shexp;
+    int64_t expert_begin, expert_end;     /* experts held here: [begin, end) */
+    int with_shared;                      /* run the shared expert in this context */
+} strata_moe_desc;
+
+/* Validates shapes and quant types (experts: Q4_K, Q5_K, Q6_K or Q8_0 with
+ * n_ff and n_embd multiples of 256; n_expert <= 1024; top_k <= 64). The
+ * handles must outlive the layer. */
+int strata_cuda_moe_create(strata_ctx *ctx, const strata_moe_desc *desc, strata_moe **out);
+int strata_cuda_moe_destroy(strata_moe *layer);
+
+/* MoeLayer::route + MoeLayer::combine (moe.rs:48-144) for `tokens` tokens:
+ * x and out are tokens x n_embd f32. Routing comes from router_logits
+ * (tokens x n_expert f32) when given, else from the router GEMV on the
+ * bf16-rounded x (moe.rs:55-56). Under expert parallelism `out` holds this
+ * context's partial sum (its experts, plus the shared expert where held);
+ * the sum over contexts is the layer output. ids_out / weights_out
+ * (tokens x top_k, optional) receive the routing: global expert ids in
+ * ascending order and their renormalised weights. */
+int strata_cuda_moe_ffn(strata_ctx *ctx, const strata_moe *layer, const float *x, const float *router_logits,
+                        int64_t tokens, float *out, int32_t *ids_out, float *weights_out);
+int strata_cuda_moe_ffn_dev(strata_ctx *ctx, const strata_moe *layer, const float *x_dev,
+                            const float *router_logits_dev, int64_t tokens, float *out_dev,
+                            int32_t *ids_dev, float *weights_dev, void *stream);
+
 /* ------------------------------------------------- decode GEMV, no allocation */
 
 /* No counterpart in the reference: an addition for callers that must not

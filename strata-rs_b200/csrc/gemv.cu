@@ -155,6 +155,9 @@ template <uint32_t Q, int NB, int R, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_kquant_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
                    const float* __restrict__ X, float* __restrict__ Y) {
+    // token chunk blockIdx.y: rows [NB y, NB y + NB) of X and Y
+    X += (int64_t)blockIdx.y * NB * K;
+    Y += (int64_t)blockIdx.y * NB * N;
     constexpr int BB = block_bytes(Q);
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -230,6 +233,8 @@ template <int NB, int R, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
                  const float* __restrict__ X, float* __restrict__ Y) {
+    X += (int64_t)blockIdx.y * NB * K;
+    Y += (int64_t)blockIdx.y * NB * N;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int64_t nblk = K / 32;
@@ -298,6 +303,8 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, in
 template <uint32_t Q, int NB>
 __global__ void gemv_float_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
                                   const float* __restrict__ X, float* __restrict__ Y) {
+    X += (int64_t)blockIdx.y * NB * K;
+    Y += (int64_t)blockIdx.y * NB * N;
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < N; row += (int64_t)gridDim.x * warps) {
@@ -322,31 +329,33 @@ __global__ void gemv_float_kernel(const uint8_t* __restrict__ W, int64_t row_byt
 }
 
 template <uint32_t Q, int NB, int R>
-void launch_kq(const GemvArgs& a, cudaStream_t s) {
+void launch_kq(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     constexpr int WARPS = 4;
     int64_t tiles = (a.N + R - 1) / R;
     int64_t grid = (tiles + WARPS - 1) / WARPS;
     int64_t cap = (int64_t)a.sm_count * 8;
     if (grid > cap) grid = cap;
-    gemv_kquant_kernel<Q, NB, R, WARPS><<<(unsigned)grid, WARPS * 32, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y);
+    gemv_kquant_kernel<Q, NB, R, WARPS><<<dim3((unsigned)grid, chunks), WARPS * 32, 0, s>>>(a.W, a.row_bytes, a.N,
+                                                                                       a.K, a.X, a.Y);
 }
 
 template <int NB, int R>
-void launch_q8(const GemvArgs& a, cudaStream_t s) {
+void launch_q8(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     constexpr int WARPS = 4;
     int64_t tiles = (a.N + R - 1) / R;
     int64_t grid = (tiles + WARPS - 1) / WARPS;
     int64_t cap = (int64_t)a.sm_count * 8;
     if (grid > cap) grid = cap;
-    gemv_q8_0_kernel<NB, R, WARPS><<<(unsigned)grid, WARPS * 32, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y);
+    gemv_q8_0_kernel<NB, R, WARPS><<<dim3((unsigned)grid, chunks), WARPS * 32, 0, s>>>(a.W, a.row_bytes, a.N, a.K,
+                                                                                  a.X, a.Y);
 }
 
 template <uint32_t Q, int NB>
-void launch_float(const GemvArgs& a, cudaStream_t s) {
+void launch_float(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     int64_t grid = (a.N + 7) / 8;
     int64_t cap = (int64_t)a.sm_count * 16;
     if (grid > cap) grid = cap;
-    gemv_float_kernel<Q, NB><<<(unsigned)grid, 256, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y);
+    gemv_float_kernel<Q, NB><<<dim3((unsigned)grid, chunks), 256, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y);
 }
 
 // Rows per warp by batch: more rows share each activation load when the batch
@@ -400,8 +409,33 @@ int dispatch_float(const GemvArgs& a, cudaStream_t s) {
 
 }  // namespace
 
+// Batches above 8 run as full 8-token chunks (one launch, the chunk index on
+// grid.y) plus one launch for the remainder.
+static int launch_gemv_chunks(uint32_t quant, const GemvArgs& a, unsigned chunks, cudaStream_t s) {
+    switch (quant) {
+    case kQ4_K: launch_kq<kQ4_K, 8, 1>(a, s, chunks); return 0;
+    case kQ5_K: launch_kq<kQ5_K, 8, 1>(a, s, chunks); return 0;
+    case kQ6_K: launch_kq<kQ6_K, 8, 1>(a, s, chunks); return 0;
+    case kQ8_0: launch_q8<8, 1>(a, s, chunks); return 0;
+    case kF32: launch_float<kF32, 8>(a, s, chunks); return 0;
+    case kF16: launch_float<kF16, 8>(a, s, chunks); return 0;
+    case kBF16: launch_float<kBF16, 8>(a, s, chunks); return 0;
+    default: return -1;
+    }
+}
+
 int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s) {
     if (a.N <= 0 || a.batch <= 0) return 0;
+    if (a.batch > 8) {
+        const int full = a.batch / 8, rem = a.batch % 8;
+        if (launch_gemv_chunks(quant, a, (unsigned)full, s)) return -1;
+        if (rem == 0) return 0;
+        GemvArgs r = a;
+        r.X = a.X + (int64_t)full * 8 * a.K;
+        r.Y = a.Y + (int64_t)full * 8 * a.N;
+        r.batch = rem;
+        return launch_gemv(quant, r, s);
+    }
     switch (quant) {
     case kQ4_K: return dispatch_kq<kQ4_K>(a, s);
     case kQ5_K: return dispatch_kq<kQ5_K>(a, s);

@@ -43,8 +43,6 @@ namespace strata {
 
 namespace {
 
-constexpr int kMmaWarps = 8;
-
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 

@@ -167,7 +167,7 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     cudaSetDevice(ctx->device);
     int rc = wait_stream(ctx, ctx->stream);
     comm_release(ctx);
-    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag, &ctx->gemm_work, &ctx->x_bf16})
+    for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag, &ctx->gemm_work, &ctx->x_bf16, &ctx->moe_work})
         if (b->ptr) cudaFree(b->ptr);
     for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host})
         if (b->ptr) cudaFreeHost(b->ptr);

@@ -39,7 +39,7 @@ struct strata_ctx {
     uint32_t wait_timeout_ms = 60000;
     int gemv_path = 0;  // STRATA_GEMV_AUTO / _CUDA_CORES / _TENSOR_CORES
     int gemm_terms = 2;  // bf16 terms per staged GEMM weight
-    strata::DevBuf x_dev, y_dev, work, xfrag, gemm_work, x_bf16;
+    strata::DevBuf x_dev, y_dev, work, xfrag, gemm_work, x_bf16, moe_work;
     strata::PinnedBuf x_host, y_host;
     strata::CommState* comm = nullptr;
     int* err_host = nullptr;  // host-mapped word kernels set when a bounded wait expires

@@ -82,6 +82,10 @@ def lib() -> C.CDLL:
             "strata_cuda_gemm_f32": (i32, [vp, vp, fp, fp, i64]),
             "strata_cuda_gemm_f32_dev": (i32, [vp, vp, vp, vp, i64, vp]),
             "strata_cuda_set_gemm_terms": (i32, [vp, i32]),
+            "strata_cuda_moe_create": (i32, [vp, C.POINTER(MoeDesc), C.POINTER(vp)]),
+            "strata_cuda_moe_destroy": (i32, [vp]),
+            "strata_cuda_moe_ffn": (i32, [vp, vp, fp, fp, i64, fp, C.POINTER(C.c_int32), fp]),
+            "strata_cuda_moe_ffn_dev": (i32, [vp, vp, vp, vp, i64, vp, vp, vp, vp]),
         }
         for name, (res, args) in sig.items():
             if not hasattr(L, name):
@@ -90,6 +94,15 @@ def lib() -> C.CDLL:
             f.restype, f.argtypes = res, args
         _lib = L
     return _lib
+
+
+class MoeDesc(C.Structure):
+    """strata_moe_desc (strata_cuda.h)."""
+    _fields_ = [(nm, C.c_void_p) for nm in ("router", "gate_exps", "up_exps", "down_exps", "gate_shexp", "up_shexp",
+                                            "down_shexp", "gate_inp_shexp")]
+    _fields_ += [(nm, C.c_int64) for nm in ("n_embd", "n_expert", "top_k", "n_ff", "n_ff_shexp", "expert_begin",
+                                            "expert_end")]
+    _fields_ += [("with_shared", C.c_int)]
 
 
 def _fptr(a: np.ndarray):
@@ -130,6 +143,17 @@ class Weight:
     def free(self):
         if self.handle:
             lib().strata_cuda_free_weight(self.handle)
+            self.handle = None
+
+
+class MoeLayer:
+    def __init__(self, ctx: "Context", handle: C.c_void_p, n_embd: int, n_expert: int, top_k: int):
+        self.ctx, self.handle = ctx, handle
+        self.n_embd, self.n_expert, self.top_k = n_embd, n_expert, top_k
+
+    def free(self):
+        if self.handle:
+            lib().strata_cuda_moe_destroy(self.handle)
             self.handle = None
 
 
@@ -227,6 +251,42 @@ class Context:
         y = np.empty((m, w.rows), np.float32)
         self.check(lib().strata_cuda_gemm_f32(self.h, w.handle, _fptr(x), _fptr(y), m))
         return y
+
+    def moe_create(self, weights: dict, n_embd: int, n_expert: int, top_k: int, n_ff: int, n_ff_shexp: int = 0,
+                   expert_begin: int = 0, expert_end: int | None = None, with_shared: bool = True) -> "MoeLayer":
+        """weights maps MoeLayer field names (router, gate_exps, ...) to uploaded Weights."""
+        d = MoeDesc()
+        for nm in ("router", "gate_exps", "up_exps", "down_exps", "gate_shexp", "up_shexp", "down_shexp",
+                   "gate_inp_shexp"):
+            w = weights.get(nm)
+            h = w.handle if w is not None else None
+            setattr(d, nm, h.value if isinstance(h, C.c_void_p) else h)
+        d.n_embd, d.n_expert, d.top_k, d.n_ff, d.n_ff_shexp = n_embd, n_expert, top_k, n_ff, n_ff_shexp
+        d.expert_begin = expert_begin
+        d.expert_end = n_expert if expert_end is None else expert_end
+        d.with_shared = 1 if with_shared else 0
+        h = C.c_void_p()
+        self.check(lib().strata_cuda_moe_create(self.h, C.byref(d), C.byref(h)))
+        return MoeLayer(self, h, n_embd, n_expert, top_k)
+
+    def moe_ffn(self, layer: "MoeLayer", x: np.ndarray, logits: np.ndarray | None = None):
+        """MoE layer for each row of x (tokens x n_embd) -> (out, ids, weights)."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, layer.n_embd)
+        T = x.shape[0]
+        lg = None
+        if logits is not None:
+            lg = np.ascontiguousarray(logits, dtype=np.float32).reshape(T, layer.n_expert)
+        out = np.empty((T, layer.n_embd), np.float32)
+        ids = np.empty((T, layer.top_k), np.int32)
+        w = np.empty((T, layer.top_k), np.float32)
+        self.check(lib().strata_cuda_moe_ffn(self.h, layer.handle, _fptr(x), _fptr(lg) if lg is not None else None, T,
+                                             _fptr(out), ids.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(w)))
+        return out, ids, w
+
+    def moe_ffn_dev(self, layer: "MoeLayer", x_ptr: int, logits_ptr: int, tokens: int, out_ptr: int,
+                    ids_ptr: int = 0, wts_ptr: int = 0, stream: int = 0):
+        self.check(lib().strata_cuda_moe_ffn_dev(self.h, layer.handle, x_ptr, logits_ptr or None, tokens, out_ptr,
+                                                 ids_ptr or None, wts_ptr or None, stream or None))
 
     def set_gemm_terms(self, terms: int):
         self.check(lib().strata_cuda_set_gemm_terms(self.h, terms))

@@ -1,0 +1,207 @@
+"""Parity of the device MoE layer (through the C ABI) with the CPU oracle.
+
+MoeLayer::route + MoeLayer::combine (crates/strata-core/src/moe.rs:48-144):
+routing from given logits is compared exactly (ids) and to the bit or one
+ulp (weights); the layer output within rel_err 1e-3 (fp32 accumulation
+against the reference's f32/f64 mix).
+"""
+import numpy as np
+import pytest
+
+import oracle
+import strata_cuda as sc
+from conftest import rel_err
+from synth import Q4_K, Q5_K, Q6_K, Q8_0, F32, activations, bf16_round, quant_matrix, rng
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = sc.Context(0)
+    yield c
+    c.close()
+
+
+def make_layer(seed, n_embd, E, n_ff, n_ff_s, qe=Q4_K, qs=Q4_K, qr=Q4_K, shared=True, router=True):
+    t = {}
+    if router:
+        t["router"] = (qr, quant_matrix(seed, qr, E, n_embd))
+    t["gate_exps"] = (qe, quant_matrix(seed + 1, qe, n_embd, n_ff, E))
+    t["up_exps"] = (qe, quant_matrix(seed + 2, qe, n_embd, n_ff, E))
+    t["down_exps"] = (qe, quant_matrix(seed + 3, qe, n_ff, n_embd, E))
+    if shared:
+        t["gate_shexp"] = (qs, quant_matrix(seed + 4, qs, n_ff_s, n_embd))
+        t["up_shexp"] = (qs, quant_matrix(seed + 5, qs, n_ff_s, n_embd))
+        t["down_shexp"] = (qs, quant_matrix(seed + 6, qs, n_embd, n_ff_s))
+        t["gate_inp_shexp"] = (qs, quant_matrix(seed + 7, qs, 1, n_embd))
+    return t
+
+
+SHAPE = {"router": lambda d: (d["E"], d["n_embd"], 0), "gate_exps": lambda d: (d["n_embd"], d["n_ff"], d["E"]),
+         "up_exps": lambda d: (d["n_embd"], d["n_ff"], d["E"]), "down_exps": lambda d: (d["n_ff"], d["n_embd"], d["E"]),
+         "gate_shexp": lambda d: (d["n_ff_s"], d["n_embd"], 0), "up_shexp": lambda d: (d["n_ff_s"], d["n_embd"], 0),
+         "down_shexp": lambda d: (d["n_embd"], d["n_ff_s"], 0), "gate_inp_shexp": lambda d: (1, d["n_embd"], 0)}
+
+
+def upload(ctx, t, dims, e0=0, e1=None):
+    """Uploads the tensors; expert tensors restricted to experts [e0, e1)."""
+    ws = {}
+    for nm, (q, arr) in t.items():
+        rows, cols, ne = SHAPE[nm](dims)
+        if ne:
+            e1_ = ne if e1 is None else e1
+            per = arr.size // ne
+            ws[nm] = ctx.upload(arr[e0 * per:e1_ * per], q, rows, cols, n_expert=e1_ - e0)
+        else:
+            ws[nm] = ctx.upload(arr, q, rows, cols)
+    return ws
+
+
+def free_all(ws, layer=None):
+    if layer is not None:
+        layer.free()
+    for w in ws.values():
+        w.free()
+
+
+def check_routing(ids, wts, want_ids, want_w):
+    assert np.array_equal(ids.astype(np.int64), want_ids)
+    # weights: the same f32 operations; exp may differ from the host's expf by an ulp
+    d = np.abs(wts.view(np.int32).astype(np.int64) - want_w.view(np.int32).astype(np.int64))
+    assert d.max() <= 2, d.max()
+
+
+@pytest.mark.parametrize("T", [1, 3, 17])
+@pytest.mark.parametrize("qe", [Q4_K, Q5_K, Q6_K, Q8_0])
+def test_moe_small_from_logits(ctx, T, qe, threads):
+    dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
+    t = make_layer(1000 + qe, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"], qe=qe)
+    ws = upload(ctx, t, dims)
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    x = activations(1001 + T, T, dims["n_embd"])
+    logits = rng(1002 + T).standard_normal((T, dims["E"])).astype(np.float32)
+    out, ids, w = ctx.moe_ffn(layer, x, logits)
+    want, want_ids, want_w = oracle.moe_layer(t, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                                              x, logits, threads=threads)
+    check_routing(ids, w, want_ids, want_w)
+    for i in range(T):
+        assert rel_err(out[i], want[i]) < TOL, (i, rel_err(out[i], want[i]))
+    free_all(ws, layer)
+
+
+def test_moe_router_gemv_path(ctx, threads):
+    dims = dict(n_embd=512, E=32, k=4, n_ff=256, n_ff_s=256)
+    t = make_layer(1100, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"])
+    ws = upload(ctx, t, dims)
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    T = 9
+    x = activations(1101, T, dims["n_embd"])
+    out, ids, w = ctx.moe_ffn(layer, x, None)
+    want, want_ids, want_w = oracle.moe_layer(t, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                                              x, None, threads=threads)
+    # the router GEMV accumulates in f32 (the reference in f64): routing may only
+    # differ where the k-th and (k+1)-th probabilities are within that noise
+    lg = oracle.gemv(Q4_K, t["router"][1], dims["E"], dims["n_embd"], bf16_round(x), threads=threads)
+    for i in range(T):
+        srt = np.sort(lg[i])[::-1]
+        if srt[dims["k"] - 1] - srt[dims["k"]] < 1e-4 * max(1.0, abs(srt[0])):
+            continue
+        assert np.array_equal(ids[i], want_ids[i])
+        # weights go as exp(logit): the logits' f32 noise (~1e-6 of their
+        # magnitude, here tens) moves them by ~1e-5 relative
+        assert np.allclose(w[i], want_w[i], rtol=1e-3, atol=0)
+        assert rel_err(out[i], want[i]) < TOL
+    free_all(ws, layer)
+
+
+@pytest.mark.parametrize("T", [1, 64])
+def test_moe_config_layer(ctx, T, threads):
+    """The MoE FFN configuration: hidden 2048, 256 experts of SwiGLU width 512,
+    top-8 from N(0,1) logits, a shared expert of width 512, all Q4_K."""
+    dims = dict(n_embd=2048, E=256, k=8, n_ff=512, n_ff_s=512)
+    t = make_layer(1200, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"], router=False)
+    ws = upload(ctx, t, dims)
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    x = activations(1201 + T, T, dims["n_embd"])
+    logits = rng(1202 + T).standard_normal((T, dims["E"])).astype(np.float32)
+    out, ids, w = ctx.moe_ffn(layer, x, logits)
+    want, want_ids, want_w = oracle.moe_layer(t, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                                              x, logits, threads=threads)
+    check_routing(ids, w, want_ids, want_w)
+    errs = [rel_err(out[i], want[i]) for i in range(T)]
+    assert max(errs) < TOL, max(errs)
+    # deterministic run to run
+    out2, _, _ = ctx.moe_ffn(layer, x, logits)
+    assert np.array_equal(out.view(np.uint32), out2.view(np.uint32))
+    free_all(ws, layer)
+
+
+@pytest.mark.parametrize("G", [2, 4])
+def test_moe_expert_parallel_partials_sum(ctx, G):
+    """Expert parallelism on one GPU: G layers over expert slices (the shared
+    expert in the first) produce partial outputs whose sum is the layer."""
+    dims = dict(n_embd=512, E=32, k=4, n_ff=256, n_ff_s=256)
+    t = make_layer(1300, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"], router=False)
+    T = 11
+    x = activations(1301, T, dims["n_embd"])
+    logits = rng(1302).standard_normal((T, dims["E"])).astype(np.float32)
+    ws = upload(ctx, t, dims)
+    full = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    want, want_ids, want_w = ctx.moe_ffn(full, x, logits)
+    total = np.zeros_like(want)
+    per = dims["E"] // G
+    for r in range(G):
+        wr = upload(ctx, {k: v for k, v in t.items()}, dims, e0=r * per, e1=(r + 1) * per)
+        lr = ctx.moe_create(wr, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                            expert_begin=r * per, expert_end=(r + 1) * per, with_shared=(r == 0))
+        part, ids, w = ctx.moe_ffn(lr, x, logits)
+        assert np.array_equal(ids, want_ids) and np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+        total += part
+        free_all(wr, lr)
+    for i in range(T):
+        assert rel_err(total[i], want[i]) < 1e-5
+    free_all(ws, full)
+
+
+def test_moe_dev_entry_on_torch_stream(ctx):
+    torch = pytest.importorskip("torch")
+    dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
+    t = make_layer(1400, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"], router=False)
+    ws = upload(ctx, t, dims)
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    T = 5
+    x = activations(1401, T, dims["n_embd"])
+    logits = rng(1402).standard_normal((T, dims["E"])).astype(np.float32)
+    host, _, _ = ctx.moe_ffn(layer, x, logits)
+    xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+    od = torch.empty((T, dims["n_embd"]), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ctx.moe_ffn_dev(layer, xd.data_ptr(), ld.data_ptr(), T, od.data_ptr(), stream=s.cuda_stream)
+    s.synchronize()
+    assert np.array_equal(od.cpu().numpy().view(np.uint32), host.view(np.uint32))
+    free_all(ws, layer)
+
+
+def test_moe_rejects(ctx):
+    dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
+    t = make_layer(1500, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"], router=False)
+    ws = upload(ctx, t, dims)
+    with pytest.raises(sc.BackendError) as e:
+        ctx.moe_create(ws, dims["n_embd"], dims["E"], 65, dims["n_ff"], dims["n_ff_s"])
+    assert e.value.code == sc.ERR_INVALID
+    with pytest.raises(sc.BackendError) as e:  # down_exps passed as gate_exps: wrong shape
+        ctx.moe_create(dict(ws, gate_exps=ws["down_exps"]), dims["n_embd"], dims["E"], 4, dims["n_ff"], dims["n_ff_s"])
+    assert e.value.code == sc.ERR_INVALID
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    with pytest.raises(sc.BackendError) as e:  # no router weight and no logits
+        ctx.moe_ffn(layer, activations(1, 2, dims["n_embd"]), None)
+    assert e.value.code == sc.ERR_INVALID
+    free_all(ws, layer)
+    fe = ctx.upload(np.zeros(16 * 512 * 256 * 4, np.uint8), F32, 512, 256, n_expert=16)
+    with pytest.raises(sc.BackendError) as e:
+        ctx.moe_create(dict(gate_exps=fe, up_exps=fe, down_exps=fe), 512, 16, 4, 256)
+    assert e.value.code in (sc.ERR_UNSUPPORTED_QUANT, sc.ERR_INVALID)
+    fe.free()
