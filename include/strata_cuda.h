@@ -208,6 +208,35 @@ int strata_cuda_moe_ffn_dev(strata_ctx *ctx, const strata_moe *layer, const floa
                             const float *router_logits_dev, int64_t tokens, float *out_dev,
                             int32_t *ids_dev, float *weights_dev, void *stream);
 
+/* ------------------------------------------------------------------ multi-GPU */
+
+/* No counterpart in the reference, which runs on one device: the sharded
+ * forms of its gemv and MoE layer, one process (and one context) per GPU.
+ * strata_cuda_comm_unique_id is called on one rank; its bytes reach the other
+ * ranks by the caller's means (e.g. a torch.distributed broadcast), then every
+ * rank calls strata_cuda_comm_init. Init waits at most the context's wait
+ * timeout for the other ranks (STRATA_ERR_TIMEOUT), so a rank that never
+ * joins does not block the others forever. */
+#define STRATA_COMM_ID_BYTES 128
+int strata_cuda_comm_unique_id(uint8_t *id_out /* STRATA_COMM_ID_BYTES */);
+int strata_cuda_comm_init(strata_ctx *ctx, int rank, int world, const uint8_t *id);
+int strata_cuda_comm_info(const strata_ctx *ctx, int *rank, int *world);
+
+/* Row-sharded projection: w holds this rank's rows [rank R, (rank + 1) R) of
+ * an OUT = world * R row matrix (every rank the same R). The local GEMV
+ * (batch 1..8) or prefill GEMM (m tokens, bf16 x) writes its slice and an
+ * all-gather over NVLink fills y_dev (batch | m) x OUT on every rank. */
+int strata_cuda_gemv_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, const float *x_dev, float *y_dev,
+                                 int batch, void *stream);
+int strata_cuda_gemm_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, const uint16_t *x_dev,
+                                 float *y_dev, int64_t m, void *stream);
+
+/* Expert-parallel MoE layer: this rank's partial sum (its experts, plus the
+ * shared expert on the rank whose layer has with_shared) all-reduced, so
+ * out_dev holds the full layer output on every rank. */
+int strata_cuda_moe_ffn_ep_dev(strata_ctx *ctx, const strata_moe *layer, const float *x_dev,
+                               const float *router_logits_dev, int64_t tokens, float *out_dev, void *stream);
+
 /* ------------------------------------------------- decode GEMV, no allocation */
 
 /* No counterpart in the reference: an addition for callers that must not

@@ -55,7 +55,7 @@ def build(ptxas_v: bool = False, quiet: bool = True) -> Path:
                 print(log, file=sys.stderr)
     if not OUT.exists() or any(o.stat().st_mtime > OUT.stat().st_mtime for o in objs):
         cmd = [NVCC, *ARCH, "-shared", "-o", str(OUT), *map(str, objs),
-               "-L/usr/lib/x86_64-linux-gnu", "-lnccl", "-Xlinker", "-rpath,/usr/lib/x86_64-linux-gnu"]
+               "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -188,7 +188,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     if (err) atomicExch(err, 1);
     return false;
 }
-// 1-D bulk copy global -> this CTA's shared memory, completing on `bar` (no multicast).
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar` (this CTA only).
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
@@ -202,7 +202,7 @@ __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int 
     }
 }
 
-// 3-D tensor-map load into this CTA's shared memory, completing on `bar` (no multicast).
+// 3-D tensor-map load into this CTA's shared memory, completing on `bar` (this CTA only).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "

@@ -113,6 +113,20 @@ int check_moe(strata_ctx* ctx, const strata_moe* L) {
 
 }  // namespace
 
+namespace strata {
+
+int moe_enqueue_checked(strata_ctx* ctx, const strata_moe* L, const float* x, const float* logits, int64_t T,
+                        float* out, int32_t* ids, float* wts, cudaStream_t s) {
+    int rc = check_moe(ctx, L);
+    if (rc) return rc;
+    if (!x || !out) return fail(ctx, STRATA_ERR_INVALID, "moe: null x or out");
+    return moe_enqueue(ctx, L, x, logits, T, out, ids, wts, s);
+}
+
+int64_t moe_embd(const strata_moe* L) { return L->d.n_embd; }
+
+}  // namespace strata
+
 extern "C" {
 
 int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe** out) {

@@ -317,8 +317,12 @@ int strata_cuda_dequant(strata_ctx* ctx, const strata_weight* w, int64_t expert,
 
 // ---- decode GEMV
 
-static int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
-                        cudaStream_t s) {
+}  // extern "C"
+
+namespace strata {
+
+int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
+                 cudaStream_t s) {
     if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
         return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
@@ -337,6 +341,10 @@ static int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_
         return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no gemv kernel for quant %u", w->quant);
     return check_launch(ctx, "gemv kernel");
 }
+
+}  // namespace strata
+
+extern "C" {
 
 int strata_cuda_gemv_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                          void* stream) {
@@ -376,8 +384,12 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
 
 // ---- prefill GEMM
 
-static int gemm_enqueue(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev, int64_t m,
-                        cudaStream_t s) {
+}  // extern "C"
+
+namespace strata {
+
+int gemm_enqueue(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev, int64_t m,
+                 cudaStream_t s) {
     if (m < 1 || m >= (1ll << 31)) return fail(ctx, STRATA_ERR_INVALID, "m %lld outside 1..2^31-1", (long long)m);
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 15))
         return fail(ctx, STRATA_ERR_INVALID, "x and y must be 16-byte aligned");
@@ -399,6 +411,10 @@ static int gemm_enqueue(strata_ctx* ctx, const strata_weight* w, const uint16_t*
     if (k) return fail(ctx, STRATA_ERR_CUDA, "prefill gemm launch setup failed (%d)", k);
     return check_launch(ctx, "prefill gemm kernel");
 }
+
+}  // namespace strata
+
+extern "C" {
 
 static int gemm_check(strata_ctx* ctx, const strata_weight* w, const void* x, const void* y) {
     int rc = check_weight(ctx, w, false);

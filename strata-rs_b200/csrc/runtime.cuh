@@ -83,6 +83,17 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
 bool encode_gemv_tmap(uint32_t quant, const void* base, int64_t rows, int64_t row_bytes, void* out128);
 int check_device_error(strata_ctx* ctx);
 
+// runtime.cu: enqueue on a stream (the context lock is held by the caller)
+int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
+                 cudaStream_t s);
+int gemm_enqueue(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev, int64_t m,
+                 cudaStream_t s);
+
+// moe_host.cu
+int moe_enqueue_checked(strata_ctx* ctx, const strata_moe* layer, const float* x, const float* logits, int64_t T,
+                        float* out, int32_t* ids, float* wts, cudaStream_t s);
+int64_t moe_embd(const strata_moe* layer);
+
 // comm.cu
 void comm_release(strata_ctx* ctx);
 

@@ -86,6 +86,12 @@ def lib() -> C.CDLL:
             "strata_cuda_moe_destroy": (i32, [vp]),
             "strata_cuda_moe_ffn": (i32, [vp, vp, fp, fp, i64, fp, C.POINTER(C.c_int32), fp]),
             "strata_cuda_moe_ffn_dev": (i32, [vp, vp, vp, vp, i64, vp, vp, vp, vp]),
+            "strata_cuda_comm_unique_id": (i32, [vp]),
+            "strata_cuda_comm_init": (i32, [vp, i32, i32, vp]),
+            "strata_cuda_comm_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
+            "strata_cuda_gemv_sharded_dev": (i32, [vp, vp, vp, vp, i32, vp]),
+            "strata_cuda_gemm_sharded_dev": (i32, [vp, vp, vp, vp, i64, vp]),
+            "strata_cuda_moe_ffn_ep_dev": (i32, [vp, vp, vp, vp, i64, vp, vp]),
         }
         for name, (res, args) in sig.items():
             if not hasattr(L, name):
@@ -144,6 +150,15 @@ class Weight:
         if self.handle:
             lib().strata_cuda_free_weight(self.handle)
             self.handle = None
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for strata_cuda_comm_init."""
+    buf = C.create_string_buffer(128)
+    rc = lib().strata_cuda_comm_unique_id(buf)
+    if rc != OK:
+        raise BackendError(rc, "strata_cuda_comm_unique_id failed")
+    return buf.raw
 
 
 class MoeLayer:
@@ -287,6 +302,27 @@ class Context:
                     ids_ptr: int = 0, wts_ptr: int = 0, stream: int = 0):
         self.check(lib().strata_cuda_moe_ffn_dev(self.h, layer.handle, x_ptr, logits_ptr or None, tokens, out_ptr,
                                                  ids_ptr or None, wts_ptr or None, stream or None))
+
+    # multi-GPU (one context per process and GPU)
+    def comm_init(self, rank: int, world: int, uid: bytes):
+        buf = C.create_string_buffer(bytes(uid), 128)
+        self.check(lib().strata_cuda_comm_init(self.h, rank, world, buf))
+
+    def comm_info(self) -> tuple[int, int]:
+        r, w = C.c_int(), C.c_int()
+        self.check(lib().strata_cuda_comm_info(self.h, C.byref(r), C.byref(w)))
+        return r.value, w.value
+
+    def gemv_sharded_dev(self, w: Weight, x_ptr: int, y_ptr: int, batch: int, stream: int = 0):
+        self.check(lib().strata_cuda_gemv_sharded_dev(self.h, w.handle, x_ptr, y_ptr, batch, stream or None))
+
+    def gemm_sharded_dev(self, w: Weight, x_ptr: int, y_ptr: int, m: int, stream: int = 0):
+        self.check(lib().strata_cuda_gemm_sharded_dev(self.h, w.handle, x_ptr, y_ptr, m, stream or None))
+
+    def moe_ffn_ep_dev(self, layer: "MoeLayer", x_ptr: int, logits_ptr: int, tokens: int, out_ptr: int,
+                       stream: int = 0):
+        self.check(lib().strata_cuda_moe_ffn_ep_dev(self.h, layer.handle, x_ptr, logits_ptr or None, tokens, out_ptr,
+                                                    stream or None))
 
     def set_gemm_terms(self, terms: int):
         self.check(lib().strata_cuda_set_gemm_terms(self.h, terms))

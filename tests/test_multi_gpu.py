@@ -1,0 +1,156 @@
+"""Multi-GPU paths through the C ABI: one spawned process per GPU.
+
+Row-sharded GEMV / GEMM + all-gather and expert-parallel MoE + all-reduce are
+compared with the single-GPU results of the same context (themselves pinned
+to the oracle by the other GPU tests). The communicator-timeout case needs
+only one GPU: rank 0 of a world of 2 whose rank 1 never joins.
+"""
+import multiprocessing as mp
+import os
+import sys
+import traceback
+
+import numpy as np
+import pytest
+
+import strata_cuda as sc
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _ngpu():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _worker(rank, world, uid, q):
+    try:
+        sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "strata-rs_b200"),
+                        os.path.join(os.path.dirname(HERE), "oracle")]
+        import torch
+        import strata_cuda as sc
+        import sharding
+        from conftest import rel_err
+        from synth import Q4_K, Q5_K, activations, bf16_bits, quant_matrix, rng
+        torch.cuda.set_device(rank)
+        ctx = sc.Context(rank)
+        ctx.set_wait_timeout_ms(60000)
+        ctx.comm_init(rank, world, uid)
+        assert ctx.comm_info() == (rank, world)
+        st = torch.cuda.Stream()
+        dev = f"cuda:{rank}"
+
+        # row-sharded GEMV (batch 1 and 3): bitwise the single-GPU GEMV
+        N, K = 4096, 2048
+        data = quant_matrix(2000, Q4_K, N, K)
+        full = ctx.upload(data, Q4_K, N, K)
+        shard = ctx.upload(sharding.row_shard(data, Q4_K, N, K, world, rank), Q4_K, N // world, K)
+        for B in (1, 3):
+            x = torch.from_numpy(activations(2001 + B, B, K)).to(dev)
+            y = torch.empty((B, N), dtype=torch.float32, device=dev)
+            with torch.cuda.stream(st):
+                ctx.gemv_sharded_dev(shard, x.data_ptr(), y.data_ptr(), B, st.cuda_stream)
+            st.synchronize()
+            want = ctx.gemv(full, x.cpu().numpy())
+            assert np.array_equal(y.cpu().numpy().reshape(B, N).view(np.uint32),
+                                  want.reshape(B, N).view(np.uint32)), ("gemv", B)
+
+        # row-sharded GEMM (m = 70): the single-GPU GEMM within fp32 reassociation
+        Kg, Ng, M = 2048, 1024, 70
+        dg = quant_matrix(2010, Q5_K, Ng, Kg)
+        fg = ctx.upload(dg, Q5_K, Ng, Kg)
+        sgw = ctx.upload(sharding.row_shard(dg, Q5_K, Ng, Kg, world, rank), Q5_K, Ng // world, Kg)
+        bits = bf16_bits(activations(2011, M, Kg))
+        xb = torch.from_numpy(bits.view(np.int16)).to(dev)
+        yg = torch.empty((M, Ng), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(st):
+            ctx.gemm_sharded_dev(sgw, xb.data_ptr(), yg.data_ptr(), M, st.cuda_stream)
+        st.synchronize()
+        wantg = ctx.gemm_bf16(fg, bits)
+        got = yg.cpu().numpy()
+        for t in range(M):
+            assert rel_err(got[t], wantg[t]) < 1e-5, ("gemm", t)
+
+        # expert-parallel MoE: the all-reduced partials equal the one-GPU layer
+        n_embd, E, k, n_ff = 512, 16, 4, 256
+        ge = quant_matrix(2020, Q4_K, n_embd, n_ff, E)
+        ue = quant_matrix(2021, Q4_K, n_embd, n_ff, E)
+        de = quant_matrix(2022, Q4_K, n_ff, n_embd, E)
+        sh = {nm: ctx.upload(quant_matrix(2023 + i, Q4_K, r, c), Q4_K, r, c)
+              for i, (nm, r, c) in enumerate([("gate_shexp", 256, n_embd), ("up_shexp", 256, n_embd),
+                                              ("down_shexp", n_embd, 256), ("gate_inp_shexp", 1, n_embd)])}
+        wf = dict(sh, gate_exps=ctx.upload(ge, Q4_K, n_embd, n_ff, n_expert=E),
+                  up_exps=ctx.upload(ue, Q4_K, n_embd, n_ff, n_expert=E),
+                  down_exps=ctx.upload(de, Q4_K, n_ff, n_embd, n_expert=E))
+        lf = ctx.moe_create(wf, n_embd, E, k, n_ff, 256)
+        e0, e1 = sharding.expert_range(E, world, rank)
+        wr = dict(sh, gate_exps=ctx.upload(sharding.expert_shard(ge, E, world, rank), Q4_K, n_embd, n_ff,
+                                           n_expert=e1 - e0),
+                  up_exps=ctx.upload(sharding.expert_shard(ue, E, world, rank), Q4_K, n_embd, n_ff, n_expert=e1 - e0),
+                  down_exps=ctx.upload(sharding.expert_shard(de, E, world, rank), Q4_K, n_ff, n_embd,
+                                       n_expert=e1 - e0))
+        lr = ctx.moe_create(wr, n_embd, E, k, n_ff, 256, expert_begin=e0, expert_end=e1, with_shared=(rank == 0))
+        T = 9
+        x = activations(2030, T, n_embd)
+        lg = rng(2031).standard_normal((T, E)).astype(np.float32)
+        want_m, _, _ = ctx.moe_ffn(lf, x, lg)
+        xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
+        od = torch.empty((T, n_embd), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(st):
+            ctx.moe_ffn_ep_dev(lr, xd.data_ptr(), ld.data_ptr(), T, od.data_ptr(), st.cuda_stream)
+        st.synchronize()
+        got_m = od.cpu().numpy()
+        for t in range(T):
+            assert rel_err(got_m[t], want_m[t]) < 1e-5, ("moe", t)
+        ctx.close()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def _run_world(world):
+    uid = sc.comm_unique_id()
+    ctxm = mp.get_context("spawn")
+    q = ctxm.Queue()
+    procs = [ctxm.Process(target=_worker, args=(r, world, uid, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, msg = q.get(timeout=600)
+        res[r] = msg
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_sharded_paths_world2():
+    res = _run_world(2)
+    assert all(m == "ok" for m in res.values()), res
+
+
+@pytest.mark.skipif(_ngpu() < 4, reason="needs 4 GPUs")
+def test_sharded_paths_world4():
+    res = _run_world(4)
+    assert all(m == "ok" for m in res.values()), res
+
+
+def test_comm_init_times_out_when_a_rank_never_joins():
+    ctx = sc.Context(0)
+    ctx.set_wait_timeout_ms(3000)
+    with pytest.raises(sc.BackendError) as e:
+        ctx.comm_init(0, 2, sc.comm_unique_id())
+    assert e.value.code in (sc.ERR_TIMEOUT, sc.ERR_NCCL)
+    # the context is still usable afterwards
+    from synth import Q4_K, activations, quant_matrix
+    w = ctx.upload(quant_matrix(2040, Q4_K, 64, 256), Q4_K, 64, 256)
+    assert np.isfinite(ctx.gemv(w, activations(2041, 1, 256))).all()
+    w.free()
+    ctx.close()
