@@ -19,10 +19,22 @@ roofline  = that kernel against the measured HBM copy bandwidth.
 cpu_baseline = the CPU oracle (the C restatement of ops::gemv, all host
             threads, row-parallel) on the same sweep.
 
+The same line carries the other measured rows of the path:
+  gemm      the mixed K-quant prefill configuration (Q5_K, Q6_K; K4096->N12288
+            and K12288->N4096; M = 64, 512, 2048 bf16 tokens) on the tcgen05
+            GEMM: TFLOP/s (2MNK per launch) against the measured bf16 peak;
+  moe       the MoE FFN configuration (hidden 2048, 256 Q4_K experts of width
+            512, top-8 from N(0,1) logits, shared expert) at 1 and 64 tokens:
+            tokens/s, expert-parallel across the ranks;
+  sharded   the large row-sharded projections (Q4_K 8192->28672, 28672->8192)
+            as a batch-1 GEMV and an M=1024 GEMM, rows split across the ranks.
+
 `--impl reference` times only the reference path on the CPU (the oracle port;
 the Rust reference cannot be built on this image) and prints its own line.
-Multi-GPU (torchrun): output rows of every matrix are sharded across ranks and
-the per-rank outputs are all-gathered over NCCL each step (strong scaling).
+Multi-GPU (torchrun): every projection is row-sharded across the ranks and
+assembled by the library's all-gather (strata_cuda_gemv_sharded_dev: local
+GEMV + NCCL all-gather inside the C ABI call), MoE is expert-parallel with
+the library's all-reduce (strong scaling: the same total work at every N).
 """
 from __future__ import annotations
 
@@ -42,7 +54,9 @@ ROOT = Path(__file__).resolve().parent
 PKG = ROOT / "strata-rs_b200"
 sys.path.insert(0, str(PKG))
 
-from synth import Q4K_SWEEP, SWEEP_BATCHES, Q4_K, activations, quant_matrix  # noqa: E402
+from synth import (Q4K_SWEEP, SWEEP_BATCHES, Q4_K, Q5_K, Q6_K, activations, bf16_bits,  # noqa: E402
+                   quant_matrix, rng)
+import sharding  # noqa: E402
 
 METRIC = "Q4_K GEMV GB/s (% of HBM peak); MoE layer tokens/s at 1/2/4/8 B200"
 UNIT = "GB/s"
@@ -74,6 +88,28 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Measured dense bf16 TFLOP/s (burst: each GEMM case is timed alone)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback (burst)"
+
+
+def timed(torch, stream, fn, reps: int, warm: int = 3) -> float:
+    """Average ms of fn() over reps launches on `stream` (CUDA events)."""
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            fn()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(reps):
+            fn()
+        a1.record(stream)
+    a1.synchronize()
+    return a0.elapsed_time(a1) / reps
 
 
 class ClockSampler:
@@ -190,6 +226,214 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- GPU
 
+GEMM_SHAPES = [(4096, 12288), (12288, 4096)]   # (K, N)
+GEMM_MS = [64, 512, 2048]
+
+
+def bench_gemm(ctx, torch, stream, l2: int, world: int, rank: int, dist) -> dict:
+    """The prefill GEMM configuration: per case TFLOP/s = 2MNK / launch time.
+    Weights rotate over copies (>= 4x L2 per case) so the M=64 (HBM-bound)
+    cases stream from HBM; at N > 1 the rows are sharded and gathered by the
+    library (strata_cuda_gemm_sharded_dev)."""
+    peak, peak_kind = tensor_peak()
+    hbm, _ = peaks()
+    cases = []
+    xbits = {k: torch.from_numpy(bf16_bits(activations(77 + k, max(GEMM_MS), k)).view(np.int16)).cuda()
+             for k, _ in GEMM_SHAPES}
+    for q, qn, bb in ((Q5_K, "Q5_K", 176), (Q6_K, "Q6_K", 210)):
+        for k, n in GEMM_SHAPES:
+            full = quant_matrix(500 + k + q, q, n, k)
+            part = sharding.row_shard(full, q, n, k, world, rank) if world > 1 else full
+            copies = max(1, -(-4 * l2 // part.nbytes))
+            ws = [ctx.upload(part, q, n // world, k) for _ in range(copies)]
+            for m in GEMM_MS:
+                y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+                it = [0]
+
+                def fn():
+                    w = ws[it[0] % len(ws)]
+                    it[0] += 1
+                    if world > 1:
+                        ctx.gemm_sharded_dev(w, xbits[k].data_ptr(), y.data_ptr(), m, stream.cuda_stream)
+                    else:
+                        ctx.gemm_bf16_dev(w, xbits[k].data_ptr(), y.data_ptr(), m, stream.cuda_stream)
+                reps = max(len(ws), {64: 60, 512: 30, 2048: 10}[m])
+                ms = timed(torch, stream, fn, reps)
+                if dist:
+                    t = torch.tensor([ms], device="cuda")
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    ms = float(t.item())
+                tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+                wbytes = n * (k // 256) * bb
+                gbs = (wbytes + m * k * 2 + m * n * 4) / (ms * 1e-3) / 1e9
+                cases.append({"quant": qn, "k": k, "n": n, "m": m, "us": round(ms * 1e3, 1),
+                              "tflops": round(tf, 1), "frac_bf16_peak": round(tf / peak, 3),
+                              "tensor_tflops_issued": round(2 * tf, 1),
+                              "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)})
+            for w in ws:
+                w.free()
+    big = [c for c in cases if c["m"] >= 512]
+    return {"cases": cases, "peak_tflops": peak, "peak_kind": peak_kind,
+            "tflops_m512_2048_mean": round(statistics.mean(c["tflops"] for c in big), 1),
+            "note": "2MNK per launch over the launch time (CUDA events, 10-60 launches on rotated weight copies); "
+                    "the weights are staged as two bf16 terms (hi + residual), so the tensor cores issue "
+                    "2x these FLOPs (tensor_tflops_issued); M = 64 is HBM-bound and reported as GB/s too"}
+
+
+MOE_DIMS = dict(n_embd=2048, E=256, k=8, n_ff=512, n_ff_s=512)
+
+
+def bench_moe(ctx, torch, stream, world: int, rank: int, dist, with_e2e: bool) -> dict:
+    """The MoE FFN configuration at 1 and 64 tokens (strata_cuda_moe_ffn_dev;
+    expert-parallel over the ranks with strata_cuda_moe_ffn_ep_dev). Each
+    layer call reads its weights from HBM: the layer is replicated over
+    enough copies to exceed 4x L2 and rotated."""
+    d = MOE_DIMS
+    e0, e1 = sharding.expert_range(d["E"], world, rank)
+    ge = quant_matrix(1200 + 1, Q4_K, d["n_embd"], d["n_ff"], d["E"])
+    ue = quant_matrix(1200 + 2, Q4_K, d["n_embd"], d["n_ff"], d["E"])
+    de = quant_matrix(1200 + 3, Q4_K, d["n_ff"], d["n_embd"], d["E"])
+    shared = {"gate_shexp": quant_matrix(1200 + 4, Q4_K, d["n_ff_s"], d["n_embd"]),
+              "up_shexp": quant_matrix(1200 + 5, Q4_K, d["n_ff_s"], d["n_embd"]),
+              "down_shexp": quant_matrix(1200 + 6, Q4_K, d["n_embd"], d["n_ff_s"]),
+              "gate_inp_shexp": quant_matrix(1200 + 7, Q4_K, 1, d["n_embd"])}
+    held = e1 - e0
+    layer_bytes = 3 * held * d["n_embd"] * d["n_ff"] // 256 * 144 + sum(v.nbytes for v in shared.values())
+    copies = max(1, -(-4 * 126 * 2**20 // layer_bytes))
+    layers, handles = [], []
+    for _ in range(copies):
+        ws = {"gate_exps": ctx.upload(sharding.expert_shard(ge, d["E"], world, rank), Q4_K, d["n_embd"], d["n_ff"],
+                                      n_expert=held),
+              "up_exps": ctx.upload(sharding.expert_shard(ue, d["E"], world, rank), Q4_K, d["n_embd"], d["n_ff"],
+                                    n_expert=held),
+              "down_exps": ctx.upload(sharding.expert_shard(de, d["E"], world, rank), Q4_K, d["n_ff"], d["n_embd"],
+                                      n_expert=held)}
+        for nm, arr in shared.items():
+            r, c = {"gate_shexp": (d["n_ff_s"], d["n_embd"]), "up_shexp": (d["n_ff_s"], d["n_embd"]),
+                    "down_shexp": (d["n_embd"], d["n_ff_s"]), "gate_inp_shexp": (1, d["n_embd"])}[nm]
+            ws[nm] = ctx.upload(arr, Q4_K, r, c)
+        handles.append(ws)
+        layers.append(ctx.moe_create(ws, d["n_embd"], d["E"], d["k"], d["n_ff"], d["n_ff_s"], expert_begin=e0,
+                                     expert_end=e1, with_shared=(rank == 0)))
+    out = {}
+    R = 16  # routings rotated with the layer copies, so one token's experts are not L2-resident
+    for T in (1, 64):
+        x = torch.from_numpy(activations(1201 + T, T, d["n_embd"])).cuda()
+        lg_np = [rng(1202 + 100 * T + r).standard_normal((T, d["E"])).astype(np.float32) for r in range(R)]
+        lgs = [torch.from_numpy(a).cuda() for a in lg_np]
+        y = torch.empty((T, d["n_embd"]), dtype=torch.float32, device="cuda")
+        it = [0]
+
+        def call(i):
+            L, lg = layers[i % len(layers)], lgs[i % R]
+            if world > 1:
+                ctx.moe_ffn_ep_dev(L, x.data_ptr(), lg.data_ptr(), T, y.data_ptr(), stream.cuda_stream)
+            else:
+                ctx.moe_ffn_dev(L, x.data_ptr(), lg.data_ptr(), T, y.data_ptr(), stream=stream.cuda_stream)
+
+        def fn():
+            call(it[0])
+            it[0] += 1
+        graph_us = None
+        if world == 1:
+            # launch-bound at one token: also the layer replayed from a CUDA graph
+            with torch.cuda.stream(stream):
+                call(0)
+            stream.synchronize()
+            n_cap = R * len(layers)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n_cap):
+                    call(i)
+            gms = timed(torch, stream, g.replay, 5) / n_cap
+            graph_us = round(gms * 1e3, 2)
+            del g
+        ms = timed(torch, stream, fn, max(R * len(layers), 48))
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        best_ms = min(ms, graph_us / 1e3) if graph_us else ms
+        # bytes: the distinct experts each routing touches (x3 tensors) + the shared expert
+        distinct = statistics.mean(len(np.unique(np.argsort(-a, axis=1)[:, :d["k"]])) for a in lg_np)
+        wbytes = int(distinct * 3 * d["n_embd"] * d["n_ff"] // 256 * 144 + sum(v.nbytes for v in shared.values()))
+        rec = {"tokens": T, "us_per_layer": round(best_ms * 1e3, 2), "us_per_layer_stream": round(ms * 1e3, 2),
+               "us_per_layer_graph": graph_us, "tokens_per_s": round(T / (best_ms * 1e-3), 1),
+               "distinct_experts": distinct, "weight_bytes": wbytes,
+               "gbs": round(wbytes / (best_ms * 1e-3) / 1e9, 1)}
+        if with_e2e and world == 1:
+            hx = activations(1201 + T, T, d["n_embd"])
+            for i in range(3):
+                ctx.moe_ffn(layers[i % len(layers)], hx, lg_np[i % R])
+            n_e = 64
+            t0 = time.perf_counter()
+            for i in range(n_e):
+                ctx.moe_ffn(layers[i % len(layers)], hx, lg_np[i % R])
+            dt = (time.perf_counter() - t0) / n_e
+            rec["e2e"] = {"tokens_per_s": round(T / dt, 1), "us_per_layer": round(dt * 1e6, 1),
+                          "h2d_bytes_per_step": hx.nbytes + lg_np[0].nbytes,
+                          "d2h_bytes_per_step": T * d["n_embd"] * 4 + 2 * T * d["k"] * 4,
+                          "timer": "host perf_counter, strata_cuda_moe_ffn"}
+        out[f"T{T}"] = rec
+    for L in layers:
+        L.free()
+    for ws in handles:
+        for w in ws.values():
+            w.free()
+    return out
+
+
+SHARDED_SHAPES = [(8192, 28672), (28672, 8192)]  # (K, N), Q4_K
+
+
+def bench_sharded(ctx, torch, stream, world: int, rank: int, dist) -> dict:
+    """The large row-sharded projections: Q4_K batch-1 GEMV (GB/s of the whole
+    weight) and M=1024 GEMM (TFLOP/s), rows split over the ranks and gathered
+    by the library (one GPU: the unsharded call)."""
+    out = []
+    for k, n in SHARDED_SHAPES:
+        full = quant_matrix(700 + k, Q4_K, n, k)
+        part = sharding.row_shard(full, Q4_K, n, k, world, rank)
+        ws = [ctx.upload(part, Q4_K, n // world, k) for _ in range(max(1, -(-4 * 126 * 2**20 // part.nbytes)))]
+        x = torch.from_numpy(activations(701, 1, k)).cuda()
+        y = torch.empty((1, n), dtype=torch.float32, device="cuda")
+        xb = torch.from_numpy(bf16_bits(activations(702, 1024, k)).view(np.int16)).cuda()
+        yb = torch.empty((1024, n), dtype=torch.float32, device="cuda")
+        it = [0]
+
+        def gemv():
+            w = ws[it[0] % len(ws)]
+            it[0] += 1
+            if world > 1:
+                ctx.gemv_sharded_dev(w, x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
+            else:
+                ctx.gemv_dev(w, x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
+
+        def gemm():
+            w = ws[it[0] % len(ws)]
+            it[0] += 1
+            if world > 1:
+                ctx.gemm_sharded_dev(w, xb.data_ptr(), yb.data_ptr(), 1024, stream.cuda_stream)
+            else:
+                ctx.gemm_bf16_dev(w, xb.data_ptr(), yb.data_ptr(), 1024, stream.cuda_stream)
+        res = {}
+        for nm, fn, reps in (("gemv_b1", gemv, 100), ("gemm_m1024", gemm, 10)):
+            ms = timed(torch, stream, fn, max(reps, len(ws)))
+            if dist:
+                t = torch.tensor([ms], device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            res[nm] = ms
+        wbytes = n * (k // 256) * 144
+        out.append({"k": k, "n": n, "gemv_b1_us": round(res["gemv_b1"] * 1e3, 2),
+                    "gemv_b1_gbs": round((wbytes + k * 4 + n * 4) / (res["gemv_b1"] * 1e-3) / 1e9, 1),
+                    "gemm_m1024_us": round(res["gemm_m1024"] * 1e3, 1),
+                    "gemm_m1024_tflops": round(2.0 * 1024 * n * k / (res["gemm_m1024"] * 1e-3) / 1e12, 1)})
+        for w in ws:
+            w.free()
+    return {"cases": out, "parallelism": f"rows x{world}, library all-gather" if world > 1 else "single GPU"}
+
+
 def run_gpu(args):
     import torch
     import strata_cuda as sc
@@ -206,60 +450,59 @@ def run_gpu(args):
 
     shapes, batches = Q4K_SWEEP, SWEEP_BATCHES
     ctx = sc.Context(local)
+    if world > 1:
+        # the library's own communicator: rank 0's NCCL id reaches the others over torch.distributed
+        uid = [sc.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.comm_init(rank, world, uid[0])
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
     stream = torch.cuda.Stream()
 
     # this rank's row shard of every matrix, uploaded `copies` times
     weights, shard = {}, {}
     for (k, n) in shapes:
-        r0, r1 = n * rank // world, n * (rank + 1) // world
+        r0, r1 = sharding.row_range(n, world, rank)
         full = quant_matrix(k + n, Q4_K, n, k)
-        rb = (k // 256) * 144
-        part = full[r0 * rb:r1 * rb]
+        part = sharding.row_shard(full, Q4_K, n, k, world, rank)
         copies = max(1, -(-4 * l2 // max(part.nbytes, 1)))
         weights[(k, n)] = [ctx.upload(part, Q4_K, r1 - r0, k) for _ in range(copies)]
         shard[(k, n)] = (r0, r1)
     rot = max(len(v) for v in weights.values())
     xs = {b: torch.from_numpy(activations(900 + b, b, max(k for k, _ in shapes))).cuda() for b in batches}
     xk = {(b, k): xs[b][:, :k].contiguous() for b in batches for (k, _) in shapes}
-    ys = {(k, n, b): torch.empty(b, shard[(k, n)][1] - shard[(k, n)][0], device="cuda")
-          for (k, n) in shapes for b in batches}
-    gathered = {(k, n, b): torch.empty(world, b, (n + world - 1) // world, device="cuda")
-                for (k, n) in shapes for b in batches} if world > 1 else None
+    # single GPU: each GEMV writes its whole output; N GPUs: the library gathers every rank's rows
+    ys = {(k, n, b): torch.empty(b, n, device="cuda") for (k, n) in shapes for b in batches}
 
     def enqueue(step_idx: int, s: int):
         for b in batches:
             for (k, n) in shapes:
                 w = weights[(k, n)][step_idx % len(weights[(k, n)])]
-                ctx.gemv_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, s)
+                if world > 1:
+                    ctx.gemv_sharded_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, s)
+                else:
+                    ctx.gemv_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, s)
 
     graphs = []
     with torch.cuda.stream(stream):
         enqueue(0, stream.cuda_stream)  # warm the kernels before capture
     stream.synchronize()
-    for i in range(rot):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            enqueue(i, stream.cuda_stream)
-        graphs.append(g)
-    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel
+    if world == 1:
+        for i in range(rot):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                enqueue(i, stream.cuda_stream)
+            graphs.append(g)
+    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel;
+    # sharded, batches > 1 add the gather transpose (the NCCL kernel is not counted)
     launches_per_step = 2 * len(batches) * len(shapes)
-
-    def allgather():
-        for (k, n) in shapes:
-            for b in batches:
-                y = ys[(k, n, b)]
-                pad = gathered[(k, n, b)]
-                chunk = pad.shape[2]
-                src = torch.zeros(b, chunk, device="cuda") if y.shape[1] != chunk else y
-                if y.shape[1] != chunk:
-                    src[:, :y.shape[1]] = y
-                dist.all_gather_into_tensor(pad.view(-1), src.reshape(-1))
+    if world > 1:
+        launches_per_step += sum(1 for b in batches if b > 1) * len(shapes)
 
     def step(i):
-        graphs[i % rot].replay()
-        if world > 1:
-            allgather()
+        if world == 1:
+            graphs[i % rot].replay()
+        else:
+            enqueue(i, stream.cuda_stream)
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -301,7 +544,7 @@ def run_gpu(args):
 
     # per-case device time: each case as its own graph over its rotated copies
     cases = []
-    if not args.quick:
+    if not args.quick and world == 1:
         for b in batches:
             for (k, n) in shapes:
                 ws = weights[(k, n)]
@@ -358,6 +601,45 @@ def run_gpu(args):
         e2e = {"value": round(total * n_e2e / dt / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": n_e2e, "timer": "host perf_counter"}
 
+    if not args.no_e2e and world > 1:
+        # N GPUs: the sharded C ABI call with the step's inputs copied in from pinned
+        # host memory and every output copied back, all inside the timed region
+        hx = {key: v.cpu().pin_memory() for key, v in xk.items()}
+        hy = {key: torch.empty(v.shape, dtype=v.dtype).pin_memory() for key, v in ys.items()}
+
+        def e2e_step(i):
+            for b in batches:
+                for (k, n) in shapes:
+                    xk[(b, k)].copy_(hx[(b, k)], non_blocking=True)
+                    w = weights[(k, n)][i % len(weights[(k, n)])]
+                    ctx.gemv_sharded_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, stream.cuda_stream)
+                    hy[(k, n, b)].copy_(ys[(k, n, b)], non_blocking=True)
+        n_e2e = max(10, min(args.steps, 200))
+        ms_e = timed(torch, stream, lambda: e2e_step(0), 3, warm=2)  # warm
+        with torch.cuda.stream(stream):
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for i in range(n_e2e):
+                e2e_step(i)
+            a1.record(stream)
+        a1.synchronize()
+        ms_e = a0.elapsed_time(a1)
+        t = torch.tensor([ms_e], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e = float(t.item())
+        h2d = sum(b * k * 4 for b in batches for (k, _) in shapes)
+        d2h = sum(b * n * 4 for b in batches for (_, n) in shapes)
+        e2e = {"value": round(total * n_e2e / (ms_e / 1e3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": n_e2e,
+               "timer": "CUDA events around pinned H2D + strata_cuda_gemv_sharded_dev + D2H, max over ranks"}
+
+    # the other rows of the path (every rank takes part: their collectives run in the same order)
+    gemm = moe = sharded_proj = None
+    if not args.skip_sections:
+        gemm = bench_gemm(ctx, torch, stream, l2, world, rank, dist)
+        moe = bench_moe(ctx, torch, stream, world, rank, dist, with_e2e=not args.no_e2e)
+        sharded_proj = bench_sharded(ctx, torch, stream, world, rank, dist)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -374,8 +656,9 @@ def run_gpu(args):
                                    "2048->151936 at batch 1,2,4,8 (16 GEMVs per step, batch-major)",
                        "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 "
                              "per matrix), no matrix re-read within 241 MB of traffic",
-                       "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                       "launch": "CUDA graph per step"},
+                       "parallelism": (f"row-sharded x{world}: local GEMV + NCCL all-gather inside "
+                                       f"strata_cuda_gemv_sharded_dev" if world > 1 else "single GPU"),
+                       "launch": "CUDA graph per step" if world == 1 else "direct launches (collectives inside)"},
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(value / hbm, 3), "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": total // (len(batches) * len(shapes)),
@@ -387,6 +670,9 @@ def run_gpu(args):
             "cases": cases,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "gemm": gemm,
+            "moe": moe,
+            "sharded_projection": sharded_proj,
         }
         print(json.dumps(line), flush=True)
 
@@ -435,6 +721,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the per-case table")
+    ap.add_argument("--skip-sections", action="store_true", help="only the GEMV sweep (no gemm / moe / sharded lines)")
     ap.add_argument("--profile-case", default=None, metavar="K,N,B",
                     help="launch one Q4_K GEMV case repeatedly (for ncu captures) instead of the bench")
     args = ap.parse_args()

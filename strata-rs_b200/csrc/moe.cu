@@ -28,9 +28,6 @@ namespace strata {
 namespace {
 
 constexpr int kMoeThreads = 256;
-constexpr int kUnits = 16;    // 16 units of 16 columns = one 256-column super-block
-constexpr int kRowLanes = kMoeThreads / kUnits;
-constexpr int kTokPass = 4;   // tokens per pass over the rows
 
 // f32 exp rounded from a double exp (correctly rounded except within about
 // 2^-29 ulp of a rounding boundary), standing in for Rust's f32::exp.
@@ -72,25 +69,60 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
     const float inv = (float)(1.0 / red_d[0]);
     for (int i = tid; i < E; i += blockDim.x) sp[i] = sp[i] * inv;
     __syncthreads();
-    // expert i is chosen when fewer than k experts precede it in the order
-    // (probability desc, index asc); its slot is the number of chosen ids below it
+    // the k first experts of the order (probability desc, index asc): k rounds
+    // of a block arg-max over the experts not yet taken
     const int kk = k < E ? k : E;
-    int* chosen = reinterpret_cast<int*>(sp + E);  // E flags after the probabilities
-    for (int i = tid; i < E; i += blockDim.x) {
-        const float pi = sp[i];
-        int rank = 0;
-        for (int j = 0; j < E && rank < kk; ++j) {
-            const float pj = sp[j];
-            rank += (pj > pi || (pj == pi && j < i)) ? 1 : 0;
-        }
-        chosen[i] = rank < kk ? 1 : 0;
-    }
+    int* taken = reinterpret_cast<int*>(sp + E);  // E flags after the probabilities
+    for (int i = tid; i < E; i += blockDim.x) taken[i] = 0;
+    __shared__ float wbest_p[32];
+    __shared__ int wbest_i[32];
     __syncthreads();
-    for (int i = tid; i < E; i += blockDim.x) {
-        if (!chosen[i]) continue;
-        int slot = 0;
-        for (int j = 0; j < i; ++j) slot += chosen[j];
-        sel[slot] = i;
+    const int lane = tid & 31, wid = tid >> 5, nw = (blockDim.x + 31) >> 5;
+    for (int r = 0; r < kk; ++r) {
+        float bp = -1.0f;
+        int bi = 0x7FFFFFFF;
+        for (int i = tid; i < E; i += blockDim.x)
+            if (!taken[i] && (sp[i] > bp || (sp[i] == bp && i < bi))) {
+                bp = sp[i];
+                bi = i;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float op = __shfl_xor_sync(0xFFFFFFFFu, bp, o);
+            const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+            if (op > bp || (op == bp && oi < bi)) {
+                bp = op;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            wbest_p[wid] = bp;
+            wbest_i[wid] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float p = wbest_p[0];
+            int i = wbest_i[0];
+            for (int w = 1; w < nw; ++w)
+                if (wbest_p[w] > p || (wbest_p[w] == p && wbest_i[w] < i)) {
+                    p = wbest_p[w];
+                    i = wbest_i[w];
+                }
+            sel[r] = i;
+            taken[i] = 1;
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {  // ids ascending
+        for (int a = 1; a < kk; ++a) {
+            const int v = sel[a];
+            int b = a - 1;
+            while (b >= 0 && sel[b] > v) {
+                sel[b + 1] = sel[b];
+                --b;
+            }
+            sel[b + 1] = v;
+        }
     }
     __syncthreads();
     if (tid == 0) {
@@ -110,13 +142,20 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
 
 // ------------------------------------------------------------------ assignment
 
-// One CTA of >= E threads; thread e handles expert e.
-__global__ void moe_assign_kernel(const int* __restrict__ ids, int T, int k, int E, int e_begin, int e_end,
-                                  MoeIndex ix) {
+// One CTA of >= E threads; thread e handles expert e. The routing ids are
+// staged in shared memory when they fit (staged = true).
+__global__ void moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begin, int e_end,
+                                  bool staged, MoeIndex ix) {
+    extern __shared__ int ids_s[];
     __shared__ int scan[1024];
     const int e = threadIdx.x;
     const int64_t TK = (int64_t)T * k;
-    for (int64_t i = threadIdx.x; i < TK; i += blockDim.x) ix.pos[i] = -1;
+    for (int64_t i = threadIdx.x; i < TK; i += blockDim.x) {
+        ix.pos[i] = -1;
+        if (staged) ids_s[i] = ids_g[i];
+    }
+    __syncthreads();
+    const int* ids = staged ? ids_s : ids_g;
     const bool local = e < E && e >= e_begin && e < e_end;
     int c = 0;
     if (local)
@@ -152,7 +191,7 @@ __global__ void moe_assign_kernel(const int* __restrict__ ids, int T, int k, int
     }
     if (c > 0) {
         int r = 0;
-        for (int64_t i = 0; i < TK; ++i)
+        for (int64_t i = 0; i < TK && r < c; ++i)
             if (ids[i] == e) {
                 ix.tok[off + r] = (int)(i / k);
                 ix.pos[i] = off + r;
@@ -184,11 +223,11 @@ __device__ __forceinline__ void unit_cols(int t, int& colA, int& colB) {
 }
 
 template <uint32_t Q>
-__device__ __forceinline__ void decode_unit(const uint8_t* __restrict__ blk, int t, float (&w)[16]) {
+__device__ __forceinline__ void decode_unit(const uint8_t* blk, int t, float (&w)[16]) {
     if constexpr (Q == kQ4_K || Q == kQ5_K) {
         // 16-byte aligned: rows are whole 144 / 176-byte blocks from a 256-byte aligned base
         const int c = t >> 2, p = t & 3;
-        const uint4 h = __ldg(reinterpret_cast<const uint4*>(blk));
+        const uint4 h = *reinterpret_cast<const uint4*>(blk);
         uint32_t sc_lo, sc_hi, m_lo, m_hi;
         scales_k4_packed(h.y, h.z, h.w, sc_lo, sc_hi, m_lo, m_hi);
         const float d = h2f(h.x), dm = h2f(h.x >> 16);
@@ -197,9 +236,9 @@ __device__ __forceinline__ void decode_unit(const uint8_t* __restrict__ blk, int
         const float dB = d * (float)(((jB < 4 ? sc_lo : sc_hi) >> (8 * (jB & 3))) & 0xFFu);
         const float nA = dm * (float)(((jA < 4 ? m_lo : m_hi) >> (8 * (jA & 3))) & 0xFFu);
         const float nB = dm * (float)(((jB < 4 ? m_lo : m_hi) >> (8 * (jB & 3))) & 0xFFu);
-        const uint2 q = __ldg(reinterpret_cast<const uint2*>(blk + ((Q == kQ4_K) ? 16 : 48) + 32 * c + 8 * p));
+        const uint2 q = *reinterpret_cast<const uint2*>(blk + ((Q == kQ4_K) ? 16 : 48) + 32 * c + 8 * p);
         uint2 qh = make_uint2(0, 0);
-        if constexpr (Q == kQ5_K) qh = __ldg(reinterpret_cast<const uint2*>(blk + 16 + 8 * p));
+        if constexpr (Q == kQ5_K) qh = *reinterpret_cast<const uint2*>(blk + 16 + 8 * p);
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
             const uint32_t b = ((l < 4 ? q.x : q.y) >> (8 * (l & 3))) & 0xFFu;
@@ -218,13 +257,13 @@ __device__ __forceinline__ void decode_unit(const uint8_t* __restrict__ blk, int
         const uint8_t* ql = blk + 64 * H + 32 * g + l0;
         const uint8_t* qh = blk + 128 + 32 * H + l0;
         const uint8_t* sc = blk + 192 + 8 * H;
-        const float d = f16_bits_to_f32((uint32_t)__ldg(blk + 208) | ((uint32_t)__ldg(blk + 209) << 8));
+        const float d = f16_bits_to_f32((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
         const int is = l0 >> 4;
         // u8 scales, as the reference reads them (crates/strata-gguf/src/dequant.rs:208-234)
-        const float sA = d * (float)__ldg(sc + is + 2 * g), sB = d * (float)__ldg(sc + is + 2 * g + 4);
+        const float sA = d * (float)sc[is + 2 * g], sB = d * (float)sc[is + 2 * g + 4];
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
-            const uint32_t b = __ldg(ql + l), h = __ldg(qh + l);
+            const uint32_t b = ql[l], h = qh[l];
             const int qa = (int)((b & 0xFu) | (((h >> (2 * g)) & 3u) << 4)) - 32;
             const int qb = (int)((b >> 4) | (((h >> (2 * g + 4)) & 3u) << 4)) - 32;
             w[l] = sA * (float)qa;
@@ -232,10 +271,10 @@ __device__ __forceinline__ void decode_unit(const uint8_t* __restrict__ blk, int
         }
     } else {  // Q8_0
         const uint8_t* b = blk + 34 * (t >> 1);
-        const float d = f16_bits_to_f32((uint32_t)__ldg(b) | ((uint32_t)__ldg(b + 1) << 8));
+        const float d = f16_bits_to_f32((uint32_t)b[0] | ((uint32_t)b[1] << 8));
         const uint8_t* q = b + 2 + 16 * (t & 1);
 #pragma unroll
-        for (int l = 0; l < 16; ++l) w[l] = (float)(int8_t)__ldg(q + l) * d;
+        for (int l = 0; l < 16; ++l) w[l] = (float)(int8_t)q[l] * d;
     }
 }
 
@@ -244,79 +283,146 @@ __host__ __device__ constexpr int sblock_bytes() {
     return Q == kQ8_0 ? 8 * 34 : block_bytes(Q);  // bytes of one 256-column group of a row
 }
 
-// Partial sums P[rc][m][a][OUT] (m < NMAT) of sum_i X[src(a)][i] W_m[e][i][c]
-// over rows [IN rc / RC, IN (rc + 1) / RC) for the assignments a of the
-// active expert in slot blockIdx.x / groups, columns of super-block
-// blockIdx.x % groups. src(a) = tok[a] when by_token, else a itself.
-template <uint32_t Q, int NMAT>
-__global__ void __launch_bounds__(kMoeThreads)
-moe_expert_partial_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
-                          int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token,
-                          MoeIndex ix, int e_begin, int A_cap, float* __restrict__ P) {
-    __shared__ float red[kMoeThreads][17];
-    const int groups = OUT / 256;
-    const int slot = blockIdx.x / groups, cg = blockIdx.x % groups;
+// ---- streamed expert pass
+//
+// CTA (slot, m, rc): matrix m of the active expert in `slot`, input rows
+// [IN rc / RC, IN (rc + 1) / RC). The rows of an expert are contiguous
+// (row_bytes each, all output columns), so the CTA streams them through a
+// kStages-deep shared-memory ring with cp.async (every thread copies 16 or 4
+// bytes per request; several row tiles in flight), and thread (u, lane)
+// decodes 16-column unit u of rows lane, lane + RL, ... of each tile from
+// shared memory. Output: partial sums P[rc][m][a][OUT] of
+// sum_i X[src(a)][i] W_m[e][i][c] for the expert's assignments a, TP tokens
+// per pass over the rows; src(a) = tok[a] when by_token, else a.
+constexpr int kStages = 4;
+constexpr int kStageBytes = 16384;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Rows per tile: a multiple of the row lanes, about kStageBytes of weights.
+__host__ __device__ inline int tile_rows(int64_t row_bytes, int RL) {
+    int rs = (int)(kStageBytes / row_bytes);
+    rs = rs < RL ? RL : rs;
+    rs -= rs % RL;
+    return rs > 64 ? 64 : rs;
+}
+
+template <uint32_t Q, int TP>
+__global__ void __launch_bounds__(kMoeThreads, 2)
+moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
+                  int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
+                  int e_begin, int A_cap, float* __restrict__ P) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    const int nmat = W1 ? 2 : 1;
+    const int slot = blockIdx.x / nmat, m = blockIdx.x % nmat;
     if (slot >= ix.n_active[0]) return;
     const int e = ix.active[slot];
     const int a0 = ix.off[e], n = ix.cnt[e];
     const int RC = gridDim.y, rc = blockIdx.y;
     const int r0 = (int)((int64_t)IN * rc / RC), r1 = (int)((int64_t)IN * (rc + 1) / RC);
-    const int tid = threadIdx.x, t = tid % kUnits, pr = tid / kUnits;
+    const int U = OUT / 16, RL = kMoeThreads / U;
+    const int tid = threadIdx.x, u = tid % U, lane = tid / U;
+    const int RS = tile_rows(row_bytes, RL);
+    const int64_t tile_bytes = (int64_t)RS * row_bytes;
+    uint8_t* wring = dsm;                                                   // kStages x tile_bytes
+    float* xring = reinterpret_cast<float*>(dsm + kStages * tile_bytes);    // kStages x TP x RS
+    float* red = xring + kStages * TP * RS;                                 // kMoeThreads x 17
+    const uint8_t* Wm = (m == 0 ? W0 : W1) + (int64_t)(e - e_begin) * expert_bytes;
+    const bool vec16 = (row_bytes % 16) == 0;
+    // unit u covers columns of 256-column group g = u / 16, unit t = u % 16 of that group
+    const int g = u >> 4, t = u & 15;
     int colA, colB;
     unit_cols<Q>(t, colA, colB);
-    const int64_t ebase = (int64_t)(e - e_begin) * expert_bytes + (int64_t)cg * sblock_bytes<Q>();
-    for (int p0 = 0; p0 < n; p0 += kTokPass) {
-        const int np = n - p0 < kTokPass ? n - p0 : kTokPass;
-        const float* xs[kTokPass];
-#pragma unroll
-        for (int b = 0; b < kTokPass; ++b) {
-            const int a = a0 + p0 + (b < np ? b : 0);
-            xs[b] = X + (int64_t)(by_token ? ix.tok[a] : a) * IN;
+    const int ntiles = (r1 - r0 + RS - 1) / RS;
+
+    for (int p0 = 0; p0 < n; p0 += TP) {
+        const int np = n - p0 < TP ? n - p0 : TP;
+        __shared__ int src[TP];  // activation row of each token of the pass
+        if (tid < TP) {
+            const int a = a0 + p0 + (tid < np ? tid : 0);
+            src[tid] = by_token ? ix.tok[a] : a;
         }
-        float acc[NMAT][kTokPass][16];
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-            for (int b = 0; b < kTokPass; ++b)
-#pragma unroll
-                for (int l = 0; l < 16; ++l) acc[m][b][l] = 0.0f;
-        for (int i = r0 + pr; i < r1; i += kRowLanes) {
-            float xv[kTokPass];
-#pragma unroll
-            for (int b = 0; b < kTokPass; ++b) xv[b] = __ldg(xs[b] + i);
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                float w[16];
-                decode_unit<Q>((m == 0 ? W0 : W1) + ebase + (int64_t)i * row_bytes, t, w);
-#pragma unroll
-                for (int b = 0; b < kTokPass; ++b)
-#pragma unroll
-                    for (int l = 0; l < 16; ++l) acc[m][b][l] = fmaf(xv[b], w[l], acc[m][b][l]);
-            }
-        }
-        // add the row lanes of each column unit in a fixed order
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-            for (int b = 0; b < np; ++b) {
-#pragma unroll
-                for (int l = 0; l < 16; ++l) red[tid][l] = acc[m][b][l];
-                __syncthreads();
-                if (pr == 0) {
-                    float s[16];
-#pragma unroll
-                    for (int l = 0; l < 16; ++l) s[l] = red[t][l];
-                    for (int q = 1; q < kRowLanes; ++q)
-#pragma unroll
-                        for (int l = 0; l < 16; ++l) s[l] += red[q * kUnits + t][l];
-                    float* dst = P + (((int64_t)rc * NMAT + m) * A_cap + a0 + p0 + b) * OUT + cg * 256;
-#pragma unroll
-                    for (int l = 0; l < 8; ++l) {
-                        dst[colA + l] = s[l];
-                        dst[colB + l] = s[8 + l];
-                    }
+        __syncthreads();
+        auto issue = [&](int tile) {
+            if (tile < ntiles) {
+                const int i0 = r0 + tile * RS;
+                const int rows = r1 - i0 < RS ? r1 - i0 : RS;
+                uint8_t* dst = wring + (int64_t)(tile % kStages) * tile_bytes;
+                const uint8_t* gsrc = Wm + (int64_t)i0 * row_bytes;
+                const int64_t bytes = (int64_t)rows * row_bytes;
+                if (vec16) {
+                    for (int64_t c = tid; c < bytes / 16; c += kMoeThreads) cp_async16(dst + 16 * c, gsrc + 16 * c);
+                } else {
+                    for (int64_t c = tid; c < bytes / 4; c += kMoeThreads) cp_async4(dst + 4 * c, gsrc + 4 * c);
                 }
-                __syncthreads();
+                float* xd = xring + (tile % kStages) * TP * RS;
+                for (int q = tid; q < TP * rows; q += kMoeThreads) {
+                    const int b = q / rows, r = q % rows;
+                    cp_async4(xd + b * RS + r, X + (int64_t)src[b] * IN + i0 + r);
+                }
             }
+            cp_async_commit();  // empty groups keep the count uniform
+        };
+        float acc[TP][16];
+#pragma unroll
+        for (int b = 0; b < TP; ++b)
+#pragma unroll
+            for (int l = 0; l < 16; ++l) acc[b][l] = 0.0f;
+#pragma unroll
+        for (int s = 0; s < kStages - 1; ++s) issue(s);
+        for (int tile = 0; tile < ntiles; ++tile) {
+            issue(tile + kStages - 1);
+            cp_async_wait<kStages - 1>();
+            __syncthreads();
+            const int i0 = r0 + tile * RS;
+            const int rows = r1 - i0 < RS ? r1 - i0 : RS;
+            const uint8_t* wt = wring + (int64_t)(tile % kStages) * tile_bytes;
+            const float* xt = xring + (tile % kStages) * TP * RS;
+            for (int r = lane; r < rows; r += RL) {
+                float w[16];
+                decode_unit<Q>(wt + (int64_t)r * row_bytes + (int64_t)g * sblock_bytes<Q>(), t, w);
+#pragma unroll
+                for (int b = 0; b < TP; ++b) {
+                    const float xv = xt[b * RS + r];
+#pragma unroll
+                    for (int l = 0; l < 16; ++l) acc[b][l] = fmaf(xv, w[l], acc[b][l]);
+                }
+            }
+            __syncthreads();  // the stage is rewritten by the next issue
+        }
+        cp_async_wait<0>();
+        // add the row lanes of each unit in a fixed order
+        for (int b = 0; b < np; ++b) {
+#pragma unroll
+            for (int l = 0; l < 16; ++l) red[tid * 17 + l] = acc[b][l];
+            __syncthreads();
+            if (lane == 0) {
+                float sum[16];
+#pragma unroll
+                for (int l = 0; l < 16; ++l) sum[l] = red[u * 17 + l];
+                for (int q = 1; q < RL; ++q)
+#pragma unroll
+                    for (int l = 0; l < 16; ++l) sum[l] += red[(q * U + u) * 17 + l];
+                float* dst = P + (((int64_t)rc * nmat + m) * A_cap + a0 + p0 + b) * OUT + (int64_t)g * 256;
+#pragma unroll
+                for (int l = 0; l < 8; ++l) {
+                    dst[colA + l] = sum[l];
+                    dst[colB + l] = sum[8 + l];
+                }
+            }
+            __syncthreads();
         }
     }
 }
@@ -386,20 +492,51 @@ unsigned grid_for(int64_t n, int sm_count, int per_sm = 8) {
     return (unsigned)(g < 1 ? 1 : g);
 }
 
-template <int NMAT>
-int launch_partial(uint32_t q, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN,
-                   int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
-                   int slots, int RC, cudaStream_t s) {
-    const dim3 grid((unsigned)(slots * (OUT / 256)), (unsigned)RC);
+size_t stream_smem(int64_t row_bytes, int OUT, int TP) {
+    const int RL = kMoeThreads / (OUT / 16);
+    const int RS = tile_rows(row_bytes, RL);
+    return (size_t)kStages * RS * row_bytes + (size_t)kStages * TP * RS * 4 + (size_t)kMoeThreads * 17 * 4;
+}
+
+template <uint32_t Q, int TP>
+int launch_stream_t(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN, int OUT,
+                    const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P, int slots,
+                    int RC, cudaStream_t s) {
+    const size_t smem = stream_smem(row_bytes, OUT, TP);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(moe_stream_kernel<Q, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return -1;
+    const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
+    moe_stream_kernel<Q, TP><<<grid, kMoeThreads, smem, s>>>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token,
+                                                             ix, e_begin, A_cap, P);
+    return 0;
+}
+
+template <uint32_t Q>
+int launch_stream_q(int TP, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN,
+                    int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
+                    int slots, int RC, cudaStream_t s) {
+    if (TP == 1)
+        return launch_stream_t<Q, 1>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                     slots, RC, s);
+    return launch_stream_t<Q, 4>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P, slots,
+                                 RC, s);
+}
+
+int launch_stream(uint32_t q, int TP, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes,
+                  int IN, int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
+                  int slots, int RC, cudaStream_t s) {
+    if (OUT % 256 != 0 || OUT / 16 > kMoeThreads) return -1;
     switch (q) {
-#define STRATA_MOE_Q(QQ)                                                                                     \
-    case QQ:                                                                                                 \
-        moe_expert_partial_kernel<QQ, NMAT><<<grid, kMoeThreads, 0, s>>>(W0, W1, row_bytes, expert_bytes, IN, \
-                                                                         OUT, X, by_token, ix, e_begin,     \
-                                                                         A_cap, P);                         \
-        return 0;
-        STRATA_MOE_Q(kQ4_K) STRATA_MOE_Q(kQ5_K) STRATA_MOE_Q(kQ6_K) STRATA_MOE_Q(kQ8_0)
-#undef STRATA_MOE_Q
+    case kQ4_K: return launch_stream_q<kQ4_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin,
+                                              A_cap, P, slots, RC, s);
+    case kQ5_K: return launch_stream_q<kQ5_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin,
+                                              A_cap, P, slots, RC, s);
+    case kQ6_K: return launch_stream_q<kQ6_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin,
+                                              A_cap, P, slots, RC, s);
+    case kQ8_0: return launch_stream_q<kQ8_0>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin,
+                                              A_cap, P, slots, RC, s);
     default: return -1;
     }
 }
@@ -408,12 +545,12 @@ int launch_partial(uint32_t q, const uint8_t* W0, const uint8_t* W1, int64_t row
 
 bool moe_expert_quant_supported(uint32_t q) { return q == kQ4_K || q == kQ5_K || q == kQ6_K || q == kQ8_0; }
 
-// Row chunks for a grouped partial pass: enough CTAs for about two per SM, at
-// least 64 rows per chunk.
-int moe_row_chunks(int slots, int groups, int IN, int sm_count) {
-    const int units = slots * groups;
-    int rc = (2 * (sm_count > 0 ? sm_count : 148) + units - 1) / units;
-    const int maxrc = IN / 64 > 0 ? IN / 64 : 1;
+// Row chunks for a streamed pass over `mats` matrices: about four CTAs per SM
+// in all, at least 32 rows per chunk.
+int moe_row_chunks(int slots, int mats, int IN, int sm_count) {
+    const int ctas = slots * mats;
+    int rc = (4 * (sm_count > 0 ? sm_count : 148) + ctas - 1) / ctas;
+    const int maxrc = IN / 32 > 0 ? IN / 32 : 1;
     if (rc > maxrc) rc = maxrc;
     return rc < 1 ? 1 : rc;
 }
@@ -473,17 +610,20 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     moe_route_kernel<<<p.T, 256, (size_t)p.E * (sizeof(float) + sizeof(int)), s>>>(logits, p.E, p.k, I(w.ids), F(w.wts));
     int athreads = 32;
     while (athreads < p.E) athreads <<= 1;
-    moe_assign_kernel<<<1, athreads, 0, s>>>(I(w.ids), p.T, p.k, p.E, p.e_begin, p.e_end, ix);
+    const bool staged = (int64_t)p.T * p.k * 4 <= 40 * 1024;
+    moe_assign_kernel<<<1, athreads, staged ? (size_t)p.T * p.k * 4 : 0, s>>>(I(w.ids), p.T, p.k, p.E, p.e_begin,
+                                                                              p.e_end, staged, ix);
 
     // routed experts
     const int slots = p.slots;
-    if (launch_partial<2>(L.gate.quant, L.gate.W, L.up.W, L.gate.row_bytes, L.gate.expert_bytes, p.n_embd, p.n_ff,
-                          L.x, true, ix, p.e_begin, A, F(w.pgu), slots, p.rc_gu, s))
+    const int TP = p.T == 1 ? 1 : 4;
+    if (launch_stream(L.gate.quant, TP, L.gate.W, L.up.W, L.gate.row_bytes, L.gate.expert_bytes, p.n_embd, p.n_ff,
+                      L.x, true, ix, p.e_begin, A, F(w.pgu), slots, p.rc_gu, s))
         return -2;
     moe_swiglu_kernel<<<grid_for((int64_t)A * p.n_ff, p.sm_count), 256, 0, s>>>(F(w.pgu), p.rc_gu, A, p.n_ff,
                                                                                  ix.n_assign, F(w.h));
-    if (launch_partial<1>(L.down.quant, L.down.W, nullptr, L.down.row_bytes, L.down.expert_bytes, p.n_ff, p.n_embd,
-                          F(w.h), false, ix, p.e_begin, A, F(w.pd), slots, p.rc_d, s))
+    if (launch_stream(L.down.quant, TP, L.down.W, nullptr, L.down.row_bytes, L.down.expert_bytes, p.n_ff, p.n_embd,
+                      F(w.h), false, ix, p.e_begin, A, F(w.pd), slots, p.rc_d, s))
         return -3;
 
     // shared expert (moe.rs:129-142)

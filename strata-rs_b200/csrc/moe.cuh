@@ -52,7 +52,7 @@ struct MoeLaunch {
 };
 
 bool moe_expert_quant_supported(uint32_t q);
-int moe_row_chunks(int slots, int groups, int IN, int sm_count);
+int moe_row_chunks(int slots, int mats, int IN, int sm_count);
 MoeWork moe_work_layout(const MoePlan& p);
 int launch_moe_layer(const MoeLaunch& L, cudaStream_t s);
 

@@ -78,8 +78,8 @@ int moe_enqueue(strata_ctx* ctx, const strata_moe* L, const float* x, const floa
     const int64_t held = d.expert_end - d.expert_begin;
     p.slots = (int)(T * d.top_k < held ? T * d.top_k : held);
     p.sm_count = ctx->sm_count;
-    p.rc_gu = moe_row_chunks(p.slots, p.n_ff / 256, p.n_embd, p.sm_count);
-    p.rc_d = moe_row_chunks(p.slots, p.n_embd / 256, p.n_ff, p.sm_count);
+    p.rc_gu = moe_row_chunks(p.slots, 2, p.n_embd, p.sm_count);
+    p.rc_d = moe_row_chunks(p.slots, 1, p.n_ff, p.sm_count);
     MoeWork layout = moe_work_layout(p);
     int rc = ensure_device(ctx, ctx->moe_work, (size_t)layout.bytes, "cudaMalloc(moe workspace)");
     if (rc) return rc;

@@ -160,8 +160,11 @@ def test_moe_expert_parallel_partials_sum(ctx, G):
         assert np.array_equal(ids, want_ids) and np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
         total += part
         free_all(wr, lr)
+    # both are fp32 sums, in different orders (the row split depends on the experts
+    # held); outputs here reach ~3e4, so the near-zero floor (1e-3 |ref|inf) sees
+    # their rounding: compare at the parity bar
     for i in range(T):
-        assert rel_err(total[i], want[i]) < 1e-5
+        assert rel_err(total[i], want[i]) < TOL
     free_all(ws, full)
 
 

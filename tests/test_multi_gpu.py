@@ -104,8 +104,8 @@ def _worker(rank, world, uid, q):
             ctx.moe_ffn_ep_dev(lr, xd.data_ptr(), ld.data_ptr(), T, od.data_ptr(), st.cuda_stream)
         st.synchronize()
         got_m = od.cpu().numpy()
-        for t in range(T):
-            assert rel_err(got_m[t], want_m[t]) < 1e-5, ("moe", t)
+        for t in range(T):  # fp32 sums in another order (see test_moe_expert_parallel_partials_sum)
+            assert rel_err(got_m[t], want_m[t]) < 1e-3, ("moe", t)
         ctx.close()
         q.put((rank, "ok"))
     except Exception:
