@@ -189,7 +189,7 @@ typedef struct {
 } strata_moe_desc;
 
 /* Validates shapes and quant types (experts: Q4_K, Q5_K, Q6_K or Q8_0 with
- * n_ff and n_embd multiples of 256; n_expert <= 1024; top_k <= 64). The
+ * n_ff and n_embd multiples of 256; n_expert <= 1024; top_k <= 32). The
  * handles must outlive the layer. */
 int strata_cuda_moe_create(strata_ctx *ctx, const strata_moe_desc *desc, strata_moe **out);
 int strata_cuda_moe_destroy(strata_moe *layer);

@@ -87,9 +87,14 @@ __device__ __forceinline__ void mma16816_z(float d[4], uint32_t a0, uint32_t a1,
 // XQ layout: [blk][t = 0..3][n][2] __half: the sums of v over sub-blocks 2t
 // and 2t+1, limb (n & 1) of batch (n >> 1) -- the B operand of the min MMA.
 __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int batch, uint2* __restrict__ XF,
-                                    float* __restrict__ XS, __half* __restrict__ XQ) {
+                                    float* __restrict__ XS, __half* __restrict__ XQ, int64_t chunk_bytes) {
     // XF is addressed here in uint2 halves of the uint4 entries
     asm volatile("griddepcontrol.launch_dependents;");
+    // token chunk blockIdx.y: its own activation rows and workspace slice
+    X += (int64_t)blockIdx.y * batch * K;
+    XF = reinterpret_cast<uint2*>(reinterpret_cast<char*>(XF) + blockIdx.y * chunk_bytes);
+    XS = reinterpret_cast<float*>(reinterpret_cast<char*>(XS) + blockIdx.y * chunk_bytes);
+    XQ = reinterpret_cast<__half*>(reinterpret_cast<char*>(XQ) + blockIdx.y * chunk_bytes);
     const int nblk = (int)(K / 256);
     const int lane = threadIdx.x & 31;
     const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -352,7 +357,13 @@ template <uint32_t Q, int NB, bool TM>
 __global__ void __launch_bounds__((kConsumers + 1) * 32, 3)
 gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
-                   float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap) {
+                   float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap,
+                   int64_t chunk_bytes) {
+    // token chunk blockIdx.y (batches above 8): its limbs and its NB output rows
+    XF = reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(XF) + blockIdx.y * chunk_bytes);
+    XS = reinterpret_cast<const float*>(reinterpret_cast<const char*>(XS) + blockIdx.y * chunk_bytes);
+    XQ = reinterpret_cast<const __half*>(reinterpret_cast<const char*>(XQ) + blockIdx.y * chunk_bytes);
+    Y += (int64_t)blockIdx.y * NB * N;
     constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
     constexpr int BB = block_bytes(Q);
     // smem stride of one row of a stage. TM (one tensor-map copy per stage):
@@ -513,7 +524,8 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
 }
 
 template <uint32_t Q, int NB, bool TM>
-void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
+void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+                unsigned chunks = 1, int64_t chunk_bytes = 0) {
     const int nblk = (int)(a.K / 256);
     const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
     const int smem = kStages * kTileRows * (kChunk * block_bytes(Q) + (TM ? 0 : 16)) + 1024;
@@ -530,7 +542,7 @@ void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __hal
     int64_t grid = (int64_t)a.sm_count * per_sm;
     if (grid > ntiles) grid = ntiles;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
+    cfg.gridDim = dim3((unsigned)grid, chunks);
     cfg.blockDim = dim3((kConsumers + 1) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -540,11 +552,16 @@ void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __hal
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err,
-                       map);
+                       map, chunk_bytes);
 }
 
 template <uint32_t Q, bool TM>
-void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
+void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+                  unsigned chunks = 1, int64_t chunk_bytes = 0) {
+    if (chunks > 1) {
+        launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
+        return;
+    }
     switch (a.batch) {
     case 1: launch_tma<Q, 1, TM>(a, xf, xs, xq, err, s); break;
     case 2: launch_tma<Q, 2, TM>(a, xf, xs, xq, err, s); break;
@@ -587,14 +604,22 @@ bool encode_gemv_tmap(uint32_t quant, const void* base, int64_t rows, int64_t ro
     return r == CUDA_SUCCESS;
 }
 
-// workspace: XF (nblk*64*2B uint2), XS (B*nblk float), XQ (nblk*4*2B half2)
-int64_t gemv_mma_work_bytes(int64_t K, int batch) {
+// workspace of one call of up to 8 tokens: XF (nblk*64*2B uint2), XS
+// (B*nblk float), XQ (nblk*4*2B half2); larger batches take one such slice
+// (256-byte aligned) per 8-token chunk plus one for the remainder.
+static int64_t work_bytes_8(int64_t K, int batch) {
     const int64_t nblk = K / 256;
-    return nblk * 64 * 2 * batch * 8 + (int64_t)batch * nblk * 4 + nblk * 4 * 2 * batch * 4 + 512;
+    const int64_t b = nblk * 64 * 2 * batch * 8 + (int64_t)batch * nblk * 4 + nblk * 4 * 2 * batch * 4 + 512;
+    return (b + 255) / 256 * 256;
+}
+
+int64_t gemv_mma_work_bytes(int64_t K, int batch) {
+    if (batch <= 8) return work_bytes_8(K, batch);
+    return (batch / 8) * work_bytes_8(K, 8) + (batch % 8 ? work_bytes_8(K, batch % 8) : 0);
 }
 
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a) {
-    return (quant == kQ4_K || quant == kQ5_K) && a.K % 256 == 0 && a.batch >= 1 && a.batch <= 8 &&
+    return (quant == kQ4_K || quant == kQ5_K) && a.K % 256 == 0 && a.batch >= 1 && a.batch <= 4096 &&
            a.N < (1ll << 31) && a.N * a.batch < (1ll << 31) && a.K < (1ll << 26) &&
            (a.row_bytes % 16) == 0 && ((uintptr_t)a.W % 16) == 0 && ((uintptr_t)a.X % 16) == 0;
 }
@@ -602,17 +627,33 @@ bool gemv_mma_supported(uint32_t quant, const GemvArgs& a) {
 // x limbs into `work` (gemv_mma_work_bytes), then the tensor-core GEMV.
 int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s) {
     const int nblk = (int)(a.K / 256);
+    const int full = a.batch > 8 ? a.batch / 8 : 0;  // 8-token chunks on grid.y
+    const int nb = full ? 8 : a.batch;
+    const unsigned chunks = full ? (unsigned)full : 1u;
+    const int64_t chunk_bytes = work_bytes_8(a.K, nb);
     char* base = reinterpret_cast<char*>(work);
     uint2* xf = reinterpret_cast<uint2*>(base);
-    const int64_t xf_bytes = (int64_t)nblk * 64 * 2 * a.batch * 8;
+    const int64_t xf_bytes = (int64_t)nblk * 64 * 2 * nb * 8;
     float* xs = reinterpret_cast<float*>(base + xf_bytes);
-    const int64_t xs_bytes = ((int64_t)a.batch * nblk * 4 + 255) / 256 * 256;
+    const int64_t xs_bytes = ((int64_t)nb * nblk * 4 + 255) / 256 * 256;
     __half* xq = reinterpret_cast<__half*>(base + xf_bytes + xs_bytes);
-    const int64_t warps = (int64_t)nblk * a.batch;
-    prep_x_limbs_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a.X, a.K, a.batch, xf, xs, xq);
+    const int64_t warps = (int64_t)nblk * nb;
+    prep_x_limbs_kernel<<<dim3((unsigned)((warps + 7) / 8), chunks), 256, 0, s>>>(a.X, a.K, nb, xf, xs, xq,
+                                                                                chunk_bytes);
+    GemvArgs c = a;
+    c.batch = nb;
     const bool tm = a.tmap != nullptr;
-    if (quant == kQ4_K) tm ? dispatch_mma<kQ4_K, true>(a, xf, xs, xq, err, s) : dispatch_mma<kQ4_K, false>(a, xf, xs, xq, err, s);
-    else tm ? dispatch_mma<kQ5_K, true>(a, xf, xs, xq, err, s) : dispatch_mma<kQ5_K, false>(a, xf, xs, xq, err, s);
+    if (quant == kQ4_K) tm ? dispatch_mma<kQ4_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
+                           : dispatch_mma<kQ4_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
+    else tm ? dispatch_mma<kQ5_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
+            : dispatch_mma<kQ5_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
+    if (full && a.batch % 8) {  // the remaining tokens, after the chunks' workspace
+        GemvArgs r = a;
+        r.X = a.X + (int64_t)full * 8 * a.K;
+        r.Y = a.Y + (int64_t)full * 8 * a.N;
+        r.batch = a.batch % 8;
+        return launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s);
+    }
     return 0;
 }
 

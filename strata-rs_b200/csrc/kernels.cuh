@@ -20,7 +20,14 @@ struct GemvArgs {
 
 int launch_dequant(uint32_t quant, const uint8_t* w, int64_t row_bytes, int64_t cols, int64_t nrows,
                    float* out, cudaStream_t stream);
+// CUDA-core GEMV: every quant type, any batch (8-token chunks beyond 8)
 int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s);
+
+// Tensor-core GEMV (Q4_K / Q5_K): activation-limb prologue + GEMV kernel,
+// any batch (8-token chunks beyond 8); `work` holds gemv_mma_work_bytes.
+int64_t gemv_mma_work_bytes(int64_t K, int batch);
+bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
 
 // Expert GEMV on the transposed expert layout [E][IN rows][OUT cols]
 // (rows quantized along OUT): Y[b][c] = sum_i X[b][i] * W_e[i][c].

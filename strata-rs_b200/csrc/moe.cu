@@ -18,6 +18,8 @@
 //              shared(x) (moe.rs:129-142).
 // The shared expert's dense projections use the CUDA-core GEMV. Every
 // reduction has a fixed order, so the layer is deterministic run to run.
+#include <cuda_fp16.h>
+
 #include <cmath>
 
 #include "kernels.cuh"
@@ -37,55 +39,49 @@ __device__ __forceinline__ float sigmoid_f32(float x) { return 1.0f / (1.0f + ex
 
 // ------------------------------------------------------------------ routing
 
-__global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, int E, int k,
-                                                        int* __restrict__ ids, float* __restrict__ wts) {
-    extern __shared__ float sp[];  // E probabilities
-    __shared__ float red_f[256];
-    __shared__ double red_d[256];
-    __shared__ int sel[64];
-    const int t = blockIdx.x, tid = threadIdx.x;
+// One warp per token (kRouteWarps tokens per CTA); the token's E
+// probabilities live in shared memory.
+constexpr int kRouteWarps = 4;
+__global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float* __restrict__ logits, int T, int E,
+                                                                     int k, int* __restrict__ ids,
+                                                                     float* __restrict__ wts) {
+    extern __shared__ float sp_all[];  // kRouteWarps x E
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kRouteWarps + warp;
+    if (t >= T) return;
+    float* sp = sp_all + warp * E;
     const float* lg = logits + (int64_t)t * E;
     float mx = -INFINITY;
-    for (int i = tid; i < E; i += blockDim.x) mx = fmaxf(mx, lg[i]);
-    red_f[tid] = mx;
-    __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (tid < s) red_f[tid] = fmaxf(red_f[tid], red_f[tid + s]);
-        __syncthreads();
-    }
-    mx = red_f[0];
+    for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
     double sum = 0.0;
-    for (int i = tid; i < E; i += blockDim.x) {
+    for (int i = lane; i < E; i += 32) {
         const float e = exp_f32(lg[i] - mx);
         sp[i] = e;
         sum += (double)e;
     }
-    red_d[tid] = sum;
-    __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (tid < s) red_d[tid] += red_d[tid + s];
-        __syncthreads();
-    }
-    const float inv = (float)(1.0 / red_d[0]);
-    for (int i = tid; i < E; i += blockDim.x) sp[i] = sp[i] * inv;
-    __syncthreads();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    const float inv = (float)(1.0 / sum);
+    for (int i = lane; i < E; i += 32) sp[i] = sp[i] * inv;
+    __syncwarp();
     // the k first experts of the order (probability desc, index asc): k rounds
-    // of a block arg-max over the experts not yet taken
+    // of a warp arg-max over the experts not yet taken (lane-owned bit masks:
+    // expert i belongs to lane i % 32, bit i / 32)
     const int kk = k < E ? k : E;
-    int* taken = reinterpret_cast<int*>(sp + E);  // E flags after the probabilities
-    for (int i = tid; i < E; i += blockDim.x) taken[i] = 0;
-    __shared__ float wbest_p[32];
-    __shared__ int wbest_i[32];
-    __syncthreads();
-    const int lane = tid & 31, wid = tid >> 5, nw = (blockDim.x + 31) >> 5;
+    uint32_t taken = 0;
+    int sel = 0x7FFFFFFF;  // lane j < kk ends holding the j-th chosen id
     for (int r = 0; r < kk; ++r) {
         float bp = -1.0f;
         int bi = 0x7FFFFFFF;
-        for (int i = tid; i < E; i += blockDim.x)
-            if (!taken[i] && (sp[i] > bp || (sp[i] == bp && i < bi))) {
-                bp = sp[i];
+        for (int i = lane, m = 0; i < E; i += 32, ++m) {
+            const float v = sp[i];
+            if (!((taken >> m) & 1u) && (v > bp || (v == bp && i < bi))) {
+                bp = v;
                 bi = i;
             }
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float op = __shfl_xor_sync(0xFFFFFFFFu, bp, o);
@@ -95,108 +91,107 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
                 bi = oi;
             }
         }
-        if (lane == 0) {
-            wbest_p[wid] = bp;
-            wbest_i[wid] = bi;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float p = wbest_p[0];
-            int i = wbest_i[0];
-            for (int w = 1; w < nw; ++w)
-                if (wbest_p[w] > p || (wbest_p[w] == p && wbest_i[w] < i)) {
-                    p = wbest_p[w];
-                    i = wbest_i[w];
-                }
-            sel[r] = i;
-            taken[i] = 1;
-        }
-        __syncthreads();
+        if (lane == r) sel = bi;
+        if (lane == (bi & 31)) taken |= 1u << (bi >> 5);
     }
-    if (tid == 0) {  // ids ascending
-        for (int a = 1; a < kk; ++a) {
-            const int v = sel[a];
-            int b = a - 1;
-            while (b >= 0 && sel[b] > v) {
-                sel[b + 1] = sel[b];
-                --b;
-            }
-            sel[b + 1] = v;
+    // ids ascending: lane q receives the chosen id of rank q
+    const float psel = lane < kk ? sp[sel] : 0.0f;
+    int rank = 0;
+    for (int j = 0; j < kk; ++j) {
+        const int oj = __shfl_sync(0xFFFFFFFFu, sel, j);
+        rank += (lane < kk && oj < sel) ? 1 : 0;
+    }
+    int id_q = 0x7FFFFFFF;
+    float p_q = 0.0f;
+    for (int j = 0; j < kk; ++j) {
+        const int rj = __shfl_sync(0xFFFFFFFFu, rank, j);
+        const int sj = __shfl_sync(0xFFFFFFFFu, sel, j);
+        const float pj = __shfl_sync(0xFFFFFFFFu, psel, j);
+        if (lane == rj) {
+            id_q = sj;
+            p_q = pj;
         }
     }
-    __syncthreads();
-    if (tid == 0) {
-        double ws = 0.0;
-        for (int j = 0; j < kk; ++j) ws += (double)sp[sel[j]];
-        const double s = ws > 0x1p-14 ? ws : 0x1p-14;
-        for (int j = 0; j < kk; ++j) {
-            ids[(int64_t)t * k + j] = sel[j];
-            wts[(int64_t)t * k + j] = (float)((double)sp[sel[j]] / s);
-        }
-        for (int j = kk; j < k; ++j) {
-            ids[(int64_t)t * k + j] = -1;
-            wts[(int64_t)t * k + j] = 0.0f;
-        }
+    // weights: f64 sum in ascending id order, as moe.rs:80-90
+    double ws = 0.0;
+    for (int j = 0; j < kk; ++j) ws += (double)__shfl_sync(0xFFFFFFFFu, p_q, j);
+    const double sden = ws > 0x1p-14 ? ws : 0x1p-14;
+    if (lane < k) {
+        ids[(int64_t)t * k + lane] = lane < kk ? id_q : -1;
+        wts[(int64_t)t * k + lane] = lane < kk ? (float)((double)p_q / sden) : 0.0f;
     }
 }
 
 // ------------------------------------------------------------------ assignment
 
-// One CTA of >= E threads; thread e handles expert e. The routing ids are
-// staged in shared memory when they fit (staged = true).
-__global__ void moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begin, int e_end,
-                                  bool staged, MoeIndex ix) {
+// One CTA (kAssignThreads threads, E <= 1024). Counts per expert come from
+// shared-memory atomics (order-free); offsets and the active list from scans
+// over the experts in ascending order; an entry's rank within its expert is
+// the number of earlier entries (earlier tokens) routed to the same expert,
+// so every list is in token order whatever the thread schedule. The routing
+// ids are staged in shared memory when they fit (staged = true).
+constexpr int kAssignThreads = 1024;
+__global__ void __launch_bounds__(kAssignThreads)
+moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begin, int e_end, bool staged,
+                  MoeIndex ix) {
     extern __shared__ int ids_s[];
-    __shared__ int scan[1024];
-    const int e = threadIdx.x;
+    __shared__ int cnt_s[1024], scan[1024];
+    const int tid = threadIdx.x;
     const int64_t TK = (int64_t)T * k;
-    for (int64_t i = threadIdx.x; i < TK; i += blockDim.x) {
-        ix.pos[i] = -1;
-        if (staged) ids_s[i] = ids_g[i];
+    for (int e = tid; e < 1024; e += blockDim.x) cnt_s[e] = 0;
+    __syncthreads();
+    for (int64_t i = tid; i < TK; i += blockDim.x) {
+        const int e = ids_g[i];
+        if (staged) ids_s[i] = e;
+        if (e >= e_begin && e < e_end) atomicAdd(&cnt_s[e], 1);
     }
     __syncthreads();
     const int* ids = staged ? ids_s : ids_g;
-    const bool local = e < E && e >= e_begin && e < e_end;
-    int c = 0;
-    if (local)
-        for (int64_t i = 0; i < TK; ++i) c += ids[i] == e ? 1 : 0;
-    // exclusive scans (over e ascending) of the counts and of the active flags
-    scan[e] = c;
+    // exclusive scans over e ascending: counts -> offsets, active flags -> slots
+    const int c = tid < E ? cnt_s[tid] : 0;
+    scan[tid] = c;
     __syncthreads();
-    for (int s = 1; s < (int)blockDim.x; s <<= 1) {
-        const int v = e >= s ? scan[e - s] : 0;
+    for (int sh = 1; sh < (int)blockDim.x; sh <<= 1) {
+        const int v = tid >= sh ? scan[tid - sh] : 0;
         __syncthreads();
-        scan[e] += v;
+        scan[tid] += v;
         __syncthreads();
     }
-    const int off = scan[e] - c;
+    const int off = scan[tid] - c;
     const int total = scan[blockDim.x - 1];
     __syncthreads();
-    scan[e] = c > 0 ? 1 : 0;
+    scan[tid] = c > 0 ? 1 : 0;
     __syncthreads();
-    for (int s = 1; s < (int)blockDim.x; s <<= 1) {
-        const int v = e >= s ? scan[e - s] : 0;
+    for (int sh = 1; sh < (int)blockDim.x; sh <<= 1) {
+        const int v = tid >= sh ? scan[tid - sh] : 0;
         __syncthreads();
-        scan[e] += v;
+        scan[tid] += v;
         __syncthreads();
     }
-    if (e < E) {
-        ix.cnt[e] = c;
-        ix.off[e] = off;
-        if (c > 0) ix.active[scan[e] - 1] = e;
+    if (tid < E) {
+        ix.cnt[tid] = c;
+        ix.off[tid] = off;
+        if (c > 0) ix.active[scan[tid] - 1] = tid;
     }
-    if (e == 0) {
+    if (tid == 0) {
         ix.n_active[0] = scan[blockDim.x - 1];
         ix.n_assign[0] = total;
     }
-    if (c > 0) {
+    __syncthreads();
+    cnt_s[tid] = off;  // offsets, for the placement below
+    __syncthreads();
+    for (int64_t i = tid; i < TK; i += blockDim.x) {
+        const int e = ids[i];
+        if (e < e_begin || e >= e_end) {
+            ix.pos[i] = -1;
+            continue;
+        }
         int r = 0;
-        for (int64_t i = 0; i < TK && r < c; ++i)
-            if (ids[i] == e) {
-                ix.tok[off + r] = (int)(i / k);
-                ix.pos[i] = off + r;
-                ++r;
-            }
+#pragma unroll 8
+        for (int64_t q = 0; q < i; ++q) r += ids[q] == e ? 1 : 0;
+        const int at = cnt_s[e] + r;
+        ix.tok[at] = (int)(i / k);
+        ix.pos[i] = at;
     }
 }
 
@@ -283,6 +278,14 @@ __host__ __device__ constexpr int sblock_bytes() {
     return Q == kQ8_0 ? 8 * 34 : block_bytes(Q);  // bytes of one 256-column group of a row
 }
 
+// Bytes b0 and b0 + 1 of v (each < 256) as exact floats: the byte lands in
+// the mantissa of 2^23 and 2^23 is subtracted.
+__device__ __forceinline__ float2 byte_pair_f(uint32_t v, int b0) {
+    const float2 m = make_float2(__uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | b0)),
+                                 __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | (b0 + 1))));
+    return __fadd2_rn(m, make_float2(-8388608.0f, -8388608.0f));
+}
+
 // ---- streamed expert pass
 //
 // CTA (slot, m, rc): matrix m of the active expert in `slot`, input rows
@@ -319,6 +322,22 @@ __host__ __device__ inline int tile_rows(int64_t row_bytes, int RL) {
     return rs > 64 ? 64 : rs;
 }
 
+// Pitches of the tensor-core pass's shared arrays: a staged row pitch whose
+// 32-bit word count is 8 mod 32, and an x pitch of 4 mod 32 floats, so that
+// the 4 consecutive rows a fragment load touches use different banks.
+__host__ __device__ inline int64_t mma_row_pitch(int64_t row_bytes) {
+    const int64_t words = row_bytes / 4;
+    return row_bytes + 4 * ((8 - words % 32 + 32) % 32);
+}
+__host__ __device__ inline int mma_x_pitch(int rs) { return rs + (4 - rs % 32 + 32) % 32; }
+
+// Rows per tile of the tensor-core pass: a multiple of 16 (one k-tile), about kStageBytes.
+__host__ __device__ inline int mma_tile_rows(int64_t row_bytes) {
+    int rs = (int)(kStageBytes / row_bytes);
+    rs -= rs % 16;
+    return rs < 16 ? 16 : (rs > 64 ? 64 : rs);
+}
+
 template <uint32_t Q, int TP>
 __global__ void __launch_bounds__(kMoeThreads, 2)
 moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
@@ -339,6 +358,8 @@ moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1
     uint8_t* wring = dsm;                                                   // kStages x tile_bytes
     float* xring = reinterpret_cast<float*>(dsm + kStages * tile_bytes);    // kStages x TP x RS
     float* red = xring + kStages * TP * RS;                                 // kMoeThreads x 17
+    const int G = OUT / 256;
+    float* tab = red + kMoeThreads * 17;                                    // RS x G x 16 scales
     const uint8_t* Wm = (m == 0 ? W0 : W1) + (int64_t)(e - e_begin) * expert_bytes;
     const bool vec16 = (row_bytes % 16) == 0;
     // unit u covers columns of 256-column group g = u / 16, unit t = u % 16 of that group
@@ -376,10 +397,13 @@ moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1
             cp_async_commit();  // empty groups keep the count uniform
         };
         float acc[TP][16];
+        float accm[TP][2];  // sum_i x dmin m of the unit's two sub-blocks (K-quants with mins)
 #pragma unroll
-        for (int b = 0; b < TP; ++b)
+        for (int b = 0; b < TP; ++b) {
+            accm[b][0] = accm[b][1] = 0.0f;
 #pragma unroll
             for (int l = 0; l < 16; ++l) acc[b][l] = 0.0f;
+        }
 #pragma unroll
         for (int s = 0; s < kStages - 1; ++s) issue(s);
         for (int tile = 0; tile < ntiles; ++tile) {
@@ -390,19 +414,89 @@ moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1
             const int rows = r1 - i0 < RS ? r1 - i0 : RS;
             const uint8_t* wt = wring + (int64_t)(tile % kStages) * tile_bytes;
             const float* xt = xring + (tile % kStages) * TP * RS;
-            for (int r = lane; r < rows; r += RL) {
-                float w[16];
-                decode_unit<Q>(wt + (int64_t)r * row_bytes + (int64_t)g * sblock_bytes<Q>(), t, w);
+            if constexpr (Q == kQ4_K || Q == kQ5_K) {
+                // the tile's scales: d sc_j and dmin m_j of every (row, 256-column group)
+                for (int q = tid; q < rows * G; q += kMoeThreads) {
+                    const int rr = q / G, gg = q - rr * G;
+                    const uint4 h = *reinterpret_cast<const uint4*>(wt + (int64_t)rr * row_bytes + gg * block_bytes(Q));
+                    uint32_t sc_lo, sc_hi, m_lo, m_hi;
+                    scales_k4_packed(h.y, h.z, h.w, sc_lo, sc_hi, m_lo, m_hi);
+                    const float d = h2f(h.x), dm = h2f(h.x >> 16);
+                    float* tb = tab + q * 16;
 #pragma unroll
-                for (int b = 0; b < TP; ++b) {
-                    const float xv = xt[b * RS + r];
+                    for (int j = 0; j < 8; ++j) {
+                        tb[j] = d * (float)(((j < 4 ? sc_lo : sc_hi) >> (8 * (j & 3))) & 0xFFu);
+                        tb[8 + j] = dm * (float)(((j < 4 ? m_lo : m_hi) >> (8 * (j & 3))) & 0xFFu);
+                    }
+                }
+                __syncthreads();
+                // y = sum_i q (x d sc) - sum_i x (dmin m): the scale rides on x
+                const int cc = t >> 2, pp = t & 3, jA = 2 * cc;
+                const int qoff = ((Q == kQ4_K) ? 16 : 48) + 32 * cc + 8 * pp;
+                for (int r = lane; r < rows; r += RL) {
+                    const uint8_t* blk = wt + (int64_t)r * row_bytes + (int64_t)g * block_bytes(Q);
+                    const uint2 qv = *reinterpret_cast<const uint2*>(blk + qoff);
+                    uint32_t lo0 = qv.x & 0x0F0F0F0Fu, lo1 = qv.y & 0x0F0F0F0Fu;
+                    uint32_t hi0 = (qv.x >> 4) & 0x0F0F0F0Fu, hi1 = (qv.y >> 4) & 0x0F0F0F0Fu;
+                    if constexpr (Q == kQ5_K) {
+                        const uint2 hv = *reinterpret_cast<const uint2*>(blk + 16 + 8 * pp);
+                        lo0 |= ((hv.x >> jA) & 0x01010101u) << 4;
+                        lo1 |= ((hv.y >> jA) & 0x01010101u) << 4;
+                        hi0 |= ((hv.x >> (jA + 1)) & 0x01010101u) << 4;
+                        hi1 |= ((hv.y >> (jA + 1)) & 0x01010101u) << 4;
+                    }
+                    float2 qf[8];  // columns colA..colA+7 (pairs), then colB..colB+7
+                    qf[0] = byte_pair_f(lo0, 0);
+                    qf[1] = byte_pair_f(lo0, 2);
+                    qf[2] = byte_pair_f(lo1, 0);
+                    qf[3] = byte_pair_f(lo1, 2);
+                    qf[4] = byte_pair_f(hi0, 0);
+                    qf[5] = byte_pair_f(hi0, 2);
+                    qf[6] = byte_pair_f(hi1, 0);
+                    qf[7] = byte_pair_f(hi1, 2);
+                    const float* tb = tab + (r * G + g) * 16;
+                    const float2 dsc = *reinterpret_cast<const float2*>(tb + jA);
+                    const float2 dmm = *reinterpret_cast<const float2*>(tb + 8 + jA);
 #pragma unroll
-                    for (int l = 0; l < 16; ++l) acc[b][l] = fmaf(xv, w[l], acc[b][l]);
+                    for (int b = 0; b < TP; ++b) {
+                        if (b < np) {
+                            const float xv = xt[b * RS + r];
+                            const float2 xa = make_float2(xv * dsc.x, xv * dsc.x);
+                            const float2 xb = make_float2(xv * dsc.y, xv * dsc.y);
+                            accm[b][0] = fmaf(xv, dmm.x, accm[b][0]);
+                            accm[b][1] = fmaf(xv, dmm.y, accm[b][1]);
+                            float2* a2 = reinterpret_cast<float2*>(acc[b]);
+#pragma unroll
+                            for (int k2 = 0; k2 < 4; ++k2) a2[k2] = __ffma2_rn(qf[k2], xa, a2[k2]);
+#pragma unroll
+                            for (int k2 = 4; k2 < 8; ++k2) a2[k2] = __ffma2_rn(qf[k2], xb, a2[k2]);
+                        }
+                    }
+                }
+            } else {
+                for (int r = lane; r < rows; r += RL) {
+                    float w[16];
+                    decode_unit<Q>(wt + (int64_t)r * row_bytes + (int64_t)g * sblock_bytes<Q>(), t, w);
+#pragma unroll
+                    for (int b = 0; b < TP; ++b) {
+                        const float xv = xt[b * RS + r];
+#pragma unroll
+                        for (int l = 0; l < 16; ++l) acc[b][l] = fmaf(xv, w[l], acc[b][l]);
+                    }
                 }
             }
             __syncthreads();  // the stage is rewritten by the next issue
         }
         cp_async_wait<0>();
+        if constexpr (Q == kQ4_K || Q == kQ5_K) {
+#pragma unroll
+            for (int b = 0; b < TP; ++b)
+#pragma unroll
+                for (int l = 0; l < 8; ++l) {
+                    acc[b][l] -= accm[b][0];
+                    acc[b][8 + l] -= accm[b][1];
+                }
+        }
         // add the row lanes of each unit in a fixed order
         for (int b = 0; b < np; ++b) {
 #pragma unroll
@@ -452,25 +546,35 @@ __global__ void moe_shared_act_kernel(const float* __restrict__ Gs, const float*
         sg[t] = sigmoid_f32(gi[t]);
 }
 
-// out[t][c] = sum_j w[t][j] * down[pos(t,j)][c] over t's local experts in
-// ascending id (skipping zero weights, moe.rs:111-113), + sg[t] * Ds[t][c].
+// out[t][c] = sum_j w[t][j] * down[pos(t,j)][c] over t's local experts
+// (skipping zero weights, moe.rs:111-113), + sg[t] * Ds[t][c]. A group of
+// L >= k lanes serves one output: lane j adds expert j's row-chunk partials,
+// the group sums its lanes with a fixed shuffle tree.
 __global__ void moe_combine_kernel(const float* __restrict__ Pd, int RC, int A_cap, int OUT, const int* __restrict__ pos,
-                                   const float* __restrict__ wts, int T, int k, const float* __restrict__ Ds,
+                                   const float* __restrict__ wts, int T, int k, int L, const float* __restrict__ Ds,
                                    const float* __restrict__ sg, float* __restrict__ out) {
     const int64_t n = (int64_t)T * OUT;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t t = i / OUT, c = i - t * OUT;
-        float acc = 0.0f;
-        for (int j = 0; j < k; ++j) {
+    const int j = threadIdx.x % L;
+    const int64_t per_block = blockDim.x / L;
+    for (int64_t base = blockIdx.x * per_block; base < n; base += (int64_t)gridDim.x * per_block) {
+        const int64_t i = base + threadIdx.x / L;
+        const bool live = i < n;
+        const int64_t t = live ? i / OUT : 0, c = live ? i - t * OUT : 0;
+        float v = 0.0f;
+        if (live && j < k) {
             const int a = pos[t * k + j];
             const float w = wts[t * k + j];
-            if (a < 0 || w == 0.0f) continue;
-            float d = 0.0f;
-            for (int rc = 0; rc < RC; ++rc) d += Pd[((int64_t)rc * A_cap + a) * OUT + c];
-            acc += w * d;
+            if (a >= 0 && w != 0.0f) {
+                float d = 0.0f;
+                for (int rc = 0; rc < RC; ++rc) d += Pd[((int64_t)rc * A_cap + a) * OUT + c];
+                v = w * d;
+            }
         }
-        if (Ds) acc += sg[t] * Ds[i];
-        out[i] = acc;
+        for (int o = L / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+        if (live && j == 0) {
+            if (Ds) v += sg[t] * Ds[i];
+            out[i] = v;
+        }
     }
 }
 
@@ -492,10 +596,308 @@ unsigned grid_for(int64_t n, int sm_count, int per_sm = 8) {
     return (unsigned)(g < 1 ? 1 : g);
 }
 
+// ---- tensor-core form of the streamed pass (Q4_K / Q5_K)
+//
+// Same CTA shape, ring and scale table as moe_stream_kernel; the products
+// run on mma.sync m16n8k16 (f16 in, f32 out, one k-tile per MMA, summed over
+// k-tiles with fp32 adds). With m = 16 output
+// columns of one sub-block j and k = 16 input rows:
+//   A[c][i] = q[i][c]                       exact small integers in fp16
+//   B[i][n] = x_t[i] S_t d_i sc_ij          n = (token t, limb): two fp16
+//                                           limbs, hi + lo 2^-11 (22 bits)
+//   D[c][n] = sum_i A B                     f32
+// so that y[t][c] = (D[c][t,hi] + D[c][t,lo] 2^-11) / S_t
+//                   - sum_i x_t[i] dmin_i m_ij   (min term, CUDA cores).
+// S_t is a power of two chosen per CTA pass from max|x_t| and max d over the
+// CTA's rows so that |B| < 2^14 (no fp16 overflow; the limbs keep ~22 bits).
+// Warp w owns m-tiles MPW w .. MPW w + MPW - 1 (MPW = OUT / 128). Within a
+// sub-block's two m-tiles, fragment row g of m-tile mt holds column 4g + 2mt
+// and row g + 8 column 4g + 2mt + 1, so a lane's four columns are one 32-bit
+// word of every quant row.
+// d = A B (zero accumulator input): one k-tile's products, added to the running
+// sums by the caller with fp32 adds (the tensor cores' own accumulation of
+// long chains loses low bits; one 16-product sum does not)
+__device__ __forceinline__ void mma16816z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    const float z = 0.0f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+    return d;
+}
+__device__ __forceinline__ uint32_t f16x2_bits(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <uint32_t Q, int MPW>
+__global__ void __launch_bounds__(kMoeThreads, 2)
+moe_mma_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
+               int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
+               int e_begin, int A_cap, float* __restrict__ P) {
+    constexpr int TP = 4;  // tokens per pass: n = 8 = 4 tokens x 2 limbs
+    constexpr int SPW = MPW / 2;  // sub-blocks per warp
+    extern __shared__ __align__(16) uint8_t dsm[];
+    const int nmat = W1 ? 2 : 1;
+    const int slot = blockIdx.x / nmat, m = blockIdx.x % nmat;
+    if (slot >= ix.n_active[0]) return;
+    const int e = ix.active[slot];
+    const int a0 = ix.off[e], n = ix.cnt[e];
+    // row chunk rc of RC, on 16-row (k-tile) boundaries
+    const int RC = gridDim.y, rc = blockIdx.y, nk = IN / 16;
+    const int r0 = 16 * (int)((int64_t)nk * rc / RC), r1 = 16 * (int)((int64_t)nk * (rc + 1) / RC);
+    const int G = OUT / 256;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    // shared-memory pitches chosen so that the 4 rows a fragment load touches
+    // (t4 = 0..3, consecutive rows) fall on different banks
+    const int RS = mma_tile_rows(row_bytes);
+    const int64_t RB = mma_row_pitch(row_bytes);  // staged row pitch (bytes)
+    const int RSX = mma_x_pitch(RS);              // x ring pitch per token (floats)
+    const int TPITCH = G * 16 + 8;                // scale table pitch per row (floats)
+    const int64_t tile_bytes = (int64_t)RS * RB;
+    uint8_t* wring = dsm;
+    float* xring = reinterpret_cast<float*>(dsm + kStages * tile_bytes);  // kStages x TP x RSX
+    float* tab = xring + kStages * TP * RSX;                              // RS x TPITCH
+    __shared__ float red_max[2][kMoeThreads / 32];
+    __shared__ int src[TP];
+    __shared__ float sinv[TP], sval[TP];
+    const uint8_t* Wm = (m == 0 ? W0 : W1) + (int64_t)(e - e_begin) * expert_bytes;
+    // this warp's sub-blocks: global sub-block index sb = SPW warp + s (8 per group)
+    const int sb0 = SPW * warp;
+    const int ntiles = (r1 - r0 + RS - 1) / RS;
+
+    // max d over the CTA's rows (once per CTA)
+    float dmax = 0.0f;
+    for (int q = tid; q < (r1 - r0) * G; q += kMoeThreads) {
+        const int rr = q / G, gg = q - rr * G;
+        const uint8_t* hb = Wm + (int64_t)(r0 + rr) * row_bytes + gg * block_bytes(Q);
+        dmax = fmaxf(dmax, fabsf(h2f((uint32_t)hb[0] | ((uint32_t)hb[1] << 8))));
+    }
+    for (int o = 16; o > 0; o >>= 1) dmax = fmaxf(dmax, __shfl_xor_sync(0xFFFFFFFFu, dmax, o));
+    if (lane == 0) red_max[0][warp] = dmax;
+    __syncthreads();
+    if (tid == 0) {
+        float v = 0.0f;
+        for (int w = 0; w < kMoeThreads / 32; ++w) v = fmaxf(v, red_max[0][w]);
+        red_max[1][0] = v;
+    }
+    __syncthreads();
+    dmax = red_max[1][0];
+
+    for (int p0 = 0; p0 < n; p0 += TP) {
+        const int np = n - p0 < TP ? n - p0 : TP;
+        if (tid < TP) {
+            const int a = a0 + p0 + (tid < np ? tid : 0);
+            src[tid] = by_token ? ix.tok[a] : a;
+        }
+        __syncthreads();
+        // per-token scale S = 2^e with max |x| d 63 S <= 2^14 (|sc| <= 63)
+        if (warp < TP) {
+            float xm = 0.0f;
+            const float* xr = X + (int64_t)src[warp] * IN;
+            for (int i = r0 + lane; i < r1; i += 32) xm = fmaxf(xm, fabsf(xr[i]));
+            for (int o = 16; o > 0; o >>= 1) xm = fmaxf(xm, __shfl_xor_sync(0xFFFFFFFFu, xm, o));
+            if (lane == 0) {
+                const float bound = xm * dmax * 63.0f;
+                int ex = 0;
+                if (bound > 0.0f && bound < INFINITY) {
+                    frexpf(bound, &ex);        // bound < 2^ex
+                    ex = 14 - ex;              // bound * 2^ex < 2^14
+                    ex = ex > 100 ? 100 : (ex < -100 ? -100 : ex);
+                }
+                sval[warp] = ldexpf(1.0f, ex);
+                sinv[warp] = ldexpf(1.0f, -ex);
+            }
+        }
+        __syncthreads();
+        auto issue = [&](int tile) {
+            if (tile < ntiles) {
+                const int i0 = r0 + tile * RS;
+                const int rows = r1 - i0 < RS ? r1 - i0 : RS;
+                uint8_t* dst = wring + (int64_t)(tile % kStages) * tile_bytes;
+                const uint8_t* gsrc = Wm + (int64_t)i0 * row_bytes;
+                const int cpr = (int)(row_bytes / 16);  // 16-byte chunks per row
+                for (int c = tid; c < rows * cpr; c += kMoeThreads) {
+                    const int rr = c / cpr, cc = c - rr * cpr;
+                    cp_async16(dst + rr * RB + 16 * cc, gsrc + (int64_t)rr * row_bytes + 16 * cc);
+                }
+                float* xd = xring + (tile % kStages) * TP * RSX;
+                for (int q = tid; q < TP * rows; q += kMoeThreads) {
+                    const int b = q / rows, r = q % rows;
+                    cp_async4(xd + b * RSX + r, X + (int64_t)src[b] * IN + i0 + r);
+                }
+            }
+            cp_async_commit();
+        };
+        float acc[MPW][4];
+        float accm[SPW];  // min term of this thread's token (g >> 1) and rows, per sub-block
+#pragma unroll
+        for (int mt = 0; mt < MPW; ++mt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[mt][c] = 0.0f;
+#pragma unroll
+        for (int s2 = 0; s2 < SPW; ++s2) accm[s2] = 0.0f;
+        const int tok = g >> 1, limb = g & 1;
+        const float S = sval[tok];
+#pragma unroll
+        for (int s = 0; s < kStages - 1; ++s) issue(s);
+        for (int tile = 0; tile < ntiles; ++tile) {
+            issue(tile + kStages - 1);
+            cp_async_wait<kStages - 1>();
+            __syncthreads();
+            const int i0 = r0 + tile * RS;
+            const int rows = r1 - i0 < RS ? r1 - i0 : RS;
+            const uint8_t* wt = wring + (int64_t)(tile % kStages) * tile_bytes;
+            const float* xt = xring + (tile % kStages) * TP * RSX;
+            for (int q = tid; q < rows * G; q += kMoeThreads) {
+                const int rr = q / G, gg = q - rr * G;
+                const uint4 h = *reinterpret_cast<const uint4*>(wt + (int64_t)rr * RB + gg * block_bytes(Q));
+                uint32_t sc_lo, sc_hi, m_lo, m_hi;
+                scales_k4_packed(h.y, h.z, h.w, sc_lo, sc_hi, m_lo, m_hi);
+                const float d = h2f(h.x), dm = h2f(h.x >> 16);
+                float* tb = tab + rr * TPITCH + gg * 16;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    tb[j] = d * (float)(((j < 4 ? sc_lo : sc_hi) >> (8 * (j & 3))) & 0xFFu);
+                    tb[8 + j] = dm * (float)(((j < 4 ? m_lo : m_hi) >> (8 * (j & 3))) & 0xFFu);
+                }
+            }
+            __syncthreads();
+            for (int k0 = 0; k0 + 16 <= rows; k0 += 16) {
+                // the k index of the MMA maps to rows of the tile as k = 2t4 -> t4,
+                // 2t4 + 1 -> t4 + 4, 2t4 + 8 -> t4 + 8, 2t4 + 9 -> t4 + 12 (A and B
+                // agree, so the sum over k is the sum over the 16 rows); the 4 lanes
+                // t4 of a load then read 4 consecutive rows. B column: token `tok`, limb `limb`.
+                const int ra = k0 + t4, rb = ra + 8;
+                const float xa0 = xt[tok * RSX + ra], xa1 = xt[tok * RSX + ra + 4];
+                const float xb0 = xt[tok * RSX + rb], xb1 = xt[tok * RSX + rb + 4];
+                const float sa0 = xa0 * S, sa1 = xa1 * S, sb0v = xb0 * S, sb1v = xb1 * S;
+                // Q5_K: the fifth bits of this lane's 4 columns, rows ra .. rb + 1
+                uint32_t qh_a0 = 0, qh_a1 = 0, qh_b0 = 0, qh_b1 = 0;
+                int grp_loaded = -1;
+                uint32_t wa0 = 0, wa1 = 0, wb0 = 0, wb1 = 0;
+#pragma unroll
+                for (int s2 = 0; s2 < SPW; ++s2) {
+                    const int sbg = sb0 + s2;            // sub-block over the whole row
+                    const int grp = sbg >> 3, j = sbg & 7;
+                    const int cc = j >> 1, h = j & 1;
+                    const uint8_t* rowa = wt + (int64_t)ra * RB + grp * block_bytes(Q);
+                    const uint8_t* rowb = wt + (int64_t)rb * RB + grp * block_bytes(Q);
+                    constexpr int R4 = 4;  // the second row of each pair is 4 rows on
+                    // the 4 quant bytes of columns 4g .. 4g + 3 of sub-blocks 2cc, 2cc + 1,
+                    // loaded once for both nibbles (h = 0 then h = 1 on the next s2)
+                    if (h == 0 || s2 == 0) {
+                        const int qo = ((Q == kQ4_K) ? 16 : 48) + 32 * cc + 4 * g;
+                        wa0 = *reinterpret_cast<const uint32_t*>(rowa + qo);
+                        wa1 = *reinterpret_cast<const uint32_t*>(rowa + R4 * RB + qo);
+                        wb0 = *reinterpret_cast<const uint32_t*>(rowb + qo);
+                        wb1 = *reinterpret_cast<const uint32_t*>(rowb + R4 * RB + qo);
+                    }
+                    if constexpr (Q == kQ5_K) {
+                        if (grp != grp_loaded) {
+                            qh_a0 = *reinterpret_cast<const uint32_t*>(rowa + 16 + 4 * g);
+                            qh_a1 = *reinterpret_cast<const uint32_t*>(rowa + R4 * RB + 16 + 4 * g);
+                            qh_b0 = *reinterpret_cast<const uint32_t*>(rowb + 16 + 4 * g);
+                            qh_b1 = *reinterpret_cast<const uint32_t*>(rowb + R4 * RB + 16 + 4 * g);
+                            grp_loaded = grp;
+                        }
+                    }
+                    // B fragment: both limbs computed, the lane's one selected (no divergence)
+                    const float* ta = tab + ra * TPITCH + grp * 16;
+                    const float* tbp = tab + rb * TPITCH + grp * 16;
+                    const float va0 = sa0 * ta[j], va1 = sa1 * ta[R4 * TPITCH + j];
+                    const float vb0 = sb0v * tbp[j], vb1 = sb1v * tbp[R4 * TPITCH + j];
+                    const uint32_t ha = f16x2_bits(va0, va1), hbw = f16x2_bits(vb0, vb1);
+                    const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&ha));
+                    const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&hbw));
+                    const uint32_t la = f16x2_bits((va0 - fa.x) * 2048.0f, (va1 - fa.y) * 2048.0f);
+                    const uint32_t lb = f16x2_bits((vb0 - fb.x) * 2048.0f, (vb1 - fb.y) * 2048.0f);
+                    const uint32_t b0 = limb ? la : ha, b1 = limb ? lb : hbw;
+                    accm[s2] = fmaf(xa0, ta[8 + j], accm[s2]);
+                    accm[s2] = fmaf(xa1, ta[R4 * TPITCH + 8 + j], accm[s2]);
+                    accm[s2] = fmaf(xb0, tbp[8 + j], accm[s2]);
+                    accm[s2] = fmaf(xb1, tbp[R4 * TPITCH + 8 + j], accm[s2]);
+                    // A fragments. Column permutation: m-tile mt, fragment row g -> column
+                    // 4g + 2mt, row g + 8 -> column 4g + 2mt + 1 (all 4 in one word per row).
+#pragma unroll
+                    for (int mt = 0; mt < 2; ++mt) {
+                        uint32_t a[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {  // a0 (ra, m=g), a1 (ra, g+8), a2 (rb, g), a3 (rb, g+8)
+                            const int bsel = 2 * mt + (q & 1);
+                            const uint32_t sel = (uint32_t)(bsel | (bsel << 4) | ((4 + bsel) << 8) | ((4 + bsel) << 12));
+                            const uint32_t pr = (q < 2) ? __byte_perm(wa0, wa1, sel) : __byte_perm(wb0, wb1, sel);
+                            uint32_t hb5 = 0;
+                            if constexpr (Q == kQ5_K) {
+                                const uint32_t ph = (q < 2) ? __byte_perm(qh_a0, qh_a1, sel) : __byte_perm(qh_b0, qh_b1, sel);
+                                hb5 = ((ph >> j) & 0x00010001u) << (h ? 8 : 4);
+                            }
+                            if (h == 0) {  // 1024 + q -> q
+                                const uint32_t v = lop3_and_or(pr, 0x000F000Fu, 0x64006400u | hb5);
+                                const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&v),
+                                                          __half2(__float2half_rn(1024.0f), __float2half_rn(1024.0f)));
+                                a[q] = *reinterpret_cast<const uint32_t*>(&r);
+                            } else {       // 1024 + 16 q -> q (exact: 1/16 and 64 are powers of two)
+                                const uint32_t v = lop3_and_or(pr, 0x00F000F0u, 0x64006400u | hb5);
+                                const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&v),
+                                                          __half2(__float2half_rn(0.0625f), __float2half_rn(0.0625f)),
+                                                          __half2(__float2half_rn(-64.0f), __float2half_rn(-64.0f)));
+                                a[q] = *reinterpret_cast<const uint32_t*>(&r);
+                            }
+                        }
+                        float dk[4];
+                        mma16816z(dk, a[0], a[1], a[2], a[3], b0, b1);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) acc[2 * s2 + mt][c] += dk[c];
+                    }
+                }
+            }
+            __syncthreads();  // the stage is rewritten by the next issue
+        }
+        cp_async_wait<0>();
+        // min term of (sub-block, token): sum over the 4 lanes t4 (every lane of a
+        // token holds the same sums)
+#pragma unroll
+        for (int s2 = 0; s2 < SPW; ++s2) {
+            accm[s2] += __shfl_xor_sync(0xFFFFFFFFu, accm[s2], 1);
+            accm[s2] += __shfl_xor_sync(0xFFFFFFFFu, accm[s2], 2);
+        }
+        // outputs: lane (g, t4) holds columns g and g + 8 of each m-tile for token t4
+        // (D columns 2 t4 and 2 t4 + 1 are its hi and lo limbs). The min term of token
+        // t4 lives on lanes with g = 2 t4 (lane 8 t4 + t4').
+        const float invS = sinv[t4 < TP ? t4 : 0];
+#pragma unroll
+        for (int s2 = 0; s2 < SPW; ++s2) {
+            const float mn = __shfl_sync(0xFFFFFFFFu, accm[s2], 8 * t4);
+            const int sbg = sb0 + s2, grp = sbg >> 3, j = sbg & 7;
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const float* dd = acc[2 * s2 + mt];
+                const float y0 = fmaf(dd[1], 1.0f / 2048.0f, dd[0]) * invS - mn;
+                const float y1 = fmaf(dd[3], 1.0f / 2048.0f, dd[2]) * invS - mn;
+                if (t4 < np) {  // columns 4g + 2mt and 4g + 2mt + 1 of the sub-block
+                    float* dst = P + (((int64_t)rc * nmat + m) * A_cap + a0 + p0 + t4) * OUT + grp * 256 + 32 * j +
+                                 4 * g + 2 * mt;
+                    dst[0] = y0;
+                    dst[1] = y1;
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
 size_t stream_smem(int64_t row_bytes, int OUT, int TP) {
     const int RL = kMoeThreads / (OUT / 16);
     const int RS = tile_rows(row_bytes, RL);
-    return (size_t)kStages * RS * row_bytes + (size_t)kStages * TP * RS * 4 + (size_t)kMoeThreads * 17 * 4;
+    return (size_t)kStages * RS * row_bytes + (size_t)kStages * TP * RS * 4 + (size_t)kMoeThreads * 17 * 4 +
+           (size_t)RS * (OUT / 256) * 16 * 4;
 }
 
 template <uint32_t Q, int TP>
@@ -524,10 +926,58 @@ int launch_stream_q(int TP, const uint8_t* W0, const uint8_t* W1, int64_t row_by
                                  RC, s);
 }
 
+size_t mma_smem(int64_t row_bytes, int OUT) {
+    const int RS = mma_tile_rows(row_bytes);
+    return (size_t)kStages * RS * mma_row_pitch(row_bytes) + (size_t)kStages * 4 * mma_x_pitch(RS) * 4 +
+           (size_t)RS * ((OUT / 256) * 16 + 8) * 4;
+}
+
+template <uint32_t Q, int MPW>
+int launch_mma_t(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN, int OUT,
+                 const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P, int slots,
+                 int RC, cudaStream_t s) {
+    const size_t smem = mma_smem(row_bytes, OUT);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(moe_mma_kernel<Q, MPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return -1;
+    const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
+    moe_mma_kernel<Q, MPW><<<grid, kMoeThreads, smem, s>>>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix,
+                                                          e_begin, A_cap, P);
+    return 0;
+}
+
+template <uint32_t Q>
+int launch_mma_q(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN, int OUT,
+                 const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P, int slots,
+                 int RC, cudaStream_t s) {
+    switch (OUT / 128) {
+    case 2: return launch_mma_t<Q, 2>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                      slots, RC, s);
+    case 4: return launch_mma_t<Q, 4>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                      slots, RC, s);
+    case 8: return launch_mma_t<Q, 8>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                      slots, RC, s);
+    case 16: return launch_mma_t<Q, 16>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap,
+                                        P, slots, RC, s);
+    default: return -1;
+    }
+}
+
 int launch_stream(uint32_t q, int TP, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes,
                   int IN, int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
                   int slots, int RC, cudaStream_t s) {
     if (OUT % 256 != 0 || OUT / 16 > kMoeThreads) return -1;
+    // Q4_K / Q5_K with up to 2048 output columns: the tensor-core form
+    const int mpw = OUT / 128;
+    if ((q == kQ4_K || q == kQ5_K) && IN % 16 == 0 && row_bytes % 16 == 0 &&
+        (mpw == 2 || mpw == 4 || mpw == 8 || mpw == 16)) {
+        if (q == kQ4_K)
+            return launch_mma_q<kQ4_K>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                       slots, RC, s);
+        return launch_mma_q<kQ5_K>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                   slots, RC, s);
+    }
     switch (q) {
     case kQ4_K: return launch_stream_q<kQ4_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin,
                                               A_cap, P, slots, RC, s);
@@ -546,11 +996,14 @@ int launch_stream(uint32_t q, int TP, const uint8_t* W0, const uint8_t* W1, int6
 bool moe_expert_quant_supported(uint32_t q) { return q == kQ4_K || q == kQ5_K || q == kQ6_K || q == kQ8_0; }
 
 // Row chunks for a streamed pass over `mats` matrices: about four CTAs per SM
-// in all, at least 32 rows per chunk.
-int moe_row_chunks(int slots, int mats, int IN, int sm_count) {
+// in all, at least 32 rows per chunk (at most 8 chunks for up to 8 tokens).
+int moe_row_chunks(int slots, int mats, int IN, int sm_count, int T) {
     const int ctas = slots * mats;
     int rc = (4 * (sm_count > 0 ? sm_count : 148) + ctas - 1) / ctas;
-    const int maxrc = IN / 32 > 0 ? IN / 32 : 1;
+    // few tokens: every chunk adds one partial per output to the reductions,
+    // which then dominate; 8 chunks still give 64+ CTAs for top-8 routing
+    int maxrc = IN / 32 > 0 ? IN / 32 : 1;
+    if (T <= 8 && maxrc > 8) maxrc = 8;
     if (rc > maxrc) rc = maxrc;
     return rc < 1 ? 1 : rc;
 }
@@ -585,6 +1038,8 @@ MoeWork moe_work_layout(const MoePlan& p) {
         w.sg = take((int64_t)p.T * 4);
         w.ds = take((int64_t)p.T * p.n_embd * 4);
     }
+    const int64_t kmax = p.n_embd > p.n_ff_s ? p.n_embd : p.n_ff_s;
+    w.xfrag = take(gemv_mma_work_bytes(kmax, p.T));
     w.bytes = o;
     return w;
 }
@@ -598,21 +1053,26 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     MoeIndex ix{I(w.cnt), I(w.off), I(w.active), I(w.counters), I(w.counters) + 1, I(w.tok), I(w.pos)};
     const int A = p.T * p.k;
 
+    // dense projections (router, shared expert): tensor-core GEMV where it applies
+    auto dense = [&](const MoeTensor& Wt, int64_t rows, int64_t cols, const float* X, float* Y) -> int {
+        GemvArgs g{Wt.W, Wt.row_bytes, rows, cols, X, Y, p.T, p.sm_count, Wt.tmap};
+        if (gemv_mma_supported(Wt.quant, g)) return launch_gemv_mma(Wt.quant, g, base + w.xfrag, L.err, s);
+        return launch_gemv(Wt.quant, g, s);
+    };
+
     // route
     const float* logits = L.logits;
     if (!logits) {
         const int64_t n = (int64_t)p.T * p.n_embd;
         moe_bf16_round_kernel<<<grid_for(n, p.sm_count), 256, 0, s>>>(L.x, F(w.xb), n);
-        GemvArgs g{L.router.W, L.router.row_bytes, p.E, p.n_embd, F(w.xb), F(w.logits), p.T, p.sm_count, nullptr};
-        if (launch_gemv(L.router.quant, g, s)) return -1;
+        if (dense(L.router, p.E, p.n_embd, F(w.xb), F(w.logits))) return -1;
         logits = F(w.logits);
     }
-    moe_route_kernel<<<p.T, 256, (size_t)p.E * (sizeof(float) + sizeof(int)), s>>>(logits, p.E, p.k, I(w.ids), F(w.wts));
-    int athreads = 32;
-    while (athreads < p.E) athreads <<= 1;
-    const bool staged = (int64_t)p.T * p.k * 4 <= 40 * 1024;
-    moe_assign_kernel<<<1, athreads, staged ? (size_t)p.T * p.k * 4 : 0, s>>>(I(w.ids), p.T, p.k, p.E, p.e_begin,
-                                                                              p.e_end, staged, ix);
+    moe_route_kernel<<<(p.T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32,
+                       (size_t)kRouteWarps * p.E * sizeof(float), s>>>(logits, p.T, p.E, p.k, I(w.ids), F(w.wts));
+    const bool staged = (int64_t)p.T * p.k * 4 <= 32 * 1024;
+    moe_assign_kernel<<<1, kAssignThreads, staged ? (size_t)p.T * p.k * 4 : 0, s>>>(I(w.ids), p.T, p.k, p.E,
+                                                                                    p.e_begin, p.e_end, staged, ix);
 
     // routed experts
     const int slots = p.slots;
@@ -630,21 +1090,19 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     const float* Ds = nullptr;
     const float* sg = nullptr;
     if (p.shared) {
-        GemvArgs gg{L.gate_s.W, L.gate_s.row_bytes, p.n_ff_s, p.n_embd, L.x, F(w.gs), p.T, p.sm_count, nullptr};
-        GemvArgs gu{L.up_s.W, L.up_s.row_bytes, p.n_ff_s, p.n_embd, L.x, F(w.us), p.T, p.sm_count, nullptr};
-        GemvArgs gi{L.gate_inp_s.W, L.gate_inp_s.row_bytes, 1, p.n_embd, L.x, F(w.gi), p.T, p.sm_count, nullptr};
-        if (launch_gemv(L.gate_s.quant, gg, s) || launch_gemv(L.up_s.quant, gu, s) ||
-            launch_gemv(L.gate_inp_s.quant, gi, s))
+        if (dense(L.gate_s, p.n_ff_s, p.n_embd, L.x, F(w.gs)) || dense(L.up_s, p.n_ff_s, p.n_embd, L.x, F(w.us)) ||
+            dense(L.gate_inp_s, 1, p.n_embd, L.x, F(w.gi)))
             return -4;
         moe_shared_act_kernel<<<grid_for((int64_t)p.T * p.n_ff_s, p.sm_count), 256, 0, s>>>(
             F(w.gs), F(w.us), F(w.gi), p.T, p.n_ff_s, F(w.hs), F(w.sg));
-        GemvArgs gd{L.down_s.W, L.down_s.row_bytes, p.n_embd, p.n_ff_s, F(w.hs), F(w.ds), p.T, p.sm_count, nullptr};
-        if (launch_gemv(L.down_s.quant, gd, s)) return -5;
+        if (dense(L.down_s, p.n_embd, p.n_ff_s, F(w.hs), F(w.ds))) return -5;
         Ds = F(w.ds);
         sg = F(w.sg);
     }
-    moe_combine_kernel<<<grid_for((int64_t)p.T * p.n_embd, p.sm_count), 256, 0, s>>>(
-        F(w.pd), p.rc_d, A, p.n_embd, I(w.pos), F(w.wts), p.T, p.k, Ds, sg, L.out);
+    int lanes = 1;
+    while (lanes < p.k) lanes <<= 1;
+    moe_combine_kernel<<<grid_for((int64_t)p.T * p.n_embd * lanes, p.sm_count), 256, 0, s>>>(
+        F(w.pd), p.rc_d, A, p.n_embd, I(w.pos), F(w.wts), p.T, p.k, lanes, Ds, sg, L.out);
     if (L.ids_out) cudaMemcpyAsync(L.ids_out, I(w.ids), (size_t)A * 4, cudaMemcpyDeviceToDevice, s);
     if (L.wts_out) cudaMemcpyAsync(L.wts_out, F(w.wts), (size_t)A * 4, cudaMemcpyDeviceToDevice, s);
     return 0;

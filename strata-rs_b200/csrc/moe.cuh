@@ -28,7 +28,7 @@ struct MoePlan {
 
 // Byte offsets of the workspace arrays.
 struct MoeWork {
-    int64_t ids, wts, pos, tok, cnt, off, active, counters, logits, xb, pgu, h, pd, gs, us, hs, gi, sg, ds;
+    int64_t ids, wts, pos, tok, cnt, off, active, counters, logits, xb, pgu, h, pd, gs, us, hs, gi, sg, ds, xfrag;
     int64_t bytes;
 };
 
@@ -37,6 +37,7 @@ struct MoeTensor {
     const uint8_t* W = nullptr;   // device bytes (experts: the first held expert)
     int64_t row_bytes = 0;
     int64_t expert_bytes = 0;     // rows * row_bytes for expert tensors
+    const void* tmap = nullptr;   // tensor map of a dense Q4_K / Q5_K matrix (tensor-core GEMV), or null
 };
 
 struct MoeLaunch {
@@ -48,11 +49,12 @@ struct MoeLaunch {
     float* out;                       // [T][n_embd]
     int* ids_out;                     // optional [T][k] device copies of the routing
     float* wts_out;
+    int* err;                         // set by a kernel whose bounded wait expired
     MoeTensor router, gate, up, down, gate_s, up_s, down_s, gate_inp_s;
 };
 
 bool moe_expert_quant_supported(uint32_t q);
-int moe_row_chunks(int slots, int mats, int IN, int sm_count);
+int moe_row_chunks(int slots, int mats, int IN, int sm_count, int T);
 MoeWork moe_work_layout(const MoePlan& p);
 int launch_moe_layer(const MoeLaunch& L, cudaStream_t s);
 

@@ -29,6 +29,7 @@ MoeTensor tensor_of(const strata_weight* w) {
     t.W = w->dev;
     t.row_bytes = w->row_bytes;
     t.expert_bytes = w->rows * w->row_bytes;
+    t.tmap = w->has_tmap ? w->tmap : nullptr;
     return t;
 }
 
@@ -78,8 +79,8 @@ int moe_enqueue(strata_ctx* ctx, const strata_moe* L, const float* x, const floa
     const int64_t held = d.expert_end - d.expert_begin;
     p.slots = (int)(T * d.top_k < held ? T * d.top_k : held);
     p.sm_count = ctx->sm_count;
-    p.rc_gu = moe_row_chunks(p.slots, 2, p.n_embd, p.sm_count);
-    p.rc_d = moe_row_chunks(p.slots, 1, p.n_ff, p.sm_count);
+    p.rc_gu = moe_row_chunks(p.slots, 2, p.n_embd, p.sm_count, p.T);
+    p.rc_d = moe_row_chunks(p.slots, 1, p.n_ff, p.sm_count, p.T);
     MoeWork layout = moe_work_layout(p);
     int rc = ensure_device(ctx, ctx->moe_work, (size_t)layout.bytes, "cudaMalloc(moe workspace)");
     if (rc) return rc;
@@ -92,6 +93,7 @@ int moe_enqueue(strata_ctx* ctx, const strata_moe* L, const float* x, const floa
     ml.out = out;
     ml.ids_out = reinterpret_cast<int*>(ids);
     ml.wts_out = wts;
+    ml.err = ctx->err_dev;
     ml.router = tensor_of(d.router);
     ml.gate = tensor_of(d.gate_exps);
     ml.up = tensor_of(d.up_exps);
@@ -133,10 +135,10 @@ int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe
     if (!ctx || !d || !out) return STRATA_ERR_INVALID;
     std::lock_guard<std::mutex> g(ctx->mu);
     *out = nullptr;
-    if (d->n_embd <= 0 || d->n_expert <= 0 || d->n_expert > 1024 || d->top_k <= 0 || d->top_k > 64 ||
+    if (d->n_embd <= 0 || d->n_expert <= 0 || d->n_expert > 1024 || d->top_k <= 0 || d->top_k > 32 ||
         d->n_ff <= 0 || d->n_embd % 256 != 0 || d->n_ff % 256 != 0)
         return fail(ctx, STRATA_ERR_INVALID,
-                    "moe: need n_embd, n_ff multiples of 256, 1 <= n_expert <= 1024, 1 <= top_k <= 64");
+                    "moe: need n_embd, n_ff multiples of 256, 1 <= n_expert <= 1024, 1 <= top_k <= 32");
     if (d->expert_begin < 0 || d->expert_end > d->n_expert || d->expert_begin >= d->expert_end)
         return fail(ctx, STRATA_ERR_INVALID, "moe: expert range [%lld, %lld) of %lld", (long long)d->expert_begin,
                     (long long)d->expert_end, (long long)d->n_expert);

@@ -76,10 +76,7 @@ int64_t expert_gemv_work_floats(int64_t IN, int64_t OUT, int sm_count);
 int launch_expert_gemv_ws(uint32_t quant, const ExpertGemvArgs& a, float* work, int64_t work_floats,
                           cudaStream_t s);
 
-// gemv_mma.cu
-int64_t gemv_mma_work_bytes(int64_t K, int batch);
-bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
+// gemv_mma.cu (launchers declared in kernels.cuh)
 bool encode_gemv_tmap(uint32_t quant, const void* base, int64_t rows, int64_t row_bytes, void* out128);
 int check_device_error(strata_ctx* ctx);
 
