@@ -712,6 +712,61 @@ def run_profile_case(args):
     ctx.close()
 
 
+def run_profile_gemm(args):
+    """One prefill GEMM case (QUANT,K,N,M, e.g. Q5_K,4096,12288,2048) launched
+    warmup + steps times: the workload of the GEMM ncu capture under profiles/."""
+    import torch
+    import strata_cuda as sc
+    qn, k, n, m = args.profile_gemm.split(",")
+    q = {"Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}[qn]
+    k, n, m = int(k), int(n), int(m)
+    ctx = sc.Context(0)
+    w = ctx.upload(quant_matrix(500 + k + q, q, n, k), q, n, k)
+    x = torch.from_numpy(bf16_bits(activations(77 + k, m, k)).view(np.int16)).cuda()
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    ms = timed(torch, st, lambda: ctx.gemm_bf16_dev(w, x.data_ptr(), y.data_ptr(), m, st.cuda_stream),
+               max(1, args.steps), warm=args.warmup)
+    print(json.dumps({"profile_gemm": [qn, k, n, m], "us": round(ms * 1e3, 1),
+                      "tflops": round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 1),
+                      "note": "same weights every launch: a profiling workload, not a bench value"}))
+    w.free()
+    ctx.close()
+
+
+def run_profile_moe(args):
+    """One MoE FFN configuration layer call at T tokens, warmup + steps times:
+    the workload of the MoE ncu captures under profiles/."""
+    import torch
+    import strata_cuda as sc
+    T = int(args.profile_moe)
+    d = MOE_DIMS
+    ctx = sc.Context(0)
+    ws = {"gate_exps": ctx.upload(quant_matrix(1201, Q4_K, d["n_embd"], d["n_ff"], d["E"]), Q4_K, d["n_embd"],
+                                  d["n_ff"], n_expert=d["E"]),
+          "up_exps": ctx.upload(quant_matrix(1202, Q4_K, d["n_embd"], d["n_ff"], d["E"]), Q4_K, d["n_embd"],
+                                d["n_ff"], n_expert=d["E"]),
+          "down_exps": ctx.upload(quant_matrix(1203, Q4_K, d["n_ff"], d["n_embd"], d["E"]), Q4_K, d["n_ff"],
+                                  d["n_embd"], n_expert=d["E"]),
+          "gate_shexp": ctx.upload(quant_matrix(1204, Q4_K, d["n_ff_s"], d["n_embd"]), Q4_K, d["n_ff_s"], d["n_embd"]),
+          "up_shexp": ctx.upload(quant_matrix(1205, Q4_K, d["n_ff_s"], d["n_embd"]), Q4_K, d["n_ff_s"], d["n_embd"]),
+          "down_shexp": ctx.upload(quant_matrix(1206, Q4_K, d["n_embd"], d["n_ff_s"]), Q4_K, d["n_embd"], d["n_ff_s"]),
+          "gate_inp_shexp": ctx.upload(quant_matrix(1207, Q4_K, 1, d["n_embd"]), Q4_K, 1, d["n_embd"])}
+    L = ctx.moe_create(ws, d["n_embd"], d["E"], d["k"], d["n_ff"], d["n_ff_s"])
+    x = torch.from_numpy(activations(1201 + T, T, d["n_embd"])).cuda()
+    lg = torch.from_numpy(rng(1202 + T).standard_normal((T, d["E"])).astype(np.float32)).cuda()
+    y = torch.empty((T, d["n_embd"]), dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    ms = timed(torch, st, lambda: ctx.moe_ffn_dev(L, x.data_ptr(), lg.data_ptr(), T, y.data_ptr(),
+                                                  stream=st.cuda_stream), max(1, args.steps), warm=args.warmup)
+    print(json.dumps({"profile_moe": T, "us_per_layer": round(ms * 1e3, 2),
+                      "note": "same weights and routing every call: a profiling workload, not a bench value"}))
+    L.free()
+    for w in ws.values():
+        w.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -724,11 +779,19 @@ def main():
     ap.add_argument("--skip-sections", action="store_true", help="only the GEMV sweep (no gemm / moe / sharded lines)")
     ap.add_argument("--profile-case", default=None, metavar="K,N,B",
                     help="launch one Q4_K GEMV case repeatedly (for ncu captures) instead of the bench")
+    ap.add_argument("--profile-gemm", default=None, metavar="QUANT,K,N,M",
+                    help="launch one prefill GEMM case repeatedly (for ncu captures) instead of the bench")
+    ap.add_argument("--profile-moe", default=None, metavar="T",
+                    help="run the MoE configuration layer at T tokens repeatedly (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.profile_case:
         run_profile_case(args)
+    elif args.profile_gemm:
+        run_profile_gemm(args)
+    elif args.profile_moe:
+        run_profile_moe(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -631,6 +631,18 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
     return d;
 }
+// f16x2 arithmetic on bit patterns (constants as immediate bit patterns:
+// 0x6400 = 1024, 0x2C00 = 1/16, 0xD400 = -64)
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 __device__ __forceinline__ uint32_t f16x2_bits(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
@@ -839,16 +851,10 @@ moe_mma_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, i
                                 hb5 = ((ph >> j) & 0x00010001u) << (h ? 8 : 4);
                             }
                             if (h == 0) {  // 1024 + q -> q
-                                const uint32_t v = lop3_and_or(pr, 0x000F000Fu, 0x64006400u | hb5);
-                                const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&v),
-                                                          __half2(__float2half_rn(1024.0f), __float2half_rn(1024.0f)));
-                                a[q] = *reinterpret_cast<const uint32_t*>(&r);
+                                a[q] = hsub2_bits(lop3_and_or(pr, 0x000F000Fu, 0x64006400u | hb5), 0x64006400u);
                             } else {       // 1024 + 16 q -> q (exact: 1/16 and 64 are powers of two)
-                                const uint32_t v = lop3_and_or(pr, 0x00F000F0u, 0x64006400u | hb5);
-                                const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&v),
-                                                          __half2(__float2half_rn(0.0625f), __float2half_rn(0.0625f)),
-                                                          __half2(__float2half_rn(-64.0f), __float2half_rn(-64.0f)));
-                                a[q] = *reinterpret_cast<const uint32_t*>(&r);
+                                a[q] = hfma2_bits(lop3_and_or(pr, 0x00F000F0u, 0x64006400u | hb5), 0x2C002C00u,
+                                                  0xD400D400u);
                             }
                         }
                         float dk[4];
