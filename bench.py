@@ -474,6 +474,8 @@ def run_gpu(args):
     ys = {(k, n, b): torch.empty(b, n, device="cuda") for (k, n) in shapes for b in batches}
 
     def enqueue(step_idx: int, s: int):
+        if world > 1:  # the step's 16 gathers go out as one NCCL group
+            ctx.comm_group_start()
         for b in batches:
             for (k, n) in shapes:
                 w = weights[(k, n)][step_idx % len(weights[(k, n)])]
@@ -481,25 +483,37 @@ def run_gpu(args):
                     ctx.gemv_sharded_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, s)
                 else:
                     ctx.gemv_dev(w, xk[(b, k)].data_ptr(), ys[(k, n, b)].data_ptr(), b, s)
+        if world > 1:
+            ctx.comm_group_end()
 
     graphs = []
     with torch.cuda.stream(stream):
         enqueue(0, stream.cuda_stream)  # warm the kernels before capture
     stream.synchronize()
-    if world == 1:
+    try:  # N > 1: the library's NCCL group is captured with the kernels
         for i in range(rot):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
                 enqueue(i, stream.cuda_stream)
             graphs.append(g)
-    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel;
-    # sharded, batches > 1 add the gather transpose (the NCCL kernel is not counted)
+        g = None  # the list holds the graphs (released before the communicator)
+        captured = 1
+    except Exception as exc:  # noqa: BLE001 - fall back to direct launches on every rank
+        print(f"graph capture unavailable ({exc}); launching directly", file=sys.stderr)
+        graphs = []
+        captured = 0
+    if dist:
+        ok = torch.tensor([captured], device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            graphs = []
+    torch.cuda.synchronize()
+    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel
+    # (sharded: plus the NCCL group's kernel, not counted)
     launches_per_step = 2 * len(batches) * len(shapes)
-    if world > 1:
-        launches_per_step += sum(1 for b in batches if b > 1) * len(shapes)
 
     def step(i):
-        if world == 1:
+        if graphs:
             graphs[i % rot].replay()
         else:
             enqueue(i, stream.cuda_stream)
@@ -656,9 +670,10 @@ def run_gpu(args):
                                    "2048->151936 at batch 1,2,4,8 (16 GEMVs per step, batch-major)",
                        "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 "
                              "per matrix), no matrix re-read within 241 MB of traffic",
-                       "parallelism": (f"row-sharded x{world}: local GEMV + NCCL all-gather inside "
-                                       f"strata_cuda_gemv_sharded_dev" if world > 1 else "single GPU"),
-                       "launch": "CUDA graph per step" if world == 1 else "direct launches (collectives inside)"},
+                       "parallelism": (f"row-sharded x{world}: local GEMV into its columns of y + in-place "
+                                       f"NCCL all-gathers inside strata_cuda_gemv_sharded_dev, the step's "
+                                       f"16 in one NCCL group" if world > 1 else "single GPU"),
+                       "launch": "CUDA graph per step" if graphs else "direct launches"},
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(value / hbm, 3), "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": total // (len(batches) * len(shapes)),

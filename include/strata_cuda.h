@@ -222,6 +222,15 @@ int strata_cuda_comm_unique_id(uint8_t *id_out /* STRATA_COMM_ID_BYTES */);
 int strata_cuda_comm_init(strata_ctx *ctx, int rank, int world, const uint8_t *id);
 int strata_cuda_comm_info(const strata_ctx *ctx, int *rank, int *world);
 
+/* Collectives issued between group_start and group_end (the gathers of
+ * several sharded GEMV calls, MoE all-reduces) are launched together at
+ * group_end, as one NCCL group: one collective launch for a whole decode step.
+ * The GEMV and MoE calls enqueue their own kernels at once; only their
+ * collectives wait for group_end. The sharded GEMM cannot run inside a group
+ * (its transpose follows its gather). Groups nest. */
+int strata_cuda_comm_group_start(strata_ctx *ctx);
+int strata_cuda_comm_group_end(strata_ctx *ctx);
+
 /* Row-sharded projection: w holds this rank's rows [rank R, (rank + 1) R) of
  * an OUT = world * R row matrix (every rank the same R). The local GEMV
  * (batch 1..8) or prefill GEMM (m tokens, bf16 x) writes its slice and an

@@ -41,6 +41,8 @@ struct Nccl {
     ncclResult_t (*CommAbort)(ncclComm_t);
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*GroupStart)();
+    ncclResult_t (*GroupEnd)();
     const char* (*GetErrorString)(ncclResult_t);
 };
 
@@ -69,6 +71,8 @@ const Nccl& nccl() {
         sym(n.CommAbort, "ncclCommAbort");
         sym(n.AllGather, "ncclAllGather");
         sym(n.AllReduce, "ncclAllReduce");
+        sym(n.GroupStart, "ncclGroupStart");
+        sym(n.GroupEnd, "ncclGroupEnd");
         sym(n.GetErrorString, "ncclGetErrorString");
         n.ok = all;
     });
@@ -78,7 +82,8 @@ const Nccl& nccl() {
 struct CommState {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
-    DevBuf send, recv;  // gather staging for batches > 1
+    int group_depth = 0;  // > 0 inside strata_cuda_comm_group_start / end
+    DevBuf send, recv;    // gather staging of the GEMM (m > 1)
 };
 
 void comm_release(strata_ctx* ctx) {
@@ -129,19 +134,35 @@ __global__ void gather_transpose_kernel(const float* __restrict__ part, float* _
     }
 }
 
-// The all-gather of a [B][ns] slice per rank into y = [B][G ns]. With B = 1
-// the slices are contiguous in y and the gather is in place.
-int gather_rows(strata_ctx* ctx, const float* local, float* y, int B, int64_t ns, cudaStream_t s) {
+// The all-gather of every rank's rows of y = [B][G ns]: one in-place
+// all-gather per output row b (rank r's slice of row b is contiguous at
+// y[b][r ns]), issued as one NCCL group, so no staging and no transpose. The
+// local GEMV has already written this rank's slices in place.
+int gather_rows_inplace(strata_ctx* ctx, float* y, int B, int64_t ns, cudaStream_t s) {
+    CommState* c = ctx->comm;
+    const int64_t N = ns * c->world;
+    const bool own_group = c->group_depth == 0;
+    int rc;
+    if (own_group && (rc = nccl_done(ctx, c->comm, nccl().GroupStart(), "ncclGroupStart"))) return rc;
+    for (int b = 0; b < B; ++b) {
+        float* row = y + (int64_t)b * N;
+        rc = nccl_done(ctx, c->comm, nccl().AllGather(row + c->rank * ns, row, (size_t)ns, ncclFloat, c->comm, s),
+                       "ncclAllGather");
+        if (rc) {
+            if (own_group) nccl().GroupEnd();
+            return rc;
+        }
+    }
+    if (own_group) return nccl_done(ctx, c->comm, nccl().GroupEnd(), "ncclGroupEnd");
+    return STRATA_OK;
+}
+
+// GEMM: [M][ns] per rank gathered into [G][M][ns], then transposed into [M][N].
+int gather_rows_staged(strata_ctx* ctx, const float* local, float* y, int B, int64_t ns, cudaStream_t s) {
     CommState* c = ctx->comm;
     const int G = c->world;
-    if (B == 1) {
-        if (local != y + c->rank * ns) {
-            cudaError_t e = cudaMemcpyAsync(y + c->rank * ns, local, (size_t)ns * 4, cudaMemcpyDeviceToDevice, s);
-            if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(shard)");
-        }
-        return nccl_done(ctx, c->comm, nccl().AllGather(y + c->rank * ns, y, (size_t)ns, ncclFloat, c->comm, s),
-                         "ncclAllGather");
-    }
+    if (c->group_depth > 0)
+        return fail(ctx, STRATA_ERR_INVALID, "the sharded GEMM cannot run inside a collective group");
     const size_t part = (size_t)B * (size_t)ns * 4;
     int rc = ensure_device(ctx, c->recv, part * (size_t)G, "cudaMalloc(gather)");
     if (rc) return rc;
@@ -204,6 +225,26 @@ int strata_cuda_comm_info(const strata_ctx* ctx, int* rank, int* world) {
     return STRATA_OK;
 }
 
+int strata_cuda_comm_group_start(strata_ctx* ctx) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = need_comm(ctx);
+    if (rc) return rc;
+    if (ctx->comm->group_depth++ == 0)
+        return nccl_done(ctx, ctx->comm->comm, nccl().GroupStart(), "ncclGroupStart");
+    return STRATA_OK;
+}
+
+int strata_cuda_comm_group_end(strata_ctx* ctx) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = need_comm(ctx);
+    if (rc) return rc;
+    if (ctx->comm->group_depth == 0) return fail(ctx, STRATA_ERR_INVALID, "no collective group is open");
+    if (--ctx->comm->group_depth == 0) return nccl_done(ctx, ctx->comm->comm, nccl().GroupEnd(), "ncclGroupEnd");
+    return STRATA_OK;
+}
+
 int strata_cuda_gemv_sharded_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                                  void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
@@ -216,13 +257,10 @@ int strata_cuda_gemv_sharded_dev(strata_ctx* ctx, const strata_weight* w, const 
     cudaStream_t s = pick_stream(ctx, stream);
     CommState* c = ctx->comm;
     const int64_t ns = w->rows;
-    float* local = y_dev + c->rank * ns;  // batch 1: the rank's slice of y
-    if (batch > 1) {
-        if ((rc = ensure_device(ctx, c->send, (size_t)batch * (size_t)ns * 4, "cudaMalloc(shard)"))) return rc;
-        local = (float*)c->send.ptr;
-    }
-    if ((rc = gemv_enqueue(ctx, w, x_dev, local, batch, s))) return rc;
-    return gather_rows(ctx, local, y_dev, batch, ns, s);
+    // the local GEMV writes rank r's columns of every output row in place
+    // (output row pitch N = world * ns)
+    if ((rc = gemv_enqueue_strided(ctx, w, x_dev, y_dev + c->rank * ns, batch, ns * c->world, s))) return rc;
+    return gather_rows_inplace(ctx, y_dev, batch, ns, s);
 }
 
 int strata_cuda_gemm_sharded_dev(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev,
@@ -243,7 +281,8 @@ int strata_cuda_gemm_sharded_dev(strata_ctx* ctx, const strata_weight* w, const 
         local = (float*)c->send.ptr;
     }
     if ((rc = gemm_enqueue(ctx, w, x_dev, local, m, s))) return rc;
-    return gather_rows(ctx, local, y_dev, (int)m, ns, s);
+    if (m == 1) return gather_rows_inplace(ctx, y_dev, 1, ns, s);
+    return gather_rows_staged(ctx, local, y_dev, (int)m, ns, s);
 }
 
 int strata_cuda_moe_ffn_ep_dev(strata_ctx* ctx, const strata_moe* layer, const float* x_dev,

@@ -154,10 +154,10 @@ __device__ __forceinline__ void unit_word(const UnitData& u, int t, int i, uint3
 template <uint32_t Q, int NB, int R, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_kquant_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
-                   const float* __restrict__ X, float* __restrict__ Y) {
+                   const float* __restrict__ X, float* __restrict__ Y, int64_t ldy) {
     // token chunk blockIdx.y: rows [NB y, NB y + NB) of X and Y
     X += (int64_t)blockIdx.y * NB * K;
-    Y += (int64_t)blockIdx.y * NB * N;
+    Y += (int64_t)blockIdx.y * NB * ldy;
     constexpr int BB = block_bytes(Q);
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -222,7 +222,7 @@ gemv_kquant_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, 
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 float v = warp_sum(sum[r][b]);
-                if (lane == 0 && row0 + r < N) Y[b * N + row0 + r] = v;
+                if (lane == 0 && row0 + r < N) Y[b * ldy + row0 + r] = v;
             }
     }
 }
@@ -232,9 +232,9 @@ gemv_kquant_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, 
 template <int NB, int R, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
-                 const float* __restrict__ X, float* __restrict__ Y) {
+                 const float* __restrict__ X, float* __restrict__ Y, int64_t ldy) {
     X += (int64_t)blockIdx.y * NB * K;
-    Y += (int64_t)blockIdx.y * NB * N;
+    Y += (int64_t)blockIdx.y * NB * ldy;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int64_t nblk = K / 32;
@@ -294,7 +294,7 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, in
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 float v = warp_sum(sum[r][b]);
-                if (lane == 0 && row0 + r < N) Y[b * N + row0 + r] = v;
+                if (lane == 0 && row0 + r < N) Y[b * ldy + row0 + r] = v;
             }
     }
 }
@@ -302,9 +302,9 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, in
 // Plain float weights (F32 / F16 / BF16): one warp per row, lanes stride over K.
 template <uint32_t Q, int NB>
 __global__ void gemv_float_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
-                                  const float* __restrict__ X, float* __restrict__ Y) {
+                                  const float* __restrict__ X, float* __restrict__ Y, int64_t ldy) {
     X += (int64_t)blockIdx.y * NB * K;
-    Y += (int64_t)blockIdx.y * NB * N;
+    Y += (int64_t)blockIdx.y * NB * ldy;
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < N; row += (int64_t)gridDim.x * warps) {
@@ -323,7 +323,7 @@ __global__ void gemv_float_kernel(const uint8_t* __restrict__ W, int64_t row_byt
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
             float v = warp_sum(acc[b]);
-            if (lane == 0) Y[b * N + row] = v;
+            if (lane == 0) Y[b * ldy + row] = v;
         }
     }
 }
@@ -336,7 +336,7 @@ void launch_kq(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     int64_t cap = (int64_t)a.sm_count * 8;
     if (grid > cap) grid = cap;
     gemv_kquant_kernel<Q, NB, R, WARPS><<<dim3((unsigned)grid, chunks), WARPS * 32, 0, s>>>(a.W, a.row_bytes, a.N,
-                                                                                       a.K, a.X, a.Y);
+                                                                                       a.K, a.X, a.Y, ldy_of(a));
 }
 
 template <int NB, int R>
@@ -347,7 +347,7 @@ void launch_q8(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     int64_t cap = (int64_t)a.sm_count * 8;
     if (grid > cap) grid = cap;
     gemv_q8_0_kernel<NB, R, WARPS><<<dim3((unsigned)grid, chunks), WARPS * 32, 0, s>>>(a.W, a.row_bytes, a.N, a.K,
-                                                                                  a.X, a.Y);
+                                                                                  a.X, a.Y, ldy_of(a));
 }
 
 template <uint32_t Q, int NB>
@@ -355,7 +355,8 @@ void launch_float(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     int64_t grid = (a.N + 7) / 8;
     int64_t cap = (int64_t)a.sm_count * 16;
     if (grid > cap) grid = cap;
-    gemv_float_kernel<Q, NB><<<dim3((unsigned)grid, chunks), 256, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y);
+    gemv_float_kernel<Q, NB><<<dim3((unsigned)grid, chunks), 256, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y,
+                                                                          ldy_of(a));
 }
 
 // Rows per warp by batch: more rows share each activation load when the batch
@@ -432,7 +433,7 @@ int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s) {
         if (rem == 0) return 0;
         GemvArgs r = a;
         r.X = a.X + (int64_t)full * 8 * a.K;
-        r.Y = a.Y + (int64_t)full * 8 * a.N;
+        r.Y = a.Y + (int64_t)full * 8 * ldy_of(a);
         r.batch = rem;
         return launch_gemv(quant, r, s);
     }

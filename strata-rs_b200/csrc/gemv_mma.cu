@@ -358,12 +358,12 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 3)
 gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
                    float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap,
-                   int64_t chunk_bytes) {
+                   int64_t chunk_bytes, int64_t ldy) {
     // token chunk blockIdx.y (batches above 8): its limbs and its NB output rows
     XF = reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(XF) + blockIdx.y * chunk_bytes);
     XS = reinterpret_cast<const float*>(reinterpret_cast<const char*>(XS) + blockIdx.y * chunk_bytes);
     XQ = reinterpret_cast<const __half*>(reinterpret_cast<const char*>(XQ) + blockIdx.y * chunk_bytes);
-    Y += (int64_t)blockIdx.y * NB * N;
+    Y += (int64_t)blockIdx.y * NB * ldy;
     constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
     constexpr int BB = block_bytes(Q);
     // smem stride of one row of a stage. TM (one tensor-map copy per stage):
@@ -517,7 +517,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                 for (int w = 0; w < kConsumers; ++w) v += red[set][w][nt][r][lane];
                 const int b = 4 * nt + t;
                 const int row = tile * kTileRows + 8 * r + g;
-                if (b < NB && row < N) Y[b * N + row] = v;
+                if (b < NB && row < N) Y[b * ldy + row] = v;
             }
         }
     }
@@ -552,7 +552,7 @@ void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __hal
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err,
-                       map, chunk_bytes);
+                       map, chunk_bytes, ldy_of(a));
 }
 
 template <uint32_t Q, bool TM>
@@ -650,7 +650,7 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     if (full && a.batch % 8) {  // the remaining tokens, after the chunks' workspace
         GemvArgs r = a;
         r.X = a.X + (int64_t)full * 8 * a.K;
-        r.Y = a.Y + (int64_t)full * 8 * a.N;
+        r.Y = a.Y + (int64_t)full * 8 * ldy_of(a);
         r.batch = a.batch % 8;
         return launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s);
     }

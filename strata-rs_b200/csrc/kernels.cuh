@@ -16,7 +16,9 @@ struct GemvArgs {
     int batch;
     int sm_count;
     const void* tmap = nullptr;  // CUtensorMap of W for the tensor-core GEMV, or null
+    int64_t ldy = 0;             // output row pitch in floats (0: N)
 };
+inline int64_t ldy_of(const GemvArgs& a) { return a.ldy > 0 ? a.ldy : a.N; }
 
 int launch_dequant(uint32_t quant, const uint8_t* w, int64_t row_bytes, int64_t cols, int64_t nrows,
                    float* out, cudaStream_t stream);

@@ -323,11 +323,17 @@ namespace strata {
 
 int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                  cudaStream_t s) {
+    return gemv_enqueue_strided(ctx, w, x_dev, y_dev, batch, 0, s);
+}
+
+// y row b at y_dev + b * ldy (ldy 0: rows are w->rows floats apart)
+int gemv_enqueue_strided(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
+                         int64_t ldy, cudaStream_t s) {
     if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
         return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
     GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch, ctx->sm_count,
-               w->has_tmap ? w->tmap : nullptr};
+               w->has_tmap ? w->tmap : nullptr, ldy};
     if (ctx->gemv_path != STRATA_GEMV_CUDA_CORES && gemv_mma_supported(w->quant, a)) {
         int64_t need = gemv_mma_work_bytes(w->cols, batch);
         int rc = ensure_device(ctx, ctx->xfrag, (size_t)(need > (4 << 20) ? need : (4 << 20)), "cudaMalloc(x limbs)");

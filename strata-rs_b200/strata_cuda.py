@@ -89,6 +89,8 @@ def lib() -> C.CDLL:
             "strata_cuda_comm_unique_id": (i32, [vp]),
             "strata_cuda_comm_init": (i32, [vp, i32, i32, vp]),
             "strata_cuda_comm_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
+            "strata_cuda_comm_group_start": (i32, [vp]),
+            "strata_cuda_comm_group_end": (i32, [vp]),
             "strata_cuda_gemv_sharded_dev": (i32, [vp, vp, vp, vp, i32, vp]),
             "strata_cuda_gemm_sharded_dev": (i32, [vp, vp, vp, vp, i64, vp]),
             "strata_cuda_moe_ffn_ep_dev": (i32, [vp, vp, vp, vp, i64, vp, vp]),
@@ -312,6 +314,12 @@ class Context:
         r, w = C.c_int(), C.c_int()
         self.check(lib().strata_cuda_comm_info(self.h, C.byref(r), C.byref(w)))
         return r.value, w.value
+
+    def comm_group_start(self):
+        self.check(lib().strata_cuda_comm_group_start(self.h))
+
+    def comm_group_end(self):
+        self.check(lib().strata_cuda_comm_group_end(self.h))
 
     def gemv_sharded_dev(self, w: Weight, x_ptr: int, y_ptr: int, batch: int, stream: int = 0):
         self.check(lib().strata_cuda_gemv_sharded_dev(self.h, w.handle, x_ptr, y_ptr, batch, stream or None))
