@@ -240,6 +240,24 @@ int strata_cuda_gemv_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, 
 int strata_cuda_gemm_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, const uint16_t *x_dev,
                                  float *y_dev, int64_t m, void *stream);
 
+/* How the sharded GEMV gathers its rows. PEER fuses the all-gather into the
+ * tensor-core GEMV: its epilogue stores each output value straight into every
+ * rank's exchange buffer over NVLink (peer memory opened with CUDA IPC at
+ * comm_init) and bumps each rank's arrival counter; a small kernel on each
+ * rank waits (bounded by the context's wait timeout, then
+ * STRATA_ERR_TIMEOUT) for all arrivals and copies the gathered rows to y.
+ * No NCCL call is made, so these calls ignore collective groups and are
+ * graph-capturable. NCCL uses the per-row in-place all-gathers. AUTO (the
+ * default) takes PEER where it applies -- peer memory available on every
+ * rank, a Q4_K / Q5_K shard on the tensor-core path, batch x OUT within the
+ * exchange capacity -- and NCCL otherwise. Every rank must set the same mode
+ * (the ranks of one call must take the same path). */
+enum { STRATA_GATHER_AUTO = 0, STRATA_GATHER_NCCL = 1, STRATA_GATHER_PEER = 2 };
+int strata_cuda_comm_set_gather(strata_ctx *ctx, int mode);
+/* available: 1 if every rank opened every peer's exchange buffer;
+ * capacity_floats: the largest batch x OUT the PEER path gathers. */
+int strata_cuda_comm_peer_info(const strata_ctx *ctx, int *available, int64_t *capacity_floats);
+
 /* Expert-parallel MoE layer: this rank's partial sum (its experts, plus the
  * shared expert on the rank whose layer has with_shared) all-reduced, so
  * out_dev holds the full layer output on every rank. */

@@ -26,6 +26,7 @@
 #include <mutex>
 #include <thread>
 #include <type_traits>
+#include <vector>
 
 #include "runtime.cuh"
 
@@ -79,18 +80,68 @@ const Nccl& nccl() {
     return n;
 }
 
+// Exchange buffer of the fused peer gather, one per rank, opened by every
+// other rank through CUDA IPC: control words, then two halves of
+// kPeerHalfFloats floats (consecutive calls alternate halves, so a rank that
+// is one call ahead never overwrites the half its peers are still reading).
+// Arrivals are counted per half: a peer that is one call ahead adds to the
+// other half's counter, never to the one this rank is waiting on (it cannot
+// be two calls ahead: its next wait needs this rank's arrivals).
+struct PeerCtl {
+    unsigned long long arrivals[2];  // CTAs (of every rank) whose outputs have landed in half h
+    unsigned long long expected[2];  // arrivals the calls on half h so far have waited for
+    unsigned int epoch;              // calls so far (its parity picks the half)
+    unsigned int done;               // CTAs of the running wait kernel that finished
+    int barrier;                     // all-reduce operand of the teardown barrier
+};
+constexpr int64_t kPeerCtlBytes = 256;
+constexpr int64_t kPeerHalfFloats = int64_t(8) << 20;  // 32 MiB per half
+
 struct CommState {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     int group_depth = 0;  // > 0 inside strata_cuda_comm_group_start / end
     DevBuf send, recv;    // gather staging of the GEMM (m > 1)
+    // fused peer gather
+    int gather_mode = STRATA_GATHER_AUTO;
+    bool peer_ok = false;                // every rank mapped every exchange buffer
+    char* xbuf = nullptr;                // this rank's exchange buffer
+    char* peer_base[kMaxPeers] = {};     // every rank's exchange buffer as mapped here
 };
+
+namespace {
+int nccl_done(strata_ctx* ctx, ncclComm_t comm, ncclResult_t r, const char* what);
+
+__host__ __device__ PeerCtl* ctl_of(char* base) { return reinterpret_cast<PeerCtl*>(base); }
+__host__ __device__ float* data_of(char* base) { return reinterpret_cast<float*>(base + kPeerCtlBytes); }
+
+// Unmaps the peers' exchange buffers and frees this rank's. With `barrier`,
+// first waits (bounded) until every rank has reached this point, so no rank
+// frees a buffer that another is still writing to.
+void peer_release(strata_ctx* ctx, bool barrier) {
+    CommState* c = ctx->comm;
+    if (!c->xbuf) return;
+    if (barrier && c->peer_ok) {
+        int* b = &ctl_of(c->xbuf)->barrier;
+        if (nccl_done(ctx, c->comm, nccl().AllReduce(b, b, 1, ncclInt32, ncclSum, c->comm, ctx->stream),
+                      "ncclAllReduce(barrier)") == STRATA_OK)
+            wait_stream(ctx, ctx->stream);
+    }
+    for (int q = 0; q < c->world && q < kMaxPeers; ++q)
+        if (q != c->rank && c->peer_base[q]) cudaIpcCloseMemHandle(c->peer_base[q]);
+    cudaFree(c->xbuf);
+    c->xbuf = nullptr;
+    c->peer_ok = false;
+    for (auto& p : c->peer_base) p = nullptr;
+}
+}  // namespace
 
 void comm_release(strata_ctx* ctx) {
     if (!ctx->comm) return;
     if (ctx->comm->comm) {
         ncclResult_t st = ncclSuccess;
         nccl().CommGetAsyncError(ctx->comm->comm, &st);
+        peer_release(ctx, st == ncclSuccess);
         if (st == ncclSuccess) nccl().CommDestroy(ctx->comm->comm);
         else nccl().CommAbort(ctx->comm->comm);
     }
@@ -177,6 +228,182 @@ int gather_rows_staged(strata_ctx* ctx, const float* local, float* y, int B, int
     return check_launch(ctx, "gather transpose kernel");
 }
 
+// What each rank publishes about its exchange buffer.
+struct PeerRecord {
+    cudaIpcMemHandle_t handle;
+    char bus_id[32];
+    int sm_count;
+    int ok;
+};
+
+// Allocates this rank's exchange buffer and maps every other rank's (CUDA
+// IPC handles exchanged with an NCCL all-gather). Collective: every rank runs
+// the same NCCL calls whatever fails locally, and an all-reduce (min) of the
+// ranks' outcomes decides, so all ranks agree on whether the peer gather is
+// available. Peer mapping needs distinct GPUs of the same model (the arrival
+// count of a call is computed locally from the launch shape).
+int peer_setup(strata_ctx* ctx) {
+    CommState* c = ctx->comm;
+    const int G = c->world;
+    PeerRecord mine{};
+    mine.sm_count = ctx->sm_count;
+    bool ok = G <= kMaxPeers;
+    if (ok) {
+        const size_t bytes = (size_t)kPeerCtlBytes + 2 * (size_t)kPeerHalfFloats * 4;
+        ok = cudaMalloc((void**)&c->xbuf, bytes) == cudaSuccess;
+        if (!ok) c->xbuf = nullptr;
+        ok = ok && cudaMemsetAsync(c->xbuf, 0, kPeerCtlBytes, ctx->stream) == cudaSuccess;
+        ok = ok && cudaIpcGetMemHandle(&mine.handle, c->xbuf) == cudaSuccess;
+        ok = ok && cudaDeviceGetPCIBusId(mine.bus_id, sizeof(mine.bus_id), ctx->device) == cudaSuccess;
+    }
+    cudaGetLastError();
+    mine.ok = ok;
+    // exchange the records (device staging for NCCL)
+    PeerRecord* rec_dev = nullptr;
+    std::vector<PeerRecord> recs(G);
+    if (cudaMalloc((void**)&rec_dev, sizeof(PeerRecord) * (G + 1)) != cudaSuccess)
+        return cuda_fail(ctx, cudaGetLastError(), "cudaMalloc(peer records)");
+    int* ok_dev = reinterpret_cast<int*>(rec_dev + G);
+    int rc = STRATA_OK;
+    if (cudaMemcpyAsync(rec_dev + c->rank, &mine, sizeof(mine), cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+        rc = cuda_fail(ctx, cudaGetLastError(), "cudaMemcpyAsync(peer record)");
+    if (!rc)
+        rc = nccl_done(ctx, c->comm,
+                       nccl().AllGather(rec_dev + c->rank, rec_dev, sizeof(PeerRecord), ncclUint8, c->comm,
+                                        ctx->stream),
+                       "ncclAllGather(peer records)");
+    if (!rc && cudaMemcpyAsync(recs.data(), rec_dev, sizeof(PeerRecord) * G, cudaMemcpyDeviceToHost, ctx->stream) !=
+                   cudaSuccess)
+        rc = cuda_fail(ctx, cudaGetLastError(), "cudaMemcpyAsync(peer records)");
+    if (!rc) rc = wait_stream(ctx, ctx->stream);
+    if (!rc) {
+        for (int q = 0; q < G && ok; ++q) {
+            ok = recs[q].ok && recs[q].sm_count == ctx->sm_count;
+            for (int p = 0; p < q && ok; ++p) ok = strncmp(recs[p].bus_id, recs[q].bus_id, sizeof(recs[q].bus_id)) != 0;
+        }
+        for (int q = 0; q < G && ok; ++q) {
+            if (q == c->rank) {
+                c->peer_base[q] = c->xbuf;
+                continue;
+            }
+            void* p = nullptr;
+            ok = cudaIpcOpenMemHandle(&p, recs[q].handle, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            c->peer_base[q] = ok ? static_cast<char*>(p) : nullptr;
+        }
+        cudaGetLastError();
+        const int flag = ok ? 1 : 0;
+        if (cudaMemcpyAsync(ok_dev, &flag, sizeof(int), cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+            rc = cuda_fail(ctx, cudaGetLastError(), "cudaMemcpyAsync(peer flag)");
+        if (!rc)
+            rc = nccl_done(ctx, c->comm, nccl().AllReduce(ok_dev, ok_dev, 1, ncclInt32, ncclMin, c->comm, ctx->stream),
+                           "ncclAllReduce(peer flag)");
+        int all = 0;
+        if (!rc && cudaMemcpyAsync(&all, ok_dev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
+            rc = cuda_fail(ctx, cudaGetLastError(), "cudaMemcpyAsync(peer flag)");
+        if (!rc) rc = wait_stream(ctx, ctx->stream);
+        c->peer_ok = !rc && all == 1;
+    }
+    cudaFree(rec_dev);
+    if (!c->peer_ok) peer_release(ctx, false);
+    return rc;
+}
+
+// Waits (thread 0 of each CTA, bounded) until the current half of this rank's
+// exchange buffer has received `arrivals` more CTA arrivals than the calls
+// before on that half, then copies its gathered [n] floats to y. The last CTA
+// to finish advances the half's expected count and the epoch (every CTA has
+// read both by then). After an expired wait the counts no longer match the
+// calls: the communicator has to be recreated before the next peer gather.
+__global__ void peer_gather_wait_kernel(char* __restrict__ base, unsigned long long arrivals, float* __restrict__ y,
+                                        int64_t n, uint64_t timeout_ns, int* err) {
+    PeerCtl* ctl = ctl_of(base);
+    __shared__ unsigned long long target_s;
+    __shared__ unsigned int epoch_s;
+    __shared__ int ok_s;
+    if (threadIdx.x == 0) {
+        const unsigned int e = *(volatile unsigned int*)&ctl->epoch;
+        const unsigned long long target = *(volatile unsigned long long*)&ctl->expected[e & 1u] + arrivals;
+        uint64_t t0, now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        bool ok = false;
+        for (long long i = 0; i < (1ll << 40); ++i) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(&ctl->arrivals[e & 1u]) : "memory");
+            if (v >= target) {
+                ok = true;
+                break;
+            }
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (now - t0 > timeout_ns) break;
+            __nanosleep(64);
+        }
+        if (!ok) atomicExch(err, 1);
+        target_s = target;
+        epoch_s = e;
+        ok_s = ok;
+    }
+    __syncthreads();
+    if (ok_s) {
+        const float* src = data_of(base) + (int64_t)(epoch_s & 1u) * kPeerHalfFloats;
+        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+        const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (((uintptr_t)y & 15) == 0) {
+            const int64_t n4 = n / 4;
+            for (int64_t i = i0; i < n4; i += stride)
+                reinterpret_cast<float4*>(y)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+            for (int64_t i = 4 * n4 + i0; i < n; i += stride) y[i] = __ldcg(src + i);
+        } else {
+            for (int64_t i = i0; i < n; i += stride) y[i] = __ldcg(src + i);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&ctl->done, 1u) == gridDim.x - 1) {
+            ctl->expected[epoch_s & 1u] = target_s;
+            ctl->epoch = epoch_s + 1;
+            ctl->done = 0;
+            __threadfence();
+        }
+    }
+}
+
+// Whether this sharded GEMV takes the fused peer gather.
+bool use_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, int batch) {
+    CommState* c = ctx->comm;
+    if (!c->peer_ok || c->gather_mode == STRATA_GATHER_NCCL) return false;
+    if ((int64_t)batch * w->rows * c->world > kPeerHalfFloats) return false;
+    return gemv_peer_capable(ctx, w, x, batch);
+}
+
+// Fused GEMV + all-gather: the GEMV's epilogue writes every rank's exchange
+// buffer, then this rank waits for the other ranks' CTAs and copies y out.
+int gemv_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int batch, cudaStream_t s) {
+    CommState* c = ctx->comm;
+    const int64_t ns = w->rows, N = ns * c->world;
+    PeerOut po{};
+    for (int q = 0; q < c->world; ++q) {
+        po.y[q] = data_of(c->peer_base[q]);
+        po.ctr[q] = ctl_of(c->peer_base[q])->arrivals;
+    }
+    po.epoch = &ctl_of(c->xbuf)->epoch;
+    po.half_floats = kPeerHalfFloats;
+    po.off = c->rank * ns;
+    po.G = c->world;
+    int64_t ctas = 0;
+    int rc = gemv_enqueue_strided(ctx, w, x, y + c->rank * ns, batch, N, s, &po, &ctas);
+    if (rc) return rc;
+    // every rank launched the same grid (same shard shape, same GPU model)
+    const int64_t n = (int64_t)batch * N;
+    int64_t blocks = (n / 4 + 255) / 256;
+    if (blocks > ctx->sm_count) blocks = ctx->sm_count;
+    if (blocks < 1) blocks = 1;
+    peer_gather_wait_kernel<<<(unsigned)blocks, 256, 0, s>>>(c->xbuf, (unsigned long long)(ctas * c->world), y, n,
+                                                             (uint64_t)ctx->wait_timeout_ms * 1000000ull,
+                                                             ctx->err_dev);
+    return check_launch(ctx, "peer gather wait kernel");
+}
+
 }  // namespace
 }  // namespace strata
 
@@ -215,6 +442,32 @@ int strata_cuda_comm_init(strata_ctx* ctx, int rank, int world, const uint8_t* i
         return rc;
     }
     ctx->comm = c;
+    // the fused peer gather; when peer memory is unavailable only that path is off
+    rc = peer_setup(ctx);
+    if (rc) {
+        comm_release(ctx);
+        return rc;
+    }
+    return STRATA_OK;
+}
+
+int strata_cuda_comm_set_gather(strata_ctx* ctx, int mode) {
+    if (!ctx) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    int rc = need_comm(ctx);
+    if (rc) return rc;
+    if (mode < STRATA_GATHER_AUTO || mode > STRATA_GATHER_PEER)
+        return fail(ctx, STRATA_ERR_INVALID, "gather mode %d", mode);
+    if (mode == STRATA_GATHER_PEER && !ctx->comm->peer_ok)
+        return fail(ctx, STRATA_ERR_INVALID, "peer memory is not available on every rank");
+    ctx->comm->gather_mode = mode;
+    return STRATA_OK;
+}
+
+int strata_cuda_comm_peer_info(const strata_ctx* ctx, int* available, int64_t* capacity_floats) {
+    if (!ctx || !available || !capacity_floats) return STRATA_ERR_INVALID;
+    *available = ctx->comm && ctx->comm->peer_ok;
+    *capacity_floats = *available ? kPeerHalfFloats : 0;
     return STRATA_OK;
 }
 
@@ -257,6 +510,10 @@ int strata_cuda_gemv_sharded_dev(strata_ctx* ctx, const strata_weight* w, const 
     cudaStream_t s = pick_stream(ctx, stream);
     CommState* c = ctx->comm;
     const int64_t ns = w->rows;
+    if (use_peer_gather(ctx, w, x_dev, batch)) return gemv_peer_gather(ctx, w, x_dev, y_dev, batch, s);
+    if (c->gather_mode == STRATA_GATHER_PEER)
+        return fail(ctx, STRATA_ERR_INVALID, "the peer gather does not apply to this shard (quant %u, batch %d)",
+                    w->quant, batch);
     // the local GEMV writes rank r's columns of every output row in place
     // (output row pitch N = world * ns)
     if ((rc = gemv_enqueue_strided(ctx, w, x_dev, y_dev + c->rank * ns, batch, ns * c->world, s))) return rc;

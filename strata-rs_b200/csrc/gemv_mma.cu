@@ -358,7 +358,7 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 3)
 gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
                    float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap,
-                   int64_t chunk_bytes, int64_t ldy) {
+                   int64_t chunk_bytes, int64_t ldy, const __grid_constant__ PeerOut po) {
     // token chunk blockIdx.y (batches above 8): its limbs and its NB output rows
     XF = reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(XF) + blockIdx.y * chunk_bytes);
     XS = reinterpret_cast<const float*>(reinterpret_cast<const char*>(XS) + blockIdx.y * chunk_bytes);
@@ -458,6 +458,9 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
 
     // the activation limbs come from the preceding kernel in the stream
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // fused all-gather: where this call's outputs go in every rank's exchange buffer
+    const unsigned half = po.G ? (*po.epoch & 1u) : 0u;
+    const int64_t peer_off = (int64_t)half * po.half_floats + po.off + (int64_t)blockIdx.y * NB * ldy;
 
     // After an expired wait a consumer skips its waits and math but keeps
     // walking the same stages, so every consumer still reaches every
@@ -517,15 +520,29 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                 for (int w = 0; w < kConsumers; ++w) v += red[set][w][nt][r][lane];
                 const int b = 4 * nt + t;
                 const int row = tile * kTileRows + 8 * r + g;
-                if (b < NB && row < N) Y[b * ldy + row] = v;
+                if (b < NB && row < N) {
+                    if (po.G) {
+                        for (int q = 0; q < po.G; ++q) po.y[q][peer_off + b * ldy + row] = v;
+                    } else {
+                        Y[b * ldy + row] = v;
+                    }
+                }
             }
         }
     }
+    if (po.G) {
+        // every store of this CTA (local and over NVLink) before its arrival on each rank
+        __threadfence_system();
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+        if (threadIdx.x == 0)
+            for (int q = 0; q < po.G; ++q) atomicAdd_system(po.ctr[q] + half, 1ull);
+    }
 }
 
+// Returns the CTAs launched (grid x chunks).
 template <uint32_t Q, int NB, bool TM>
-void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
-                unsigned chunks = 1, int64_t chunk_bytes = 0) {
+int64_t launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+                   unsigned chunks = 1, int64_t chunk_bytes = 0) {
     const int nblk = (int)(a.K / 256);
     const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
     const int smem = kStages * kTileRows * (kChunk * block_bytes(Q) + (TM ? 0 : 16)) + 1024;
@@ -551,26 +568,26 @@ void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __hal
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    PeerOut po{};
+    if (a.peers) po = *a.peers;
     cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err,
-                       map, chunk_bytes, ldy_of(a));
+                       map, chunk_bytes, ldy_of(a), po);
+    return grid * chunks;
 }
 
 template <uint32_t Q, bool TM>
-void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
-                  unsigned chunks = 1, int64_t chunk_bytes = 0) {
-    if (chunks > 1) {
-        launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
-        return;
-    }
+int64_t dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+                     unsigned chunks = 1, int64_t chunk_bytes = 0) {
+    if (chunks > 1) return launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
     switch (a.batch) {
-    case 1: launch_tma<Q, 1, TM>(a, xf, xs, xq, err, s); break;
-    case 2: launch_tma<Q, 2, TM>(a, xf, xs, xq, err, s); break;
-    case 3: launch_tma<Q, 3, TM>(a, xf, xs, xq, err, s); break;
-    case 4: launch_tma<Q, 4, TM>(a, xf, xs, xq, err, s); break;
-    case 5: launch_tma<Q, 5, TM>(a, xf, xs, xq, err, s); break;
-    case 6: launch_tma<Q, 6, TM>(a, xf, xs, xq, err, s); break;
-    case 7: launch_tma<Q, 7, TM>(a, xf, xs, xq, err, s); break;
-    default: launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s); break;
+    case 1: return launch_tma<Q, 1, TM>(a, xf, xs, xq, err, s);
+    case 2: return launch_tma<Q, 2, TM>(a, xf, xs, xq, err, s);
+    case 3: return launch_tma<Q, 3, TM>(a, xf, xs, xq, err, s);
+    case 4: return launch_tma<Q, 4, TM>(a, xf, xs, xq, err, s);
+    case 5: return launch_tma<Q, 5, TM>(a, xf, xs, xq, err, s);
+    case 6: return launch_tma<Q, 6, TM>(a, xf, xs, xq, err, s);
+    case 7: return launch_tma<Q, 7, TM>(a, xf, xs, xq, err, s);
+    default: return launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s);
     }
 }
 
@@ -625,7 +642,9 @@ bool gemv_mma_supported(uint32_t quant, const GemvArgs& a) {
 }
 
 // x limbs into `work` (gemv_mma_work_bytes), then the tensor-core GEMV.
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s) {
+// `ctas` (optional) receives the CTAs launched: with a.peers, the arrivals
+// this call adds to every rank's counter.
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s, int64_t* ctas) {
     const int nblk = (int)(a.K / 256);
     const int full = a.batch > 8 ? a.batch / 8 : 0;  // 8-token chunks on grid.y
     const int nb = full ? 8 : a.batch;
@@ -643,16 +662,27 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     GemvArgs c = a;
     c.batch = nb;
     const bool tm = a.tmap != nullptr;
-    if (quant == kQ4_K) tm ? dispatch_mma<kQ4_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
-                           : dispatch_mma<kQ4_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
-    else tm ? dispatch_mma<kQ5_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
-            : dispatch_mma<kQ5_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
+    int64_t n = 0;
+    if (quant == kQ4_K) n = tm ? dispatch_mma<kQ4_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
+                               : dispatch_mma<kQ4_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
+    else n = tm ? dispatch_mma<kQ5_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
+                : dispatch_mma<kQ5_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
+    if (ctas) *ctas = n;
     if (full && a.batch % 8) {  // the remaining tokens, after the chunks' workspace
         GemvArgs r = a;
         r.X = a.X + (int64_t)full * 8 * a.K;
         r.Y = a.Y + (int64_t)full * 8 * ldy_of(a);
         r.batch = a.batch % 8;
-        return launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s);
+        PeerOut pr{};
+        if (a.peers) {
+            pr = *a.peers;
+            pr.off += (int64_t)full * 8 * ldy_of(a);
+            r.peers = &pr;
+        }
+        int64_t m = 0;
+        const int rc = launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s, &m);
+        if (ctas) *ctas += m;
+        return rc;
     }
     return 0;
 }

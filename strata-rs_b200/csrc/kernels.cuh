@@ -5,6 +5,21 @@
 
 namespace strata {
 
+// Fused all-gather of a row-sharded GEMV over peer memory: every output
+// value is stored into each rank's exchange buffer instead of Y (half
+// `epoch & 1`, layout [batch][ldy], this call's first value at float `off` of
+// the half), and every CTA then adds 1 to each rank's arrival counter of that
+// half (system scope, after a system fence).
+constexpr int kMaxPeers = 8;
+struct PeerOut {
+    float* y[kMaxPeers];                  // each rank's exchange buffer
+    unsigned long long* ctr[kMaxPeers];   // each rank's arrival counters, one per half
+    const unsigned int* epoch;            // this rank's call counter (its parity picks the half)
+    int64_t half_floats;                  // floats per half of an exchange buffer
+    int64_t off;                          // float offset in a half of this launch's y[0][0]
+    int G;                                // 0: no peers (plain GEMV)
+};
+
 // Dense GEMV arguments: W is N rows of `row_bytes` (rows = OUT, quantized
 // along K = IN); X is batch x K f32, Y is batch x N f32, both row-major.
 struct GemvArgs {
@@ -17,6 +32,7 @@ struct GemvArgs {
     int sm_count;
     const void* tmap = nullptr;  // CUtensorMap of W for the tensor-core GEMV, or null
     int64_t ldy = 0;             // output row pitch in floats (0: N)
+    const PeerOut* peers = nullptr;  // fused all-gather (tensor-core GEMV only), or null
 };
 inline int64_t ldy_of(const GemvArgs& a) { return a.ldy > 0 ? a.ldy : a.N; }
 
@@ -29,7 +45,8 @@ int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s);
 // any batch (8-token chunks beyond 8); `work` holds gemv_mma_work_bytes.
 int64_t gemv_mma_work_bytes(int64_t K, int batch);
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s,
+                    int64_t* ctas = nullptr);
 
 // Expert GEMV on the transposed expert layout [E][IN rows][OUT cols]
 // (rows quantized along OUT): Y[b][c] = sum_i X[b][i] * W_e[i][c].

@@ -83,7 +83,7 @@ int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what)
 int check_device_error(strata_ctx* ctx) {
     if (ctx->err_host && *(volatile int*)ctx->err_host) {
         *(volatile int*)ctx->err_host = 0;
-        return fail(ctx, STRATA_ERR_TIMEOUT, "a kernel's bounded wait on shared-memory copies expired");
+        return fail(ctx, STRATA_ERR_TIMEOUT, "a kernel's bounded wait expired (shared-memory copies, or the other ranks' arrivals)");
     }
     return STRATA_OK;
 }
@@ -326,21 +326,32 @@ int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, fl
     return gemv_enqueue_strided(ctx, w, x_dev, y_dev, batch, 0, s);
 }
 
-// y row b at y_dev + b * ldy (ldy 0: rows are w->rows floats apart)
+// Whether the GEMV of w at this batch runs on the tensor-core path (the
+// only one with the fused peer-store epilogue).
+bool gemv_peer_capable(strata_ctx* ctx, const strata_weight* w, const float* x_dev, int batch) {
+    GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, nullptr, batch, ctx->sm_count,
+               w->has_tmap ? w->tmap : nullptr};
+    return ctx->gemv_path != STRATA_GEMV_CUDA_CORES && gemv_mma_supported(w->quant, a);
+}
+
+// y row b at y_dev + b * ldy (ldy 0: rows are w->rows floats apart). With
+// `peers` the outputs go to the ranks' exchange buffers instead (tensor-core
+// path only) and *ctas receives the CTAs launched.
 int gemv_enqueue_strided(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
-                         int64_t ldy, cudaStream_t s) {
+                         int64_t ldy, cudaStream_t s, const PeerOut* peers, int64_t* ctas) {
     if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
         return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
     GemvArgs a{w->dev, w->row_bytes, w->rows, w->cols, x_dev, y_dev, batch, ctx->sm_count,
-               w->has_tmap ? w->tmap : nullptr, ldy};
+               w->has_tmap ? w->tmap : nullptr, ldy, peers};
     if (ctx->gemv_path != STRATA_GEMV_CUDA_CORES && gemv_mma_supported(w->quant, a)) {
         int64_t need = gemv_mma_work_bytes(w->cols, batch);
         int rc = ensure_device(ctx, ctx->xfrag, (size_t)(need > (4 << 20) ? need : (4 << 20)), "cudaMalloc(x limbs)");
         if (rc) return rc;
-        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, s);
+        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, s, ctas);
         return check_launch(ctx, "tensor-core gemv kernel");
     }
+    if (peers) return fail(ctx, STRATA_ERR_INVALID, "the peer-store epilogue needs the tensor-core gemv");
     if (ctx->gemv_path == STRATA_GEMV_TENSOR_CORES)
         return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no tensor-core gemv for quant %u", w->quant);
     if (launch_gemv(w->quant, a, s))

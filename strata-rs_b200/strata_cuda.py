@@ -91,6 +91,8 @@ def lib() -> C.CDLL:
             "strata_cuda_comm_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
             "strata_cuda_comm_group_start": (i32, [vp]),
             "strata_cuda_comm_group_end": (i32, [vp]),
+            "strata_cuda_comm_set_gather": (i32, [vp, i32]),
+            "strata_cuda_comm_peer_info": (i32, [vp, C.POINTER(i32), C.POINTER(i64)]),
             "strata_cuda_gemv_sharded_dev": (i32, [vp, vp, vp, vp, i32, vp]),
             "strata_cuda_gemm_sharded_dev": (i32, [vp, vp, vp, vp, i64, vp]),
             "strata_cuda_moe_ffn_ep_dev": (i32, [vp, vp, vp, vp, i64, vp, vp]),
@@ -320,6 +322,19 @@ class Context:
 
     def comm_group_end(self):
         self.check(lib().strata_cuda_comm_group_end(self.h))
+
+    GATHER_AUTO, GATHER_NCCL, GATHER_PEER = 0, 1, 2
+
+    def comm_set_gather(self, mode: int):
+        """How sharded GEMVs gather rows: GATHER_AUTO, GATHER_NCCL or GATHER_PEER
+        (the all-gather fused into the GEMV's epilogue over peer memory)."""
+        self.check(lib().strata_cuda_comm_set_gather(self.h, mode))
+
+    def comm_peer_info(self) -> tuple[bool, int]:
+        """(peer gather available on every rank, its capacity in floats)."""
+        a, cap = C.c_int32(), C.c_int64()
+        self.check(lib().strata_cuda_comm_peer_info(self.h, C.byref(a), C.byref(cap)))
+        return bool(a.value), cap.value
 
     def gemv_sharded_dev(self, w: Weight, x_ptr: int, y_ptr: int, batch: int, stream: int = 0):
         self.check(lib().strata_cuda_gemv_sharded_dev(self.h, w.handle, x_ptr, y_ptr, batch, stream or None))

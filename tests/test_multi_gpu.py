@@ -40,24 +40,85 @@ def _worker(rank, world, uid, q):
         ctx = sc.Context(rank)
         ctx.set_wait_timeout_ms(60000)
         ctx.comm_init(rank, world, uid)
+        ctx.set_wait_timeout_ms(10000)  # bounds each peer-gather wait below
         assert ctx.comm_info() == (rank, world)
         st = torch.cuda.Stream()
         dev = f"cuda:{rank}"
 
-        # row-sharded GEMV (batch 1 and 3): bitwise the single-GPU GEMV
+        # row-sharded GEMV: bitwise the single-GPU GEMV, through both gathers
+        # (NCCL all-gathers; the all-gather fused into the GEMV over peer
+        # memory), several calls in a row so both exchange halves are used
+        avail, cap = ctx.comm_peer_info()
+        assert avail and cap >= 8 * 4096, (avail, cap)
         N, K = 4096, 2048
         data = quant_matrix(2000, Q4_K, N, K)
         full = ctx.upload(data, Q4_K, N, K)
         shard = ctx.upload(sharding.row_shard(data, Q4_K, N, K, world, rank), Q4_K, N // world, K)
-        for B in (1, 3):
-            x = torch.from_numpy(activations(2001 + B, B, K)).to(dev)
-            y = torch.empty((B, N), dtype=torch.float32, device=dev)
+        for mode in (ctx.GATHER_NCCL, ctx.GATHER_PEER, ctx.GATHER_AUTO):
+            ctx.comm_set_gather(mode)
+            for B in (1, 3, 8, 2, 5):
+                x = torch.from_numpy(activations(2001 + B, B, K)).to(dev)
+                y = torch.empty((B, N), dtype=torch.float32, device=dev)
+                st.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(st):
+                    ctx.gemv_sharded_dev(shard, x.data_ptr(), y.data_ptr(), B, st.cuda_stream)
+                st.synchronize()
+                want = ctx.gemv(full, x.cpu().numpy())
+                assert np.array_equal(y.cpu().numpy().reshape(B, N).view(np.uint32),
+                                      want.reshape(B, N).view(np.uint32)), ("gemv", mode, B)
+
+        # the fused gather captured in a CUDA graph and replayed with new inputs
+        # (its exchange half and arrival count live on the device)
+        ctx.comm_set_gather(ctx.GATHER_PEER)
+        xg = torch.zeros((2, K), dtype=torch.float32, device=dev)
+        yg2 = torch.empty((2, N), dtype=torch.float32, device=dev)
+        st.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            ctx.gemv_sharded_dev(shard, xg.data_ptr(), yg2.data_ptr(), 2, st.cuda_stream)
+            ctx.gemv_sharded_dev(shard, xg.data_ptr(), yg2.data_ptr(), 2, st.cuda_stream)
+        for rep in range(3):
+            xa = activations(2050 + rep, 2, K)
+            xg.copy_(torch.from_numpy(xa))
+            st.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(st):
-                ctx.gemv_sharded_dev(shard, x.data_ptr(), y.data_ptr(), B, st.cuda_stream)
+                graph.replay()
             st.synchronize()
-            want = ctx.gemv(full, x.cpu().numpy())
-            assert np.array_equal(y.cpu().numpy().reshape(B, N).view(np.uint32),
-                                  want.reshape(B, N).view(np.uint32)), ("gemv", B)
+            want = ctx.gemv(full, xa)
+            assert np.array_equal(yg2.cpu().numpy().view(np.uint32), want.reshape(2, N).view(np.uint32)), ("graph", rep)
+        del graph
+        ctx.comm_set_gather(ctx.GATHER_AUTO)
+
+        # several sharded GEMVs in one collective group (one NCCL launch at group_end)
+        x1 = torch.from_numpy(activations(2005, 1, K)).to(dev)
+        x4 = torch.from_numpy(activations(2006, 4, K)).to(dev)
+        y1 = torch.empty((1, N), dtype=torch.float32, device=dev)
+        y4 = torch.empty((4, N), dtype=torch.float32, device=dev)
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            ctx.comm_group_start()
+            ctx.gemv_sharded_dev(shard, x1.data_ptr(), y1.data_ptr(), 1, st.cuda_stream)
+            ctx.gemv_sharded_dev(shard, x4.data_ptr(), y4.data_ptr(), 4, st.cuda_stream)
+            ctx.comm_group_end()
+        st.synchronize()
+        for xx, yy in ((x1, y1), (x4, y4)):
+            want = ctx.gemv(full, xx.cpu().numpy())
+            assert np.array_equal(yy.cpu().numpy().view(np.uint32), want.reshape(yy.shape).view(np.uint32)), "group"
+        # the same under the NCCL gather: one NCCL group for both calls
+        ctx.comm_set_gather(ctx.GATHER_NCCL)
+        y1.zero_()
+        y4.zero_()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            ctx.comm_group_start()
+            ctx.gemv_sharded_dev(shard, x1.data_ptr(), y1.data_ptr(), 1, st.cuda_stream)
+            ctx.gemv_sharded_dev(shard, x4.data_ptr(), y4.data_ptr(), 4, st.cuda_stream)
+            ctx.comm_group_end()
+        st.synchronize()
+        for xx, yy in ((x1, y1), (x4, y4)):
+            want = ctx.gemv(full, xx.cpu().numpy())
+            assert np.array_equal(yy.cpu().numpy().view(np.uint32), want.reshape(yy.shape).view(np.uint32)), "nccl group"
+        ctx.comm_set_gather(ctx.GATHER_AUTO)
 
         # row-sharded GEMM (m = 70): the single-GPU GEMM within fp32 reassociation
         Kg, Ng, M = 2048, 1024, 70
@@ -67,6 +128,7 @@ def _worker(rank, world, uid, q):
         bits = bf16_bits(activations(2011, M, Kg))
         xb = torch.from_numpy(bits.view(np.int16)).to(dev)
         yg = torch.empty((M, Ng), dtype=torch.float32, device=dev)
+        st.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(st):
             ctx.gemm_sharded_dev(sgw, xb.data_ptr(), yg.data_ptr(), M, st.cuda_stream)
         st.synchronize()
@@ -100,6 +162,7 @@ def _worker(rank, world, uid, q):
         want_m, _, _ = ctx.moe_ffn(lf, x, lg)
         xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
         od = torch.empty((T, n_embd), dtype=torch.float32, device=dev)
+        st.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(st):
             ctx.moe_ffn_ep_dev(lr, xd.data_ptr(), ld.data_ptr(), T, od.data_ptr(), st.cuda_stream)
         st.synchronize()
@@ -112,11 +175,58 @@ def _worker(rank, world, uid, q):
         q.put((rank, traceback.format_exc()))
 
 
-def _run_world(world):
+def _peer_timeout_worker(rank, world, uid, q, bar):
+    """Rank 1 skips a sharded GEMV: rank 0's wait for its arrivals expires
+    (bounded), the call reports STRATA_ERR_TIMEOUT and the context stays
+    usable; the ranks then meet on the host and close normally."""
+    try:
+        sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "strata-rs_b200"),
+                        os.path.join(os.path.dirname(HERE), "oracle")]
+        import torch
+        import strata_cuda as sc
+        import sharding
+        from synth import Q4_K, activations, quant_matrix
+        torch.cuda.set_device(rank)
+        ctx = sc.Context(rank)
+        ctx.set_wait_timeout_ms(60000)
+        ctx.comm_init(rank, world, uid)
+        ctx.comm_set_gather(ctx.GATHER_PEER)
+        N, K = 1024, 512
+        data = quant_matrix(2060, Q4_K, N, K)
+        shard = ctx.upload(sharding.row_shard(data, Q4_K, N, K, world, rank), Q4_K, N // world, K)
+        if rank == 0:
+            ctx.set_wait_timeout_ms(1000)
+            st = torch.cuda.Stream()
+            x = torch.from_numpy(activations(2061, 1, K)).to(f"cuda:{rank}")
+            y = torch.empty((1, N), dtype=torch.float32, device=f"cuda:{rank}")
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                ctx.gemv_sharded_dev(shard, x.data_ptr(), y.data_ptr(), 1, st.cuda_stream)
+            st.synchronize()
+            try:
+                ctx.synchronize()
+                raise AssertionError("no timeout reported")
+            except sc.BackendError as e:
+                assert e.code == sc.ERR_TIMEOUT, e
+            w = ctx.upload(data, Q4_K, N, K)
+            assert np.isfinite(ctx.gemv(w, activations(2062, 1, K))).all()
+            ctx.set_wait_timeout_ms(60000)
+        bar.wait(timeout=300)
+        ctx.close()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def _run_world(world, target=None):
     uid = sc.comm_unique_id()
     ctxm = mp.get_context("spawn")
     q = ctxm.Queue()
-    procs = [ctxm.Process(target=_worker, args=(r, world, uid, q)) for r in range(world)]
+    if target is None:
+        procs = [ctxm.Process(target=_worker, args=(r, world, uid, q)) for r in range(world)]
+    else:
+        bar = ctxm.Barrier(world)
+        procs = [ctxm.Process(target=target, args=(r, world, uid, q, bar)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -133,6 +243,12 @@ def _run_world(world):
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
 def test_sharded_paths_world2():
     res = _run_world(2)
+    assert all(m == "ok" for m in res.values()), res
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_peer_gather_times_out_when_a_rank_skips_the_call():
+    res = _run_world(2, _peer_timeout_worker)
     assert all(m == "ok" for m in res.values()), res
 
 
