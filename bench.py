@@ -486,31 +486,40 @@ def run_gpu(args):
         if world > 1:
             ctx.comm_group_end()
 
-    graphs = []
-    with torch.cuda.stream(stream):
-        enqueue(0, stream.cuda_stream)  # warm the kernels before capture
-    stream.synchronize()
-    try:  # N > 1: the library's NCCL group is captured with the kernels
-        for i in range(rot):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                enqueue(i, stream.cuda_stream)
-            graphs.append(g)
-        g = None  # the list holds the graphs (released before the communicator)
-        captured = 1
-    except Exception as exc:  # noqa: BLE001 - fall back to direct launches on every rank
-        print(f"graph capture unavailable ({exc}); launching directly", file=sys.stderr)
+    def capture():
         graphs = []
-        captured = 0
-    if dist:
-        ok = torch.tensor([captured], device="cuda")
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-        if int(ok.item()) == 0:
+        with torch.cuda.stream(stream):
+            enqueue(0, stream.cuda_stream)  # warm the kernels before capture
+        stream.synchronize()
+        try:  # N > 1: the library's gathers (peer kernels or NCCL group) are captured with the GEMVs
+            for i in range(rot):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    enqueue(i, stream.cuda_stream)
+                graphs.append(g)
+            g = None  # the list holds the graphs (released before the communicator)
+            captured = 1
+        except Exception as exc:  # noqa: BLE001 - fall back to direct launches on every rank
+            print(f"graph capture unavailable ({exc}); launching directly", file=sys.stderr)
             graphs = []
-    torch.cuda.synchronize()
-    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel
-    # (sharded: plus the NCCL group's kernel, not counted)
-    launches_per_step = 2 * len(batches) * len(shapes)
+            captured = 0
+        if dist:
+            ok = torch.tensor([captured], device="cuda")
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if int(ok.item()) == 0:
+                graphs = []
+        torch.cuda.synchronize()
+        return graphs
+
+    peer = False
+    if world > 1:
+        peer = ctx.comm_peer_info()[0]
+        ctx.comm_set_gather(ctx.GATHER_AUTO)  # peer gather fused into the GEMV where available
+    graphs = capture()
+    # every GEMV is two launches: the activation-limb prologue and the GEMV kernel;
+    # with the fused peer gather a third, the wait-and-copy kernel (the NCCL
+    # group's kernel of the NCCL gather is not counted)
+    launches_per_step = (3 if peer else 2) * len(batches) * len(shapes)
 
     def step(i):
         if graphs:
@@ -555,6 +564,40 @@ def run_gpu(args):
     total = sweep_bytes(shapes, batches)
     value = total * args.steps / (ms / 1e3) / 1e9
     hbm, peak_kind = peaks()
+
+    # N > 1: the same step with the NCCL all-gathers instead of the fused peer gather
+    alt = None
+    if world > 1 and peer:
+        ctx.comm_set_gather(ctx.GATHER_NCCL)
+        ngraphs = capture()
+
+        def nstep(i):
+            if ngraphs:
+                ngraphs[i % rot].replay()
+            else:
+                enqueue(i, stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                nstep(i)
+        stream.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for i in range(args.steps):
+                nstep(i)
+            a1.record(stream)
+        a1.synchronize()
+        t = torch.tensor([a0.elapsed_time(a1)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nms = float(t.item())
+        alt = {"gather": "NCCL in-place all-gathers, the step's 16 in one NCCL group",
+               "ms_per_step": round(nms / args.steps, 4), "value": round(total * args.steps / (nms / 1e3) / 1e9, 1),
+               "unit": UNIT}
+        del ngraphs
+        torch.cuda.synchronize()
+        ctx.comm_set_gather(ctx.GATHER_AUTO)
 
     # per-case device time: each case as its own graph over its rotated copies
     cases = []
@@ -670,9 +713,12 @@ def run_gpu(args):
                                    "2048->151936 at batch 1,2,4,8 (16 GEMVs per step, batch-major)",
                        "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 "
                              "per matrix), no matrix re-read within 241 MB of traffic",
-                       "parallelism": (f"row-sharded x{world}: local GEMV into its columns of y + in-place "
-                                       f"NCCL all-gathers inside strata_cuda_gemv_sharded_dev, the step's "
-                                       f"16 in one NCCL group" if world > 1 else "single GPU"),
+                       "parallelism": ((f"row-sharded x{world}: all-gather fused into the GEMV (epilogue "
+                                        f"stores into every rank's exchange buffer over NVLink + a wait-and-"
+                                        f"copy kernel) inside strata_cuda_gemv_sharded_dev" if peer else
+                                        f"row-sharded x{world}: local GEMV into its columns of y + in-place "
+                                        f"NCCL all-gathers inside strata_cuda_gemv_sharded_dev, the step's "
+                                        f"16 in one NCCL group") if world > 1 else "single GPU"),
                        "launch": "CUDA graph per step" if graphs else "direct launches"},
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(value / hbm, 3), "traffic": profiled_traffic(),
@@ -683,6 +729,7 @@ def run_gpu(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
             "cases": cases,
+            "nccl_gather": alt,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "gemm": gemm,

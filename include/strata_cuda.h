@@ -246,7 +246,9 @@ int strata_cuda_gemm_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, 
  * comm_init) and bumps each rank's arrival counter; a small kernel on each
  * rank waits (bounded by the context's wait timeout, then
  * STRATA_ERR_TIMEOUT) for all arrivals and copies the gathered rows to y.
- * No NCCL call is made, so these calls ignore collective groups and are
+ * Inside a collective group that kernel is enqueued once, at group_end, for
+ * all the group's calls on one stream (so y is complete after group_end's
+ * work, as with NCCL). No NCCL call is made and the calls are
  * graph-capturable. NCCL uses the per-row in-place all-gathers. AUTO (the
  * default) takes PEER where it applies -- peer memory available on every
  * rank, a Q4_K / Q5_K shard on the tensor-core path, batch x OUT within the

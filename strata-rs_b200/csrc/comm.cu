@@ -97,6 +97,28 @@ struct PeerCtl {
 constexpr int64_t kPeerCtlBytes = 256;
 constexpr int64_t kPeerHalfFloats = int64_t(8) << 20;  // 32 MiB per half
 
+constexpr int kPeerSegs = 32;
+// What one wait-and-copy kernel reads out of the ranks' exchange halves: the
+// gathers of up to kPeerSegs sharded GEMVs (one call, or the calls of a
+// collective group). Segment s is y[s] = [rows][G ns] whose columns
+// [q ns, (q + 1) ns) rank q wrote into its own buffer at the same offset.
+struct PeerSegs {
+    float* y[kPeerSegs];
+    int64_t off[kPeerSegs];  // first float in the half (a multiple of 4)
+    int64_t n[kPeerSegs];    // floats: rows x G ns
+    int64_t ns[kPeerSegs];   // columns per rank
+    char* base[kMaxPeers];   // every rank's exchange buffer as mapped here
+    int G;
+    int count;
+};
+// Peer gathers issued since the last wait-and-copy kernel.
+struct PeerPending {
+    PeerSegs segs{};
+    int64_t floats = 0;  // of the half in use
+    int64_t ctas = 0;    // this rank's GEMV CTAs (each rank launches the same)
+    cudaStream_t stream = nullptr;
+};
+
 struct CommState {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
@@ -107,6 +129,7 @@ struct CommState {
     bool peer_ok = false;                // every rank mapped every exchange buffer
     char* xbuf = nullptr;                // this rank's exchange buffer
     char* peer_base[kMaxPeers] = {};     // every rank's exchange buffer as mapped here
+    PeerPending pending;                 // inside a collective group
 };
 
 namespace {
@@ -310,12 +333,14 @@ int peer_setup(strata_ctx* ctx) {
 
 // Waits (thread 0 of each CTA, bounded) until the current half of this rank's
 // exchange buffer has received `arrivals` more CTA arrivals than the calls
-// before on that half, then copies its gathered [n] floats to y. The last CTA
-// to finish advances the half's expected count and the epoch (every CTA has
-// read both by then). After an expired wait the counts no longer match the
-// calls: the communicator has to be recreated before the next peer gather.
-__global__ void peer_gather_wait_kernel(char* __restrict__ base, unsigned long long arrivals, float* __restrict__ y,
-                                        int64_t n, uint64_t timeout_ns, int* err) {
+// before on that half, then reads every segment's columns from the rank that
+// wrote them (this GPU's memory or a peer's, over NVLink) into its y.
+// The last CTA to finish advances the half's expected count and the epoch
+// (every CTA has read both by then). After an expired wait the counts no
+// longer match the calls: the communicator has to be recreated before the
+// next peer gather.
+__global__ void peer_gather_wait_kernel(char* __restrict__ base, unsigned long long arrivals,
+                                        const __grid_constant__ PeerSegs segs, uint64_t timeout_ns, int* err) {
     PeerCtl* ctl = ctl_of(base);
     __shared__ unsigned long long target_s;
     __shared__ unsigned int epoch_s;
@@ -344,16 +369,25 @@ __global__ void peer_gather_wait_kernel(char* __restrict__ base, unsigned long l
     }
     __syncthreads();
     if (ok_s) {
-        const float* src = data_of(base) + (int64_t)(epoch_s & 1u) * kPeerHalfFloats;
+        const int64_t half = kPeerCtlBytes / 4 + (int64_t)(epoch_s & 1u) * kPeerHalfFloats;
         const int64_t stride = (int64_t)gridDim.x * blockDim.x;
         const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-        if (((uintptr_t)y & 15) == 0) {
-            const int64_t n4 = n / 4;
-            for (int64_t i = i0; i < n4; i += stride)
-                reinterpret_cast<float4*>(y)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
-            for (int64_t i = 4 * n4 + i0; i < n; i += stride) y[i] = __ldcg(src + i);
-        } else {
-            for (int64_t i = i0; i < n; i += stride) y[i] = __ldcg(src + i);
+        for (int sg = 0; sg < segs.count; ++sg) {
+            float* y = segs.y[sg];
+            const int64_t n = segs.n[sg], ns = segs.ns[sg], N = ns * segs.G, src0 = half + segs.off[sg];
+            if (((uintptr_t)y & 15) == 0 && ns % 4 == 0) {
+                // four consecutive floats share their owner: 16-byte reads and writes
+                for (int64_t i = i0; i < n / 4; i += stride) {
+                    const int64_t e = 4 * i;
+                    const float* src = reinterpret_cast<const float*>(segs.base[(e % N) / ns]) + src0 + e;
+                    reinterpret_cast<float4*>(y)[i] = __ldcg(reinterpret_cast<const float4*>(src));
+                }
+            } else {
+                for (int64_t e = i0; e < n; e += stride) {
+                    const float* src = reinterpret_cast<const float*>(segs.base[(e % N) / ns]) + src0 + e;
+                    y[e] = __ldcg(src);
+                }
+            }
         }
     }
     __syncthreads();
@@ -376,32 +410,58 @@ bool use_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, in
     return gemv_peer_capable(ctx, w, x, batch);
 }
 
-// Fused GEMV + all-gather: the GEMV's epilogue writes every rank's exchange
-// buffer, then this rank waits for the other ranks' CTAs and copies y out.
-int gemv_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int batch, cudaStream_t s) {
+// Enqueues the wait-and-copy kernel for the pending peer gathers (no-op when
+// none are pending). Every rank flushes at the same points of the same call
+// sequence, so the ranks' halves and arrival counts stay in step.
+int peer_flush(strata_ctx* ctx) {
     CommState* c = ctx->comm;
-    const int64_t ns = w->rows, N = ns * c->world;
-    PeerOut po{};
-    for (int q = 0; q < c->world; ++q) {
-        po.y[q] = data_of(c->peer_base[q]);
-        po.ctr[q] = ctl_of(c->peer_base[q])->arrivals;
-    }
-    po.epoch = &ctl_of(c->xbuf)->epoch;
-    po.half_floats = kPeerHalfFloats;
-    po.off = c->rank * ns;
-    po.G = c->world;
-    int64_t ctas = 0;
-    int rc = gemv_enqueue_strided(ctx, w, x, y + c->rank * ns, batch, N, s, &po, &ctas);
-    if (rc) return rc;
-    // every rank launched the same grid (same shard shape, same GPU model)
-    const int64_t n = (int64_t)batch * N;
+    PeerPending& p = c->pending;
+    if (p.segs.count == 0) return STRATA_OK;
+    int64_t n = 0;
+    for (int i = 0; i < p.segs.count; ++i) n += p.segs.n[i];
     int64_t blocks = (n / 4 + 255) / 256;
     if (blocks > ctx->sm_count) blocks = ctx->sm_count;
     if (blocks < 1) blocks = 1;
-    peer_gather_wait_kernel<<<(unsigned)blocks, 256, 0, s>>>(c->xbuf, (unsigned long long)(ctas * c->world), y, n,
-                                                             (uint64_t)ctx->wait_timeout_ms * 1000000ull,
-                                                             ctx->err_dev);
+    p.segs.G = c->world;
+    for (int q = 0; q < c->world; ++q) p.segs.base[q] = c->peer_base[q];
+    // every rank launched the same grids (same shard shapes, same GPU model)
+    peer_gather_wait_kernel<<<(unsigned)blocks, 256, 0, p.stream>>>(
+        c->xbuf, (unsigned long long)(p.ctas * c->world), p.segs, (uint64_t)ctx->wait_timeout_ms * 1000000ull,
+        ctx->err_dev);
+    p = PeerPending{};
     return check_launch(ctx, "peer gather wait kernel");
+}
+
+// Fused GEMV + all-gather: the GEMV's epilogue writes every rank's exchange
+// buffer at this call's place in the current half; the wait-and-copy kernel
+// follows at once, or at the end of the collective group (one for all the
+// group's calls on a stream).
+int gemv_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int batch, cudaStream_t s) {
+    CommState* c = ctx->comm;
+    PeerPending& p = c->pending;
+    const int64_t ns = w->rows, N = ns * c->world;
+    const int64_t n = (int64_t)batch * N;
+    int rc;
+    if (p.segs.count > 0 && (p.stream != s || p.segs.count == kPeerSegs || p.floats + n > kPeerHalfFloats))
+        if ((rc = peer_flush(ctx))) return rc;
+    PeerOut po{};
+    po.y = data_of(c->xbuf);
+    for (int q = 0; q < c->world; ++q) po.ctr[q] = ctl_of(c->peer_base[q])->arrivals;
+    po.epoch = &ctl_of(c->xbuf)->epoch;
+    po.half_floats = kPeerHalfFloats;
+    po.off = p.floats + c->rank * ns;
+    po.G = c->world;
+    int64_t ctas = 0;
+    if ((rc = gemv_enqueue_strided(ctx, w, x, y + c->rank * ns, batch, N, s, &po, &ctas))) return rc;
+    p.stream = s;
+    p.segs.y[p.segs.count] = y;
+    p.segs.off[p.segs.count] = p.floats;
+    p.segs.n[p.segs.count] = n;
+    p.segs.ns[p.segs.count] = ns;
+    ++p.segs.count;
+    p.floats += (n + 3) & ~int64_t(3);
+    p.ctas += ctas;
+    return c->group_depth > 0 ? STRATA_OK : peer_flush(ctx);
 }
 
 }  // namespace
@@ -458,6 +518,7 @@ int strata_cuda_comm_set_gather(strata_ctx* ctx, int mode) {
     if (rc) return rc;
     if (mode < STRATA_GATHER_AUTO || mode > STRATA_GATHER_PEER)
         return fail(ctx, STRATA_ERR_INVALID, "gather mode %d", mode);
+    if (ctx->comm->group_depth > 0) return fail(ctx, STRATA_ERR_INVALID, "the gather mode cannot change inside a group");
     if (mode == STRATA_GATHER_PEER && !ctx->comm->peer_ok)
         return fail(ctx, STRATA_ERR_INVALID, "peer memory is not available on every rank");
     ctx->comm->gather_mode = mode;
@@ -494,7 +555,11 @@ int strata_cuda_comm_group_end(strata_ctx* ctx) {
     int rc = need_comm(ctx);
     if (rc) return rc;
     if (ctx->comm->group_depth == 0) return fail(ctx, STRATA_ERR_INVALID, "no collective group is open");
-    if (--ctx->comm->group_depth == 0) return nccl_done(ctx, ctx->comm->comm, nccl().GroupEnd(), "ncclGroupEnd");
+    if (--ctx->comm->group_depth == 0) {
+        rc = peer_flush(ctx);
+        const int rn = nccl_done(ctx, ctx->comm->comm, nccl().GroupEnd(), "ncclGroupEnd");
+        return rc ? rc : rn;
+    }
     return STRATA_OK;
 }
 

@@ -25,8 +25,9 @@
 //   tolerance needs.
 //
 // Work split: row tiles of 16 rows; a producer warp streams each tile into
-// shared memory with bulk copies while 8 consumer warps split its K blocks
-// (see the kernel). A prologue kernel writes the activation limbs in
+// shared memory with bulk copies while 4 (batch <= 4) or 8 consumer warps
+// split its K blocks (see the kernel). Batch 1 keeps the scales out of the A
+// operand (mma_blocks_diag). A prologue kernel writes the activation limbs in
 // the order the B fragments are read (one 8-byte load per lane per mma); the
 // GEMV is launched as its programmatic dependent, so it starts streaming
 // weights while the prologue runs and waits only before reading the limbs.
@@ -216,10 +217,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-constexpr int kStages = 2;     // smem ring depth
-constexpr int kConsumers = 4;  // consumer warps per CTA
-constexpr int kBpw = 2;        // K blocks per consumer warp per stage
-constexpr int kChunk = kConsumers * kBpw;  // K blocks per stage
+constexpr int kStages = 2;  // smem ring depth
+constexpr int kChunk = 8;   // K blocks per stage (whole 128-byte lines for the tensor map)
+// Consumer warps per CTA by batch: four warps of two blocks per stage up to
+// batch 4 (three CTAs per SM), eight warps of one block from batch 5 (two CTAs
+// per SM, the registers of the larger accumulators).
+__host__ __device__ constexpr int consumers_for(int nb) { return nb >= 5 ? 8 : 4; }
+__host__ __device__ constexpr int min_ctas_for(int nb) { return nb >= 5 ? 2 : 3; }
 constexpr int kTileRows = 16;
 
 // One (16-row tile, K block) work item of a consumer warp: rows g and g+8 of
@@ -345,6 +349,115 @@ __device__ __forceinline__ void mma_blocks(const uint8_t* stage, const uint32_t 
         }
 }
 
+// Batch 1: the same work item with the scales kept out of the A operand.
+// A holds the raw quants as fp16 subnormals (a nibble ANDed into the low
+// mantissa bits is q * 2^-24, or 16 q * 2^-24 for a high nibble; exact, no
+// HFMA2), and B is block-diagonal in the sub-blocks: column (j, limb) of token
+// b is nonzero only in the K slots of lane group t = j, so D column (t, limb)
+// is lane t's own sub-block partial sum (2t for the low-nibble chain, 2t + 1
+// for the high one) and the sub-block scales are applied in fp32 afterwards.
+// Lane (g, t) loads a B fragment only when g / 2 == t (the other columns are
+// zero); the fragment is the prologue's XF entry for column 2 b + (g & 1).
+// acc2[b][r] collects lane t's sub-blocks of row g (r = 0) or g + 8 (r = 1),
+// already scaled by XS; the four t lanes are summed when the tile ends.
+template <uint32_t Q, int NB, int U, bool SW>
+__device__ __forceinline__ void mma_blocks_diag(const uint8_t* stage, const uint32_t (&rowoff)[U][2],
+                                                const int (&kbs)[U], const uint4* const (&xfd)[NB],
+                                                const __half* __restrict__ XQ, const float* __restrict__ XS, int nblk,
+                                                int t, bool active, uint32_t sel, float (&acc2)[NB][2]) {
+    constexpr int NC = 2 * NB;
+    constexpr int QOFF = (Q == kQ4_K) ? 16 : 48;
+    const uint32_t kLoMask = 0x000F000Fu, kHiMask = 0x00F000F0u;
+    uint4 qa[U][2], qb[U][2], ha[U][2], hb[U][2];
+    float fs0[U][2], fs1[U][2], fm0[U][2], fm1[U][2];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            auto ld = [&](uint32_t o) {
+                if constexpr (SW) o ^= (o >> 3) & 0x70u;
+                return *reinterpret_cast<const uint4*>(stage + o);
+            };
+            const uint32_t o = rowoff[u][r];
+            const uint4 hd = ld(o);
+            qa[u][r] = ld(o + QOFF + 32 * t);
+            qb[u][r] = ld(o + QOFF + 32 * t + 16);
+            if constexpr (Q == kQ5_K) {
+                ha[u][r] = ld(o + 16);
+                hb[u][r] = ld(o + 32);
+            }
+            const float d = f16_bits_to_f32(hd.x & 0xFFFFu), dmin = f16_bits_to_f32(hd.x >> 16);
+            uint32_t sl, sh, ml, mh;
+            scales_k4_packed(hd.y, hd.z, hd.w, sl, sh, ml, mh);
+            const uint32_t sw = t < 2 ? sl : sh, mw = t < 2 ? ml : mh;
+            // (sc, m) of sub-blocks 2t and 2t + 1 as exact fp16 integers, then fp32
+            const float2 sc = __half22float2(__hsub2(u2h(__byte_perm(sw, 0x00006464u, sel)),
+                                                     __float2half2_rn(1024.0f)));
+            const float2 mn = __half22float2(__hsub2(u2h(__byte_perm(mw, 0x00006464u, sel)),
+                                                     __float2half2_rn(1024.0f)));
+            // undo the 2^-24 of the subnormal quants (and the 16 of a high nibble)
+            fs0[u][r] = d * 16777216.0f * sc.x;
+            fs1[u][r] = d * 1048576.0f * sc.y;
+            fm0[u][r] = dmin * mn.x;
+            fm1[u][r] = dmin * mn.y;
+        }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        float dlo[NB][4], dhi[NB][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint4 bf[NB];
+#pragma unroll
+            for (int b = 0; b < NB; ++b)
+                bf[b] = active ? __ldg(xfd[b] + (kbs[u] * 8 + i) * NC * 4) : make_uint4(0u, 0u, 0u, 0u);
+            uint32_t a_lo0[2], a_lo1[2], a_hi0[2], a_hi1[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint32_t w = word_of(qa[u][r], qb[u][r], i);
+                const uint32_t w8 = w >> 8;
+                uint32_t lo0 = w & kLoMask, lo1 = w8 & kLoMask, hi0 = w & kHiMask, hi1 = w8 & kHiMask;
+                if constexpr (Q == kQ5_K) {
+                    const uint32_t h = word_of(ha[u][r], hb[u][r], i) >> (2 * t);
+                    lo0 = and_or(h << 4, 0x00100010u, lo0);
+                    lo1 = and_or(h >> 4, 0x00100010u, lo1);
+                    hi0 = and_or(h << 7, 0x01000100u, hi0);
+                    hi1 = and_or(h >> 1, 0x01000100u, hi1);
+                }
+                a_lo0[r] = lo0;
+                a_lo1[r] = lo1;
+                a_hi0[r] = hi0;
+                a_hi1[r] = hi1;
+            }
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (i == 0) {
+                    mma16816_z(dlo[b], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[b].x, bf[b].y);
+                    mma16816_z(dhi[b], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[b].z, bf[b].w);
+                } else {
+                    mma16816(dlo[b], a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[b].x, bf[b].y);
+                    mma16816(dhi[b], a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[b].z, bf[b].w);
+                }
+            }
+        }
+        // fold: D columns 2t (limb 0) and 2t + 1 (limb 1); rows g (c = 0, 1), g + 8 (c = 2, 3)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float xs = __ldg(XS + b * nblk + kbs[u]);
+            // sums of the scaled activations over sub-blocks 2t, 2t + 1: {hi0, hi1, lo0, lo1}
+            const uint2 qs = __ldg(reinterpret_cast<const uint2*>(XQ + ((kbs[u] * 4 + t) * NC + 2 * b) * 2));
+            const float2 shi = __half22float2(u2h(qs.x)), slo = __half22float2(u2h(qs.y));
+            const float x0 = fmaf(slo.x, 1.0f / 2048.0f, shi.x), x1 = fmaf(slo.y, 1.0f / 2048.0f, shi.y);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const float vlo = fmaf(dlo[b][2 * r + 1], 1.0f / 2048.0f, dlo[b][2 * r]);
+                const float vhi = fmaf(dhi[b][2 * r + 1], 1.0f / 2048.0f, dhi[b][2 * r]);
+                const float tr = fmaf(fs0[u][r], vlo, fmaf(fs1[u][r], vhi, -fmaf(fm0[u][r], x0, fm1[u][r] * x1)));
+                acc2[b][r] = fmaf(xs, tr, acc2[b][r]);
+            }
+        }
+    }
+}
+
 // Persistent, warp-specialised kernel. CTA c takes 16-row tiles c, c + grid,
 // ...; each tile is cut into stages of kChunk K blocks. The last warp (the
 // producer) copies every stage into a kStages-deep shared-memory ring with one
@@ -354,7 +467,7 @@ __device__ __forceinline__ void mma_blocks(const uint8_t* stage, const uint32_t 
 // partial sums across a tile's stages and combine them in shared memory when
 // the tile ends. Every wait is bounded; a timeout sets *err and the CTA stops.
 template <uint32_t Q, int NB, bool TM>
-__global__ void __launch_bounds__((kConsumers + 1) * 32, 3)
+__global__ void __launch_bounds__((consumers_for(NB) + 1) * 32, min_ctas_for(NB))
 gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
                    float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap,
@@ -366,6 +479,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     Y += (int64_t)blockIdx.y * NB * ldy;
     constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
     constexpr int BB = block_bytes(Q);
+    constexpr int kConsumers = consumers_for(NB), kBpw = kChunk / kConsumers;
     // smem stride of one row of a stage. TM (one tensor-map copy per stage):
     // the rows are dense and 128-byte swizzled, which puts consecutive rows'
     // units on different banks. Otherwise (one bulk copy per row): each row is
@@ -438,8 +552,17 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     }
 
     // ---------------- consumers
+    constexpr bool kDiag = NB == 1;  // batch 1: mma_blocks_diag
     const int g = lane >> 2, t = lane & 3;
     const uint32_t sel = (4u << 12) | ((uint32_t)(2 * (t & 1) + 1) << 8) | (4u << 4) | (uint32_t)(2 * (t & 1));
+    // diagonal B: lane (g, t) holds column (g / 2, g & 1), nonzero when g / 2 == t
+    const bool active = (g >> 1) == t;
+    const uint4* xfd[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) xfd[b] = reinterpret_cast<const uint4*>(XF) + (2 * b + (g & 1)) * 4 + t;
+    float acc2[NB][2];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc2[b][0] = acc2[b][1] = 0.0f;
     // lane (g, t) feeds B column 8 nt + g; past the batch it reads the last
     // column instead (a valid address; those D columns are never stored)
     const uint4* xfl[NT];
@@ -487,14 +610,22 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                 rowoff[u][1] = (g + 8) * ROWB + ub;
                 kbs[u] = kb0 + u;
             }
-            mma_blocks<Q, NB, kBpw, TM>(ring + slot * STAGE, rowoff, kbs, xfl, xql, XS, nblk, t, sel, acc);
+            if constexpr (kDiag)
+                mma_blocks_diag<Q, NB, kBpw, TM>(ring + slot * STAGE, rowoff, kbs, xfd, XQ, XS, nblk, t, active, sel,
+                                                 acc2);
+            else
+                mma_blocks<Q, NB, kBpw, TM>(ring + slot * STAGE, rowoff, kbs, xfl, xql, XS, nblk, t, sel, acc);
         } else if (live) {
             // a ragged last chunk: the blocks that exist, one at a time
             for (int kb = kb0; kb < nblk && kb < kb0 + kBpw; ++kb) {
                 const uint32_t ub = (uint32_t)((kb - chunk * kChunk) * BB);
                 const uint32_t rowoff[1][2] = {{g * ROWB + ub, (g + 8) * ROWB + ub}};
                 const int kbs[1] = {kb};
-                mma_blocks<Q, NB, 1, TM>(ring + slot * STAGE, rowoff, kbs, xfl, xql, XS, nblk, t, sel, acc);
+                if constexpr (kDiag)
+                    mma_blocks_diag<Q, NB, 1, TM>(ring + slot * STAGE, rowoff, kbs, xfd, XQ, XS, nblk, t, active, sel,
+                                                  acc2);
+                else
+                    mma_blocks<Q, NB, 1, TM>(ring + slot * STAGE, rowoff, kbs, xfl, xql, XS, nblk, t, sel, acc);
             }
         }
         __syncwarp();
@@ -505,34 +636,61 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
             // next tile's writes cannot race this tile's reads and one barrier
             // per tile suffices.
             const int set = (j / nchunks) & 1;
+            if constexpr (kDiag) {
+                // sum the four t lanes of each row, then the warps: red[set][w] as [b][16 rows]
+                float* rw = &red[set][warp][0][0][0];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                red[set][warp][nt][0][lane] = fmaf(acc[nt][1], 1.0f / 2048.0f, acc[nt][0]);
-                red[set][warp][nt][1][lane] = fmaf(acc[nt][3], 1.0f / 2048.0f, acc[nt][2]);
+                for (int b = 0; b < NB; ++b)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
-            }
-            asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
-            if (warp < 2 * NT) {
-                const int nt = warp >> 1, r = warp & 1;
-                float v = 0.0f;
+                    for (int r = 0; r < 2; ++r) {
+                        float v = acc2[b][r];
+                        v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+                        v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+                        if (t == 0) rw[b * 16 + 8 * r + g] = v;
+                        acc2[b][r] = 0.0f;
+                    }
+                asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+                if (warp == 0 && lane < NB * 16) {
+                    const int b = lane >> 4, row = tile * kTileRows + (lane & 15);
+                    float v = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kConsumers; ++w) v += red[set][w][nt][r][lane];
-                const int b = 4 * nt + t;
-                const int row = tile * kTileRows + 8 * r + g;
-                if (b < NB && row < N) {
-                    if (po.G) {
-                        for (int q = 0; q < po.G; ++q) po.y[q][peer_off + b * ldy + row] = v;
-                    } else {
-                        Y[b * ldy + row] = v;
+                    for (int w = 0; w < kConsumers; ++w) v += (&red[set][w][0][0][0])[lane];
+                    if (row < N) {
+                        if (po.G) po.y[peer_off + b * ldy + row] = v;
+                        else Y[b * ldy + row] = v;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    red[set][warp][nt][0][lane] = fmaf(acc[nt][1], 1.0f / 2048.0f, acc[nt][0]);
+                    red[set][warp][nt][1][lane] = fmaf(acc[nt][3], 1.0f / 2048.0f, acc[nt][2]);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+                if (warp < 2 * NT) {
+                    const int nt = warp >> 1, r = warp & 1;
+                    float v = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < kConsumers; ++w) v += red[set][w][nt][r][lane];
+                    const int b = 4 * nt + t;
+                    const int row = tile * kTileRows + 8 * r + g;
+                    if (b < NB && row < N) {
+                        if (po.G) po.y[peer_off + b * ldy + row] = v;
+                        else Y[b * ldy + row] = v;
                     }
                 }
             }
         }
     }
     if (po.G) {
-        // every store of this CTA (local and over NVLink) before its arrival on each rank
-        __threadfence_system();
+        // This CTA's outputs must be in this GPU's L2 before its arrival reaches
+        // any rank: the other ranks read them over NVLink, and a peer's reads
+        // of this GPU's memory are served by this GPU's L2, so a GPU-scope
+        // fence orders them (a system-scope fence would also wait on host
+        // memory, for microseconds per CTA).
+        __threadfence();
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
         if (threadIdx.x == 0)
             for (int q = 0; q < po.G; ++q) atomicAdd_system(po.ctr[q] + half, 1ull);
@@ -549,7 +707,7 @@ int64_t launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __
     static int per_sm = 0;  // resident CTAs per SM, per instantiation
     if (per_sm == 0) {
         cudaFuncSetAttribute(gemv_kq_tma_kernel<Q, NB, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_tma_kernel<Q, NB, TM>, (kConsumers + 1) * 32,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_tma_kernel<Q, NB, TM>, (consumers_for(NB) + 1) * 32,
                                                       smem);
         if (per_sm < 1) per_sm = 1;
     }
@@ -560,7 +718,7 @@ int64_t launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __
     if (grid > ntiles) grid = ntiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid, chunks);
-    cfg.blockDim = dim3((kConsumers + 1) * 32);
+    cfg.blockDim = dim3((consumers_for(NB) + 1) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];

@@ -6,13 +6,14 @@
 namespace strata {
 
 // Fused all-gather of a row-sharded GEMV over peer memory: every output
-// value is stored into each rank's exchange buffer instead of Y (half
-// `epoch & 1`, layout [batch][ldy], this call's first value at float `off` of
-// the half), and every CTA then adds 1 to each rank's arrival counter of that
-// half (system scope, after a system fence).
+// value goes to this rank's exchange buffer instead of Y (half `epoch & 1`,
+// layout [batch][ldy], this call's first value at float `off` of the half),
+// and every CTA then adds 1 to each rank's arrival counter of that half
+// (system scope, after a system fence); the ranks read each other's columns
+// once the counts are complete.
 constexpr int kMaxPeers = 8;
 struct PeerOut {
-    float* y[kMaxPeers];                  // each rank's exchange buffer
+    float* y;                             // this rank's exchange buffer (both halves)
     unsigned long long* ctr[kMaxPeers];   // each rank's arrival counters, one per half
     const unsigned int* epoch;            // this rank's call counter (its parity picks the half)
     int64_t half_floats;                  // floats per half of an exchange buffer

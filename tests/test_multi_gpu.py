@@ -104,6 +104,19 @@ def _worker(rank, world, uid, q):
         for xx, yy in ((x1, y1), (x4, y4)):
             want = ctx.gemv(full, xx.cpu().numpy())
             assert np.array_equal(yy.cpu().numpy().view(np.uint32), want.reshape(yy.shape).view(np.uint32)), "group"
+        # more grouped calls than one wait-and-copy kernel takes (it flushes midway)
+        ys34 = [torch.empty((1, N), dtype=torch.float32, device=dev) for _ in range(34)]
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            ctx.comm_group_start()
+            for i, yy in enumerate(ys34):
+                ctx.gemv_sharded_dev(shard, (x1 if i % 2 else x4).data_ptr(), yy.data_ptr(), 1, st.cuda_stream)
+            ctx.comm_group_end()
+        st.synchronize()
+        w1, w4 = ctx.gemv(full, x1.cpu().numpy()), ctx.gemv(full, x4.cpu().numpy()[:1])
+        for i, yy in enumerate(ys34):
+            want = w1 if i % 2 else w4
+            assert np.array_equal(yy.cpu().numpy().view(np.uint32), want.reshape(1, N).view(np.uint32)), ("group34", i)
         # the same under the NCCL gather: one NCCL group for both calls
         ctx.comm_set_gather(ctx.GATHER_NCCL)
         y1.zero_()
