@@ -240,20 +240,21 @@ int strata_cuda_gemv_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, 
 int strata_cuda_gemm_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, const uint16_t *x_dev,
                                  float *y_dev, int64_t m, void *stream);
 
-/* How the sharded GEMV gathers its rows. PEER fuses the all-gather into the
- * tensor-core GEMV: its epilogue stores each output value straight into every
- * rank's exchange buffer over NVLink (peer memory opened with CUDA IPC at
- * comm_init) and bumps each rank's arrival counter; a small kernel on each
- * rank waits (bounded by the context's wait timeout, then
- * STRATA_ERR_TIMEOUT) for all arrivals and copies the gathered rows to y.
- * Inside a collective group that kernel is enqueued once, at group_end, for
- * all the group's calls on one stream (so y is complete after group_end's
- * work, as with NCCL). No NCCL call is made and the calls are
+/* How the sharded GEMV gathers its rows. PEER runs the all-gather over peer
+ * memory with no NCCL call: the tensor-core GEMV writes its columns into this
+ * rank's exchange buffer (device memory that every rank mapped with CUDA IPC
+ * at comm_init), then one all-gather kernel pushes them into every other
+ * rank's buffer over NVLink (16-byte stores), signals the other ranks, waits
+ * for their signals (bounded by the context's wait timeout, then
+ * STRATA_ERR_TIMEOUT) and assembles y. Inside a collective group that kernel
+ * runs once, at group_end, for all the group's calls on one stream (y is
+ * complete after group_end's work, as with NCCL). The calls are
  * graph-capturable. NCCL uses the per-row in-place all-gathers. AUTO (the
  * default) takes PEER where it applies -- peer memory available on every
- * rank, a Q4_K / Q5_K shard on the tensor-core path, batch x OUT within the
- * exchange capacity -- and NCCL otherwise. Every rank must set the same mode
- * (the ranks of one call must take the same path). */
+ * rank, a Q4_K / Q5_K shard on the tensor-core path with a multiple of 4 rows,
+ * y 16-byte aligned, batch x OUT within the exchange capacity -- and NCCL
+ * otherwise. Every rank must set the same mode (the ranks of one call must
+ * take the same path). */
 enum { STRATA_GATHER_AUTO = 0, STRATA_GATHER_NCCL = 1, STRATA_GATHER_PEER = 2 };
 int strata_cuda_comm_set_gather(strata_ctx *ctx, int mode);
 /* available: 1 if every rank opened every peer's exchange buffer;

@@ -80,42 +80,42 @@ const Nccl& nccl() {
     return n;
 }
 
-// Exchange buffer of the fused peer gather, one per rank, opened by every
+// Exchange buffer of the peer all-gather, one per rank, opened by every
 // other rank through CUDA IPC: control words, then two halves of
-// kPeerHalfFloats floats (consecutive calls alternate halves, so a rank that
-// is one call ahead never overwrites the half its peers are still reading).
-// Arrivals are counted per half: a peer that is one call ahead adds to the
-// other half's counter, never to the one this rank is waiting on (it cannot
-// be two calls ahead: its next wait needs this rank's arrivals).
+// kPeerHalfFloats floats. The sharded GEMVs write their columns into this
+// rank's half; the all-gather kernel pushes them into the same place of every
+// other rank's half and then copies the whole rows out. Consecutive gathers
+// alternate halves and count arrivals per half: a peer one gather ahead
+// writes and signals the other half, and none can be two ahead (its next
+// gather needs this rank's signal).
 struct PeerCtl {
-    unsigned long long arrivals[2];  // CTAs (of every rank) whose outputs have landed in half h
-    unsigned long long expected[2];  // arrivals the calls on half h so far have waited for
-    unsigned int epoch;              // calls so far (its parity picks the half)
-    unsigned int done;               // CTAs of the running wait kernel that finished
+    unsigned long long arrivals[2];  // peers' "pushed" signals received for half h
+    unsigned long long expected[2];  // signals the gathers on half h so far have waited for
+    unsigned int epoch;              // gathers so far (its parity picks the half)
+    unsigned int pushed;             // CTAs of the running gather kernel done pushing
+    unsigned int finished;           // CTAs of the running gather kernel done copying
     int barrier;                     // all-reduce operand of the teardown barrier
 };
 constexpr int64_t kPeerCtlBytes = 256;
 constexpr int64_t kPeerHalfFloats = int64_t(8) << 20;  // 32 MiB per half
 
 constexpr int kPeerSegs = 32;
-// What one wait-and-copy kernel reads out of the ranks' exchange halves: the
-// gathers of up to kPeerSegs sharded GEMVs (one call, or the calls of a
-// collective group). Segment s is y[s] = [rows][G ns] whose columns
-// [q ns, (q + 1) ns) rank q wrote into its own buffer at the same offset.
+// The outputs one all-gather kernel assembles: those of up to kPeerSegs
+// sharded GEMVs (one call, or the calls of a collective group). Segment s is
+// y[s] = [rows][G ns], at float off[s] of the half in every rank's buffer;
+// rank q wrote columns [q ns, (q + 1) ns) of every row into its own buffer.
 struct PeerSegs {
     float* y[kPeerSegs];
-    int64_t off[kPeerSegs];  // first float in the half (a multiple of 4)
-    int64_t n[kPeerSegs];    // floats: rows x G ns
-    int64_t ns[kPeerSegs];   // columns per rank
+    int64_t off[kPeerSegs];  // a multiple of 4
+    int rows[kPeerSegs];
+    int ns4[kPeerSegs];      // columns per rank / 4
     char* base[kMaxPeers];   // every rank's exchange buffer as mapped here
-    int G;
-    int count;
+    int rank, G, count;
 };
-// Peer gathers issued since the last wait-and-copy kernel.
+// Sharded GEMVs issued since the last all-gather kernel.
 struct PeerPending {
     PeerSegs segs{};
     int64_t floats = 0;  // of the half in use
-    int64_t ctas = 0;    // this rank's GEMV CTAs (each rank launches the same)
     cudaStream_t stream = nullptr;
 };
 
@@ -331,111 +331,142 @@ int peer_setup(strata_ctx* ctx) {
     return rc;
 }
 
-// Waits (thread 0 of each CTA, bounded) until the current half of this rank's
-// exchange buffer has received `arrivals` more CTA arrivals than the calls
-// before on that half, then reads every segment's columns from the rank that
-// wrote them (this GPU's memory or a peer's, over NVLink) into its y.
-// The last CTA to finish advances the half's expected count and the epoch
-// (every CTA has read both by then). After an expired wait the counts no
-// longer match the calls: the communicator has to be recreated before the
-// next peer gather.
-__global__ void peer_gather_wait_kernel(char* __restrict__ base, unsigned long long arrivals,
-                                        const __grid_constant__ PeerSegs segs, uint64_t timeout_ns, int* err) {
-    PeerCtl* ctl = ctl_of(base);
-    __shared__ unsigned long long target_s;
+// Bounded spin (thread 0) until *ctr >= target; false after timeout_ns.
+__device__ bool wait_count(unsigned long long* ctr, unsigned long long target, uint64_t timeout_ns) {
+    uint64_t t0, now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (long long i = 0; i < (1ll << 40); ++i) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (now - t0 > timeout_ns) return false;
+        __nanosleep(64);
+    }
+    return false;
+}
+
+// The all-gather of the pending segments, one cooperative launch (all CTAs
+// resident: a CTA waits on signals that other ranks send only after all of
+// this rank's CTAs pushed).
+//   1. push: this rank's columns of every row go from its own half to the
+//      same place in every other rank's half (16-byte stores over NVLink) and
+//      to y;
+//   2. signal: every CTA releases its stores (system scope) and counts
+//      itself; the last one adds 1 to every other rank's arrival counter;
+//   3. wait (bounded) for the G - 1 other ranks' signals on this half, then
+//      copy their columns from this rank's half to y;
+//   4. the last CTA to finish advances the expected count and the epoch.
+// After an expired wait the counts no longer match the gathers: the
+// communicator has to be recreated before the next peer gather.
+__global__ void peer_allgather_kernel(const __grid_constant__ PeerSegs segs, uint64_t timeout_ns, int* err) {
+    char* own = segs.base[segs.rank];
+    PeerCtl* ctl = ctl_of(own);
     __shared__ unsigned int epoch_s;
     __shared__ int ok_s;
-    if (threadIdx.x == 0) {
-        const unsigned int e = *(volatile unsigned int*)&ctl->epoch;
-        const unsigned long long target = *(volatile unsigned long long*)&ctl->expected[e & 1u] + arrivals;
-        uint64_t t0, now;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-        bool ok = false;
-        for (long long i = 0; i < (1ll << 40); ++i) {
-            unsigned long long v;
-            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(&ctl->arrivals[e & 1u]) : "memory");
-            if (v >= target) {
-                ok = true;
-                break;
-            }
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-            if (now - t0 > timeout_ns) break;
-            __nanosleep(64);
+    if (threadIdx.x == 0) epoch_s = *(volatile unsigned int*)&ctl->epoch;
+    __syncthreads();
+    const unsigned int e = epoch_s, h = e & 1u;
+    const int64_t half = kPeerCtlBytes / 4 + (int64_t)h * kPeerHalfFloats;
+    const int G = segs.G, me = segs.rank;
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x, nthr = gridDim.x * blockDim.x;
+
+    // 1. push
+    for (int sg = 0; sg < segs.count; ++sg) {
+        const int ns4 = segs.ns4[sg], units = segs.rows[sg] * ns4;
+        const int64_t n4 = (int64_t)G * ns4;  // float4 per row
+        float4* y = reinterpret_cast<float4*>(segs.y[sg]);
+        const int64_t src0 = half + segs.off[sg];
+        for (int i = tid; i < units; i += nthr) {
+            const int b = i / ns4, j = i - b * ns4;
+            const int64_t u = (int64_t)b * n4 + (int64_t)me * ns4 + j;  // float4 index in the segment
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<float*>(own) + src0) + u);
+            y[u] = v;
+            for (int q = 0; q < G; ++q)
+                if (q != me) reinterpret_cast<float4*>(reinterpret_cast<float*>(segs.base[q]) + src0)[u] = v;
         }
+    }
+    // 2. signal
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        if (atomicAdd(&ctl->pushed, 1u) == gridDim.x - 1) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            for (int q = 0; q < G; ++q)
+                if (q != me) atomicAdd_system(&ctl_of(segs.base[q])->arrivals[h], 1ull);
+        }
+        // 3. wait for the other ranks
+        const bool ok = wait_count(&ctl->arrivals[h], ctl->expected[h] + (unsigned long long)(G - 1), timeout_ns);
         if (!ok) atomicExch(err, 1);
-        target_s = target;
-        epoch_s = e;
         ok_s = ok;
     }
     __syncthreads();
     if (ok_s) {
-        const int64_t half = kPeerCtlBytes / 4 + (int64_t)(epoch_s & 1u) * kPeerHalfFloats;
-        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-        const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
         for (int sg = 0; sg < segs.count; ++sg) {
-            float* y = segs.y[sg];
-            const int64_t n = segs.n[sg], ns = segs.ns[sg], N = ns * segs.G, src0 = half + segs.off[sg];
-            if (((uintptr_t)y & 15) == 0 && ns % 4 == 0) {
-                // four consecutive floats share their owner: 16-byte reads and writes
-                for (int64_t i = i0; i < n / 4; i += stride) {
-                    const int64_t e = 4 * i;
-                    const float* src = reinterpret_cast<const float*>(segs.base[(e % N) / ns]) + src0 + e;
-                    reinterpret_cast<float4*>(y)[i] = __ldcg(reinterpret_cast<const float4*>(src));
-                }
-            } else {
-                for (int64_t e = i0; e < n; e += stride) {
-                    const float* src = reinterpret_cast<const float*>(segs.base[(e % N) / ns]) + src0 + e;
-                    y[e] = __ldcg(src);
-                }
+            const int ns4 = segs.ns4[sg], units = segs.rows[sg] * (G - 1) * ns4;
+            const int64_t n4 = (int64_t)G * ns4;
+            float4* y = reinterpret_cast<float4*>(segs.y[sg]);
+            const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<float*>(own) + half + segs.off[sg]);
+            for (int i = tid; i < units; i += nthr) {
+                const int r = i / ns4, j = i - r * ns4;
+                const int b = r / (G - 1), qq = r - b * (G - 1);
+                const int q = qq < me ? qq : qq + 1;
+                const int64_t u = (int64_t)b * n4 + (int64_t)q * ns4 + j;
+                y[u] = __ldcg(src + u);
             }
         }
     }
+    // 4. advance
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        if (atomicAdd(&ctl->done, 1u) == gridDim.x - 1) {
-            ctl->expected[epoch_s & 1u] = target_s;
-            ctl->epoch = epoch_s + 1;
-            ctl->done = 0;
+        if (atomicAdd(&ctl->finished, 1u) == gridDim.x - 1) {
+            ctl->expected[h] += (unsigned long long)(G - 1);
+            ctl->epoch = e + 1;
+            ctl->pushed = 0;
+            ctl->finished = 0;
             __threadfence();
         }
     }
 }
 
-// Whether this sharded GEMV takes the fused peer gather.
-bool use_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, int batch) {
+// Whether this sharded GEMV takes the peer all-gather.
+bool use_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, const float* y, int batch) {
     CommState* c = ctx->comm;
-    if (!c->peer_ok || c->gather_mode == STRATA_GATHER_NCCL) return false;
-    if ((int64_t)batch * w->rows * c->world > kPeerHalfFloats) return false;
+    if (!c->peer_ok || c->gather_mode == STRATA_GATHER_NCCL || c->world < 2) return false;
+    if ((int64_t)batch * w->rows * c->world > kPeerHalfFloats || w->rows % 4 != 0 || ((uintptr_t)y & 15)) return false;
     return gemv_peer_capable(ctx, w, x, batch);
 }
 
-// Enqueues the wait-and-copy kernel for the pending peer gathers (no-op when
-// none are pending). Every rank flushes at the same points of the same call
+// Enqueues the all-gather kernel for the pending segments (no-op when none
+// are pending). Every rank flushes at the same points of the same call
 // sequence, so the ranks' halves and arrival counts stay in step.
 int peer_flush(strata_ctx* ctx) {
     CommState* c = ctx->comm;
     PeerPending& p = c->pending;
     if (p.segs.count == 0) return STRATA_OK;
-    int64_t n = 0;
-    for (int i = 0; i < p.segs.count; ++i) n += p.segs.n[i];
-    int64_t blocks = (n / 4 + 255) / 256;
-    if (blocks > ctx->sm_count) blocks = ctx->sm_count;
-    if (blocks < 1) blocks = 1;
+    p.segs.rank = c->rank;
     p.segs.G = c->world;
     for (int q = 0; q < c->world; ++q) p.segs.base[q] = c->peer_base[q];
-    // every rank launched the same grids (same shard shapes, same GPU model)
-    peer_gather_wait_kernel<<<(unsigned)blocks, 256, 0, p.stream>>>(
-        c->xbuf, (unsigned long long)(p.ctas * c->world), p.segs, (uint64_t)ctx->wait_timeout_ms * 1000000ull,
-        ctx->err_dev);
+    // one CTA per SM: always co-resident, which the cooperative launch checks
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctx->sm_count);
+    cfg.blockDim = dim3(256);
+    cfg.stream = p.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, peer_allgather_kernel, p.segs, (uint64_t)ctx->wait_timeout_ms * 1000000ull,
+                       ctx->err_dev);
     p = PeerPending{};
-    return check_launch(ctx, "peer gather wait kernel");
+    return check_launch(ctx, "peer all-gather kernel");
 }
 
-// Fused GEMV + all-gather: the GEMV's epilogue writes every rank's exchange
-// buffer at this call's place in the current half; the wait-and-copy kernel
-// follows at once, or at the end of the collective group (one for all the
-// group's calls on a stream).
+// Sharded GEMV into this rank's exchange half at the call's place; the
+// all-gather kernel follows at once, or at the end of the collective group
+// (one for all the group's calls on a stream).
 int gemv_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int batch, cudaStream_t s) {
     CommState* c = ctx->comm;
     PeerPending& p = c->pending;
@@ -446,21 +477,18 @@ int gemv_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, fl
         if ((rc = peer_flush(ctx))) return rc;
     PeerOut po{};
     po.y = data_of(c->xbuf);
-    for (int q = 0; q < c->world; ++q) po.ctr[q] = ctl_of(c->peer_base[q])->arrivals;
     po.epoch = &ctl_of(c->xbuf)->epoch;
     po.half_floats = kPeerHalfFloats;
     po.off = p.floats + c->rank * ns;
     po.G = c->world;
-    int64_t ctas = 0;
-    if ((rc = gemv_enqueue_strided(ctx, w, x, y + c->rank * ns, batch, N, s, &po, &ctas))) return rc;
+    if ((rc = gemv_enqueue_strided(ctx, w, x, y + c->rank * ns, batch, N, s, &po))) return rc;
     p.stream = s;
     p.segs.y[p.segs.count] = y;
     p.segs.off[p.segs.count] = p.floats;
-    p.segs.n[p.segs.count] = n;
-    p.segs.ns[p.segs.count] = ns;
+    p.segs.rows[p.segs.count] = batch;
+    p.segs.ns4[p.segs.count] = (int)(ns / 4);
     ++p.segs.count;
     p.floats += (n + 3) & ~int64_t(3);
-    p.ctas += ctas;
     return c->group_depth > 0 ? STRATA_OK : peer_flush(ctx);
 }
 
@@ -575,7 +603,7 @@ int strata_cuda_gemv_sharded_dev(strata_ctx* ctx, const strata_weight* w, const 
     cudaStream_t s = pick_stream(ctx, stream);
     CommState* c = ctx->comm;
     const int64_t ns = w->rows;
-    if (use_peer_gather(ctx, w, x_dev, batch)) return gemv_peer_gather(ctx, w, x_dev, y_dev, batch, s);
+    if (use_peer_gather(ctx, w, x_dev, y_dev, batch)) return gemv_peer_gather(ctx, w, x_dev, y_dev, batch, s);
     if (c->gather_mode == STRATA_GATHER_PEER)
         return fail(ctx, STRATA_ERR_INVALID, "the peer gather does not apply to this shard (quant %u, batch %d)",
                     w->quant, batch);

@@ -684,22 +684,10 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
             }
         }
     }
-    if (po.G) {
-        // This CTA's outputs must be in this GPU's L2 before its arrival reaches
-        // any rank: the other ranks read them over NVLink, and a peer's reads
-        // of this GPU's memory are served by this GPU's L2, so a GPU-scope
-        // fence orders them (a system-scope fence would also wait on host
-        // memory, for microseconds per CTA).
-        __threadfence();
-        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
-        if (threadIdx.x == 0)
-            for (int q = 0; q < po.G; ++q) atomicAdd_system(po.ctr[q] + half, 1ull);
-    }
 }
 
-// Returns the CTAs launched (grid x chunks).
 template <uint32_t Q, int NB, bool TM>
-int64_t launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
                    unsigned chunks = 1, int64_t chunk_bytes = 0) {
     const int nblk = (int)(a.K / 256);
     const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
@@ -730,12 +718,11 @@ int64_t launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __
     if (a.peers) po = *a.peers;
     cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err,
                        map, chunk_bytes, ldy_of(a), po);
-    return grid * chunks;
 }
 
 template <uint32_t Q, bool TM>
-int64_t dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
-                     unsigned chunks = 1, int64_t chunk_bytes = 0) {
+void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+                  unsigned chunks = 1, int64_t chunk_bytes = 0) {
     if (chunks > 1) return launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
     switch (a.batch) {
     case 1: return launch_tma<Q, 1, TM>(a, xf, xs, xq, err, s);
@@ -800,9 +787,7 @@ bool gemv_mma_supported(uint32_t quant, const GemvArgs& a) {
 }
 
 // x limbs into `work` (gemv_mma_work_bytes), then the tensor-core GEMV.
-// `ctas` (optional) receives the CTAs launched: with a.peers, the arrivals
-// this call adds to every rank's counter.
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s, int64_t* ctas) {
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s) {
     const int nblk = (int)(a.K / 256);
     const int full = a.batch > 8 ? a.batch / 8 : 0;  // 8-token chunks on grid.y
     const int nb = full ? 8 : a.batch;
@@ -820,12 +805,10 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     GemvArgs c = a;
     c.batch = nb;
     const bool tm = a.tmap != nullptr;
-    int64_t n = 0;
-    if (quant == kQ4_K) n = tm ? dispatch_mma<kQ4_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
-                               : dispatch_mma<kQ4_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
-    else n = tm ? dispatch_mma<kQ5_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
-                : dispatch_mma<kQ5_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
-    if (ctas) *ctas = n;
+    if (quant == kQ4_K) tm ? dispatch_mma<kQ4_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
+                           : dispatch_mma<kQ4_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
+    else tm ? dispatch_mma<kQ5_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
+            : dispatch_mma<kQ5_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
     if (full && a.batch % 8) {  // the remaining tokens, after the chunks' workspace
         GemvArgs r = a;
         r.X = a.X + (int64_t)full * 8 * a.K;
@@ -837,10 +820,7 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
             pr.off += (int64_t)full * 8 * ldy_of(a);
             r.peers = &pr;
         }
-        int64_t m = 0;
-        const int rc = launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s, &m);
-        if (ctas) *ctas += m;
-        return rc;
+        return launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s);
     }
     return 0;
 }

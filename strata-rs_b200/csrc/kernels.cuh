@@ -5,20 +5,17 @@
 
 namespace strata {
 
-// Fused all-gather of a row-sharded GEMV over peer memory: every output
-// value goes to this rank's exchange buffer instead of Y (half `epoch & 1`,
-// layout [batch][ldy], this call's first value at float `off` of the half),
-// and every CTA then adds 1 to each rank's arrival counter of that half
-// (system scope, after a system fence); the ranks read each other's columns
-// once the counts are complete.
+// Row-sharded GEMV whose all-gather runs over peer memory: the outputs go to
+// this rank's exchange buffer instead of Y (half `epoch & 1`, layout
+// [batch][ldy], this call's first value at float `off` of the half), where
+// the all-gather kernel pushes them to the other ranks.
 constexpr int kMaxPeers = 8;
 struct PeerOut {
-    float* y;                             // this rank's exchange buffer (both halves)
-    unsigned long long* ctr[kMaxPeers];   // each rank's arrival counters, one per half
-    const unsigned int* epoch;            // this rank's call counter (its parity picks the half)
-    int64_t half_floats;                  // floats per half of an exchange buffer
-    int64_t off;                          // float offset in a half of this launch's y[0][0]
-    int G;                                // 0: no peers (plain GEMV)
+    float* y;                   // this rank's exchange buffer (both halves)
+    const unsigned int* epoch;  // this rank's call counter (its parity picks the half)
+    int64_t half_floats;        // floats per half of an exchange buffer
+    int64_t off;                // float offset in a half of this launch's y[0][0]
+    int G;                      // 0: no exchange (plain GEMV)
 };
 
 // Dense GEMV arguments: W is N rows of `row_bytes` (rows = OUT, quantized
@@ -46,8 +43,7 @@ int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s);
 // any batch (8-token chunks beyond 8); `work` holds gemv_mma_work_bytes.
 int64_t gemv_mma_work_bytes(int64_t K, int batch);
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s,
-                    int64_t* ctas = nullptr);
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
 
 // Expert GEMV on the transposed expert layout [E][IN rows][OUT cols]
 // (rows quantized along OUT): Y[b][c] = sum_i X[b][i] * W_e[i][c].

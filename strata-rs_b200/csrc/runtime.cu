@@ -335,10 +335,10 @@ bool gemv_peer_capable(strata_ctx* ctx, const strata_weight* w, const float* x_d
 }
 
 // y row b at y_dev + b * ldy (ldy 0: rows are w->rows floats apart). With
-// `peers` the outputs go to the ranks' exchange buffers instead (tensor-core
-// path only) and *ctas receives the CTAs launched.
+// `peers` the outputs go to this rank's exchange buffer instead (tensor-core
+// path only).
 int gemv_enqueue_strided(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
-                         int64_t ldy, cudaStream_t s, const PeerOut* peers, int64_t* ctas) {
+                         int64_t ldy, cudaStream_t s, const PeerOut* peers) {
     if (batch < 1 || batch > 8) return fail(ctx, STRATA_ERR_INVALID, "batch %d outside 1..8", batch);
     if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3))
         return fail(ctx, STRATA_ERR_INVALID, "x must be 16-byte and y 4-byte aligned");
@@ -348,7 +348,7 @@ int gemv_enqueue_strided(strata_ctx* ctx, const strata_weight* w, const float* x
         int64_t need = gemv_mma_work_bytes(w->cols, batch);
         int rc = ensure_device(ctx, ctx->xfrag, (size_t)(need > (4 << 20) ? need : (4 << 20)), "cudaMalloc(x limbs)");
         if (rc) return rc;
-        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, s, ctas);
+        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, s);
         return check_launch(ctx, "tensor-core gemv kernel");
     }
     if (peers) return fail(ctx, STRATA_ERR_INVALID, "the peer-store epilogue needs the tensor-core gemv");

@@ -84,7 +84,7 @@ int check_device_error(strata_ctx* ctx);
 int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                  cudaStream_t s);
 int gemv_enqueue_strided(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
-                         int64_t ldy, cudaStream_t s, const PeerOut* peers = nullptr, int64_t* ctas = nullptr);
+                         int64_t ldy, cudaStream_t s, const PeerOut* peers = nullptr);
 bool gemv_peer_capable(strata_ctx* ctx, const strata_weight* w, const float* x_dev, int batch);
 int gemm_enqueue(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev, int64_t m,
                  cudaStream_t s);
