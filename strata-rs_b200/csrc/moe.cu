@@ -37,6 +37,30 @@ __device__ __forceinline__ float exp_f32(float x) { return (float)exp((double)x)
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + exp_f32(-x)); }      // ops.rs:85-87
 __device__ __forceinline__ float sigmoid_f32(float x) { return 1.0f / (1.0f + exp_f32(-x)); }  // ops.rs:90-92
 
+// Programmatic dependent launch: every kernel of the layer's chain lets the
+// next one launch at once (its CTAs start while this grid's last wave runs)
+// and waits for the previous grid's completion and memory before reading it.
+__device__ __forceinline__ void pdl_entry() {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launches `kern` as a programmatic dependent of the stream's previous kernel.
+template <typename... KArgs, typename... Args>
+void launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // ------------------------------------------------------------------ routing
 
 // One warp per token (kRouteWarps tokens per CTA); the token's E
@@ -45,6 +69,7 @@ constexpr int kRouteWarps = 4;
 __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float* __restrict__ logits, int T, int E,
                                                                      int k, int* __restrict__ ids,
                                                                      float* __restrict__ wts) {
+    pdl_entry();
     extern __shared__ float sp_all[];  // kRouteWarps x E
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * kRouteWarps + warp;
@@ -134,6 +159,7 @@ constexpr int kAssignThreads = 1024;
 __global__ void __launch_bounds__(kAssignThreads)
 moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begin, int e_end, bool staged,
                   MoeIndex ix) {
+    pdl_entry();
     extern __shared__ int ids_s[];
     __shared__ int cnt_s[1024], scan[1024];
     const int tid = threadIdx.x;
@@ -343,6 +369,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
 moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
                   int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
                   int e_begin, int A_cap, float* __restrict__ P) {
+    pdl_entry();
     extern __shared__ __align__(16) uint8_t dsm[];
     const int nmat = W1 ? 2 : 1;
     const int slot = blockIdx.x / nmat, m = blockIdx.x % nmat;
@@ -524,6 +551,7 @@ moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1
 // H[a][f] = silu(sum_rc P[rc][0][a][f]) * sum_rc P[rc][1][a][f]  (moe.rs:119-121)
 __global__ void moe_swiglu_kernel(const float* __restrict__ P, int RC, int A_cap, int F, const int* __restrict__ n_assign,
                                   float* __restrict__ H) {
+    pdl_entry();
     const int64_t n = (int64_t)n_assign[0] * F;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float g = 0.0f, u = 0.0f;
@@ -553,6 +581,7 @@ __global__ void moe_shared_act_kernel(const float* __restrict__ Gs, const float*
 __global__ void moe_combine_kernel(const float* __restrict__ Pd, int RC, int A_cap, int OUT, const int* __restrict__ pos,
                                    const float* __restrict__ wts, int T, int k, int L, const float* __restrict__ Ds,
                                    const float* __restrict__ sg, float* __restrict__ out) {
+    pdl_entry();
     const int64_t n = (int64_t)T * OUT;
     const int j = threadIdx.x % L;
     const int64_t per_block = blockDim.x / L;
@@ -653,6 +682,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
 moe_mma_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
                int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
                int e_begin, int A_cap, float* __restrict__ P) {
+    pdl_entry();
     constexpr int TP = 4;  // tokens per pass: n = 8 = 4 tokens x 2 limbs
     constexpr int SPW = MPW / 2;  // sub-blocks per warp
     extern __shared__ __align__(16) uint8_t dsm[];
@@ -916,8 +946,181 @@ int launch_stream_t(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int
             cudaSuccess)
         return -1;
     const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
-    moe_stream_kernel<Q, TP><<<grid, kMoeThreads, smem, s>>>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token,
-                                                             ix, e_begin, A_cap, P);
+    launch_dep(moe_stream_kernel<Q, TP>, grid, dim3(kMoeThreads), smem, s, W0, W1, row_bytes, expert_bytes, IN, OUT, X,
+               by_token, ix, e_begin, A_cap, P);
+    return 0;
+}
+
+// ------------------------------------------------------------------ few-token pass (CUDA cores)
+//
+// One or two tokens per expert (decode): the tensor-core pass spends the same
+// instructions per weight whatever the token count, so with one token its
+// MMAs are mostly empty. Here every thread owns 16 output columns of a row --
+// bytes [8 u, 8 u + 8) of quant group `grp` of a block, i.e. columns
+// 64 grp + 8 u .. + 7 (low nibbles, sub-block 2 grp) and the same + 32 (high
+// nibbles, sub-block 2 grp + 1), so one row's scales serve all 16 -- and walks
+// its rows with fp32 FMAs: a nibble q becomes the float 1 + q/16 (one shift
+// and one LOP3; 1 + q/32 for a 5-bit Q5_K value), and
+//   sum_i x_i (d_i sc_i q_i - dmin_i m_i)
+//     = sum_i A_i f_i - sum_i (A_i + x_i dmin_i m_i),  A_i = 16 x_i d_i sc_i
+// (32 for Q5_K). Row groups of the CTA are summed in shared memory and the
+// row chunk's partials go to P like the other passes'.
+constexpr int kLaneUnroll = 4;  // rows in flight per thread
+
+template <uint32_t Q, int TPL>
+__global__ void __launch_bounds__(kMoeThreads)
+moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
+                int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
+                int e_begin, int A_cap, float* __restrict__ P) {
+    pdl_entry();
+    constexpr int BB = block_bytes(Q);
+    constexpr int QOFF = (Q == kQ4_K) ? 16 : 48;
+    constexpr float kUnit = (Q == kQ4_K) ? 16.0f : 32.0f;  // f = 1 + q / kUnit
+    extern __shared__ float red[];  // [RG][TPL][OUT]
+    const int nmat = W1 ? 2 : 1;
+    const int slot = blockIdx.x / nmat, m = blockIdx.x % nmat;
+    if (slot >= ix.n_active[0]) return;
+    const int e = ix.active[slot];
+    const int a0 = ix.off[e], n = ix.cnt[e];
+    const int RC = gridDim.y, rc = blockIdx.y;
+    const int r0 = (int)((int64_t)IN * rc / RC), r1 = (int)((int64_t)IN * (rc + 1) / RC);
+    const int TPR = OUT / 16, RG = kMoeThreads / TPR;
+    const int tid = threadIdx.x, c16 = tid % TPR, rg = tid / TPR;
+    const int blk = c16 >> 4, grp = (c16 >> 2) & 3, u = c16 & 3;
+    const int col = blk * 256 + 64 * grp + 8 * u;  // low columns col..col+7, high col+32..col+39
+    const uint8_t* Wm = (m == 0 ? W0 : W1) + (int64_t)(e - e_begin) * expert_bytes + (int64_t)blk * BB;
+    const int sh = 16 * (grp & 1);
+    __shared__ int src[TPL];
+
+    for (int p0 = 0; p0 < n; p0 += TPL) {
+        const int np = n - p0 < TPL ? n - p0 : TPL;
+        __syncthreads();  // the previous pass's reads of src and red are done
+        if (tid < TPL) {
+            const int a = a0 + p0 + (tid < np ? tid : 0);
+            src[tid] = by_token ? ix.tok[a] : a;
+        }
+        __syncthreads();
+        const float* xr[TPL];
+#pragma unroll
+        for (int p = 0; p < TPL; ++p) xr[p] = X + (int64_t)src[p] * IN;
+        float acc[TPL][16], bias[TPL][2];
+#pragma unroll
+        for (int p = 0; p < TPL; ++p) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[p][j] = 0.0f;
+            bias[p][0] = bias[p][1] = 0.0f;
+        }
+        for (int i0 = r0 + rg; i0 < r1; i0 += RG * kLaneUnroll) {
+            uint4 hd[kLaneUnroll];
+            uint2 qw[kLaneUnroll], hw[kLaneUnroll];
+            float xv[kLaneUnroll][TPL];
+#pragma unroll
+            for (int r = 0; r < kLaneUnroll; ++r) {
+                const int i = i0 + r * RG;
+                if (i < r1) {
+                    const uint8_t* row = Wm + (int64_t)i * row_bytes;
+                    hd[r] = __ldg(reinterpret_cast<const uint4*>(row));
+                    qw[r] = __ldg(reinterpret_cast<const uint2*>(row + QOFF + 32 * grp + 8 * u));
+                    if constexpr (Q == kQ5_K) hw[r] = __ldg(reinterpret_cast<const uint2*>(row + 16 + 8 * u));
+#pragma unroll
+                    for (int p = 0; p < TPL; ++p) xv[r][p] = __ldg(xr[p] + i);
+                } else {
+                    hd[r] = make_uint4(0u, 0u, 0u, 0u);  // d = dmin = 0: contributes nothing
+                    qw[r] = make_uint2(0u, 0u);
+                    hw[r] = make_uint2(0u, 0u);
+#pragma unroll
+                    for (int p = 0; p < TPL; ++p) xv[r][p] = 0.0f;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kLaneUnroll; ++r) {
+                const float d = h2f(hd[r].x), dmin = h2f(hd[r].x >> 16);
+                uint32_t sl, shi, ml, mh;
+                scales_k4_packed(hd[r].y, hd[r].z, hd[r].w, sl, shi, ml, mh);
+                const uint32_t sw = (grp < 2 ? sl : shi) >> sh, mw = (grp < 2 ? ml : mh) >> sh;
+                const float ds0 = d * kUnit * (float)(sw & 63u), ds1 = d * kUnit * (float)((sw >> 8) & 63u);
+                const float dm0 = dmin * (float)(mw & 63u), dm1 = dmin * (float)((mw >> 8) & 63u);
+                float f[16];
+#pragma unroll
+                for (int w = 0; w < 2; ++w) {
+                    const uint32_t q = w ? qw[r].y : qw[r].x;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        uint32_t lo, hi;
+                        if constexpr (Q == kQ4_K) {
+                            // nibble to bits 19..22 under the exponent of 1.0
+                            lo = (19 - 8 * b) >= 0 ? q << (19 - 8 * b) : q >> (8 * b - 19);
+                            hi = (15 - 8 * b) >= 0 ? q << (15 - 8 * b) : q >> (8 * b - 15);
+                            lo = (lo & 0x00780000u) | 0x3F800000u;
+                            hi = (hi & 0x00780000u) | 0x3F800000u;
+                        } else {
+                            // nibble to bits 18..21, its high bit (qh bit 2 grp / 2 grp + 1 of byte 4w + b) to 22
+                            const uint32_t h = w ? hw[r].y : hw[r].x;
+                            const int hb = 8 * b + 2 * grp;
+                            lo = (18 - 8 * b) >= 0 ? q << (18 - 8 * b) : q >> (8 * b - 18);
+                            hi = (14 - 8 * b) >= 0 ? q << (14 - 8 * b) : q >> (8 * b - 14);
+                            const uint32_t hl = (22 - hb) >= 0 ? h << (22 - hb) : h >> (hb - 22);
+                            const uint32_t hh = (21 - hb) >= 0 ? h << (21 - hb) : h >> (hb - 21);
+                            lo = (lo & 0x003C0000u) | (hl & 0x00400000u) | 0x3F800000u;
+                            hi = (hi & 0x003C0000u) | (hh & 0x00400000u) | 0x3F800000u;
+                        }
+                        f[4 * w + b] = __uint_as_float(lo);
+                        f[8 + 4 * w + b] = __uint_as_float(hi);
+                    }
+                }
+#pragma unroll
+                for (int p = 0; p < TPL; ++p) {
+                    const float A0 = xv[r][p] * ds0, A1 = xv[r][p] * ds1;
+                    bias[p][0] += fmaf(xv[r][p], dm0, A0);
+                    bias[p][1] += fmaf(xv[r][p], dm1, A1);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        acc[p][j] = fmaf(A0, f[j], acc[p][j]);
+                        acc[p][8 + j] = fmaf(A1, f[8 + j], acc[p][8 + j]);
+                    }
+                }
+            }
+        }
+        // this thread's 16 columns, then the row groups summed in a fixed order
+#pragma unroll
+        for (int p = 0; p < TPL; ++p) {
+            float* rr = red + ((int64_t)rg * TPL + p) * OUT;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                rr[col + j] = acc[p][j] - bias[p][0];
+                rr[col + 32 + j] = acc[p][8 + j] - bias[p][1];
+            }
+        }
+        __syncthreads();
+        for (int q = tid; q < np * OUT; q += kMoeThreads) {
+            const int p = q / OUT, c = q - p * OUT;
+            float v = 0.0f;
+            for (int g = 0; g < RG; ++g) v += red[((int64_t)g * TPL + p) * OUT + c];
+            P[(((int64_t)rc * nmat + m) * A_cap + a0 + p0 + p) * OUT + c] = v;
+        }
+    }
+}
+
+template <uint32_t Q>
+int launch_lane_q(int TPL, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN,
+                  int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
+                  int slots, int RC, cudaStream_t s) {
+    const int RG = kMoeThreads / (OUT / 16);
+    const size_t smem = (size_t)RG * TPL * OUT * sizeof(float);
+    const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
+    if (TPL == 1) {
+        if (cudaFuncSetAttribute(moe_lane_kernel<Q, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return -1;
+        launch_dep(moe_lane_kernel<Q, 1>, grid, dim3(kMoeThreads), smem, s, W0, W1, row_bytes, expert_bytes, IN, OUT,
+                   X, by_token, ix, e_begin, A_cap, P);
+    } else {
+        if (cudaFuncSetAttribute(moe_lane_kernel<Q, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return -1;
+        launch_dep(moe_lane_kernel<Q, 2>, grid, dim3(kMoeThreads), smem, s, W0, W1, row_bytes, expert_bytes, IN, OUT,
+                   X, by_token, ix, e_begin, A_cap, P);
+    }
     return 0;
 }
 
@@ -948,8 +1151,8 @@ int launch_mma_t(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_
             cudaSuccess)
         return -1;
     const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
-    moe_mma_kernel<Q, MPW><<<grid, kMoeThreads, smem, s>>>(W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix,
-                                                          e_begin, A_cap, P);
+    launch_dep(moe_mma_kernel<Q, MPW>, grid, dim3(kMoeThreads), smem, s, W0, W1, row_bytes, expert_bytes, IN, OUT, X,
+               by_token, ix, e_begin, A_cap, P);
     return 0;
 }
 
@@ -974,6 +1177,15 @@ int launch_stream(uint32_t q, int TP, const uint8_t* W0, const uint8_t* W1, int6
                   int IN, int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
                   int slots, int RC, cudaStream_t s) {
     if (OUT % 256 != 0 || OUT / 16 > kMoeThreads) return -1;
+    // one or two tokens per pass, Q4_K / Q5_K: the CUDA-core few-token form
+    // (OUT / 16 threads per row must divide the CTA)
+    if (TP <= 2 && (q == kQ4_K || q == kQ5_K) && row_bytes % 16 == 0 && kMoeThreads % (OUT / 16) == 0) {
+        if (q == kQ4_K)
+            return launch_lane_q<kQ4_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap,
+                                        P, slots, RC, s);
+        return launch_lane_q<kQ5_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
+                                    slots, RC, s);
+    }
     // Q4_K / Q5_K with up to 2048 output columns: the tensor-core form
     const int mpw = OUT / 128;
     if ((q == kQ4_K || q == kQ5_K) && IN % 16 == 0 && row_bytes % 16 == 0 &&
@@ -1002,14 +1214,20 @@ int launch_stream(uint32_t q, int TP, const uint8_t* W0, const uint8_t* W1, int6
 bool moe_expert_quant_supported(uint32_t q) { return q == kQ4_K || q == kQ5_K || q == kQ6_K || q == kQ8_0; }
 
 // Row chunks for a streamed pass over `mats` matrices: about four CTAs per SM
-// in all, at least 32 rows per chunk (at most 8 chunks for up to 8 tokens).
+// in all. Up to 8 tokens every chunk adds one partial per output to the
+// reductions, which then dominate the tensor-core pass: at most 8 chunks (at
+// least 32 rows each). The few-token pass (1 or 2 tokens) is bound by the
+// bytes each CTA keeps in flight instead: up to 64 chunks of at least 16 rows.
 int moe_row_chunks(int slots, int mats, int IN, int sm_count, int T) {
     const int ctas = slots * mats;
     int rc = (4 * (sm_count > 0 ? sm_count : 148) + ctas - 1) / ctas;
-    // few tokens: every chunk adds one partial per output to the reductions,
-    // which then dominate; 8 chunks still give 64+ CTAs for top-8 routing
     int maxrc = IN / 32 > 0 ? IN / 32 : 1;
-    if (T <= 8 && maxrc > 8) maxrc = 8;
+    if (T <= 2) {
+        maxrc = IN / 16 > 0 ? IN / 16 : 1;
+        if (maxrc > 64) maxrc = 64;
+    } else if (T <= 8 && maxrc > 8) {
+        maxrc = 8;
+    }
     if (rc > maxrc) rc = maxrc;
     return rc < 1 ? 1 : rc;
 }
@@ -1046,6 +1264,7 @@ MoeWork moe_work_layout(const MoePlan& p) {
     }
     const int64_t kmax = p.n_embd > p.n_ff_s ? p.n_embd : p.n_ff_s;
     w.xfrag = take(gemv_mma_work_bytes(kmax, p.T));
+    w.xfrag_s = p.shared ? take(gemv_mma_work_bytes(kmax, p.T)) : -1;  // the shared expert's, on its own stream
     w.bytes = o;
     return w;
 }
@@ -1060,11 +1279,39 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     const int A = p.T * p.k;
 
     // dense projections (router, shared expert): tensor-core GEMV where it applies
-    auto dense = [&](const MoeTensor& Wt, int64_t rows, int64_t cols, const float* X, float* Y) -> int {
+    auto dense_on = [&](cudaStream_t st, int64_t xf, const MoeTensor& Wt, int64_t rows, int64_t cols, const float* X,
+                        float* Y) -> int {
         GemvArgs g{Wt.W, Wt.row_bytes, rows, cols, X, Y, p.T, p.sm_count, Wt.tmap};
-        if (gemv_mma_supported(Wt.quant, g)) return launch_gemv_mma(Wt.quant, g, base + w.xfrag, L.err, s);
-        return launch_gemv(Wt.quant, g, s);
+        if (gemv_mma_supported(Wt.quant, g)) return launch_gemv_mma(Wt.quant, g, base + xf, L.err, st);
+        return launch_gemv(Wt.quant, g, st);
     };
+    auto dense = [&](const MoeTensor& Wt, int64_t rows, int64_t cols, const float* X, float* Y) -> int {
+        return dense_on(s, w.xfrag, Wt, rows, cols, X, Y);
+    };
+
+    // shared expert (moe.rs:129-142): independent of the routing until the
+    // combine, so it runs on the auxiliary stream beside the routed path
+    const float* Ds = nullptr;
+    const float* sg = nullptr;
+    const bool fork = p.shared && L.aux && L.fork && L.join;
+    if (p.shared) {
+        cudaStream_t ss = s;
+        if (fork) {
+            cudaEventRecord(L.fork, s);
+            cudaStreamWaitEvent(L.aux, L.fork, 0);
+            ss = L.aux;
+        }
+        if (dense_on(ss, w.xfrag_s, L.gate_s, p.n_ff_s, p.n_embd, L.x, F(w.gs)) ||
+            dense_on(ss, w.xfrag_s, L.up_s, p.n_ff_s, p.n_embd, L.x, F(w.us)) ||
+            dense_on(ss, w.xfrag_s, L.gate_inp_s, 1, p.n_embd, L.x, F(w.gi)))
+            return -4;
+        moe_shared_act_kernel<<<grid_for((int64_t)p.T * p.n_ff_s, p.sm_count), 256, 0, ss>>>(
+            F(w.gs), F(w.us), F(w.gi), p.T, p.n_ff_s, F(w.hs), F(w.sg));
+        if (dense_on(ss, w.xfrag_s, L.down_s, p.n_embd, p.n_ff_s, F(w.hs), F(w.ds))) return -5;
+        if (fork) cudaEventRecord(L.join, L.aux);
+        Ds = F(w.ds);
+        sg = F(w.sg);
+    }
 
     // route
     const float* logits = L.logits;
@@ -1074,41 +1321,34 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
         if (dense(L.router, p.E, p.n_embd, F(w.xb), F(w.logits))) return -1;
         logits = F(w.logits);
     }
-    moe_route_kernel<<<(p.T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32,
-                       (size_t)kRouteWarps * p.E * sizeof(float), s>>>(logits, p.T, p.E, p.k, I(w.ids), F(w.wts));
+    launch_dep(moe_route_kernel, dim3((p.T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32),
+               (size_t)kRouteWarps * p.E * sizeof(float), s, logits, p.T, p.E, p.k, I(w.ids), F(w.wts));
     const bool staged = (int64_t)p.T * p.k * 4 <= 32 * 1024;
-    moe_assign_kernel<<<1, kAssignThreads, staged ? (size_t)p.T * p.k * 4 : 0, s>>>(I(w.ids), p.T, p.k, p.E,
-                                                                                    p.e_begin, p.e_end, staged, ix);
+    launch_dep(moe_assign_kernel, dim3(1), dim3(kAssignThreads), staged ? (size_t)p.T * p.k * 4 : 0, s, I(w.ids),
+               p.T, p.k, p.E, p.e_begin, p.e_end, staged, ix);
 
     // routed experts
     const int slots = p.slots;
-    const int TP = p.T == 1 ? 1 : 4;
+    const int TP = p.T <= 2 ? p.T : 4;  // tokens per pass: 1 or 2 take the few-token form
     if (launch_stream(L.gate.quant, TP, L.gate.W, L.up.W, L.gate.row_bytes, L.gate.expert_bytes, p.n_embd, p.n_ff,
                       L.x, true, ix, p.e_begin, A, F(w.pgu), slots, p.rc_gu, s))
         return -2;
-    moe_swiglu_kernel<<<grid_for((int64_t)A * p.n_ff, p.sm_count), 256, 0, s>>>(F(w.pgu), p.rc_gu, A, p.n_ff,
-                                                                                 ix.n_assign, F(w.h));
+    launch_dep(moe_swiglu_kernel, dim3(grid_for((int64_t)A * p.n_ff, p.sm_count)), dim3(256), 0, s, F(w.pgu), p.rc_gu,
+               A, p.n_ff, ix.n_assign, F(w.h));
     if (launch_stream(L.down.quant, TP, L.down.W, nullptr, L.down.row_bytes, L.down.expert_bytes, p.n_ff, p.n_embd,
                       F(w.h), false, ix, p.e_begin, A, F(w.pd), slots, p.rc_d, s))
         return -3;
 
-    // shared expert (moe.rs:129-142)
-    const float* Ds = nullptr;
-    const float* sg = nullptr;
-    if (p.shared) {
-        if (dense(L.gate_s, p.n_ff_s, p.n_embd, L.x, F(w.gs)) || dense(L.up_s, p.n_ff_s, p.n_embd, L.x, F(w.us)) ||
-            dense(L.gate_inp_s, 1, p.n_embd, L.x, F(w.gi)))
-            return -4;
-        moe_shared_act_kernel<<<grid_for((int64_t)p.T * p.n_ff_s, p.sm_count), 256, 0, s>>>(
-            F(w.gs), F(w.us), F(w.gi), p.T, p.n_ff_s, F(w.hs), F(w.sg));
-        if (dense(L.down_s, p.n_embd, p.n_ff_s, F(w.hs), F(w.ds))) return -5;
-        Ds = F(w.ds);
-        sg = F(w.sg);
-    }
+    if (fork) cudaStreamWaitEvent(s, L.join, 0);
     int lanes = 1;
     while (lanes < p.k) lanes <<= 1;
-    moe_combine_kernel<<<grid_for((int64_t)p.T * p.n_embd * lanes, p.sm_count), 256, 0, s>>>(
-        F(w.pd), p.rc_d, A, p.n_embd, I(w.pos), F(w.wts), p.T, p.k, lanes, Ds, sg, L.out);
+    const unsigned cgrid = (unsigned)grid_for((int64_t)p.T * p.n_embd * lanes, p.sm_count);
+    if (fork)  // after the join: a full dependency on both streams
+        moe_combine_kernel<<<cgrid, 256, 0, s>>>(F(w.pd), p.rc_d, A, p.n_embd, I(w.pos), F(w.wts), p.T, p.k, lanes, Ds,
+                                                 sg, L.out);
+    else
+        launch_dep(moe_combine_kernel, dim3(cgrid), dim3(256), 0, s, F(w.pd), p.rc_d, A, p.n_embd, I(w.pos), F(w.wts),
+                   p.T, p.k, lanes, Ds, sg, L.out);
     if (L.ids_out) cudaMemcpyAsync(L.ids_out, I(w.ids), (size_t)A * 4, cudaMemcpyDeviceToDevice, s);
     if (L.wts_out) cudaMemcpyAsync(L.wts_out, F(w.wts), (size_t)A * 4, cudaMemcpyDeviceToDevice, s);
     return 0;

@@ -28,7 +28,8 @@ struct MoePlan {
 
 // Byte offsets of the workspace arrays.
 struct MoeWork {
-    int64_t ids, wts, pos, tok, cnt, off, active, counters, logits, xb, pgu, h, pd, gs, us, hs, gi, sg, ds, xfrag;
+    int64_t ids, wts, pos, tok, cnt, off, active, counters, logits, xb, pgu, h, pd, gs, us, hs, gi, sg, ds, xfrag,
+        xfrag_s;
     int64_t bytes;
 };
 
@@ -51,6 +52,10 @@ struct MoeLaunch {
     float* wts_out;
     int* err;                         // set by a kernel whose bounded wait expired
     MoeTensor router, gate, up, down, gate_s, up_s, down_s, gate_inp_s;
+    // optional: the shared expert runs on `aux` (fork recorded on the caller's
+    // stream, join waited on before the combine); null runs it in line
+    cudaStream_t aux = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 bool moe_expert_quant_supported(uint32_t q);

@@ -102,6 +102,9 @@ int moe_enqueue(strata_ctx* ctx, const strata_moe* L, const float* x, const floa
     ml.up_s = tensor_of(d.up_shexp);
     ml.down_s = tensor_of(d.down_shexp);
     ml.gate_inp_s = tensor_of(d.gate_inp_shexp);
+    ml.aux = ctx->aux;
+    ml.fork = ctx->fork;
+    ml.join = ctx->join;
     int k = launch_moe_layer(ml, s);
     if (k) return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "moe: no kernel for a tensor's quant type (%d)", k);
     return check_launch(ctx, "moe layer kernels");
@@ -156,6 +159,19 @@ int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe
         if ((rc = check_dense(ctx, d->up_shexp, d->n_ff_shexp, d->n_embd, "up_shexp"))) return rc;
         if ((rc = check_dense(ctx, d->down_shexp, d->n_embd, d->n_ff_shexp, "down_shexp"))) return rc;
         if ((rc = check_dense(ctx, d->gate_inp_shexp, 1, d->n_embd, "gate_inp_shexp"))) return rc;
+    }
+    if (!ctx->aux) {  // the shared expert's stream; without it the layer runs in line
+        cudaSetDevice(ctx->device);
+        if (cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            if (ctx->fork) cudaEventDestroy(ctx->fork);
+            if (ctx->join) cudaEventDestroy(ctx->join);
+            if (ctx->aux) cudaStreamDestroy(ctx->aux);
+            ctx->aux = nullptr;
+            ctx->fork = ctx->join = nullptr;
+        }
     }
     strata_moe* L = new strata_moe();
     L->ctx = ctx;

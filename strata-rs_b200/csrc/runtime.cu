@@ -172,6 +172,9 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host})
         if (b->ptr) cudaFreeHost(b->ptr);
     cudaEventDestroy(ctx->done);
+    if (ctx->fork) cudaEventDestroy(ctx->fork);
+    if (ctx->join) cudaEventDestroy(ctx->join);
+    if (ctx->aux) cudaStreamDestroy(ctx->aux);
     cudaStreamDestroy(ctx->stream);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;

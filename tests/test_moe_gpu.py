@@ -73,7 +73,7 @@ def check_routing(ids, wts, want_ids, want_w):
     assert d.max() <= 2, d.max()
 
 
-@pytest.mark.parametrize("T", [1, 3, 17])
+@pytest.mark.parametrize("T", [1, 2, 3, 17])
 @pytest.mark.parametrize("qe", [Q4_K, Q5_K, Q6_K, Q8_0])
 def test_moe_small_from_logits(ctx, T, qe, threads):
     dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
