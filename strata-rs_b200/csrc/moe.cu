@@ -63,19 +63,11 @@ void launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
 
 // ------------------------------------------------------------------ routing
 
-// One warp per token (kRouteWarps tokens per CTA); the token's E
-// probabilities live in shared memory.
-constexpr int kRouteWarps = 4;
-__global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float* __restrict__ logits, int T, int E,
-                                                                     int k, int* __restrict__ ids,
-                                                                     float* __restrict__ wts) {
-    pdl_entry();
-    extern __shared__ float sp_all[];  // kRouteWarps x E
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * kRouteWarps + warp;
-    if (t >= T) return;
-    float* sp = sp_all + warp * E;
-    const float* lg = logits + (int64_t)t * E;
+// Routing of one token by one warp (moe.rs:48-90): the E probabilities in
+// `sp` (shared memory), ids ascending and renormalised weights to ids/wts
+// (k each) and, when given, the ids to ids_s too.
+__device__ void route_token(const float* __restrict__ lg, int E, int k, float* sp, int lane, int* __restrict__ ids,
+                            float* __restrict__ wts, int* ids_s) {
     float mx = -INFINITY;
     for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lg[i]);
 #pragma unroll
@@ -142,9 +134,26 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float
     for (int j = 0; j < kk; ++j) ws += (double)__shfl_sync(0xFFFFFFFFu, p_q, j);
     const double sden = ws > 0x1p-14 ? ws : 0x1p-14;
     if (lane < k) {
-        ids[(int64_t)t * k + lane] = lane < kk ? id_q : -1;
-        wts[(int64_t)t * k + lane] = lane < kk ? (float)((double)p_q / sden) : 0.0f;
+        const int id = lane < kk ? id_q : -1;
+        ids[lane] = id;
+        wts[lane] = lane < kk ? (float)((double)p_q / sden) : 0.0f;
+        if (ids_s) ids_s[lane] = id;
     }
+}
+
+// One warp per token (kRouteWarps tokens per CTA); the token's E
+// probabilities live in shared memory.
+constexpr int kRouteWarps = 4;
+__global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float* __restrict__ logits, int T, int E,
+                                                                     int k, int* __restrict__ ids,
+                                                                     float* __restrict__ wts) {
+    pdl_entry();
+    extern __shared__ float sp_all[];  // kRouteWarps x E
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kRouteWarps + warp;
+    if (t >= T) return;
+    route_token(logits + (int64_t)t * E, E, k, sp_all + warp * E, lane, ids + (int64_t)t * k, wts + (int64_t)t * k,
+                nullptr);
 }
 
 // ------------------------------------------------------------------ assignment
@@ -153,26 +162,19 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float
 // shared-memory atomics (order-free); offsets and the active list from scans
 // over the experts in ascending order; an entry's rank within its expert is
 // the number of earlier entries (earlier tokens) routed to the same expert,
-// so every list is in token order whatever the thread schedule. The routing
-// ids are staged in shared memory when they fit (staged = true).
+// so every list is in token order whatever the thread schedule.
 constexpr int kAssignThreads = 1024;
-__global__ void __launch_bounds__(kAssignThreads)
-moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begin, int e_end, bool staged,
-                  MoeIndex ix) {
-    pdl_entry();
-    extern __shared__ int ids_s[];
+__device__ void assign_block(const int* ids, int T, int k, int E, int e_begin, int e_end, MoeIndex ix) {
     __shared__ int cnt_s[1024], scan[1024];
     const int tid = threadIdx.x;
     const int64_t TK = (int64_t)T * k;
     for (int e = tid; e < 1024; e += blockDim.x) cnt_s[e] = 0;
     __syncthreads();
     for (int64_t i = tid; i < TK; i += blockDim.x) {
-        const int e = ids_g[i];
-        if (staged) ids_s[i] = e;
+        const int e = ids[i];
         if (e >= e_begin && e < e_end) atomicAdd(&cnt_s[e], 1);
     }
     __syncthreads();
-    const int* ids = staged ? ids_s : ids_g;
     // exclusive scans over e ascending: counts -> offsets, active flags -> slots
     const int c = tid < E ? cnt_s[tid] : 0;
     scan[tid] = c;
@@ -219,6 +221,36 @@ moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begi
         ix.tok[at] = (int)(i / k);
         ix.pos[i] = at;
     }
+}
+
+// The routing ids are staged in shared memory when they fit (staged = true).
+__global__ void __launch_bounds__(kAssignThreads)
+moe_assign_kernel(const int* __restrict__ ids_g, int T, int k, int E, int e_begin, int e_end, bool staged,
+                  MoeIndex ix) {
+    pdl_entry();
+    extern __shared__ int ids_s[];
+    if (staged) {
+        for (int64_t i = threadIdx.x; i < (int64_t)T * k; i += blockDim.x) ids_s[i] = ids_g[i];
+        __syncthreads();
+    }
+    assign_block(staged ? ids_s : ids_g, T, k, E, e_begin, e_end, ix);
+}
+
+// Up to 32 tokens: routing (a warp per token) and assignment in one CTA, the
+// ids handed over in shared memory: one launch less on the decode path.
+constexpr int kFusedRouteTokens = 32;
+__global__ void __launch_bounds__(kAssignThreads)
+moe_route_assign_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
+                        float* __restrict__ wts, int e_begin, int e_end, MoeIndex ix) {
+    pdl_entry();
+    extern __shared__ float dyn[];  // T x E probabilities, then T x k ids
+    int* ids_s = reinterpret_cast<int*>(dyn + (int64_t)T * E);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < T)
+        route_token(logits + (int64_t)warp * E, E, k, dyn + (int64_t)warp * E, lane, ids + (int64_t)warp * k,
+                    wts + (int64_t)warp * k, ids_s + warp * k);
+    __syncthreads();
+    assign_block(ids_s, T, k, E, e_begin, e_end, ix);
 }
 
 // ------------------------------------------------------------------ grouped expert GEMV
@@ -971,12 +1003,12 @@ template <uint32_t Q, int TPL>
 __global__ void __launch_bounds__(kMoeThreads)
 moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
                 int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
-                int e_begin, int A_cap, float* __restrict__ P) {
+                int e_begin, int A_cap, float* __restrict__ P, const float* __restrict__ PG, int RCG) {
     pdl_entry();
     constexpr int BB = block_bytes(Q);
     constexpr int QOFF = (Q == kQ4_K) ? 16 : 48;
     constexpr float kUnit = (Q == kQ4_K) ? 16.0f : 32.0f;  // f = 1 + q / kUnit
-    extern __shared__ float red[];  // [RG][TPL][OUT]
+    extern __shared__ float red[];  // [RG][TPL][OUT], then (PG) the activations [TPL][rows]
     const int nmat = W1 ? 2 : 1;
     const int slot = blockIdx.x / nmat, m = blockIdx.x % nmat;
     if (slot >= ix.n_active[0]) return;
@@ -1003,6 +1035,26 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
         const float* xr[TPL];
 #pragma unroll
         for (int p = 0; p < TPL; ++p) xr[p] = X + (int64_t)src[p] * IN;
+        // down pass fused with the SwiGLU: this chunk's activations
+        // silu(sum gate partials) * (sum up partials), summed in chunk order
+        const int rows = r1 - r0;
+        float* xs = red + (int64_t)RG * TPL * OUT;
+        if (PG) {
+            for (int q = tid; q < TPL * rows; q += kMoeThreads) {
+                const int p = q / rows, i = r0 + (q - p * rows);
+                float v = 0.0f;
+                if (p < np) {
+                    float g = 0.0f, uu = 0.0f;
+                    for (int c = 0; c < RCG; ++c) {
+                        g += PG[(((int64_t)c * 2 + 0) * A_cap + src[p]) * IN + i];
+                        uu += PG[(((int64_t)c * 2 + 1) * A_cap + src[p]) * IN + i];
+                    }
+                    v = silu_f32(g) * uu;
+                }
+                xs[q] = v;
+            }
+            __syncthreads();
+        }
         float acc[TPL][16], bias[TPL][2];
 #pragma unroll
         for (int p = 0; p < TPL; ++p) {
@@ -1023,7 +1075,7 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
                     qw[r] = __ldg(reinterpret_cast<const uint2*>(row + QOFF + 32 * grp + 8 * u));
                     if constexpr (Q == kQ5_K) hw[r] = __ldg(reinterpret_cast<const uint2*>(row + 16 + 8 * u));
 #pragma unroll
-                    for (int p = 0; p < TPL; ++p) xv[r][p] = __ldg(xr[p] + i);
+                    for (int p = 0; p < TPL; ++p) xv[r][p] = PG ? xs[p * rows + (i - r0)] : __ldg(xr[p] + i);
                 } else {
                     hd[r] = make_uint4(0u, 0u, 0u, 0u);  // d = dmin = 0: contributes nothing
                     qw[r] = make_uint2(0u, 0u);
@@ -1104,22 +1156,23 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
 template <uint32_t Q>
 int launch_lane_q(int TPL, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN,
                   int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
-                  int slots, int RC, cudaStream_t s) {
+                  int slots, int RC, cudaStream_t s, const float* PG, int RCG) {
     const int RG = kMoeThreads / (OUT / 16);
-    const size_t smem = (size_t)RG * TPL * OUT * sizeof(float);
+    const int max_rows = (IN + RC - 1) / RC;
+    const size_t smem = ((size_t)RG * TPL * OUT + (PG ? (size_t)TPL * max_rows : 0)) * sizeof(float);
     const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
     if (TPL == 1) {
         if (cudaFuncSetAttribute(moe_lane_kernel<Q, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
             return -1;
         launch_dep(moe_lane_kernel<Q, 1>, grid, dim3(kMoeThreads), smem, s, W0, W1, row_bytes, expert_bytes, IN, OUT,
-                   X, by_token, ix, e_begin, A_cap, P);
+                   X, by_token, ix, e_begin, A_cap, P, PG, RCG);
     } else {
         if (cudaFuncSetAttribute(moe_lane_kernel<Q, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
             return -1;
         launch_dep(moe_lane_kernel<Q, 2>, grid, dim3(kMoeThreads), smem, s, W0, W1, row_bytes, expert_bytes, IN, OUT,
-                   X, by_token, ix, e_begin, A_cap, P);
+                   X, by_token, ix, e_begin, A_cap, P, PG, RCG);
     }
     return 0;
 }
@@ -1173,19 +1226,27 @@ int launch_mma_q(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_
     }
 }
 
+// Whether a pass takes the few-token form: one or two tokens per pass, Q4_K /
+// Q5_K, OUT / 16 threads per row dividing the CTA.
+bool lane_pass(uint32_t q, int TP, int OUT, int64_t row_bytes) {
+    return TP <= 2 && (q == kQ4_K || q == kQ5_K) && row_bytes % 16 == 0 && OUT % 256 == 0 &&
+           OUT / 16 <= kMoeThreads && kMoeThreads % (OUT / 16) == 0;
+}
+
+// PG (few-token form only): the down pass computes its activations from the
+// gate/up partials (RCG chunks) instead of reading X.
 int launch_stream(uint32_t q, int TP, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes,
                   int IN, int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
-                  int slots, int RC, cudaStream_t s) {
+                  int slots, int RC, cudaStream_t s, const float* PG = nullptr, int RCG = 0) {
     if (OUT % 256 != 0 || OUT / 16 > kMoeThreads) return -1;
-    // one or two tokens per pass, Q4_K / Q5_K: the CUDA-core few-token form
-    // (OUT / 16 threads per row must divide the CTA)
-    if (TP <= 2 && (q == kQ4_K || q == kQ5_K) && row_bytes % 16 == 0 && kMoeThreads % (OUT / 16) == 0) {
+    if (lane_pass(q, TP, OUT, row_bytes)) {
         if (q == kQ4_K)
             return launch_lane_q<kQ4_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap,
-                                        P, slots, RC, s);
+                                        P, slots, RC, s, PG, RCG);
         return launch_lane_q<kQ5_K>(TP, W0, W1, row_bytes, expert_bytes, IN, OUT, X, by_token, ix, e_begin, A_cap, P,
-                                    slots, RC, s);
+                                    slots, RC, s, PG, RCG);
     }
+    if (PG) return -1;
     // Q4_K / Q5_K with up to 2048 output columns: the tensor-core form
     const int mpw = OUT / 128;
     if ((q == kQ4_K || q == kQ5_K) && IN % 16 == 0 && row_bytes % 16 == 0 &&
@@ -1321,11 +1382,17 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
         if (dense(L.router, p.E, p.n_embd, F(w.xb), F(w.logits))) return -1;
         logits = F(w.logits);
     }
-    launch_dep(moe_route_kernel, dim3((p.T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32),
-               (size_t)kRouteWarps * p.E * sizeof(float), s, logits, p.T, p.E, p.k, I(w.ids), F(w.wts));
-    const bool staged = (int64_t)p.T * p.k * 4 <= 32 * 1024;
-    launch_dep(moe_assign_kernel, dim3(1), dim3(kAssignThreads), staged ? (size_t)p.T * p.k * 4 : 0, s, I(w.ids),
-               p.T, p.k, p.E, p.e_begin, p.e_end, staged, ix);
+    const size_t fused_smem = ((size_t)p.T * p.E + (size_t)p.T * p.k) * 4;
+    if (p.T <= kFusedRouteTokens && fused_smem <= 48 * 1024) {
+        launch_dep(moe_route_assign_kernel, dim3(1), dim3(kAssignThreads), fused_smem, s, logits, p.T, p.E, p.k,
+                   I(w.ids), F(w.wts), p.e_begin, p.e_end, ix);
+    } else {
+        launch_dep(moe_route_kernel, dim3((p.T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32),
+                   (size_t)kRouteWarps * p.E * sizeof(float), s, logits, p.T, p.E, p.k, I(w.ids), F(w.wts));
+        const bool staged = (int64_t)p.T * p.k * 4 <= 32 * 1024;
+        launch_dep(moe_assign_kernel, dim3(1), dim3(kAssignThreads), staged ? (size_t)p.T * p.k * 4 : 0, s, I(w.ids),
+                   p.T, p.k, p.E, p.e_begin, p.e_end, staged, ix);
+    }
 
     // routed experts
     const int slots = p.slots;
@@ -1333,10 +1400,14 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     if (launch_stream(L.gate.quant, TP, L.gate.W, L.up.W, L.gate.row_bytes, L.gate.expert_bytes, p.n_embd, p.n_ff,
                       L.x, true, ix, p.e_begin, A, F(w.pgu), slots, p.rc_gu, s))
         return -2;
-    launch_dep(moe_swiglu_kernel, dim3(grid_for((int64_t)A * p.n_ff, p.sm_count)), dim3(256), 0, s, F(w.pgu), p.rc_gu,
-               A, p.n_ff, ix.n_assign, F(w.h));
+    // the few-token down pass computes the SwiGLU itself from the gate/up partials
+    const bool fuse_act = lane_pass(L.down.quant, TP, p.n_embd, L.down.row_bytes);
+    if (!fuse_act)
+        launch_dep(moe_swiglu_kernel, dim3(grid_for((int64_t)A * p.n_ff, p.sm_count)), dim3(256), 0, s, F(w.pgu),
+                   p.rc_gu, A, p.n_ff, ix.n_assign, F(w.h));
     if (launch_stream(L.down.quant, TP, L.down.W, nullptr, L.down.row_bytes, L.down.expert_bytes, p.n_ff, p.n_embd,
-                      F(w.h), false, ix, p.e_begin, A, F(w.pd), slots, p.rc_d, s))
+                      F(w.h), false, ix, p.e_begin, A, F(w.pd), slots, p.rc_d, s, fuse_act ? F(w.pgu) : nullptr,
+                      p.rc_gu))
         return -3;
 
     if (fork) cudaStreamWaitEvent(s, L.join, 0);
