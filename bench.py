@@ -335,19 +335,34 @@ def bench_moe(ctx, torch, stream, world: int, rank: int, dist, with_e2e: bool) -
             call(it[0])
             it[0] += 1
         graph_us = None
-        if world == 1:
-            # launch-bound at one token: also the layer replayed from a CUDA graph
-            with torch.cuda.stream(stream):
-                call(0)
-            stream.synchronize()
-            n_cap = R * len(layers)
-            g = torch.cuda.CUDAGraph()
+        # launch-bound at one token: also the layer replayed from a CUDA graph
+        # (N > 1: every rank captures, and replays only if every rank could)
+        with torch.cuda.stream(stream):
+            call(0)
+        stream.synchronize()
+        n_cap = R * len(layers)
+        g = torch.cuda.CUDAGraph()
+        try:
             with torch.cuda.graph(g, stream=stream):
                 for i in range(n_cap):
                     call(i)
+            captured = 1
+        except Exception as exc:  # noqa: BLE001 - stream timing only
+            print(f"moe graph capture unavailable ({exc})", file=sys.stderr)
+            captured = 0
+        if dist:
+            ok = torch.tensor([captured], device="cuda")
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            captured = int(ok.item())
+        if captured:
             gms = timed(torch, stream, g.replay, 5) / n_cap
+            if dist:
+                t = torch.tensor([gms], device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                gms = float(t.item())
             graph_us = round(gms * 1e3, 2)
-            del g
+        del g
+        torch.cuda.synchronize()
         ms = timed(torch, stream, fn, max(R * len(layers), 48))
         if dist:
             t = torch.tensor([ms], device="cuda")

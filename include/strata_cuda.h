@@ -253,8 +253,11 @@ int strata_cuda_gemm_sharded_dev(strata_ctx *ctx, const strata_weight *w_shard, 
  * default) takes PEER where it applies -- peer memory available on every
  * rank, a Q4_K / Q5_K shard on the tensor-core path with a multiple of 4 rows,
  * y 16-byte aligned, batch x OUT within the exchange capacity -- and NCCL
- * otherwise. Every rank must set the same mode (the ranks of one call must
- * take the same path). */
+ * otherwise. The mode also picks the expert-parallel MoE layer's all-reduce:
+ * PEER sums the ranks' partial outputs over the same exchange buffers (every
+ * rank adds the G partials in rank order, so all ranks get the same bits),
+ * NCCL calls ncclAllReduce. Every rank must set the same mode (the ranks of
+ * one call must take the same path). */
 enum { STRATA_GATHER_AUTO = 0, STRATA_GATHER_NCCL = 1, STRATA_GATHER_PEER = 2 };
 int strata_cuda_comm_set_gather(strata_ctx *ctx, int mode);
 /* available: 1 if every rank opened every peer's exchange buffer;

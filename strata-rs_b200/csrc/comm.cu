@@ -130,6 +130,11 @@ struct CommState {
     char* xbuf = nullptr;                // this rank's exchange buffer
     char* peer_base[kMaxPeers] = {};     // every rank's exchange buffer as mapped here
     PeerPending pending;                 // inside a collective group
+    // peer collectives (and the GEMVs that write the exchange buffer) run in
+    // issue order on the device: a call on another stream than the previous
+    // one waits for it through `order`
+    cudaStream_t peer_stream = nullptr;
+    cudaEvent_t order = nullptr;
 };
 
 namespace {
@@ -154,6 +159,9 @@ void peer_release(strata_ctx* ctx, bool barrier) {
         if (q != c->rank && c->peer_base[q]) cudaIpcCloseMemHandle(c->peer_base[q]);
     cudaFree(c->xbuf);
     c->xbuf = nullptr;
+    if (c->order) cudaEventDestroy(c->order);
+    c->order = nullptr;
+    c->peer_stream = nullptr;
     c->peer_ok = false;
     for (auto& p : c->peer_base) p = nullptr;
 }
@@ -278,6 +286,7 @@ int peer_setup(strata_ctx* ctx) {
         ok = ok && cudaMemsetAsync(c->xbuf, 0, kPeerCtlBytes, ctx->stream) == cudaSuccess;
         ok = ok && cudaIpcGetMemHandle(&mine.handle, c->xbuf) == cudaSuccess;
         ok = ok && cudaDeviceGetPCIBusId(mine.bus_id, sizeof(mine.bus_id), ctx->device) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&c->order, cudaEventDisableTiming) == cudaSuccess;
     }
     cudaGetLastError();
     mine.ok = ok;
@@ -346,27 +355,68 @@ __device__ bool wait_count(unsigned long long* ctr, unsigned long long target, u
     return false;
 }
 
-// The all-gather of the pending segments, one cooperative launch (all CTAs
-// resident: a CTA waits on signals that other ranks send only after all of
-// this rank's CTAs pushed).
+// The synchronisation every peer collective shares, run by all threads of
+// every CTA of a cooperative launch (all CTAs resident: a CTA waits on
+// signals that other ranks send only after all of this rank's CTAs arrived):
+// every CTA releases its stores (system scope) and counts itself; the last
+// one adds 1 to every other rank's arrival counter of half h; then each CTA
+// waits (bounded) for the G - 1 other ranks' signals on half h. False (and
+// *err set) if the wait expired.
+__device__ bool peer_signal_wait(PeerCtl* ctl, char* const* base, int me, int G, unsigned int h, uint64_t timeout_ns,
+                                 int* err) {
+    __shared__ int ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        if (atomicAdd(&ctl->pushed, 1u) == gridDim.x - 1) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            for (int q = 0; q < G; ++q)
+                if (q != me) atomicAdd_system(&ctl_of(base[q])->arrivals[h], 1ull);
+        }
+        const bool ok = wait_count(&ctl->arrivals[h], ctl->expected[h] + (unsigned long long)(G - 1), timeout_ns);
+        if (!ok) atomicExch(err, 1);
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+// The last CTA to finish advances half h's expected count and the epoch
+// (every CTA has read both by then) and resets the CTA counters. After an
+// expired wait the counts no longer match: the communicator has to be
+// recreated before the next peer collective.
+__device__ void peer_advance(PeerCtl* ctl, unsigned int e, int G) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&ctl->finished, 1u) == gridDim.x - 1) {
+            ctl->expected[e & 1u] += (unsigned long long)(G - 1);
+            ctl->epoch = e + 1;
+            ctl->pushed = 0;
+            ctl->finished = 0;
+            __threadfence();
+        }
+    }
+}
+
+__device__ unsigned int peer_epoch(PeerCtl* ctl) {
+    __shared__ unsigned int epoch_s;
+    if (threadIdx.x == 0) epoch_s = *(volatile unsigned int*)&ctl->epoch;
+    __syncthreads();
+    return epoch_s;
+}
+
+// The all-gather of the pending segments, one cooperative launch:
 //   1. push: this rank's columns of every row go from its own half to the
 //      same place in every other rank's half (16-byte stores over NVLink) and
 //      to y;
-//   2. signal: every CTA releases its stores (system scope) and counts
-//      itself; the last one adds 1 to every other rank's arrival counter;
-//   3. wait (bounded) for the G - 1 other ranks' signals on this half, then
-//      copy their columns from this rank's half to y;
-//   4. the last CTA to finish advances the expected count and the epoch.
-// After an expired wait the counts no longer match the gathers: the
-// communicator has to be recreated before the next peer gather.
+//   2. signal and wait (peer_signal_wait);
+//   3. copy the other ranks' columns from this rank's half to y;
+//   4. advance the epoch.
 __global__ void peer_allgather_kernel(const __grid_constant__ PeerSegs segs, uint64_t timeout_ns, int* err) {
     char* own = segs.base[segs.rank];
     PeerCtl* ctl = ctl_of(own);
-    __shared__ unsigned int epoch_s;
-    __shared__ int ok_s;
-    if (threadIdx.x == 0) epoch_s = *(volatile unsigned int*)&ctl->epoch;
-    __syncthreads();
-    const unsigned int e = epoch_s, h = e & 1u;
+    const unsigned int e = peer_epoch(ctl), h = e & 1u;
     const int64_t half = kPeerCtlBytes / 4 + (int64_t)h * kPeerHalfFloats;
     const int G = segs.G, me = segs.rank;
     const int tid = blockIdx.x * blockDim.x + threadIdx.x, nthr = gridDim.x * blockDim.x;
@@ -386,22 +436,8 @@ __global__ void peer_allgather_kernel(const __grid_constant__ PeerSegs segs, uin
                 if (q != me) reinterpret_cast<float4*>(reinterpret_cast<float*>(segs.base[q]) + src0)[u] = v;
         }
     }
-    // 2. signal
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        if (atomicAdd(&ctl->pushed, 1u) == gridDim.x - 1) {
-            asm volatile("fence.acq_rel.sys;" ::: "memory");
-            for (int q = 0; q < G; ++q)
-                if (q != me) atomicAdd_system(&ctl_of(segs.base[q])->arrivals[h], 1ull);
-        }
-        // 3. wait for the other ranks
-        const bool ok = wait_count(&ctl->arrivals[h], ctl->expected[h] + (unsigned long long)(G - 1), timeout_ns);
-        if (!ok) atomicExch(err, 1);
-        ok_s = ok;
-    }
-    __syncthreads();
-    if (ok_s) {
+    // 2. signal and wait; 3. the other ranks' columns
+    if (peer_signal_wait(ctl, segs.base, me, G, h, timeout_ns, err)) {
         for (int sg = 0; sg < segs.count; ++sg) {
             const int ns4 = segs.ns4[sg], units = segs.rows[sg] * (G - 1) * ns4;
             const int64_t n4 = (int64_t)G * ns4;
@@ -417,17 +453,73 @@ __global__ void peer_allgather_kernel(const __grid_constant__ PeerSegs segs, uin
         }
     }
     // 4. advance
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(&ctl->finished, 1u) == gridDim.x - 1) {
-            ctl->expected[h] += (unsigned long long)(G - 1);
-            ctl->epoch = e + 1;
-            ctl->pushed = 0;
-            ctl->finished = 0;
-            __threadfence();
+    peer_advance(ctl, e, G);
+}
+
+// In-place all-reduce (sum) of n floats (n % 4 == 0, buf 16-byte aligned)
+// over peer memory, one cooperative launch: this rank's values go into slot
+// `rank` of every rank's half (16-byte stores over NVLink), then, after the
+// signals, every rank adds the G slots in rank order -- the same bits on
+// every rank, run to run.
+struct PeerReduce {
+    char* base[kMaxPeers];
+    float* buf;
+    int64_t n4;
+    int rank, G;
+};
+__global__ void peer_allreduce_kernel(const __grid_constant__ PeerReduce pr, uint64_t timeout_ns, int* err) {
+    char* own = pr.base[pr.rank];
+    PeerCtl* ctl = ctl_of(own);
+    const unsigned int e = peer_epoch(ctl), h = e & 1u;
+    const int64_t half = kPeerCtlBytes / 4 + (int64_t)h * kPeerHalfFloats;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nthr = (int64_t)gridDim.x * blockDim.x;
+    float4* buf = reinterpret_cast<float4*>(pr.buf);
+    const int64_t slot0 = half + (int64_t)pr.rank * pr.n4 * 4;
+    for (int64_t i = tid; i < pr.n4; i += nthr) {
+        const float4 v = buf[i];
+        for (int q = 0; q < pr.G; ++q) reinterpret_cast<float4*>(reinterpret_cast<float*>(pr.base[q]) + slot0)[i] = v;
+    }
+    if (peer_signal_wait(ctl, pr.base, pr.rank, pr.G, h, timeout_ns, err)) {
+        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<float*>(own) + half);
+        for (int64_t i = tid; i < pr.n4; i += nthr) {
+            float4 a = __ldcg(src + i);
+            for (int q = 1; q < pr.G; ++q) {
+                const float4 b = __ldcg(src + (int64_t)q * pr.n4 + i);
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+            }
+            buf[i] = a;
         }
     }
+    peer_advance(ctl, e, pr.G);
+}
+
+// Launches a peer collective kernel cooperatively, one CTA per SM.
+template <typename Arg>
+int launch_peer(strata_ctx* ctx, void (*kern)(Arg, uint64_t, int*), const Arg& arg, cudaStream_t s, const char* what) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctx->sm_count);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, arg, (uint64_t)ctx->wait_timeout_ms * 1000000ull, ctx->err_dev);
+    return check_launch(ctx, what);
+}
+
+// Orders peer work on stream s after the previous peer work (another stream).
+void peer_order(strata_ctx* ctx, cudaStream_t s) {
+    CommState* c = ctx->comm;
+    if (c->peer_stream && c->peer_stream != s) {
+        cudaEventRecord(c->order, c->peer_stream);
+        cudaStreamWaitEvent(s, c->order, 0);
+    }
+    c->peer_stream = s;
 }
 
 // Whether this sharded GEMV takes the peer all-gather.
@@ -448,20 +540,33 @@ int peer_flush(strata_ctx* ctx) {
     p.segs.rank = c->rank;
     p.segs.G = c->world;
     for (int q = 0; q < c->world; ++q) p.segs.base[q] = c->peer_base[q];
-    // one CTA per SM: always co-resident, which the cooperative launch checks
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ctx->sm_count);
-    cfg.blockDim = dim3(256);
-    cfg.stream = p.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, peer_allgather_kernel, p.segs, (uint64_t)ctx->wait_timeout_ms * 1000000ull,
-                       ctx->err_dev);
+    const PeerSegs segs = p.segs;
+    const cudaStream_t st = p.stream;
     p = PeerPending{};
-    return check_launch(ctx, "peer all-gather kernel");
+    return launch_peer(ctx, peer_allgather_kernel, segs, st, "peer all-gather kernel");
+}
+
+// Whether the expert-parallel layer output (n floats at out) takes the peer all-reduce.
+bool use_peer_reduce(strata_ctx* ctx, const float* out, int64_t n) {
+    CommState* c = ctx->comm;
+    return c->peer_ok && c->gather_mode != STRATA_GATHER_NCCL && c->world >= 2 && n % 4 == 0 &&
+           ((uintptr_t)out & 15) == 0 && n * c->world <= kPeerHalfFloats;
+}
+
+// In-place peer all-reduce of the layer output; pending grouped gathers on
+// any stream go first, so the ranks' halves stay in step.
+int peer_allreduce(strata_ctx* ctx, float* buf, int64_t n, cudaStream_t s) {
+    CommState* c = ctx->comm;
+    int rc = peer_flush(ctx);
+    if (rc) return rc;
+    peer_order(ctx, s);
+    PeerReduce pr{};
+    for (int q = 0; q < c->world; ++q) pr.base[q] = c->peer_base[q];
+    pr.buf = buf;
+    pr.n4 = n / 4;
+    pr.rank = c->rank;
+    pr.G = c->world;
+    return launch_peer(ctx, peer_allreduce_kernel, pr, s, "peer all-reduce kernel");
 }
 
 // Sharded GEMV into this rank's exchange half at the call's place; the
@@ -475,6 +580,7 @@ int gemv_peer_gather(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     int rc;
     if (p.segs.count > 0 && (p.stream != s || p.segs.count == kPeerSegs || p.floats + n > kPeerHalfFloats))
         if ((rc = peer_flush(ctx))) return rc;
+    peer_order(ctx, s);
     PeerOut po{};
     po.y = data_of(c->xbuf);
     po.epoch = &ctl_of(c->xbuf)->epoch;
@@ -645,6 +751,9 @@ int strata_cuda_moe_ffn_ep_dev(strata_ctx* ctx, const strata_moe* layer, const f
     cudaStream_t s = pick_stream(ctx, stream);
     if ((rc = moe_enqueue_checked(ctx, layer, x_dev, logits_dev, tokens, out_dev, nullptr, nullptr, s))) return rc;
     const int64_t n = tokens * moe_embd(layer);
+    if (use_peer_reduce(ctx, out_dev, n)) return peer_allreduce(ctx, out_dev, n, s);
+    if (ctx->comm->gather_mode == STRATA_GATHER_PEER)
+        return fail(ctx, STRATA_ERR_INVALID, "the peer all-reduce does not apply to this output");
     return nccl_done(ctx, ctx->comm->comm,
                      nccl().AllReduce(out_dev, out_dev, (size_t)n, ncclFloat, ncclSum, ctx->comm->comm, s),
                      "ncclAllReduce");

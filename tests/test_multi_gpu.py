@@ -182,6 +182,23 @@ def _worker(rank, world, uid, q):
         got_m = od.cpu().numpy()
         for t in range(T):  # fp32 sums in another order (see test_moe_expert_parallel_partials_sum)
             assert rel_err(got_m[t], want_m[t]) < 1e-3, ("moe", t)
+        # the peer all-reduce (rank-ordered sum: the same bits every call) against NCCL's
+        again = torch.empty_like(od)
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            ctx.moe_ffn_ep_dev(lr, xd.data_ptr(), ld.data_ptr(), T, again.data_ptr(), st.cuda_stream)
+        st.synchronize()
+        assert np.array_equal(again.cpu().numpy().view(np.uint32), got_m.view(np.uint32)), "peer all-reduce repeat"
+        ctx.comm_set_gather(ctx.GATHER_NCCL)
+        on = torch.empty_like(od)
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            ctx.moe_ffn_ep_dev(lr, xd.data_ptr(), ld.data_ptr(), T, on.data_ptr(), st.cuda_stream)
+        st.synchronize()
+        ctx.comm_set_gather(ctx.GATHER_AUTO)
+        got_n = on.cpu().numpy()
+        for t in range(T):
+            assert rel_err(got_m[t], got_n[t]) < 1e-5, ("peer vs nccl all-reduce", t)
         ctx.close()
         q.put((rank, "ok"))
     except Exception:
