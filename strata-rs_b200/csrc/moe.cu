@@ -165,9 +165,61 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const float
 // so every list is in token order whatever the thread schedule.
 constexpr int kAssignThreads = 1024;
 __device__ void assign_block(const int* ids, int T, int k, int E, int e_begin, int e_end, MoeIndex ix) {
-    __shared__ int cnt_s[1024], scan[1024];
+    __shared__ int cnt_s[1024], scan[1024], slot_s[1024];
     const int tid = threadIdx.x;
     const int64_t TK = (int64_t)T * k;
+    if (TK <= 32) {
+        // decode: one warp, entry i on lane i. Counts and offsets come from
+        // comparisons with every other entry; only the active experts' cnt /
+        // off are written (nothing reads the others).
+        if (tid >= 32) return;
+        const int lane = tid;
+        const int e = lane < TK ? ids[lane] : -1;
+        const bool held = lane < TK && e >= e_begin && e < e_end;
+        int less = 0, same_before = 0, cnt = 0;
+        bool first = true;
+        for (int j = 0; j < (int)TK; ++j) {
+            const int ej = __shfl_sync(0xFFFFFFFFu, e, j);
+            const bool hj = ej >= e_begin && ej < e_end;
+            if (held && hj) {
+                less += ej < e ? 1 : 0;
+                if (ej == e) {
+                    ++cnt;
+                    if (j < lane) {
+                        ++same_before;
+                        first = false;
+                    }
+                }
+            }
+        }
+        const unsigned firsts = __ballot_sync(0xFFFFFFFFu, held && first);
+        int distinct_less = 0;
+        for (int j = 0; j < (int)TK; ++j) {
+            const int ej = __shfl_sync(0xFFFFFFFFu, e, j);
+            distinct_less += ((firsts >> j) & 1u) && ej < e ? 1 : 0;
+        }
+        const unsigned helds = __ballot_sync(0xFFFFFFFFu, held);
+        if (held) {
+            const int at = less + same_before;  // entries of smaller experts, then earlier tokens
+            ix.tok[at] = lane / k;
+            ix.pos[lane] = at;
+            if (first) {
+                ix.cnt[e] = cnt;
+                ix.off[e] = less;
+                ix.active[distinct_less] = e;
+                if (distinct_less < ix.slots) ix.slot_info[distinct_less] = make_int4(e, less, cnt, lane / k);
+            }
+        } else if (lane < TK) {
+            ix.pos[lane] = -1;
+        }
+        const int n_act = __popc(firsts);
+        if (lane >= n_act && lane < ix.slots) ix.slot_info[lane] = make_int4(-1, 0, 0, 0);
+        if (lane == 0) {
+            ix.n_active[0] = n_act;
+            ix.n_assign[0] = __popc(helds);
+        }
+        return;
+    }
     for (int e = tid; e < 1024; e += blockDim.x) cnt_s[e] = 0;
     __syncthreads();
     for (int64_t i = tid; i < TK; i += blockDim.x) {
@@ -201,11 +253,15 @@ __device__ void assign_block(const int* ids, int T, int k, int E, int e_begin, i
         ix.off[tid] = off;
         if (c > 0) ix.active[scan[tid] - 1] = tid;
     }
+    slot_s[tid] = c > 0 ? scan[tid] - 1 : -1;
+    const int n_act = scan[blockDim.x - 1];
     if (tid == 0) {
-        ix.n_active[0] = scan[blockDim.x - 1];
+        ix.n_active[0] = n_act;
         ix.n_assign[0] = total;
     }
+    if (tid >= n_act && tid < ix.slots) ix.slot_info[tid] = make_int4(-1, 0, 0, 0);
     __syncthreads();
+    scan[tid] = c;     // counts and
     cnt_s[tid] = off;  // offsets, for the placement below
     __syncthreads();
     for (int64_t i = tid; i < TK; i += blockDim.x) {
@@ -220,6 +276,7 @@ __device__ void assign_block(const int* ids, int T, int k, int E, int e_begin, i
         const int at = cnt_s[e] + r;
         ix.tok[at] = (int)(i / k);
         ix.pos[i] = at;
+        if (r == 0 && slot_s[e] < ix.slots) ix.slot_info[slot_s[e]] = make_int4(e, cnt_s[e], scan[e], (int)(i / k));
     }
 }
 
@@ -374,10 +431,13 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // Rows per tile: a multiple of the row lanes, about kStageBytes of weights.
 __host__ __device__ inline int tile_rows(int64_t row_bytes, int RL) {
+    // a multiple of RL; even when rows are not 4-byte multiples (Q6_K), so
+    // every tile starts on a 4-byte boundary
+    const int step = (row_bytes % 4 != 0 && RL % 2 != 0) ? 2 * RL : RL;
     int rs = (int)(kStageBytes / row_bytes);
-    rs = rs < RL ? RL : rs;
-    rs -= rs % RL;
-    return rs > 64 ? 64 : rs;
+    rs = rs > 64 ? 64 : rs;
+    rs -= rs % step;
+    return rs < step ? step : rs;
 }
 
 // Pitches of the tensor-core pass's shared arrays: a staged row pitch whose
@@ -408,8 +468,10 @@ moe_stream_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1
     if (slot >= ix.n_active[0]) return;
     const int e = ix.active[slot];
     const int a0 = ix.off[e], n = ix.cnt[e];
-    const int RC = gridDim.y, rc = blockIdx.y;
-    const int r0 = (int)((int64_t)IN * rc / RC), r1 = (int)((int64_t)IN * (rc + 1) / RC);
+    // row chunk rc of RC on 16-row boundaries: a Q6_K row is 210 bytes per
+    // block, so only an even first row keeps the 4-byte copies aligned
+    const int RC = gridDim.y, rc = blockIdx.y, nk = IN / 16;
+    const int r0 = 16 * (int)((int64_t)nk * rc / RC), r1 = 16 * (int)((int64_t)nk * (rc + 1) / RC);
     const int U = OUT / 16, RL = kMoeThreads / U;
     const int tid = threadIdx.x, u = tid % U, lane = tid / U;
     const int RS = tile_rows(row_bytes, RL);
@@ -997,10 +1059,10 @@ int launch_stream_t(const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int
 //     = sum_i A_i f_i - sum_i (A_i + x_i dmin_i m_i),  A_i = 16 x_i d_i sc_i
 // (32 for Q5_K). Row groups of the CTA are summed in shared memory and the
 // row chunk's partials go to P like the other passes'.
-constexpr int kLaneUnroll = 4;  // rows in flight per thread
+constexpr int kLaneUnroll = 8;  // rows in flight per thread
 
 template <uint32_t Q, int TPL>
-__global__ void __launch_bounds__(kMoeThreads)
+__global__ void __launch_bounds__(kMoeThreads, 2)
 moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, int64_t row_bytes,
                 int64_t expert_bytes, int IN, int OUT, const float* __restrict__ X, bool by_token, MoeIndex ix,
                 int e_begin, int A_cap, float* __restrict__ P, const float* __restrict__ PG, int RCG) {
@@ -1011,11 +1073,11 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
     extern __shared__ float red[];  // [RG][TPL][OUT], then (PG) the activations [TPL][rows]
     const int nmat = W1 ? 2 : 1;
     const int slot = blockIdx.x / nmat, m = blockIdx.x % nmat;
-    if (slot >= ix.n_active[0]) return;
-    const int e = ix.active[slot];
-    const int a0 = ix.off[e], n = ix.cnt[e];
-    const int RC = gridDim.y, rc = blockIdx.y;
-    const int r0 = (int)((int64_t)IN * rc / RC), r1 = (int)((int64_t)IN * (rc + 1) / RC);
+    const int4 si = ix.slot_info[slot];  // {expert, first position, count, first token}
+    if (si.x < 0) return;
+    const int e = si.x, a0 = si.y, n = si.z;
+    const int RC = gridDim.y, rc = blockIdx.y, nk = IN / 16;  // 16-row chunk boundaries, as the other passes
+    const int r0 = 16 * (int)((int64_t)nk * rc / RC), r1 = 16 * (int)((int64_t)nk * (rc + 1) / RC);
     const int TPR = OUT / 16, RG = kMoeThreads / TPR;
     const int tid = threadIdx.x, c16 = tid % TPR, rg = tid / TPR;
     const int blk = c16 >> 4, grp = (c16 >> 2) & 3, u = c16 & 3;
@@ -1029,7 +1091,7 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
         __syncthreads();  // the previous pass's reads of src and red are done
         if (tid < TPL) {
             const int a = a0 + p0 + (tid < np ? tid : 0);
-            src[tid] = by_token ? ix.tok[a] : a;
+            src[tid] = by_token ? (a == a0 ? si.w : ix.tok[a]) : a;
         }
         __syncthreads();
         const float* xr[TPL];
@@ -1040,14 +1102,23 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
         const int rows = r1 - r0;
         float* xs = red + (int64_t)RG * TPL * OUT;
         if (PG) {
+            // every partial loaded at once into shared memory (one round of
+            // independent loads), then each activation sums its chunks in order
+            float* pb = xs + TPL * rows;  // [TPL][2][RCG][rows]
+            for (int q = tid; q < np * 2 * RCG * rows; q += kMoeThreads) {
+                const int ii = q % rows, c = (q / rows) % RCG, mm = (q / (rows * RCG)) & 1, p = q / (2 * rows * RCG);
+                pb[q] = PG[(((int64_t)c * 2 + mm) * A_cap + src[p]) * IN + r0 + ii];
+            }
+            __syncthreads();
             for (int q = tid; q < TPL * rows; q += kMoeThreads) {
-                const int p = q / rows, i = r0 + (q - p * rows);
+                const int p = q / rows, ii = q - p * rows;
                 float v = 0.0f;
                 if (p < np) {
                     float g = 0.0f, uu = 0.0f;
+                    const float* pg = pb + (int64_t)p * 2 * RCG * rows + ii;
                     for (int c = 0; c < RCG; ++c) {
-                        g += PG[(((int64_t)c * 2 + 0) * A_cap + src[p]) * IN + i];
-                        uu += PG[(((int64_t)c * 2 + 1) * A_cap + src[p]) * IN + i];
+                        g += pg[c * rows];
+                        uu += pg[(RCG + c) * rows];
                     }
                     v = silu_f32(g) * uu;
                 }
@@ -1153,13 +1224,21 @@ moe_lane_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, 
     }
 }
 
+// Dynamic shared memory of the few-token pass: the row groups' sums and,
+// with the fused SwiGLU, the chunk's activations and their partials.
+size_t lane_smem(int TPL, int IN, int OUT, int RC, bool fused, int RCG) {
+    const int RG = kMoeThreads / (OUT / 16);
+    const int max_rows = 16 * ((IN / 16 + RC - 1) / RC);
+    return ((size_t)RG * TPL * OUT + (fused ? (size_t)TPL * max_rows * (1 + 2 * (size_t)RCG) : 0)) * sizeof(float);
+}
+constexpr size_t kLaneSmemMax = 200 * 1024;
+
 template <uint32_t Q>
 int launch_lane_q(int TPL, const uint8_t* W0, const uint8_t* W1, int64_t row_bytes, int64_t expert_bytes, int IN,
                   int OUT, const float* X, bool by_token, const MoeIndex& ix, int e_begin, int A_cap, float* P,
                   int slots, int RC, cudaStream_t s, const float* PG, int RCG) {
-    const int RG = kMoeThreads / (OUT / 16);
-    const int max_rows = (IN + RC - 1) / RC;
-    const size_t smem = ((size_t)RG * TPL * OUT + (PG ? (size_t)TPL * max_rows : 0)) * sizeof(float);
+    const size_t smem = lane_smem(TPL, IN, OUT, RC, PG != nullptr, RCG);  // rows per chunk <= 16 ceil(IN / 16 / RC)
+    if (smem > kLaneSmemMax) return -1;
     const dim3 grid((unsigned)(slots * (W1 ? 2 : 1)), (unsigned)RC);
     if (TPL == 1) {
         if (cudaFuncSetAttribute(moe_lane_kernel<Q, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -1277,13 +1356,16 @@ bool moe_expert_quant_supported(uint32_t q) { return q == kQ4_K || q == kQ5_K ||
 // Row chunks for a streamed pass over `mats` matrices: about four CTAs per SM
 // in all. Up to 8 tokens every chunk adds one partial per output to the
 // reductions, which then dominate the tensor-core pass: at most 8 chunks (at
-// least 32 rows each). The few-token pass (1 or 2 tokens) is bound by the
-// bytes each CTA keeps in flight instead: up to 64 chunks of at least 16 rows.
+// least 32 rows each). The few-token pass (1 or 2 tokens) runs one wave of
+// two CTAs per SM (up to 64 chunks of at least 16 rows).
 int moe_row_chunks(int slots, int mats, int IN, int sm_count, int T) {
     const int ctas = slots * mats;
     int rc = (4 * (sm_count > 0 ? sm_count : 148) + ctas - 1) / ctas;
     int maxrc = IN / 32 > 0 ? IN / 32 : 1;
     if (T <= 2) {
+        // one wave at two CTAs per SM: each CTA pays its index and first
+        // load latencies once
+        rc = (2 * (sm_count > 0 ? sm_count : 148)) / ctas;
         maxrc = IN / 16 > 0 ? IN / 16 : 1;
         if (maxrc > 64) maxrc = 64;
     } else if (T <= 8 && maxrc > 8) {
@@ -1310,6 +1392,7 @@ MoeWork moe_work_layout(const MoePlan& p) {
     w.off = take((int64_t)p.E * 4);
     w.active = take((int64_t)p.E * 4);
     w.counters = take(16);
+    w.slot_info = take((int64_t)(p.slots > 0 ? p.slots : 1) * 16);
     w.logits = p.need_router ? take((int64_t)p.T * p.E * 4) : -1;
     w.xb = p.need_router ? take((int64_t)p.T * p.n_embd * 4) : -1;
     w.pgu = take((int64_t)p.rc_gu * 2 * A * p.n_ff * 4);
@@ -1336,7 +1419,8 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     auto F = [&](int64_t off) { return reinterpret_cast<float*>(base + off); };
     auto I = [&](int64_t off) { return reinterpret_cast<int*>(base + off); };
     const MoeWork& w = L.layout;
-    MoeIndex ix{I(w.cnt), I(w.off), I(w.active), I(w.counters), I(w.counters) + 1, I(w.tok), I(w.pos)};
+    MoeIndex ix{I(w.cnt), I(w.off), I(w.active), I(w.counters), I(w.counters) + 1, I(w.tok), I(w.pos),
+                reinterpret_cast<int4*>(base + w.slot_info), p.slots};
     const int A = p.T * p.k;
 
     // dense projections (router, shared expert): tensor-core GEMV where it applies
@@ -1401,7 +1485,8 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
                       L.x, true, ix, p.e_begin, A, F(w.pgu), slots, p.rc_gu, s))
         return -2;
     // the few-token down pass computes the SwiGLU itself from the gate/up partials
-    const bool fuse_act = lane_pass(L.down.quant, TP, p.n_embd, L.down.row_bytes);
+    const bool fuse_act = lane_pass(L.down.quant, TP, p.n_embd, L.down.row_bytes) &&
+                          lane_smem(TP, p.n_ff, p.n_embd, p.rc_d, true, p.rc_gu) <= kLaneSmemMax;
     if (!fuse_act)
         launch_dep(moe_swiglu_kernel, dim3(grid_for((int64_t)A * p.n_ff, p.sm_count)), dim3(256), 0, s, F(w.pgu),
                    p.rc_gu, A, p.n_ff, ix.n_assign, F(w.h));

@@ -14,6 +14,11 @@ struct MoeIndex {
     int* n_assign;  // [1] total assignments held here
     int* tok;       // [T k] token of each sorted assignment
     int* pos;       // [T k] sorted position of (token, slot), -1 when not held here
+    // [slots] per grid slot: {expert, first sorted position, count, token of
+    // the first assignment}, expert -1 past the active experts -- one load
+    // gives a pass everything it needs to start streaming
+    int4* slot_info;
+    int slots;
 };
 
 struct MoePlan {
@@ -29,7 +34,7 @@ struct MoePlan {
 // Byte offsets of the workspace arrays.
 struct MoeWork {
     int64_t ids, wts, pos, tok, cnt, off, active, counters, logits, xb, pgu, h, pd, gs, us, hs, gi, sg, ds, xfrag,
-        xfrag_s;
+        xfrag_s, slot_info;
     int64_t bytes;
 };
 
