@@ -162,7 +162,11 @@ int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe
     }
     if (!ctx->aux) {  // the shared expert's stream; without it the layer runs in line
         cudaSetDevice(ctx->device);
-        if (cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking) != cudaSuccess ||
+        // the highest priority: the shared expert's small grids take SM slots
+        // as the routed passes' CTAs retire instead of queueing behind them
+        int lo_pri = 0, hi_pri = 0;
+        cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri);
+        if (cudaStreamCreateWithPriority(&ctx->aux, cudaStreamNonBlocking, hi_pri) != cudaSuccess ||
             cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming) != cudaSuccess) {
             cudaGetLastError();
