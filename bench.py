@@ -532,9 +532,9 @@ def run_gpu(args):
         ctx.comm_set_gather(ctx.GATHER_AUTO)  # peer gather fused into the GEMV where available
     graphs = capture()
     # every GEMV is two launches: the activation-limb prologue and the GEMV kernel;
-    # with the fused peer gather a third, the wait-and-copy kernel (the NCCL
-    # group's kernel of the NCCL gather is not counted)
-    launches_per_step = (3 if peer else 2) * len(batches) * len(shapes)
+    # with the peer gather one all-gather kernel per step (the step is one
+    # collective group; the NCCL group's kernel of the NCCL gather is not counted)
+    launches_per_step = 2 * len(batches) * len(shapes) + (1 if peer else 0)
 
     def step(i):
         if graphs:
@@ -728,9 +728,10 @@ def run_gpu(args):
                                    "2048->151936 at batch 1,2,4,8 (16 GEMVs per step, batch-major)",
                        "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 "
                              "per matrix), no matrix re-read within 241 MB of traffic",
-                       "parallelism": ((f"row-sharded x{world}: all-gather fused into the GEMV (epilogue "
-                                        f"stores into every rank's exchange buffer over NVLink + a wait-and-"
-                                        f"copy kernel) inside strata_cuda_gemv_sharded_dev" if peer else
+                       "parallelism": ((f"row-sharded x{world}: each GEMV writes its columns into this rank's "
+                                        f"exchange buffer; one peer all-gather kernel per step (16-byte pushes "
+                                        f"over NVLink, one signal per rank) inside the library's collective "
+                                        f"group" if peer else
                                         f"row-sharded x{world}: local GEMV into its columns of y + in-place "
                                         f"NCCL all-gathers inside strata_cuda_gemv_sharded_dev, the step's "
                                         f"16 in one NCCL group") if world > 1 else "single GPU"),
