@@ -787,7 +787,9 @@ bool gemv_mma_supported(uint32_t quant, const GemvArgs& a) {
 }
 
 // x limbs into `work` (gemv_mma_work_bytes), then the tensor-core GEMV.
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s) {
+// With prep = false the limbs already in `work` are reused: they must come
+// from a call on the same stream with the same x, K and batch.
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s, bool prep) {
     const int nblk = (int)(a.K / 256);
     const int full = a.batch > 8 ? a.batch / 8 : 0;  // 8-token chunks on grid.y
     const int nb = full ? 8 : a.batch;
@@ -800,8 +802,9 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     const int64_t xs_bytes = ((int64_t)nb * nblk * 4 + 255) / 256 * 256;
     __half* xq = reinterpret_cast<__half*>(base + xf_bytes + xs_bytes);
     const int64_t warps = (int64_t)nblk * nb;
-    prep_x_limbs_kernel<<<dim3((unsigned)((warps + 7) / 8), chunks), 256, 0, s>>>(a.X, a.K, nb, xf, xs, xq,
-                                                                                chunk_bytes);
+    if (prep)
+        prep_x_limbs_kernel<<<dim3((unsigned)((warps + 7) / 8), chunks), 256, 0, s>>>(a.X, a.K, nb, xf, xs, xq,
+                                                                                    chunk_bytes);
     GemvArgs c = a;
     c.batch = nb;
     const bool tm = a.tmap != nullptr;
@@ -820,7 +823,7 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
             pr.off += (int64_t)full * 8 * ldy_of(a);
             r.peers = &pr;
         }
-        return launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s);
+        return launch_gemv_mma(quant, r, base + (int64_t)full * chunk_bytes, err, s, prep);
     }
     return 0;
 }

@@ -43,7 +43,7 @@ int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s);
 // any batch (8-token chunks beyond 8); `work` holds gemv_mma_work_bytes.
 int64_t gemv_mma_work_bytes(int64_t K, int batch);
 bool gemv_mma_supported(uint32_t quant, const GemvArgs& a);
-int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s);
+int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cudaStream_t s, bool prep = true);
 
 // Expert GEMV on the transposed expert layout [E][IN rows][OUT cols]
 // (rows quantized along OUT): Y[b][c] = sum_i X[b][i] * W_e[i][c].

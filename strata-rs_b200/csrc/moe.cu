@@ -1424,10 +1424,16 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
     const int A = p.T * p.k;
 
     // dense projections (router, shared expert): tensor-core GEMV where it applies
+    // `prepped`: the limbs of X already sit in this workspace (the previous
+    // tensor-core projection on this stream read the same X)
     auto dense_on = [&](cudaStream_t st, int64_t xf, const MoeTensor& Wt, int64_t rows, int64_t cols, const float* X,
-                        float* Y) -> int {
+                        float* Y, bool* prepped = nullptr) -> int {
         GemvArgs g{Wt.W, Wt.row_bytes, rows, cols, X, Y, p.T, p.sm_count, Wt.tmap};
-        if (gemv_mma_supported(Wt.quant, g)) return launch_gemv_mma(Wt.quant, g, base + xf, L.err, st);
+        if (gemv_mma_supported(Wt.quant, g)) {
+            const bool reuse = prepped && *prepped;
+            if (prepped) *prepped = true;
+            return launch_gemv_mma(Wt.quant, g, base + xf, L.err, st, !reuse);
+        }
         return launch_gemv(Wt.quant, g, st);
     };
     auto dense = [&](const MoeTensor& Wt, int64_t rows, int64_t cols, const float* X, float* Y) -> int {
@@ -1446,9 +1452,11 @@ int launch_moe_layer(const MoeLaunch& L, cudaStream_t s) {
             cudaStreamWaitEvent(L.aux, L.fork, 0);
             ss = L.aux;
         }
-        if (dense_on(ss, w.xfrag_s, L.gate_s, p.n_ff_s, p.n_embd, L.x, F(w.gs)) ||
-            dense_on(ss, w.xfrag_s, L.up_s, p.n_ff_s, p.n_embd, L.x, F(w.us)) ||
-            dense_on(ss, w.xfrag_s, L.gate_inp_s, 1, p.n_embd, L.x, F(w.gi)))
+        // gate, up and gate-input projections read the same x: one set of limbs
+        bool prepped = false;
+        if (dense_on(ss, w.xfrag_s, L.gate_s, p.n_ff_s, p.n_embd, L.x, F(w.gs), &prepped) ||
+            dense_on(ss, w.xfrag_s, L.up_s, p.n_ff_s, p.n_embd, L.x, F(w.us), &prepped) ||
+            dense_on(ss, w.xfrag_s, L.gate_inp_s, 1, p.n_embd, L.x, F(w.gi), &prepped))
             return -4;
         moe_shared_act_kernel<<<grid_for((int64_t)p.T * p.n_ff_s, p.sm_count), 256, 0, ss>>>(
             F(w.gs), F(w.us), F(w.gi), p.T, p.n_ff_s, F(w.hs), F(w.sg));

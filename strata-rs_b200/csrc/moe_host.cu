@@ -102,7 +102,7 @@ int moe_enqueue(strata_ctx* ctx, const strata_moe* L, const float* x, const floa
     ml.up_s = tensor_of(d.up_shexp);
     ml.down_s = tensor_of(d.down_shexp);
     ml.gate_inp_s = tensor_of(d.gate_inp_shexp);
-    ml.aux = ctx->aux;
+    ml.aux = T <= 2 ? ctx->aux : ctx->aux_lo;
     ml.fork = ctx->fork;
     ml.join = ctx->join;
     int k = launch_moe_layer(ml, s);
@@ -162,18 +162,21 @@ int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe
     }
     if (!ctx->aux) {  // the shared expert's stream; without it the layer runs in line
         cudaSetDevice(ctx->device);
-        // the highest priority: the shared expert's small grids take SM slots
-        // as the routed passes' CTAs retire instead of queueing behind them
+        // decode (one or two tokens): the highest priority, so the shared
+        // expert's small grids take SM slots as the routed passes' CTAs retire
+        // instead of queueing behind them; otherwise the default priority
         int lo_pri = 0, hi_pri = 0;
         cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri);
         if (cudaStreamCreateWithPriority(&ctx->aux, cudaStreamNonBlocking, hi_pri) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&ctx->aux_lo, cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming) != cudaSuccess) {
             cudaGetLastError();
             if (ctx->fork) cudaEventDestroy(ctx->fork);
             if (ctx->join) cudaEventDestroy(ctx->join);
             if (ctx->aux) cudaStreamDestroy(ctx->aux);
-            ctx->aux = nullptr;
+            if (ctx->aux_lo) cudaStreamDestroy(ctx->aux_lo);
+            ctx->aux = ctx->aux_lo = nullptr;
             ctx->fork = ctx->join = nullptr;
         }
     }

@@ -175,6 +175,7 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     if (ctx->fork) cudaEventDestroy(ctx->fork);
     if (ctx->join) cudaEventDestroy(ctx->join);
     if (ctx->aux) cudaStreamDestroy(ctx->aux);
+    if (ctx->aux_lo) cudaStreamDestroy(ctx->aux_lo);
     cudaStreamDestroy(ctx->stream);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;

@@ -40,9 +40,12 @@ struct strata_ctx {
     int gemv_path = 0;  // STRATA_GEMV_AUTO / _CUDA_CORES / _TENSOR_CORES
     int gemm_terms = 2;  // bf16 terms per staged GEMM weight
     strata::DevBuf x_dev, y_dev, work, xfrag, gemm_work, x_bf16, moe_work;
-    // the MoE layer's shared expert runs on `aux`, forked from and joined back
-    // into the caller's stream (created with the first MoE layer)
-    cudaStream_t aux = nullptr;
+    // the MoE layer's shared expert runs on `aux` (highest priority: decode,
+    // where it races the routed chain for SM slots) or `aux_lo` (default
+    // priority: many tokens, where the routed passes are the long pole),
+    // forked from and joined back into the caller's stream (created with the
+    // first MoE layer)
+    cudaStream_t aux = nullptr, aux_lo = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
     strata::PinnedBuf x_host, y_host;
     strata::CommState* comm = nullptr;
