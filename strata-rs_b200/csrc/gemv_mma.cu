@@ -581,7 +581,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
 
     // the activation limbs come from the preceding kernel in the stream
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // fused all-gather: where this call's outputs go in every rank's exchange buffer
+    // peer all-gather: where this call's outputs go in this rank's exchange buffer
     const unsigned half = po.G ? (*po.epoch & 1u) : 0u;
     const int64_t peer_off = (int64_t)half * po.half_floats + po.off + (int64_t)blockIdx.y * NB * ldy;
 

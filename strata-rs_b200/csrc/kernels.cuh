@@ -30,7 +30,7 @@ struct GemvArgs {
     int sm_count;
     const void* tmap = nullptr;  // CUtensorMap of W for the tensor-core GEMV, or null
     int64_t ldy = 0;             // output row pitch in floats (0: N)
-    const PeerOut* peers = nullptr;  // fused all-gather (tensor-core GEMV only), or null
+    const PeerOut* peers = nullptr;  // outputs to the peer exchange buffer (tensor-core GEMV only), or null
 };
 inline int64_t ldy_of(const GemvArgs& a) { return a.ldy > 0 ? a.ldy : a.N; }
 

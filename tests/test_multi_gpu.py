@@ -104,7 +104,7 @@ def _worker(rank, world, uid, q):
         for xx, yy in ((x1, y1), (x4, y4)):
             want = ctx.gemv(full, xx.cpu().numpy())
             assert np.array_equal(yy.cpu().numpy().view(np.uint32), want.reshape(yy.shape).view(np.uint32)), "group"
-        # more grouped calls than one wait-and-copy kernel takes (it flushes midway)
+        # more grouped calls than one all-gather kernel takes (it flushes midway)
         ys34 = [torch.empty((1, N), dtype=torch.float32, device=dev) for _ in range(34)]
         st.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(st):
