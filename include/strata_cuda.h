@@ -208,6 +208,36 @@ int strata_cuda_moe_ffn_dev(strata_ctx *ctx, const strata_moe *layer, const floa
                             const float *router_logits_dev, int64_t tokens, float *out_dev,
                             int32_t *ids_dev, float *weights_dev, void *stream);
 
+/* ------------------------------------------------------- elementwise trait ops */
+
+/* ComputeBackend's elementwise methods (crates/strata-core/src/backend.rs:37-50),
+ * with CpuBackend's arithmetic (crates/strata-backend-cpu/src/lib.rs:44-67,
+ * crates/strata-core/src/ops.rs): f64 sums and products where ops.rs uses f64,
+ * the f32 exp of softmax as the f64 exp rounded to f32. The host forms take
+ * one slice per call, as the trait does (synchronous, host buffers); the
+ * device forms take `rows` (or `heads`) vectors at once on `stream`, so a
+ * layer's activations can stay in device memory.
+ *   rms_norm   x = x * w / sqrt(mean(x^2) + eps)          ops.rs:45-56
+ *   l2_norm    x = x / sqrt(sum(x^2) + eps)               ops.rs:71-81
+ *   softmax    max-shifted, f64 sum                       ops.rs:107-119
+ *   rope_neox  NEOX pairs (i, i + n_rot/2) of the first min(n_rot, head_dim,
+ *              len) & ~1 dims, angle = freq_base^(-2i/n_rot') * pos  ops.rs:121-140
+ *   add        a += b                                     ops.rs:164-168 */
+int strata_cuda_rms_norm(strata_ctx *ctx, float *x, const float *w, int64_t n, double eps);
+int strata_cuda_l2_norm(strata_ctx *ctx, float *head, int64_t n, double eps);
+int strata_cuda_softmax(strata_ctx *ctx, float *xs, int64_t n);
+int strata_cuda_rope_neox(strata_ctx *ctx, float *head, int64_t len, int64_t pos, int64_t n_rot, int64_t head_dim,
+                          double freq_base);
+int strata_cuda_add(strata_ctx *ctx, float *a, const float *b, int64_t n);
+int strata_cuda_rms_norm_dev(strata_ctx *ctx, float *x_dev, const float *w_dev, int64_t n, int64_t rows, double eps,
+                             void *stream);
+int strata_cuda_l2_norm_dev(strata_ctx *ctx, float *x_dev, int64_t head_dim, int64_t heads, double eps,
+                            void *stream);
+int strata_cuda_softmax_dev(strata_ctx *ctx, float *x_dev, int64_t n, int64_t rows, void *stream);
+int strata_cuda_rope_neox_dev(strata_ctx *ctx, float *x_dev, int64_t head_dim, int64_t heads, int64_t n_rot,
+                              int64_t pos, double freq_base, void *stream);
+int strata_cuda_add_dev(strata_ctx *ctx, float *a_dev, const float *b_dev, int64_t n, void *stream);
+
 /* ------------------------------------------------------------------ multi-GPU */
 
 /* No counterpart in the reference, which runs on one device: the sharded

@@ -53,6 +53,11 @@ def lib() -> C.CDLL:
             "orc_moe_route": (i32, [vp, fp, lp, fp]),
             "orc_moe_combine": (i32, [vp, fp, lp, fp, fp]),
             "orc_moe_layer": (i32, [vp, fp, fp, i64, fp, lp, fp, i32]),
+            "orc_rms_norm": (None, [fp, fp, i64, C.c_double]),
+            "orc_l2_norm": (None, [fp, i64, C.c_double]),
+            "orc_softmax": (None, [fp, i64]),
+            "orc_rope_neox": (None, [fp, i64, i64, i64, i64, C.c_double]),
+            "orc_add": (None, [fp, fp, i64]),
         }
         for name, (res, args) in sigs.items():
             f = getattr(L, name)
@@ -122,6 +127,51 @@ def expert_gemv(quant: int, data: np.ndarray, n_expert: int, rows: int, cols: in
                                      _fp(yb)), "expert_gemv")
         y[b] = yb
     return y[0] if x.ndim == 1 else y
+
+
+def _rows(x: np.ndarray, n: int) -> np.ndarray:
+    return np.array(x, dtype=np.float32, copy=True).reshape(-1, n)
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """ops::rms_norm (ops.rs:45-56) of every row of x (last axis = w's length)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = _rows(x, w.size)
+    for r in out:
+        lib().orc_rms_norm(_fp(r), _fp(w), w.size, eps)
+    return out.reshape(np.shape(x))
+
+
+def l2_norm(x: np.ndarray, head_dim: int, eps: float) -> np.ndarray:
+    """ops::l2_norm (ops.rs:71-81) of every head_dim-long head of x."""
+    out = _rows(x, head_dim)
+    for r in out:
+        lib().orc_l2_norm(_fp(r), head_dim, eps)
+    return out.reshape(np.shape(x))
+
+
+def softmax(x: np.ndarray, n: int) -> np.ndarray:
+    """ops::softmax (ops.rs:107-119) of every n-long row of x."""
+    out = _rows(x, n)
+    for r in out:
+        lib().orc_softmax(_fp(r), n)
+    return out.reshape(np.shape(x))
+
+
+def rope_neox(x: np.ndarray, head_dim: int, pos: int, n_rot: int, freq_base: float) -> np.ndarray:
+    """ops::rope_neox (ops.rs:121-140) of every head_dim-long head of x at one position."""
+    out = _rows(x, head_dim)
+    for r in out:
+        lib().orc_rope_neox(_fp(r), head_dim, pos, n_rot, head_dim, freq_base)
+    return out.reshape(np.shape(x))
+
+
+def add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """ops::add_into (ops.rs:164-168): a + b in f32."""
+    out = np.array(a, dtype=np.float32, copy=True).reshape(-1)
+    bb = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
+    lib().orc_add(_fp(out), _fp(bb), out.size)
+    return out.reshape(np.shape(a))
 
 
 def route_logits(logits: np.ndarray, top_k: int) -> tuple[np.ndarray, np.ndarray]:

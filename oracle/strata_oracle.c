@@ -16,6 +16,9 @@
  *   ops::gemv ..................... crates/strata-core/src/ops.rs:14-28
  *   ops::expert_gemv .............. crates/strata-core/src/ops.rs:169-195
  *   ops::silu / sigmoid ........... crates/strata-core/src/ops.rs:84-92
+ *   ops::rms_norm / l2_norm ....... crates/strata-core/src/ops.rs:45-56,71-81
+ *   ops::softmax / rope_neox ...... crates/strata-core/src/ops.rs:107-140
+ *   ops::add_into ................. crates/strata-core/src/ops.rs:164-168
  *   bf16_round (half 2.7.1) ....... crates/strata-core/src/hyper.rs:21-24
  *   MoeLayer::route / combine ..... crates/strata-core/src/moe.rs:48-144
  */
@@ -467,4 +470,60 @@ int orc_moe_layer(const orc_moe_weights *L, const float *x, const float *logits,
     }
     free(jobs); free(tid);
     return rc;
+}
+
+/* ---------------------------------------------------------------- elementwise ops */
+
+/* ops::rms_norm (ops.rs:45-56): sequential f64 sum of squares, divided by n;
+ * scale = 1 / sqrt(ss + eps); x = f32((x * scale) * w) in f64. */
+void orc_rms_norm(float *x, const float *w, int64_t n, double eps) {
+    double ss = 0.0;
+    for (int64_t i = 0; i < n; ++i) ss += (double)x[i] * (double)x[i];
+    ss /= (double)n;
+    const double scale = 1.0 / sqrt(ss + eps);
+    for (int64_t i = 0; i < n; ++i) x[i] = (float)((double)x[i] * scale * (double)w[i]);
+}
+
+/* ops::l2_norm (ops.rs:71-81): inv = 1 / sqrt(sum x^2 + eps), x = f32(x * inv). */
+void orc_l2_norm(float *head, int64_t n, double eps) {
+    double ss = 0.0;
+    for (int64_t i = 0; i < n; ++i) ss += (double)head[i] * (double)head[i];
+    const double inv = 1.0 / sqrt(ss + eps);
+    for (int64_t i = 0; i < n; ++i) head[i] = (float)((double)head[i] * inv);
+}
+
+/* ops::softmax (ops.rs:107-119): f32 max, v = expf(v - max) in f32, f64 sum,
+ * v = f32(v * (1 / sum)). */
+void orc_softmax(float *xs, int64_t n) {
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < n; ++i) mx = xs[i] > mx ? xs[i] : mx;
+    double sum = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        xs[i] = expf(xs[i] - mx);
+        sum += (double)xs[i];
+    }
+    const double inv = 1.0 / sum;
+    for (int64_t i = 0; i < n; ++i) xs[i] = (float)((double)xs[i] * inv);
+}
+
+/* ops::rope_neox (ops.rs:121-140): n_rot clamped to the head and made even;
+ * pair (i, i + half) rotated by angle = base^(-2i/n_rot) * pos in f64. */
+void orc_rope_neox(float *head, int64_t len, int64_t pos, int64_t n_rot, int64_t head_dim, double freq_base) {
+    int64_t nr = n_rot < head_dim ? n_rot : head_dim;
+    nr = nr < len ? nr : len;
+    nr &= ~(int64_t)1;
+    const int64_t half = nr / 2;
+    for (int64_t i = 0; i < half; ++i) {
+        const double theta = pow(freq_base, -2.0 * (double)i / (double)nr);
+        const double angle = theta * (double)pos;
+        const double s = sin(angle), c = cos(angle);
+        const double a = head[i], b = head[i + half];
+        head[i] = (float)(a * c - b * s);
+        head[i + half] = (float)(a * s + b * c);
+    }
+}
+
+/* ops::add_into (ops.rs:164-168): out += a in f32. */
+void orc_add(float *out, const float *a, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] += a[i];
 }

@@ -67,6 +67,19 @@ int orc_expert_gemv(uint32_t quant, const uint8_t *w, size_t w_len, int64_t n_ex
 float orc_silu(float x);
 float orc_sigmoid(float x);
 
+/* The elementwise trait methods of ComputeBackend (crates/strata-core/src/backend.rs:37-50)
+ * as CpuBackend runs them (crates/strata-backend-cpu/src/lib.rs:44-67), one vector per call:
+ *   ops::rms_norm   crates/strata-core/src/ops.rs:45-56  f64 sum of squares / n, x*scale*w
+ *   ops::l2_norm    crates/strata-core/src/ops.rs:71-81  f64 sum of squares, x*inv
+ *   ops::softmax    crates/strata-core/src/ops.rs:107-119 max shift, f32 exp, f64 sum
+ *   ops::rope_neox  crates/strata-core/src/ops.rs:121-140 NEOX pairs (i, i + n_rot/2), f64 angles
+ *   ops::add_into   crates/strata-core/src/ops.rs:164-168 out += a in f32 */
+void orc_rms_norm(float *x, const float *w, int64_t n, double eps);
+void orc_l2_norm(float *head, int64_t n, double eps);
+void orc_softmax(float *xs, int64_t n);
+void orc_rope_neox(float *head, int64_t len, int64_t pos, int64_t n_rot, int64_t head_dim, double freq_base);
+void orc_add(float *out, const float *a, int64_t n);
+
 /* MoeLayer::route from the router logits on (crates/strata-core/src/moe.rs:57-91):
  * softmax (max-shift, f64 sum, f32 inv), stable top-k, ids ascending,
  * renormalised with a 2^-14 floor. logits is overwritten with the probs. */

@@ -92,6 +92,16 @@ def lib() -> C.CDLL:
             "strata_cuda_comm_group_start": (i32, [vp]),
             "strata_cuda_comm_group_end": (i32, [vp]),
             "strata_cuda_comm_set_gather": (i32, [vp, i32]),
+            "strata_cuda_rms_norm": (i32, [vp, fp, fp, i64, C.c_double]),
+            "strata_cuda_l2_norm": (i32, [vp, fp, i64, C.c_double]),
+            "strata_cuda_softmax": (i32, [vp, fp, i64]),
+            "strata_cuda_rope_neox": (i32, [vp, fp, i64, i64, i64, i64, C.c_double]),
+            "strata_cuda_add": (i32, [vp, fp, fp, i64]),
+            "strata_cuda_rms_norm_dev": (i32, [vp, vp, vp, i64, i64, C.c_double, vp]),
+            "strata_cuda_l2_norm_dev": (i32, [vp, vp, i64, i64, C.c_double, vp]),
+            "strata_cuda_softmax_dev": (i32, [vp, vp, i64, i64, vp]),
+            "strata_cuda_rope_neox_dev": (i32, [vp, vp, i64, i64, i64, i64, C.c_double, vp]),
+            "strata_cuda_add_dev": (i32, [vp, vp, vp, i64, vp]),
             "strata_cuda_comm_peer_info": (i32, [vp, C.POINTER(i32), C.POINTER(i64)]),
             "strata_cuda_gemv_sharded_dev": (i32, [vp, vp, vp, vp, i32, vp]),
             "strata_cuda_gemm_sharded_dev": (i32, [vp, vp, vp, vp, i64, vp]),
@@ -322,6 +332,54 @@ class Context:
 
     def comm_group_end(self):
         self.check(lib().strata_cuda_comm_group_end(self.h))
+
+    # ---- the elementwise trait methods (host slices, one vector per call)
+
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        x = np.array(x, dtype=np.float32, copy=True).reshape(-1)
+        w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+        self.check(lib().strata_cuda_rms_norm(self.h, _fptr(x), _fptr(w), x.size, eps))
+        return x
+
+    def l2_norm(self, head: np.ndarray, eps: float) -> np.ndarray:
+        x = np.array(head, dtype=np.float32, copy=True).reshape(-1)
+        self.check(lib().strata_cuda_l2_norm(self.h, _fptr(x), x.size, eps))
+        return x
+
+    def softmax(self, xs: np.ndarray) -> np.ndarray:
+        x = np.array(xs, dtype=np.float32, copy=True).reshape(-1)
+        self.check(lib().strata_cuda_softmax(self.h, _fptr(x), x.size))
+        return x
+
+    def rope_neox(self, head: np.ndarray, pos: int, n_rot: int, head_dim: int, freq_base: float) -> np.ndarray:
+        x = np.array(head, dtype=np.float32, copy=True).reshape(-1)
+        self.check(lib().strata_cuda_rope_neox(self.h, _fptr(x), x.size, pos, n_rot, head_dim, freq_base))
+        return x
+
+    def add(self, a: np.ndarray, b: np.ndarray) -> np.ndarray:
+        x = np.array(a, dtype=np.float32, copy=True).reshape(-1)
+        bb = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
+        self.check(lib().strata_cuda_add(self.h, _fptr(x), _fptr(bb), x.size))
+        return x
+
+    # ---- the same on device pointers, many vectors per call
+
+    def rms_norm_dev(self, x_ptr: int, w_ptr: int, n: int, rows: int, eps: float, stream: int = 0):
+        self.check(lib().strata_cuda_rms_norm_dev(self.h, x_ptr, w_ptr, n, rows, eps, stream or None))
+
+    def l2_norm_dev(self, x_ptr: int, head_dim: int, heads: int, eps: float, stream: int = 0):
+        self.check(lib().strata_cuda_l2_norm_dev(self.h, x_ptr, head_dim, heads, eps, stream or None))
+
+    def softmax_dev(self, x_ptr: int, n: int, rows: int, stream: int = 0):
+        self.check(lib().strata_cuda_softmax_dev(self.h, x_ptr, n, rows, stream or None))
+
+    def rope_neox_dev(self, x_ptr: int, head_dim: int, heads: int, n_rot: int, pos: int, freq_base: float,
+                      stream: int = 0):
+        self.check(lib().strata_cuda_rope_neox_dev(self.h, x_ptr, head_dim, heads, n_rot, pos, freq_base,
+                                                   stream or None))
+
+    def add_dev(self, a_ptr: int, b_ptr: int, n: int, stream: int = 0):
+        self.check(lib().strata_cuda_add_dev(self.h, a_ptr, b_ptr, n, stream or None))
 
     GATHER_AUTO, GATHER_NCCL, GATHER_PEER = 0, 1, 2
 

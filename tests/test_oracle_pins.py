@@ -165,3 +165,57 @@ def test_threaded_gemv_equals_single_thread():
     a = oracle.gemv(Q4_K, w, 64, 2048, x, threads=1)
     b = oracle.gemv(Q4_K, w, 64, 2048, x, threads=4)
     assert np.array_equal(a, b)
+
+
+# ---- the elementwise trait methods: the reference's own known values
+# (crates/strata-core/tests/ops_tests.rs:80-134) and a numpy f64 restatement
+
+def test_rms_norm_known_values():
+    """ops_tests.rs:80-88: [3, 4] with w = [2, 2], eps 0 -> [3, 4] * 2 / sqrt(12.5)."""
+    got = oracle.rms_norm(np.array([3.0, 4.0], np.float32), np.array([2.0, 2.0], np.float32), 0.0)
+    s = 2.0 / np.sqrt(12.5)
+    assert abs(got[0] - np.float32(3.0 * s)) < 1e-6 and abs(got[1] - np.float32(4.0 * s)) < 1e-6
+
+
+def test_l2_norm_gives_unit_heads():
+    """ops_tests.rs:90-96."""
+    got = oracle.l2_norm(np.array([3.0, 4.0, 0.0], np.float32), 3, 0.0)
+    assert abs(float(np.sqrt(np.sum(got * got))) - 1.0) < 1e-6
+
+
+def test_rope_neox_known_values():
+    """ops_tests.rs:98-125: position 0 is the identity; (1, 0) at pos 1, base 1 -> (cos 1, sin 1)."""
+    x = np.array([1.0, 2.0, 3.0, 4.0], np.float32)
+    assert np.array_equal(oracle.rope_neox(x, 4, 0, 4, 1e7), x)
+    got = oracle.rope_neox(np.array([1.0, 0.0], np.float32), 2, 1, 2, 1.0)
+    assert abs(got[0] - np.float32(np.cos(1.0))) < 1e-6 and abs(got[1] - np.float32(np.sin(1.0))) < 1e-6
+
+
+def test_softmax_sums_to_one():
+    """ops_tests.rs:127-134."""
+    got = oracle.softmax(np.array([1.0, 2.0, 3.0, 0.5], np.float32), 4)
+    assert abs(float(np.sum(got.astype(np.float64))) - 1.0) < 1e-6
+    assert got[2] > got[1] > got[0] > got[3]
+
+
+def test_elementwise_ops_match_numpy_f64():
+    """The same arithmetic restated in numpy (f64 where ops.rs uses f64)."""
+    g = rng(77)
+    x = g.standard_normal((3, 256)).astype(np.float32)
+    w = g.standard_normal(256).astype(np.float32)
+    ss = np.sum(x.astype(np.float64) ** 2, axis=1, keepdims=True) / 256
+    want = ((x.astype(np.float64) * (1.0 / np.sqrt(ss + 1e-6))) * w.astype(np.float64)).astype(np.float32)
+    assert np.max(np.abs(oracle.rms_norm(x, w, 1e-6) - want)) <= 1e-6 * np.max(np.abs(want))
+    h = x.reshape(-1, 128)
+    inv = 1.0 / np.sqrt(np.sum(h.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6)
+    assert np.max(np.abs(oracle.l2_norm(h, 128, 1e-6) - (h * inv).astype(np.float32))) < 1e-6
+    e = np.exp((x - x.max(axis=1, keepdims=True)).astype(np.float64))
+    assert np.max(np.abs(oracle.softmax(x, 256) - (e / e.sum(axis=1, keepdims=True)).astype(np.float32))) < 1e-6
+    half = 32
+    th = 1e6 ** (-2.0 * np.arange(half) / 64) * 17
+    a, b = h[:, :half].astype(np.float64), h[:, half:2 * half].astype(np.float64)
+    r = oracle.rope_neox(h, 128, 17, 64, 1e6)
+    assert np.max(np.abs(r[:, :half] - (a * np.cos(th) - b * np.sin(th)))) < 1e-5
+    assert np.max(np.abs(r[:, half:2 * half] - (a * np.sin(th) + b * np.cos(th)))) < 1e-5
+    assert np.array_equal(r[:, 64:], h[:, 64:])
+    assert np.array_equal(oracle.add(x, w[None, :].repeat(3, 0)), x + w)
