@@ -13,6 +13,10 @@
  *   get_scale_min_k4 .............. crates/strata-gguf/src/dequant.rs:237-245
  *   dequant_q4_k .................. crates/strata-gguf/src/dequant.rs:247-270
  *   dequant_q5_k .................. crates/strata-gguf/src/dequant.rs:272-302
+ *   Q2_0, Q8_1, Q4_0/1, Q5_0/1 .... crates/strata-gguf/src/dequant.rs:87-180
+ *   IQ4_NL, IQ4_XS ................ crates/strata-gguf/src/dequant.rs:182-206
+ *   Q3_K, Q2_K .................... crates/strata-gguf/src/dequant.rs:304-380
+ *   MXFP4, NVFP4 .................. crates/strata-gguf/src/dequant.rs:382-445
  *   ops::gemv ..................... crates/strata-core/src/ops.rs:14-28
  *   ops::expert_gemv .............. crates/strata-core/src/ops.rs:169-195
  *   ops::silu / sigmoid ........... crates/strata-core/src/ops.rs:84-92
@@ -35,8 +39,10 @@
 int64_t orc_block_size(uint32_t q) {
     switch (q) {
     case ORC_F32: case ORC_F16: case ORC_BF16: return 1;
-    case ORC_Q8_0: return 32;
-    case ORC_Q4_K: case ORC_Q5_K: case ORC_Q6_K: return 256;
+    case ORC_Q4_0: case ORC_Q4_1: case ORC_Q5_0: case ORC_Q5_1: case ORC_Q8_0: case ORC_Q8_1:
+    case ORC_IQ4_NL: case ORC_MXFP4: return 32;
+    case ORC_NVFP4: case ORC_Q2_0: return 64;
+    case ORC_Q2_K: case ORC_Q3_K: case ORC_Q4_K: case ORC_Q5_K: case ORC_Q6_K: case ORC_IQ4_XS: return 256;
     default: return 0;
     }
 }
@@ -45,10 +51,20 @@ int64_t orc_type_size(uint32_t q) {
     switch (q) {
     case ORC_F32: return 4;
     case ORC_F16: case ORC_BF16: return 2;
+    case ORC_Q4_0: case ORC_IQ4_NL: case ORC_Q2_0: return 18;
+    case ORC_Q4_1: return 20;
+    case ORC_Q5_0: return 22;
+    case ORC_Q5_1: return 24;
     case ORC_Q8_0: return 34;
+    case ORC_Q8_1: return 36;
+    case ORC_Q2_K: return 84;
+    case ORC_Q3_K: return 110;
     case ORC_Q4_K: return 144;
     case ORC_Q5_K: return 176;
     case ORC_Q6_K: return 210;
+    case ORC_IQ4_XS: return 136;
+    case ORC_MXFP4: return 17;
+    case ORC_NVFP4: return 36;
     default: return 0;
     }
 }
@@ -181,6 +197,211 @@ static void dequant_q5_k(const uint8_t *b, float *out) {
     }
 }
 
+/* ---- the other block formats (dequant.rs:87-206, 304-445), each element in
+ * the reference's operation order: f32 ops, one rounding each (no FMA). */
+
+/* dequant.rs:87-96, Q2_0: 2-bit codes LSB first, v = (code - 1) * d. */
+static void dequant_q2_0(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b));
+    for (int j = 0; j < 64; ++j) {
+        int code = (b[2 + j / 4] >> ((j % 4) * 2)) & 3;
+        out[j] = ((float)code - 1.0f) * d;
+    }
+}
+
+/* dequant.rs:130-136, Q8_1: as Q8_0 with the quants after d and s. */
+static void dequant_q8_1(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b));
+    for (int j = 0; j < 32; ++j) out[j] = (float)(int8_t)b[4 + j] * d;
+}
+
+/* dequant.rs:138-144, Q4_0: (nibble - 8) * d; low nibbles j, high j + 16. */
+static void dequant_q4_0(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b));
+    for (int j = 0; j < 16; ++j) {
+        out[j] = ((float)(b[2 + j] & 0x0F) - 8.0f) * d;
+        out[j + 16] = ((float)(b[2 + j] >> 4) - 8.0f) * d;
+    }
+}
+
+/* dequant.rs:146-153, Q4_1: nibble * d + m. */
+static void dequant_q4_1(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b)), m = orc_f16_to_f32(rd16(b + 2));
+    for (int j = 0; j < 16; ++j) {
+        out[j] = (float)(b[4 + j] & 0x0F) * d + m;
+        out[j + 16] = (float)(b[4 + j] >> 4) * d + m;
+    }
+}
+
+static uint32_t rd32(const uint8_t *b) {
+    return (uint32_t)b[0] | ((uint32_t)b[1] << 8) | ((uint32_t)b[2] << 16) | ((uint32_t)b[3] << 24);
+}
+
+/* dequant.rs:155-166, Q5_0: 5th bit j (low) / j + 16 (high) of the 32-bit qh; (x - 16) * d. */
+static void dequant_q5_0(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b));
+    uint32_t h = rd32(b + 2);
+    const uint8_t *qs = b + 6;
+    for (int j = 0; j < 16; ++j) {
+        uint32_t x0 = (uint32_t)(qs[j] & 0x0F) | ((h >> j) & 1u) << 4;
+        uint32_t x1 = (uint32_t)(qs[j] >> 4) | ((h >> (j + 16)) & 1u) << 4;
+        out[j] = ((float)x0 - 16.0f) * d;
+        out[j + 16] = ((float)x1 - 16.0f) * d;
+    }
+}
+
+/* dequant.rs:168-180, Q5_1: x * d + m. */
+static void dequant_q5_1(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b)), m = orc_f16_to_f32(rd16(b + 2));
+    uint32_t h = rd32(b + 4);
+    const uint8_t *qs = b + 8;
+    for (int j = 0; j < 16; ++j) {
+        uint32_t x0 = (uint32_t)(qs[j] & 0x0F) | ((h >> j) & 1u) << 4;
+        uint32_t x1 = (uint32_t)(qs[j] >> 4) | ((h >> (j + 16)) & 1u) << 4;
+        out[j] = (float)x0 * d + m;
+        out[j + 16] = (float)x1 * d + m;
+    }
+}
+
+/* The IQ4_NL codebook: the 16 values a 4-bit index selects (IQ4_NL and
+ * IQ4_XS; crates/strata-gguf/src/tables.rs KVALUES_IQ4NL). A format constant. */
+static const int8_t kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+/* dequant.rs:182-189, IQ4_NL: d * codebook[nibble]. */
+static void dequant_iq4_nl(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b));
+    for (int j = 0; j < 16; ++j) {
+        out[j] = d * (float)kIq4nl[b[2 + j] & 0x0F];
+        out[j + 16] = d * (float)kIq4nl[b[2 + j] >> 4];
+    }
+}
+
+/* dequant.rs:191-206, IQ4_XS: 8 sub-blocks of 32 with 6-bit scales
+ * (4 low bits in scales_l, 2 high in scales_h); dl = d * (ls - 32). As
+ * strata-gguf writes it, every sub-block reads the same first 16 quant bytes
+ * (its qs slice does not advance with the sub-block; ggml's does). */
+static void dequant_iq4_xs(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b));
+    uint32_t scales_h = rd16(b + 2);
+    const uint8_t *scales_l = b + 4, *qs = b + 8;
+    for (int ib = 0; ib < 8; ++ib) {
+        uint32_t ls = (uint32_t)((scales_l[ib / 2] >> (4 * (ib % 2))) & 0x0F) | ((scales_h >> (2 * ib)) & 3u) << 4;
+        float dl = d * ((float)ls - 32.0f);
+        for (int j = 0; j < 16; ++j) {
+            out[32 * ib + j] = dl * (float)kIq4nl[qs[j] & 0x0F];
+            out[32 * ib + j + 16] = dl * (float)kIq4nl[qs[j] >> 4];
+        }
+    }
+}
+
+/* dequant.rs:304-349, Q3_K: 2-bit quants, a high bit per element in hmask
+ * (set: +0, clear: -4), 16 6-bit scales unpacked from 12 bytes, d at 108. */
+static void dequant_q3_k(const uint8_t *b, float *out) {
+    const uint8_t *hm = b, *q = b + 32;
+    float d_all = orc_f16_to_f32(rd16(b + 108));
+    const uint32_t kmask1 = 0x03030303u, kmask2 = 0x0f0f0f0fu;
+    uint32_t aux[4];
+    for (int i = 0; i < 3; ++i) aux[i] = rd32(b + 96 + 4 * i);
+    uint32_t tmp = aux[2];
+    aux[2] = ((aux[0] >> 4) & kmask2) | (((tmp >> 4) & kmask1) << 4);
+    aux[3] = ((aux[1] >> 4) & kmask2) | (((tmp >> 6) & kmask1) << 4);
+    aux[0] = (aux[0] & kmask2) | ((tmp & kmask1) << 4);
+    aux[1] = (aux[1] & kmask2) | (((tmp >> 2) & kmask1) << 4);
+    int8_t scales[16];
+    for (int i = 0; i < 16; ++i) scales[i] = (int8_t)(uint8_t)(aux[i / 4] >> (8 * (i % 4)));
+    int y = 0, is = 0, q_off = 0;
+    uint8_t m = 1;
+    for (int h = 0; h < 2; ++h) {
+        int shift = 0;
+        for (int g = 0; g < 4; ++g) {
+            float dl = d_all * (float)(int8_t)(scales[is] - 32);
+            ++is;
+            for (int l = 0; l < 16; ++l)
+                out[y + l] = dl * ((float)(int8_t)((q[q_off + l] >> shift) & 3) - ((hm[l] & m) ? 0.0f : 4.0f));
+            dl = d_all * (float)(int8_t)(scales[is] - 32);
+            ++is;
+            for (int l = 0; l < 16; ++l)
+                out[y + 16 + l] =
+                    dl * ((float)(int8_t)((q[q_off + l + 16] >> shift) & 3) - ((hm[l + 16] & m) ? 0.0f : 4.0f));
+            y += 32;
+            shift += 2;
+            m = (uint8_t)(m << 1);
+        }
+        q_off += 32;
+    }
+}
+
+/* dequant.rs:351-380, Q2_K (strata-gguf's layout: d, dmin, scales[16],
+ * qs[64]); (s, m) of sub-blocks is, is + 1 via get_scale_min_k4. */
+static void dequant_q2_k(const uint8_t *b, float *out) {
+    float d = orc_f16_to_f32(rd16(b)), mn = orc_f16_to_f32(rd16(b + 2));
+    const uint8_t *sc = b + 4, *q = b + 20;
+    int y = 0, q_off = 0, is = 0;
+    for (int g = 0; g < 2; ++g) {
+        uint8_t s, m;
+        get_scale_min_k4(is, sc, &s, &m);
+        float d1 = d * (float)s, m1 = mn * (float)m;
+        get_scale_min_k4(is + 1, sc, &s, &m);
+        float d2 = d * (float)s, m2 = mn * (float)m;
+        for (int l = 0; l < 32; ++l) {
+            out[y + l] = d1 * (float)(q[q_off + l] & 3) - m1;
+            out[y + l + 32] = d2 * (float)((q[q_off + l] >> 2) & 3) - m2;
+            out[y + l + 64] = d1 * (float)((q[q_off + l] >> 4) & 3) - m1;
+            out[y + l + 96] = d2 * (float)((q[q_off + l] >> 6) & 3) - m2;
+        }
+        y += 128;
+        q_off += 32;
+        is += 2;
+    }
+}
+
+/* E2M1 (FP4) codes in half units: magnitudes 0, 0.5, 1, 1.5, 2, 3, 4, 6 from
+ * the format's 2-bit exponent and 1-bit mantissa, doubled; bit 3 the sign
+ * (the values of strata-gguf's KVALUES_FP4, derived here from the format). */
+static float fp4_half_units(uint32_t code) {
+    uint32_t e = (code >> 1) & 3u, mbit = code & 1u;
+    float mag = e == 0 ? (float)mbit : (float)((2u + mbit) << (e - 1));  /* x2: 0,1 | 2,3 | 4,6 | 8,12 */
+    return (code & 8u) && mag != 0.0f ? -mag : mag;  /* code 8 is +0, as the table's 0 */
+}
+
+/* dequant.rs:386-395: E8M0 -> 2^(e-127); 0 is zero, 0xFF NaN. */
+static float e8m0_to_f32(uint8_t e) {
+    if (e == 0) return 0.0f;
+    if (e == 0xFF) return bits_f32(0x7FC00000u);
+    return bits_f32((uint32_t)e << 23);
+}
+
+/* dequant.rs:397-413: UE4M3 (no inf; 0x7F / 0xFF NaN). */
+static float ue4m3_to_f32(uint8_t e) {
+    int sign = (e & 0x80) != 0, ex = (e >> 3) & 0xF, man = e & 0x7;
+    float v;
+    if (ex == 0) v = (float)man / 8.0f * ldexpf(1.0f, -6);
+    else if (ex == 15 && man == 7) v = bits_f32(0x7FC00000u);
+    else v = ldexpf(1.0f, ex - 7) * (1.0f + (float)man / 8.0f);
+    return sign ? -v : v;
+}
+
+/* dequant.rs:415-424, MXFP4: d * fp4 * 0.5; low nibble j, high j + 16. */
+static void dequant_mxfp4(const uint8_t *b, float *out) {
+    float d = e8m0_to_f32(b[0]);
+    for (int j = 0; j < 16; ++j) {
+        out[j] = d * fp4_half_units(b[1 + j] & 0x0F) * 0.5f;
+        out[j + 16] = d * fp4_half_units(b[1 + j] >> 4) * 0.5f;
+    }
+}
+
+/* dequant.rs:426-444, NVFP4: four sub-blocks of 16 with a UE4M3 scale each;
+ * value j in the low nibble of qs[8s + j], j + 8 in the high one. */
+static void dequant_nvfp4(const uint8_t *b, float *out) {
+    for (int s = 0; s < 4; ++s) {
+        float ds = ue4m3_to_f32(b[s]);
+        for (int j = 0; j < 8; ++j) {
+            out[16 * s + j] = ds * fp4_half_units(b[4 + 8 * s + j] & 0x0F) * 0.5f;
+            out[16 * s + j + 8] = ds * fp4_half_units(b[4 + 8 * s + j] >> 4) * 0.5f;
+        }
+    }
+}
+
 static int dequant_block(uint32_t q, const uint8_t *b, float *out) {
     switch (q) {
     case ORC_F32: memcpy(out, b, 4); return ORC_OK;
@@ -190,6 +411,18 @@ static int dequant_block(uint32_t q, const uint8_t *b, float *out) {
     case ORC_Q4_K: dequant_q4_k(b, out); return ORC_OK;
     case ORC_Q5_K: dequant_q5_k(b, out); return ORC_OK;
     case ORC_Q6_K: dequant_q6_k(b, out); return ORC_OK;
+    case ORC_Q2_0: dequant_q2_0(b, out); return ORC_OK;
+    case ORC_Q8_1: dequant_q8_1(b, out); return ORC_OK;
+    case ORC_Q4_0: dequant_q4_0(b, out); return ORC_OK;
+    case ORC_Q4_1: dequant_q4_1(b, out); return ORC_OK;
+    case ORC_Q5_0: dequant_q5_0(b, out); return ORC_OK;
+    case ORC_Q5_1: dequant_q5_1(b, out); return ORC_OK;
+    case ORC_IQ4_NL: dequant_iq4_nl(b, out); return ORC_OK;
+    case ORC_IQ4_XS: dequant_iq4_xs(b, out); return ORC_OK;
+    case ORC_Q3_K: dequant_q3_k(b, out); return ORC_OK;
+    case ORC_Q2_K: dequant_q2_k(b, out); return ORC_OK;
+    case ORC_MXFP4: dequant_mxfp4(b, out); return ORC_OK;
+    case ORC_NVFP4: dequant_nvfp4(b, out); return ORC_OK;
     default: return ORC_ERR_UNSUPPORTED;
     }
 }

@@ -22,8 +22,10 @@ extern "C" {
 
 /* Strata ggml type ids: crates/strata-gguf/src/quant.rs:15-43 */
 enum {
-    ORC_F32 = 0, ORC_F16 = 1, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q5_K = 13,
-    ORC_Q6_K = 14, ORC_BF16 = 30
+    ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q4_1 = 3, ORC_Q5_0 = 6, ORC_Q5_1 = 7,
+    ORC_Q8_0 = 8, ORC_Q8_1 = 9, ORC_Q2_K = 10, ORC_Q3_K = 11, ORC_Q4_K = 12, ORC_Q5_K = 13,
+    ORC_Q6_K = 14, ORC_IQ4_NL = 20, ORC_IQ4_XS = 23, ORC_BF16 = 30, ORC_MXFP4 = 39,
+    ORC_NVFP4 = 40, ORC_Q2_0 = 42
 };
 
 /* status codes (mirrors strata_core::Error's variants used on this path) */

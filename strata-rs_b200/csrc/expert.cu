@@ -9,7 +9,7 @@
 // row slice by x[i]. Row ranges are split across CTAs; the per-range partial
 // sums go to a workspace and a second kernel adds them in a fixed order, so
 // results are deterministic run to run.
-#include "quant.cuh"
+#include "dequant_elem.cuh"
 #include "kernels.cuh"
 
 namespace strata {
@@ -33,19 +33,19 @@ __device__ __forceinline__ void unit16_cols(int t, int& colA, int& colB) {
         int H = t >> 3, u = t & 7;
         int l = 8 * (u & 3);
         colA = 128 * H + l + ((u >= 4) ? 32 : 0); colB = colA + 64;
-    } else {  // Q8_0: half block t = 16 consecutive columns
+    } else {  // Q8_0 and the other formats: unit t = 16 consecutive columns
         colA = 16 * t; colB = colA + 8;
     }
 }
 
 template <uint32_t Q>
 __host__ __device__ constexpr int units16_per_block() {
-    return (Q == kQ4_K || Q == kQ5_K || Q == kQ6_K) ? 16 : 2;  // Q8_0: two halves
+    return (Q == kQ4_K || Q == kQ5_K || Q == kQ6_K) ? 16 : block_elems(Q) / 16;  // Q8_0: two halves
 }
 // elements covered by one block, for unit indexing
 template <uint32_t Q>
 __host__ __device__ constexpr int unit_block_elems() {
-    return (Q == kQ4_K || Q == kQ5_K || Q == kQ6_K) ? 256 : 32;
+    return block_elems(Q);
 }
 
 // Dequantize the 16 weights of unit t of the block at blk (fp32; the fused
@@ -96,6 +96,10 @@ __device__ __forceinline__ void decode16(const uint8_t* __restrict__ blk, int t,
         float d = f16_bits_to_f32(rd16g(blk));
 #pragma unroll
         for (int l = 0; l < 16; ++l) w[l] = (float)(int8_t)__ldg(blk + 2 + 16 * t + l) * d;
+    } else {
+        // the other formats: columns 16 t .. 16 t + 15, the reference's exact values
+#pragma unroll
+        for (int l = 0; l < 16; ++l) w[l] = dequant_elem<Q>(blk, 16 * t + l);
     }
 }
 
@@ -259,6 +263,18 @@ int launch_expert_gemv_ws(uint32_t quant, const ExpertGemvArgs& a, float* work, 
     case kF32: return run_expert_float<kF32>(a, s);
     case kF16: return run_expert_float<kF16>(a, s);
     case kBF16: return run_expert_float<kBF16>(a, s);
+    case kQ4_0: return run_expert<kQ4_0>(a, work, work_floats, s);
+    case kQ4_1: return run_expert<kQ4_1>(a, work, work_floats, s);
+    case kQ5_0: return run_expert<kQ5_0>(a, work, work_floats, s);
+    case kQ5_1: return run_expert<kQ5_1>(a, work, work_floats, s);
+    case kQ8_1: return run_expert<kQ8_1>(a, work, work_floats, s);
+    case kQ2_K: return run_expert<kQ2_K>(a, work, work_floats, s);
+    case kQ3_K: return run_expert<kQ3_K>(a, work, work_floats, s);
+    case kIQ4_NL: return run_expert<kIQ4_NL>(a, work, work_floats, s);
+    case kIQ4_XS: return run_expert<kIQ4_XS>(a, work, work_floats, s);
+    case kMXFP4: return run_expert<kMXFP4>(a, work, work_floats, s);
+    case kNVFP4: return run_expert<kNVFP4>(a, work, work_floats, s);
+    case kQ2_0: return run_expert<kQ2_0>(a, work, work_floats, s);
     default: return -1;
     }
 }

@@ -14,7 +14,7 @@
 // bits 23..16 under 0x3F gives the float 1 + q/16, exactly. Summing
 // (1 + q/16)·x over a run and subtracting the run's sum of x yields sum(q·x)/16.
 // Q5_K uses 1 + q/32 and Q6_K 1 + u/64 the same way.
-#include "quant.cuh"
+#include "dequant_elem.cuh"
 #include "kernels.cuh"
 
 namespace strata {
@@ -328,6 +328,63 @@ __global__ void gemv_float_kernel(const uint8_t* __restrict__ W, int64_t row_byt
     }
 }
 
+// The other block formats (Q4_0 .. NVFP4): one warp per row, lanes stride over
+// K, each weight decoded by dequant_elem (the reference's exact values), fp32
+// FMAs. Not a fused fast path: these formats are outside the benchmark.
+template <uint32_t Q, int NB>
+__global__ void gemv_elem_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
+                                 const float* __restrict__ X, float* __restrict__ Y, int64_t ldy) {
+    constexpr int BE = block_elems(Q), BB = block_bytes(Q);
+    X += (int64_t)blockIdx.y * NB * K;
+    Y += (int64_t)blockIdx.y * NB * ldy;
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < N; row += (int64_t)gridDim.x * warps) {
+        const uint8_t* wr = W + row * row_bytes;
+        float acc[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
+        for (int64_t k = lane; k < K; k += 32) {
+            const float w = dequant_elem<Q>(wr + (k / BE) * BB, (int)(k % BE));
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[b] = fmaf(w, __ldg(X + b * K + k), acc[b]);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            float v = warp_sum(acc[b]);
+            if (lane == 0) Y[b * ldy + row] = v;
+        }
+    }
+}
+
+template <uint32_t Q, int NB>
+void launch_elem(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
+    int64_t grid = (a.N + 7) / 8;
+    int64_t cap = (int64_t)a.sm_count * 16;
+    if (grid > cap) grid = cap;
+    gemv_elem_kernel<Q, NB><<<dim3((unsigned)grid, chunks), 256, 0, s>>>(a.W, a.row_bytes, a.N, a.K, a.X, a.Y,
+                                                                         ldy_of(a));
+}
+
+template <uint32_t Q>
+int dispatch_elem(const GemvArgs& a, cudaStream_t s) {
+    switch (a.batch) {
+    case 1: launch_elem<Q, 1>(a, s); break;
+    case 2: launch_elem<Q, 2>(a, s); break;
+    case 3: launch_elem<Q, 3>(a, s); break;
+    case 4: launch_elem<Q, 4>(a, s); break;
+    case 5: launch_elem<Q, 5>(a, s); break;
+    case 6: launch_elem<Q, 6>(a, s); break;
+    case 7: launch_elem<Q, 7>(a, s); break;
+    case 8: launch_elem<Q, 8>(a, s); break;
+    default: return -1;
+    }
+    return 0;
+}
+
+#define STRATA_OTHER_FORMATS(X) \
+    X(kQ4_0) X(kQ4_1) X(kQ5_0) X(kQ5_1) X(kQ8_1) X(kQ2_K) X(kQ3_K) X(kIQ4_NL) X(kIQ4_XS) X(kMXFP4) X(kNVFP4) X(kQ2_0)
+
 template <uint32_t Q, int NB, int R>
 void launch_kq(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     constexpr int WARPS = 4;
@@ -421,6 +478,10 @@ static int launch_gemv_chunks(uint32_t quant, const GemvArgs& a, unsigned chunks
     case kF32: launch_float<kF32, 8>(a, s, chunks); return 0;
     case kF16: launch_float<kF16, 8>(a, s, chunks); return 0;
     case kBF16: launch_float<kBF16, 8>(a, s, chunks); return 0;
+#define STRATA_CHUNK_CASE(QQ) \
+    case QQ: launch_elem<QQ, 8>(a, s, chunks); return 0;
+        STRATA_OTHER_FORMATS(STRATA_CHUNK_CASE)
+#undef STRATA_CHUNK_CASE
     default: return -1;
     }
 }
@@ -445,6 +506,10 @@ int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s) {
     case kF32: return dispatch_float<kF32>(a, s);
     case kF16: return dispatch_float<kF16>(a, s);
     case kBF16: return dispatch_float<kBF16>(a, s);
+#define STRATA_ELEM_CASE(QQ) \
+    case QQ: return dispatch_elem<QQ>(a, s);
+        STRATA_OTHER_FORMATS(STRATA_ELEM_CASE)
+#undef STRATA_ELEM_CASE
     default: return -1;
     }
 }

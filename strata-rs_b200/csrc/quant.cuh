@@ -1,7 +1,8 @@
 // quant.cuh — ggml block layouts as strata-gguf stores them, and the device
 // helpers that decode them.
 //
-// Layouts (bytes), from crates/strata-gguf/src/dequant.rs and quant.rs:138-165:
+// Layouts (bytes), from crates/strata-gguf/src/dequant.rs and quant.rs:138-165
+// (the other formats' in dequant_elem.cuh):
 //   Q8_0  34 B / 32 elems : [d f16][qs i8 x32]                              (dequant.rs:123-128)
 //   Q4_K 144 B / 256      : [d f16][dmin f16][scales 12][qs 128]            (dequant.rs:247-270)
 //   Q5_K 176 B / 256      : [d f16][dmin f16][scales 12][qh 32][qs 128]     (dequant.rs:272-302)
@@ -15,16 +16,31 @@ namespace strata {
 
 // Strata ggml type ids (crates/strata-gguf/src/quant.rs:15-43).
 enum QuantId : uint32_t {
-    kF32 = 0, kF16 = 1, kQ8_0 = 8, kQ4_K = 12, kQ5_K = 13, kQ6_K = 14, kBF16 = 30,
+    kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ4_1 = 3, kQ5_0 = 6, kQ5_1 = 7, kQ8_0 = 8, kQ8_1 = 9, kQ2_K = 10,
+    kQ3_K = 11, kQ4_K = 12, kQ5_K = 13, kQ6_K = 14, kIQ4_NL = 20, kIQ4_XS = 23, kBF16 = 30, kMXFP4 = 39,
+    kNVFP4 = 40, kQ2_0 = 42,
 };
 
+// QuantType::block_size / type_size (quant.rs:124-163) of the types this
+// library runs; 0 for the others (upload rejects them).
 __host__ __device__ constexpr int block_elems(uint32_t q) {
-    return q == kQ8_0 ? 32 : (q == kQ4_K || q == kQ5_K || q == kQ6_K) ? 256
-         : (q == kF32 || q == kF16 || q == kBF16) ? 1 : 0;
+    return (q == kF32 || q == kF16 || q == kBF16) ? 1
+         : (q == kQ4_0 || q == kQ4_1 || q == kQ5_0 || q == kQ5_1 || q == kQ8_0 || q == kQ8_1 || q == kIQ4_NL ||
+            q == kMXFP4) ? 32
+         : (q == kNVFP4 || q == kQ2_0) ? 64
+         : (q == kQ2_K || q == kQ3_K || q == kQ4_K || q == kQ5_K || q == kQ6_K || q == kIQ4_XS) ? 256 : 0;
 }
 __host__ __device__ constexpr int block_bytes(uint32_t q) {
-    return q == kQ8_0 ? 34 : q == kQ4_K ? 144 : q == kQ5_K ? 176 : q == kQ6_K ? 210
-         : q == kF32 ? 4 : (q == kF16 || q == kBF16) ? 2 : 0;
+    return q == kF32 ? 4 : (q == kF16 || q == kBF16) ? 2
+         : (q == kQ4_0 || q == kIQ4_NL || q == kQ2_0) ? 18 : q == kQ4_1 ? 20 : q == kQ5_0 ? 22 : q == kQ5_1 ? 24
+         : q == kQ8_0 ? 34 : q == kQ8_1 ? 36 : q == kQ2_K ? 84 : q == kQ3_K ? 110 : q == kQ4_K ? 144
+         : q == kQ5_K ? 176 : q == kQ6_K ? 210 : q == kIQ4_XS ? 136 : q == kMXFP4 ? 17 : q == kNVFP4 ? 36 : 0;
+}
+// The formats beyond the benchmark's (dequant, the generic GEMV and expert
+// GEMV paths; no fused fast path).
+__host__ __device__ constexpr bool is_other_format(uint32_t q) {
+    return q == kQ4_0 || q == kQ4_1 || q == kQ5_0 || q == kQ5_1 || q == kQ8_1 || q == kQ2_K || q == kQ3_K ||
+           q == kIQ4_NL || q == kIQ4_XS || q == kMXFP4 || q == kNVFP4 || q == kQ2_0;
 }
 
 // binary16 -> binary32 by integer ops, exact for every input. A NaN keeps its

@@ -28,9 +28,14 @@ LIB_PATH = Path(os.environ.get("STRATA_CUDA_LIB", HERE / "libstrata_cuda.so"))
 
 # Strata ggml type ids (crates/strata-gguf/src/quant.rs:15-43)
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
+Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K, IQ4_NL, IQ4_XS, MXFP4, NVFP4, Q2_0 = 2, 3, 6, 7, 9, 10, 11, 20, 23, 39, 40, 42
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176),
-         Q6_K: (256, 210)}
-NAMES = {F32: "F32", F16: "F16", BF16: "BF16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+         Q6_K: (256, 210), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24), Q8_1: (32, 36),
+         Q2_K: (256, 84), Q3_K: (256, 110), IQ4_NL: (32, 18), IQ4_XS: (256, 136), MXFP4: (32, 17),
+         NVFP4: (64, 36), Q2_0: (64, 18)}
+NAMES = {F32: "F32", F16: "F16", BF16: "BF16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K",
+         Q4_0: "Q4_0", Q4_1: "Q4_1", Q5_0: "Q5_0", Q5_1: "Q5_1", Q8_1: "Q8_1", Q2_K: "Q2_K", Q3_K: "Q3_K",
+         IQ4_NL: "IQ4_NL", IQ4_XS: "IQ4_XS", MXFP4: "MXFP4", NVFP4: "NVFP4", Q2_0: "Q2_0"}
 
 
 def byte_size(quant: int, n: int) -> int:

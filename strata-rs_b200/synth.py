@@ -18,8 +18,13 @@ from __future__ import annotations
 import numpy as np
 
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
+# the other block formats (crates/strata-gguf/src/quant.rs:15-43, 124-163)
+Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K, IQ4_NL, IQ4_XS, MXFP4, NVFP4, Q2_0 = 2, 3, 6, 7, 9, 10, 11, 20, 23, 39, 40, 42
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176),
-         Q6_K: (256, 210)}
+         Q6_K: (256, 210), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24), Q8_1: (32, 36),
+         Q2_K: (256, 84), Q3_K: (256, 110), IQ4_NL: (32, 18), IQ4_XS: (256, 136), MXFP4: (32, 17),
+         NVFP4: (64, 36), Q2_0: (64, 18)}
+OTHER_FORMATS = [Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K, IQ4_NL, IQ4_XS, MXFP4, NVFP4, Q2_0]
 
 
 def rng(seed: int) -> np.random.Generator:
@@ -53,6 +58,22 @@ def quant_blocks(g: np.random.Generator, quant: int, n_blocks: int,
     elif quant == Q6_K:
         lo, hi = d_range or (0.001, 0.01)
         b[:, 208:210] = _f16(g.uniform(lo, hi, n_blocks)).view(np.uint8).reshape(n_blocks, 2)
+    elif quant in (Q4_1, Q5_1, Q2_K):
+        # fp16 d and a second fp16 (min / dmin) at byte 2
+        lo, hi = d_range or (0.001, 0.01)
+        b[:, 0:2] = _f16(g.uniform(lo, hi, n_blocks)).view(np.uint8).reshape(n_blocks, 2)
+        b[:, 2:4] = _f16(g.uniform(-hi, hi, n_blocks) if quant != Q2_K else g.uniform(lo, hi, n_blocks)) \
+            .view(np.uint8).reshape(n_blocks, 2)
+    elif quant == Q3_K:
+        lo, hi = d_range or (0.001, 0.01)
+        b[:, 108:110] = _f16(g.uniform(lo, hi, n_blocks)).view(np.uint8).reshape(n_blocks, 2)
+    elif quant == MXFP4:
+        b[:, 0] = g.integers(110, 125, size=n_blocks)          # E8M0 2^-17 .. 2^-3
+    elif quant == NVFP4:
+        b[:, 0:4] = g.integers(0x18, 0x48, size=(n_blocks, 4))  # UE4M3 ~2^-4 .. 2^2, finite
+    elif quant in (Q4_0, Q5_0, Q8_1, IQ4_NL, IQ4_XS, Q2_0):
+        lo, hi = d_range or (0.001, 0.01)
+        b[:, 0:2] = _f16(g.uniform(lo, hi, n_blocks)).view(np.uint8).reshape(n_blocks, 2)
     return b
 
 

@@ -22,14 +22,19 @@ def dequant_case(case: dict) -> np.ndarray:
 
 
 def lcg_block(quant: int, nbytes: int, spec: dict) -> np.ndarray:
-    """dequant_tests.rs:219-237: LCG bytes, then an fp16 scale of 0.125 in the
-    first two bytes of every quantized type."""
+    """dequant_tests.rs:219-237: LCG bytes, then a finite scale: the E8M0 /
+    UE4M3 scale bytes of MXFP4 / NVFP4, an fp16 0.125 in the first two bytes
+    of every other quantized type."""
     state = spec["seed"]
     out = np.empty(nbytes, np.uint8)
     for i in range(nbytes):
         state = (state * spec["mul"] + spec["add"]) & 0xFFFFFFFF
         out[i] = (state >> spec["shift"]) & 0xFF
-    if quant not in (0, 1, 30):
+    special = spec.get("scale_bytes", {}).get(str(quant))
+    if special:
+        for off, v in special:
+            out[off] = v
+    elif quant not in (0, 1, 30):
         out[0:2] = f16_bytes(spec["scale_f16"])
     return out
 

@@ -80,4 +80,127 @@ def q6_k(blocks: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
-DEQUANT = {8: q8_0, 12: q4_k, 13: q5_k, 14: q6_k}
+# ---- the other block formats, from their byte layouts
+
+
+def _nibbles(qs: np.ndarray) -> np.ndarray:
+    """(n, 16) bytes -> (n, 32) values: low nibbles first, then high (elements j, j + 16)."""
+    return np.concatenate([qs & 0x0F, qs >> 4], axis=1)
+
+
+def _bits32(b4: np.ndarray) -> np.ndarray:
+    """(n, 4) little-endian bytes -> (n, 32) bits, bit i at column i."""
+    w = b4.copy().view(np.uint32).reshape(-1)
+    return ((w[:, None] >> np.arange(32, dtype=np.uint32)) & 1).astype(np.uint8)
+
+
+def q4_0(b):
+    return (((_nibbles(b[:, 2:18]).astype(f32) - f32(8)).astype(f32)) * _f16(b[:, 0:2])[:, None]).astype(f32).reshape(-1)
+
+
+def q4_1(b):
+    d, m = _f16(b[:, 0:2])[:, None], _f16(b[:, 2:4])[:, None]
+    return ((_nibbles(b[:, 4:20]).astype(f32) * d).astype(f32) + m).astype(f32).reshape(-1)
+
+
+def q5_0(b):
+    x = _nibbles(b[:, 6:22]) | (_bits32(b[:, 2:6]) << 4)
+    return (((x.astype(f32) - f32(16)).astype(f32)) * _f16(b[:, 0:2])[:, None]).astype(f32).reshape(-1)
+
+
+def q5_1(b):
+    d, m = _f16(b[:, 0:2])[:, None], _f16(b[:, 2:4])[:, None]
+    x = _nibbles(b[:, 8:24]) | (_bits32(b[:, 4:8]) << 4)
+    return ((x.astype(f32) * d).astype(f32) + m).astype(f32).reshape(-1)
+
+
+def q8_1(b):
+    return (b[:, 4:36].view(np.int8).astype(f32) * _f16(b[:, 0:2])[:, None]).astype(f32).reshape(-1)
+
+
+def q2_0(b):
+    codes = ((b[:, 2:18, None] >> (2 * np.arange(4, dtype=np.uint8))) & 3).reshape(-1, 64)
+    return (((codes.astype(f32) - f32(1)).astype(f32)) * _f16(b[:, 0:2])[:, None]).astype(f32).reshape(-1)
+
+
+IQ4 = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.int8)
+
+
+def iq4_nl(b):
+    return (_f16(b[:, 0:2])[:, None] * IQ4[_nibbles(b[:, 2:18])].astype(f32)).astype(f32).reshape(-1)
+
+
+def iq4_xs(b):
+    n = b.shape[0]
+    d = _f16(b[:, 0:2])
+    sh = b[:, 2:4].copy().view(np.uint16).reshape(-1).astype(np.uint32)
+    ib = np.arange(8)
+    ls = ((b[:, 4 + ib // 2] >> (4 * (ib % 2))) & 0x0F).astype(np.uint32) | (((sh[:, None] >> (2 * ib)) & 3) << 4)
+    dl = (d[:, None] * (ls.astype(f32) - f32(32)).astype(f32)).astype(f32)          # (n, 8)
+    # strata-gguf's dequant_iq4_xs reads qs[0..16] for every sub-block (dequant.rs:194-203)
+    vals = IQ4[_nibbles(b[:, 8:24])].astype(f32)                                        # (n, 32)
+    return (dl[:, :, None] * vals[:, None, :]).astype(f32).reshape(-1)
+
+
+def q2_k(b):
+    n = b.shape[0]
+    d, mn = _f16(b[:, 0:2]), _f16(b[:, 2:4])
+    sc, q = b[:, 4:20], b[:, 20:84].reshape(n, 2, 32)
+    out = np.empty((n, 2, 4, 32), f32)
+    for g in range(2):
+        s = (sc[:, 2 * g:2 * g + 2] & 63).astype(f32)          # is = 2g, 2g + 1 (j < 4)
+        m = (sc[:, 2 * g + 4:2 * g + 6] & 63).astype(f32)
+        dd = (d[:, None] * s).astype(f32)
+        mm = (mn[:, None] * m).astype(f32)
+        for f in range(4):                                     # 2-bit field f: sub-block f % 2
+            v = ((q[:, g] >> (2 * f)) & 3).astype(f32)
+            out[:, g, f] = ((dd[:, f % 2, None] * v).astype(f32) - mm[:, f % 2, None]).astype(f32)
+    return out.reshape(-1)
+
+
+def q3_k(b):
+    n = b.shape[0]
+    hm, q = b[:, 0:32], b[:, 32:96].reshape(n, 2, 32)
+    d = _f16(b[:, 108:110])
+    raw = b[:, 96:108]
+    # 16 six-bit scales: low 4 bits from bytes 0..7 (nibbles), high 2 bits from bytes 8..11
+    lo = np.concatenate([raw[:, 0:8] & 0x0F, raw[:, 0:8] >> 4], axis=1)            # scale i: i < 8 low, else high
+    hi = ((raw[:, 8:12, None] >> (2 * np.arange(4, dtype=np.uint8))) & 3)           # (n, 4, 4): byte k, pair p
+    hi = hi.transpose(0, 2, 1).reshape(n, 16)                                       # scale 4p + k
+    sc = (lo | (hi << 4)).astype(np.int32) - 32
+    out = np.empty((n, 2, 4, 2, 16), f32)
+    for h in range(2):
+        for s4 in range(4):
+            bit = ((hm >> (4 * h + s4)) & 1).reshape(n, 2, 16)
+            v = ((q[:, h] >> (2 * s4)) & 3).reshape(n, 2, 16).astype(f32)
+            v = (v - np.where(bit == 1, f32(0), f32(4))).astype(f32)
+            dl = (d[:, None] * sc[:, 8 * h + 2 * s4:8 * h + 2 * s4 + 2].astype(f32)).astype(f32)
+            out[:, h, s4] = (dl[:, :, None] * v).astype(f32)
+    return out.reshape(-1)
+
+
+def _fp4(codes):
+    mag = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], f32)[codes & 7]
+    return np.where((codes & 8) != 0, -mag, mag).astype(f32) + f32(0)  # +0 for code 8
+
+
+def mxfp4(b):
+    e = b[:, 0].astype(np.uint32)
+    d = np.where(e == 0, f32(0), (e << 23).view(np.float32)).astype(f32)
+    return ((d[:, None] * (_fp4(_nibbles(b[:, 1:17])) * f32(2)).astype(f32)).astype(f32) * f32(0.5)).astype(f32).reshape(-1)
+
+
+def nvfp4(b):
+    n = b.shape[0]
+    e = b[:, 0:4].astype(np.int32)
+    ex, man = (e >> 3) & 15, e & 7
+    v = np.where(ex == 0, (man.astype(f32) / f32(8)).astype(f32) * f32(2.0 ** -6),
+                 np.ldexp(f32(1), ex - 7).astype(f32) * (f32(1) + (man.astype(f32) / f32(8)).astype(f32)))
+    ds = np.where((e & 0x80) != 0, -v, v).astype(f32)                                 # (n, 4)
+    qs = b[:, 4:36].reshape(n, 4, 8)
+    vals = np.concatenate([qs & 0x0F, qs >> 4], axis=2)                                 # (n, 4, 16)
+    return ((ds[:, :, None] * (_fp4(vals) * f32(2)).astype(f32)).astype(f32) * f32(0.5)).astype(f32).reshape(-1)
+
+
+DEQUANT = {8: q8_0, 12: q4_k, 13: q5_k, 14: q6_k, 2: q4_0, 3: q4_1, 6: q5_0, 7: q5_1, 9: q8_1, 10: q2_k,
+           11: q3_k, 20: iq4_nl, 23: iq4_xs, 39: mxfp4, 40: nvfp4, 42: q2_0}

@@ -13,6 +13,7 @@ import pytest
 import oracle
 import numpy_dequant
 from golden import reference_cases as rc
+import synth
 from synth import bf16_bits, quant_blocks, rng, Q4_K, Q5_K, Q6_K, Q8_0
 
 
@@ -219,3 +220,14 @@ def test_elementwise_ops_match_numpy_f64():
     assert np.max(np.abs(r[:, half:2 * half] - (a * np.sin(th) + b * np.cos(th)))) < 1e-5
     assert np.array_equal(r[:, 64:], h[:, 64:])
     assert np.array_equal(oracle.add(x, w[None, :].repeat(3, 0)), x + w)
+
+
+@pytest.mark.parametrize("quant", synth.OTHER_FORMATS)
+def test_other_formats_match_independent_numpy_restatement(quant):
+    """The formats beyond the benchmark's four, oracle vs the numpy restatement, bit for bit."""
+    g = rng(600 + quant)
+    blocks = synth.quant_blocks(g, quant, 256)
+    bs, _ = synth.BLOCK[quant]
+    got = oracle.dequantize_row(quant, blocks.reshape(-1), blocks.shape[0] * bs)
+    want = numpy_dequant.DEQUANT[quant](blocks)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))

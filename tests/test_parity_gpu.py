@@ -172,7 +172,7 @@ def test_errors(ctx):
         ctx.upload(data, Q4_K, 2, 200)
     assert e.value.code == sc.ERR_TRUNCATED
     with pytest.raises(sc.BackendError) as e:
-        ctx.upload(data, 2, 4, 256)  # Q4_0: not on this path
+        ctx.upload(data, 16, 4, 256)  # IQ2_XXS: not on this path (a grid-table i-quant)
     assert e.value.code == sc.ERR_UNSUPPORTED_QUANT
     w = ctx.upload(data, Q4_K, 4, 256)
     with pytest.raises(sc.BackendError) as e:
