@@ -169,8 +169,10 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     comm_release(ctx);
     for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag, &ctx->gemm_work, &ctx->x_bf16, &ctx->moe_work})
         if (b->ptr) cudaFree(b->ptr);
-    for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host})
+    for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host, &ctx->stage[0], &ctx->stage[1]})
         if (b->ptr) cudaFreeHost(b->ptr);
+    for (cudaEvent_t& e : ctx->stage_ev)
+        if (e) cudaEventDestroy(e);
     cudaEventDestroy(ctx->done);
     if (ctx->fork) cudaEventDestroy(ctx->fork);
     if (ctx->join) cudaEventDestroy(ctx->join);
@@ -230,6 +232,65 @@ int strata_cuda_stream(const strata_ctx* ctx, void** out) {
     return STRATA_OK;
 }
 
+namespace {
+
+constexpr size_t kStageChunk = size_t(32) << 20;  // bytes per staging chunk
+constexpr int kStageThreads = 8;                  // host threads filling a chunk
+
+// Copies `n` bytes of host memory (typically a read-only mmap of the model
+// file, paged in on first touch) to the device. Small tensors go in one
+// cudaMemcpy; large ones through two pinned chunks: host threads fill one
+// (taking the page faults in parallel) while the DMA engine drains the other.
+int copy_in(strata_ctx* ctx, void* dst, const uint8_t* src, size_t n) {
+    if (n < 2 * kStageChunk) {
+        cudaError_t e = cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice);
+        return e == cudaSuccess ? STRATA_OK : cuda_fail(ctx, e, "cudaMemcpy(weights)");
+    }
+    int rc;
+    for (int k = 0; k < 2; ++k) {
+        if ((rc = ensure_pinned(ctx, ctx->stage[k], kStageChunk, "cudaMallocHost(upload staging)"))) return rc;
+        if (!ctx->stage_ev[k]) {
+            cudaError_t e = cudaEventCreateWithFlags(&ctx->stage_ev[k], cudaEventDisableTiming);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventCreate(upload staging)");
+        }
+    }
+    size_t off = 0;
+    for (int i = 0; off < n; ++i) {
+        const int k = i & 1;
+        const size_t len = n - off < kStageChunk ? n - off : kStageChunk;
+        if (i >= 2) {  // the chunk's previous copy must have left the pinned buffer (bounded wait)
+            auto t0 = std::chrono::steady_clock::now();
+            for (;;) {
+                cudaError_t e = cudaEventQuery(ctx->stage_ev[k]);
+                if (e == cudaSuccess) break;
+                if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "upload staging");
+                auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+                if ((uint64_t)ms.count() > ctx->wait_timeout_ms)
+                    return fail(ctx, STRATA_ERR_TIMEOUT, "upload copy did not finish within %u ms", ctx->wait_timeout_ms);
+                std::this_thread::yield();
+            }
+        }
+        uint8_t* stage = static_cast<uint8_t*>(ctx->stage[k].ptr);
+        std::thread th[kStageThreads];
+        const size_t part = (len + kStageThreads - 1) / kStageThreads;
+        for (int t = 0; t < kStageThreads; ++t) {
+            const size_t a = t * part, b = a + part < len ? a + part : len;
+            if (a < b) th[t] = std::thread([=] { memcpy(stage + a, src + off + a, b - a); });
+        }
+        for (auto& t : th)
+            if (t.joinable()) t.join();
+        cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, stage, len, cudaMemcpyHostToDevice,
+                                        ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(weights)");
+        e = cudaEventRecord(ctx->stage_ev[k], ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventRecord(upload staging)");
+        off += len;
+    }
+    return wait_stream(ctx, ctx->stream);
+}
+
+}  // namespace
+
 int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32_t quant, int64_t n_expert,
                        int64_t rows, int64_t cols, strata_weight** out) {
     if (!ctx || !out) return STRATA_ERR_INVALID;
@@ -267,11 +328,11 @@ int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32
             delete w;
             return cuda_fail(ctx, e, "cudaMalloc(weights)");
         }
-        e = cudaMemcpy(w->dev, bytes, (size_t)need, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
+        const int rc = copy_in(ctx, w->dev, bytes, (size_t)need);
+        if (rc) {
             cudaFree(w->dev);
             delete w;
-            return cuda_fail(ctx, e, "cudaMemcpy(weights)");
+            return rc;
         }
     }
     if (n_expert == 0 && need > 0)

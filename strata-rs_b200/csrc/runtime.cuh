@@ -48,6 +48,10 @@ struct strata_ctx {
     cudaStream_t aux = nullptr, aux_lo = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
     strata::PinnedBuf x_host, y_host;
+    // upload staging: two pinned chunks filled by host threads while the
+    // other one is copied to the device (large tensors), with their events
+    strata::PinnedBuf stage[2];
+    cudaEvent_t stage_ev[2] = {nullptr, nullptr};
     strata::CommState* comm = nullptr;
     int* err_host = nullptr;  // host-mapped word kernels set when a bounded wait expires
     int* err_dev = nullptr;
