@@ -115,6 +115,22 @@ int strata_cuda_upload(strata_ctx *ctx, const uint8_t *bytes, size_t len, uint32
                        int64_t n_expert, int64_t rows, int64_t cols, strata_weight **out);
 int strata_cuda_free_weight(strata_weight *w);
 
+/* Many tensors in one pass (a model load: WeightStore::new,
+ * crates/strata-core/src/weights.rs:49-67, walking every shard's tensors).
+ * Each item means what strata_cuda_upload's arguments mean. The bytes of all
+ * items stream through the same two pinned chunks, so the host threads that
+ * fill one chunk take the next tensor's page faults while the DMA engine
+ * drains the other. All or nothing: on an error no item stays resident and
+ * every out[i] is NULL; the message names the failing item. */
+typedef struct {
+    const uint8_t *bytes;
+    size_t len;
+    uint32_t quant;
+    int64_t n_expert, rows, cols;
+} strata_upload;
+int strata_cuda_upload_many(strata_ctx *ctx, const strata_upload *items, int64_t n,
+                            strata_weight **out);
+
 /* Dequantizes rows [row0, row0 + nrows) of expert `expert` (0 for dense)
  * into out_host (nrows * cols f32). Bit-exact with dequantize_row. */
 int strata_cuda_dequant(strata_ctx *ctx, const strata_weight *w, int64_t expert, int64_t row0,

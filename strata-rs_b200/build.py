@@ -1,6 +1,6 @@
 """Builds libstrata_cuda.so in-tree with nvcc for sm_100a.
 
-Every .cu under csrc/ is compiled to an object with
+Every .cu (and host-only .cpp) under csrc/ is compiled to an object with
 `-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`, then linked into one
 shared library next to this file. Objects go to _build/ (git-ignored).
 Run: python strata-rs_b200/build.py [--verbose-ptxas]
@@ -26,7 +26,7 @@ CXXFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-Wall", "--ex
 def _needs(obj: Path, src: Path) -> bool:
     if not obj.exists():
         return True
-    deps = [src] + sorted(CSRC.glob("*.cuh")) + sorted((HERE.parent / "include").glob("*.h"))
+    deps = [src] + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted((HERE.parent / "include").glob("*.h"))
     return any(d.stat().st_mtime > obj.stat().st_mtime for d in deps)
 
 
@@ -45,7 +45,7 @@ def _compile(src: Path, ptxas_v: bool) -> tuple[Path, str]:
 
 def build(ptxas_v: bool = False, quiet: bool = True) -> Path:
     BUILD.mkdir(exist_ok=True)
-    srcs = sorted(CSRC.glob("*.cu"))
+    srcs = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         results = list(ex.map(lambda s: _compile(s, ptxas_v), srcs))
     objs = [o for o, _ in results]

@@ -10,6 +10,10 @@
 #include <cstdio>
 #include <cstring>
 #include <thread>
+#include <vector>
+
+#include "host.h"
+#include "staging.h"
 
 using namespace strata;
 
@@ -26,6 +30,14 @@ int fail(strata_ctx* ctx, int code, const char* fmt, ...) {
     }
     return code;
 }
+
+int report(strata_ctx* ctx, int code, const char* msg) {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    ctx->last_error = msg;
+    return code;
+}
+
+bool quant_on_device(uint32_t quant) { return block_elems(quant) != 0; }
 
 int cuda_fail(strata_ctx* ctx, cudaError_t e, const char* what) {
     return fail(ctx, e == cudaErrorMemoryAllocation ? STRATA_ERR_OOM : STRATA_ERR_CUDA, "%s: %s (%s)", what,
@@ -237,14 +249,36 @@ namespace {
 constexpr size_t kStageChunk = size_t(32) << 20;  // bytes per staging chunk
 constexpr int kStageThreads = 8;                  // host threads filling a chunk
 
-// Copies `n` bytes of host memory (typically a read-only mmap of the model
-// file, paged in on first touch) to the device. Small tensors go in one
-// cudaMemcpy; large ones through two pinned chunks: host threads fill one
-// (taking the page faults in parallel) while the DMA engine drains the other.
-int copy_in(strata_ctx* ctx, void* dst, const uint8_t* src, size_t n) {
-    if (n < 2 * kStageChunk) {
-        cudaError_t e = cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice);
-        return e == cudaSuccess ? STRATA_OK : cuda_fail(ctx, e, "cudaMemcpy(weights)");
+// Bounded wait for a staging chunk's previous copy to leave the pinned buffer.
+int wait_stage(strata_ctx* ctx, cudaEvent_t ev) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return STRATA_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "upload staging");
+        auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+        if ((uint64_t)ms.count() > ctx->wait_timeout_ms)
+            return fail(ctx, STRATA_ERR_TIMEOUT, "upload copy did not finish within %u ms", ctx->wait_timeout_ms);
+        std::this_thread::yield();
+    }
+}
+
+// Copies host byte ranges (typically slices of a read-only mmap of the model
+// file, paged in on first touch) to their device destinations. Under 64 MiB
+// in all: one cudaMemcpy per range. More: the ranges, taken as one stream, go
+// through two pinned 32 MiB chunks; host threads fill one (taking the page
+// faults in parallel) while the DMA engine drains the other, and a chunk may
+// carry the end of one range and the start of the next.
+int copy_in(strata_ctx* ctx, const StageSeg* segs, int64_t nseg) {
+    size_t total = 0;
+    for (int64_t i = 0; i < nseg; ++i) total += segs[i].n;
+    if (total < 2 * kStageChunk) {
+        for (int64_t i = 0; i < nseg; ++i) {
+            if (!segs[i].n) continue;
+            cudaError_t e = cudaMemcpy(segs[i].dst, segs[i].src, segs[i].n, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpy(weights)");
+        }
+        return STRATA_OK;
     }
     int rc;
     for (int k = 0; k < 2; ++k) {
@@ -254,39 +288,118 @@ int copy_in(strata_ctx* ctx, void* dst, const uint8_t* src, size_t n) {
             if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventCreate(upload staging)");
         }
     }
-    size_t off = 0;
-    for (int i = 0; off < n; ++i) {
+    rc = STRATA_OK;
+    StageCursor cur;
+    std::vector<StagePiece> pieces;
+    for (int i = 0;; ++i) {
         const int k = i & 1;
-        const size_t len = n - off < kStageChunk ? n - off : kStageChunk;
-        if (i >= 2) {  // the chunk's previous copy must have left the pinned buffer (bounded wait)
-            auto t0 = std::chrono::steady_clock::now();
-            for (;;) {
-                cudaError_t e = cudaEventQuery(ctx->stage_ev[k]);
-                if (e == cudaSuccess) break;
-                if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "upload staging");
-                auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
-                if ((uint64_t)ms.count() > ctx->wait_timeout_ms)
-                    return fail(ctx, STRATA_ERR_TIMEOUT, "upload copy did not finish within %u ms", ctx->wait_timeout_ms);
-                std::this_thread::yield();
-            }
-        }
+        const size_t len = stage_plan(segs, nseg, cur, kStageChunk, pieces);
+        if (!len) break;
+        if (i >= 2 && (rc = wait_stage(ctx, ctx->stage_ev[k]))) break;
         uint8_t* stage = static_cast<uint8_t*>(ctx->stage[k].ptr);
         std::thread th[kStageThreads];
         const size_t part = (len + kStageThreads - 1) / kStageThreads;
         for (int t = 0; t < kStageThreads; ++t) {
             const size_t a = t * part, b = a + part < len ? a + part : len;
-            if (a < b) th[t] = std::thread([=] { memcpy(stage + a, src + off + a, b - a); });
+            if (a < b) th[t] = std::thread([&pieces, segs, stage, a, b] { stage_fill(pieces, segs, stage, a, b); });
         }
         for (auto& t : th)
             if (t.joinable()) t.join();
-        cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, stage, len, cudaMemcpyHostToDevice,
-                                        ctx->stream);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(weights)");
-        e = cudaEventRecord(ctx->stage_ev[k], ctx->stream);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventRecord(upload staging)");
-        off += len;
+        cudaError_t e = cudaSuccess;
+        for (const StagePiece& p : pieces) {
+            e = cudaMemcpyAsync(segs[p.seg].dst + p.seg_off, stage + p.off, p.n, cudaMemcpyHostToDevice,
+                                ctx->stream);
+            if (e != cudaSuccess) break;
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(ctx->stage_ev[k], ctx->stream);
+        if (e != cudaSuccess) {
+            rc = cuda_fail(ctx, e, "cudaMemcpyAsync(weights)");
+            break;
+        }
+    }
+    if (rc) {  // copies already queued still read the pinned chunks: let them finish
+        cudaStreamSynchronize(ctx->stream);
+        return rc;
     }
     return wait_stream(ctx, ctx->stream);
+}
+
+// Validates one upload and returns the bytes it keeps resident (row_bytes in *rb).
+int check_upload(strata_ctx* ctx, const strata_upload& u, int64_t* need, int64_t* rb) {
+    const int be = block_elems(u.quant);
+    if (be == 0) return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "quant type id %u is not on the CUDA path", u.quant);
+    if (u.n_expert < 0 || u.rows < 0 || u.cols <= 0 || (!u.bytes && u.len > 0))
+        return fail(ctx, STRATA_ERR_INVALID, "bad shape n_expert=%lld rows=%lld cols=%lld", (long long)u.n_expert,
+                    (long long)u.rows, (long long)u.cols);
+    if (u.cols % be != 0)
+        return fail(ctx, STRATA_ERR_TRUNCATED, "cols=%lld is not a whole number of %d-element blocks",
+                    (long long)u.cols, be);
+    *rb = quant_row_bytes(u.quant, u.cols);
+    const int64_t mats = u.n_expert > 0 ? u.n_expert : 1;
+    if (u.rows > 0 && (mats > INT64_MAX / u.rows || mats * u.rows > INT64_MAX / *rb))
+        return fail(ctx, STRATA_ERR_INVALID, "tensor of %lld x %lld rows is too large", (long long)mats,
+                    (long long)u.rows);
+    *need = mats * u.rows * *rb;
+    if ((uint64_t)u.len < (uint64_t)*need)
+        return fail(ctx, STRATA_ERR_TRUNCATED, "tensor needs %lld bytes, got %zu", (long long)*need, u.len);
+    return STRATA_OK;
+}
+
+// strata_cuda_upload_many with the context lock held.
+int upload_locked(strata_ctx* ctx, const strata_upload* items, int64_t n, strata_weight** out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = nullptr;
+    std::vector<int64_t> need(n), rb(n);
+    uint64_t total = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int rc = check_upload(ctx, items[i], &need[i], &rb[i]);
+        if (rc) return n > 1 ? fail(ctx, rc, "upload %lld of %lld: %s", (long long)i, (long long)n,
+                                   ctx->last_error.c_str())
+                             : rc;
+        total += (uint64_t)need[i];
+    }
+    if (ctx->budget_bytes && ctx->resident_bytes + total > ctx->budget_bytes)
+        return fail(ctx, STRATA_ERR_BUDGET, "upload of %llu bytes exceeds the weight budget (%llu resident of %llu)",
+                    (unsigned long long)total, (unsigned long long)ctx->resident_bytes,
+                    (unsigned long long)ctx->budget_bytes);
+    cudaSetDevice(ctx->device);
+    std::vector<strata_weight*> ws(n, nullptr);
+    std::vector<StageSeg> segs;
+    segs.reserve(n);
+    int rc = STRATA_OK;
+    for (int64_t i = 0; i < n && !rc; ++i) {
+        strata_weight* w = new strata_weight();
+        w->ctx = ctx;
+        w->quant = items[i].quant;
+        w->n_expert = items[i].n_expert;
+        w->rows = items[i].rows;
+        w->cols = items[i].cols;
+        w->row_bytes = rb[i];
+        w->bytes = (size_t)need[i];
+        ws[i] = w;
+        if (need[i] > 0) {
+            cudaError_t e = cudaMalloc(&w->dev, (size_t)need[i]);
+            if (e != cudaSuccess)
+                rc = cuda_fail(ctx, e, "cudaMalloc(weights)");
+            else
+                segs.push_back({w->dev, items[i].bytes, (size_t)need[i]});
+        }
+    }
+    if (!rc) rc = copy_in(ctx, segs.data(), (int64_t)segs.size());
+    if (rc) {
+        for (strata_weight* w : ws) {
+            if (w && w->dev) cudaFree(w->dev);
+            delete w;
+        }
+        return rc;
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        strata_weight* w = ws[i];
+        if (w->n_expert == 0 && w->bytes > 0)
+            w->has_tmap = encode_gemv_tmap(w->quant, w->dev, w->rows, w->row_bytes, w->tmap);
+        out[i] = w;
+    }
+    ctx->resident_bytes += total;
+    return STRATA_OK;
 }
 
 }  // namespace
@@ -295,51 +408,14 @@ int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32
                        int64_t rows, int64_t cols, strata_weight** out) {
     if (!ctx || !out) return STRATA_ERR_INVALID;
     std::lock_guard<std::mutex> g(ctx->mu);
-    *out = nullptr;
-    int be = block_elems(quant);
-    if (be == 0) return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "quant type id %u is not on the CUDA path", quant);
-    if (n_expert < 0 || rows < 0 || cols <= 0 || (!bytes && len > 0))
-        return fail(ctx, STRATA_ERR_INVALID, "bad shape n_expert=%lld rows=%lld cols=%lld", (long long)n_expert,
-                    (long long)rows, (long long)cols);
-    if (cols % be != 0)
-        return fail(ctx, STRATA_ERR_TRUNCATED, "cols=%lld is not a whole number of %d-element blocks",
-                    (long long)cols, be);
-    int64_t rb = quant_row_bytes(quant, cols);
-    int64_t mats = n_expert > 0 ? n_expert : 1;
-    int64_t need = mats * rows * rb;
-    if ((int64_t)len < need)
-        return fail(ctx, STRATA_ERR_TRUNCATED, "tensor needs %lld bytes, got %zu", (long long)need, len);
-    if (ctx->budget_bytes && ctx->resident_bytes + (uint64_t)need > ctx->budget_bytes)
-        return fail(ctx, STRATA_ERR_BUDGET, "upload of %lld bytes exceeds the weight budget (%llu resident of %llu)",
-                    (long long)need, (unsigned long long)ctx->resident_bytes,
-                    (unsigned long long)ctx->budget_bytes);
-    cudaSetDevice(ctx->device);
-    strata_weight* w = new strata_weight();
-    w->ctx = ctx;
-    w->quant = quant;
-    w->n_expert = n_expert;
-    w->rows = rows;
-    w->cols = cols;
-    w->row_bytes = rb;
-    w->bytes = (size_t)need;
-    if (need > 0) {
-        cudaError_t e = cudaMalloc(&w->dev, (size_t)need);
-        if (e != cudaSuccess) {
-            delete w;
-            return cuda_fail(ctx, e, "cudaMalloc(weights)");
-        }
-        const int rc = copy_in(ctx, w->dev, bytes, (size_t)need);
-        if (rc) {
-            cudaFree(w->dev);
-            delete w;
-            return rc;
-        }
-    }
-    if (n_expert == 0 && need > 0)
-        w->has_tmap = encode_gemv_tmap(quant, w->dev, rows, rb, w->tmap);
-    ctx->resident_bytes += (uint64_t)need;
-    *out = w;
-    return STRATA_OK;
+    const strata_upload u{bytes, len, quant, n_expert, rows, cols};
+    return upload_locked(ctx, &u, 1, out);
+}
+
+int strata_cuda_upload_many(strata_ctx* ctx, const strata_upload* items, int64_t n, strata_weight** out) {
+    if (!ctx || n < 0 || (n > 0 && (!items || !out))) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(ctx->mu);
+    return upload_locked(ctx, items, n, out);
 }
 
 int strata_cuda_free_weight(strata_weight* w) {

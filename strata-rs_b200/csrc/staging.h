@@ -1,0 +1,67 @@
+// staging.h — how an upload of many host byte ranges is cut into pinned chunks.
+//
+// The bytes of every segment, taken in order, form one stream; chunk i of a
+// `cap`-byte staging buffer holds stream bytes [i*cap, (i+1)*cap). A chunk is
+// described by its pieces: which segment, where in it, where in the chunk,
+// how many bytes. Host threads fill a chunk by stage ranges (stage_fill), and
+// each piece then goes to its own device destination in one copy. Plain host
+// code with no CUDA types, so the arithmetic is checked on the CPU as well.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+namespace strata {
+
+struct StageSeg {
+    uint8_t* dst;        // device destination (opaque here)
+    const uint8_t* src;  // host source
+    size_t n;            // bytes
+};
+
+struct StagePiece {
+    int64_t seg;     // index into the segment list
+    size_t seg_off;  // first byte within the segment
+    size_t off;      // first byte within the chunk
+    size_t n;        // bytes
+};
+
+struct StageCursor {
+    int64_t seg = 0;  // next segment to read
+    size_t off = 0;   // bytes of it already planned
+};
+
+// Plans the next chunk of at most `cap` bytes starting at `cur`, which it
+// advances; returns the bytes planned (0 once every segment is done).
+// Empty segments are passed over.
+inline size_t stage_plan(const StageSeg* segs, int64_t nseg, StageCursor& cur, size_t cap,
+                         std::vector<StagePiece>& out) {
+    out.clear();
+    size_t fill = 0;
+    while (fill < cap && cur.seg < nseg) {
+        const size_t left = segs[cur.seg].n - cur.off;
+        const size_t take = left < cap - fill ? left : cap - fill;
+        if (take) out.push_back({cur.seg, cur.off, fill, take});
+        fill += take;
+        cur.off += take;
+        if (cur.off == segs[cur.seg].n) {
+            ++cur.seg;
+            cur.off = 0;
+        }
+    }
+    return fill;
+}
+
+// Copies chunk bytes [a, b) from their sources into `stage` (one host
+// thread's share of a chunk).
+inline void stage_fill(const std::vector<StagePiece>& pieces, const StageSeg* segs, uint8_t* stage, size_t a,
+                       size_t b) {
+    for (const StagePiece& p : pieces) {
+        const size_t lo = p.off > a ? p.off : a;
+        const size_t hi = p.off + p.n < b ? p.off + p.n : b;
+        if (lo < hi) memcpy(stage + lo, segs[p.seg].src + p.seg_off + (lo - p.off), hi - lo);
+    }
+}
+
+}  // namespace strata

@@ -25,6 +25,9 @@ LIB_PATH = Path(os.environ.get("STRATA_CUDA_LIB", HERE / "libstrata_cuda.so"))
 # status codes (include/strata_cuda.h)
 (OK, ERR_INVALID, ERR_UNSUPPORTED_QUANT, ERR_TRUNCATED, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_NCCL, ERR_BUDGET,
  ERR_SCRATCH_LIMIT) = range(10)
+# include/strata_gguf.h: one per strata_gguf::Error variant the reader raises
+(ERR_IO, ERR_BAD_MAGIC, ERR_UNSUPPORTED_VERSION, ERR_BAD_VALUE_TYPE, ERR_BAD_KEY_LENGTH, ERR_STRING_NOT_UTF8,
+ ERR_TENSOR_NOT_FOUND, ERR_WRONG_TENSOR_DIMS) = range(10, 18)
 
 # Strata ggml type ids (crates/strata-gguf/src/quant.rs:15-43)
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
@@ -75,6 +78,18 @@ def lib() -> C.CDLL:
             "strata_cuda_set_gemv_path": (i32, [vp, i32]),
             "strata_cuda_stream": (i32, [vp, C.POINTER(vp)]),
             "strata_cuda_upload": (i32, [vp, vp, sz, u32, i64, i64, i64, C.POINTER(vp)]),
+            "strata_cuda_upload_many": (i32, [vp, C.POINTER(UploadItem), i64, C.POINTER(vp)]),
+            "strata_cuda_gguf_open": (i32, [C.c_char_p, C.POINTER(vp), C.c_char_p, sz]),
+            "strata_cuda_gguf_close": (None, [vp]),
+            "strata_cuda_gguf_split_paths": (i32, [C.c_char_p, C.c_char_p, sz, C.POINTER(sz), C.c_char_p, sz]),
+            "strata_cuda_gguf_n_shards": (i32, [vp]),
+            "strata_cuda_gguf_shard": (i32, [vp, i32, C.POINTER(GgufShardInfo)]),
+            "strata_cuda_gguf_tensor_count": (i64, [vp]),
+            "strata_cuda_gguf_tensor": (i32, [vp, i64, C.POINTER(GgufTensorInfo)]),
+            "strata_cuda_gguf_find": (i32, [vp, C.c_char_p, C.POINTER(i64)]),
+            "strata_cuda_gguf_tensor_data": (i32, [vp, i64, C.POINTER(vp), C.POINTER(u64), C.c_char_p, sz]),
+            "strata_cuda_gguf_meta": (i32, [vp, C.c_char_p, C.POINTER(GgufValue)]),
+            "strata_cuda_gguf_ingest": (i32, [vp, vp, C.POINTER(i64), i64, C.POINTER(vp)]),
             "strata_cuda_free_weight": (i32, [vp]),
             "strata_cuda_dequant": (i32, [vp, vp, i64, i64, i64, fp]),
             "strata_cuda_gemv": (i32, [vp, vp, fp, fp, i32]),
@@ -130,6 +145,31 @@ class MoeDesc(C.Structure):
     _fields_ += [("with_shared", C.c_int)]
 
 
+class UploadItem(C.Structure):
+    """strata_upload (strata_cuda.h)."""
+    _fields_ = [("bytes", C.c_void_p), ("len", C.c_size_t), ("quant", C.c_uint32), ("n_expert", C.c_int64),
+                ("rows", C.c_int64), ("cols", C.c_int64)]
+
+
+class GgufShardInfo(C.Structure):
+    """strata_gguf_shard (strata_gguf.h)."""
+    _fields_ = [("path", C.c_char_p), ("version", C.c_uint32), ("alignment", C.c_uint64),
+                ("data_start", C.c_uint64), ("file_size", C.c_uint64), ("n_tensors", C.c_int64),
+                ("n_metadata", C.c_int64)]
+
+
+class GgufTensorInfo(C.Structure):
+    """strata_gguf_tensor (strata_gguf.h)."""
+    _fields_ = [("name", C.c_char_p), ("type", C.c_uint32), ("n_dims", C.c_int32), ("dims", C.c_uint64 * 4),
+                ("offset", C.c_uint64), ("shard", C.c_int32)]
+
+
+class GgufValue(C.Structure):
+    """strata_gguf_value (strata_gguf.h)."""
+    _fields_ = [("type", C.c_uint32), ("i", C.c_int64), ("u", C.c_uint64), ("f", C.c_double),
+                ("str", C.c_void_p), ("str_len", C.c_uint64), ("elem", C.c_uint32), ("count", C.c_uint64)]
+
+
 def _fptr(a: np.ndarray):
     return a.ctypes.data_as(C.POINTER(C.c_float))
 
@@ -178,6 +218,136 @@ def comm_unique_id() -> bytes:
     if rc != OK:
         raise BackendError(rc, "strata_cuda_comm_unique_id failed")
     return buf.raw
+
+
+@dataclass
+class GgufTensor:
+    """strata_gguf::TensorInfo (crates/strata-gguf/src/reader.rs:179-199) plus the shard holding it."""
+    name: str
+    shape: list
+    ty: int
+    offset: int
+    shard: int
+
+
+@dataclass
+class MetaValue:
+    """strata_gguf::MetaValue (crates/strata-gguf/src/metadata.rs:51-111) without array items."""
+    ty: int
+    int: int
+    uint: int
+    float: float
+    string: str
+    elem: int
+    count: int
+
+    def as_int(self):
+        return self.int if self.ty not in (6, 8, 9, 12) else None
+
+    def as_float(self):
+        if self.ty in (8, 9):
+            return None
+        return self.float if self.ty in (6, 12) else float(self.int)
+
+    def as_str(self):
+        return self.string if self.ty == 8 else None
+
+
+def split_paths(any_shard: str) -> list:
+    """strata_gguf::split_paths (crates/strata-gguf/src/reader.rs:527-572)."""
+    err = C.create_string_buffer(1024)
+    need = C.c_size_t()
+    L = lib()
+    rc = L.strata_cuda_gguf_split_paths(str(any_shard).encode(), None, 0, C.byref(need), err, len(err))
+    if rc not in (OK, ERR_INVALID) or (rc == ERR_INVALID and need.value == 0):
+        raise BackendError(rc, err.value.decode())
+    buf = C.create_string_buffer(need.value)
+    rc = L.strata_cuda_gguf_split_paths(str(any_shard).encode(), buf, len(buf), C.byref(need), err, len(err))
+    if rc != OK:
+        raise BackendError(rc, err.value.decode())
+    return buf.value.decode().splitlines()
+
+
+class GgufModel:
+    """strata_gguf::GgufModel (crates/strata-gguf/src/reader.rs:448-523): every shard of a
+    model, mapped read-only, with one name index. Needs no GPU. Errors raise
+    BackendError with the strata_gguf::Error code and text."""
+
+    def __init__(self, any_shard):
+        err = C.create_string_buffer(1024)
+        h = C.c_void_p()
+        rc = lib().strata_cuda_gguf_open(str(any_shard).encode(), C.byref(h), err, len(err))
+        if rc != OK:
+            raise BackendError(rc, err.value.decode())
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().strata_cuda_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def n_shards(self) -> int:
+        return lib().strata_cuda_gguf_n_shards(self.h)
+
+    def shard(self, i: int) -> dict:
+        info = GgufShardInfo()
+        rc = lib().strata_cuda_gguf_shard(self.h, i, C.byref(info))
+        if rc != OK:
+            raise BackendError(rc, f"no shard {i}")
+        return {k: (getattr(info, k).decode() if k == "path" else getattr(info, k)) for k, _ in info._fields_}
+
+    def tensor_count(self) -> int:
+        return lib().strata_cuda_gguf_tensor_count(self.h)
+
+    def tensor(self, index: int) -> GgufTensor:
+        t = GgufTensorInfo()
+        rc = lib().strata_cuda_gguf_tensor(self.h, index, C.byref(t))
+        if rc != OK:
+            raise BackendError(rc, f"no tensor {index}")
+        return GgufTensor(t.name.decode(), list(t.dims[:t.n_dims]), t.type, t.offset, t.shard)
+
+    def tensors(self) -> list:
+        return [self.tensor(i) for i in range(self.tensor_count())]
+
+    def index_of(self, name: str) -> int:
+        """The tensor's position, or -1 when absent (GgufModel::find)."""
+        i = C.c_int64()
+        lib().strata_cuda_gguf_find(self.h, name.encode(), C.byref(i))
+        return i.value
+
+    def find(self, name: str):
+        i = self.index_of(name)
+        return None if i < 0 else self.tensor(i)
+
+    def tensor_data(self, name_or_index) -> np.ndarray:
+        """The payload bytes as a read-only view of the mapping (valid while the model is open)."""
+        i = self.index_of(name_or_index) if isinstance(name_or_index, str) else name_or_index
+        if i < 0:
+            raise BackendError(ERR_TENSOR_NOT_FOUND, f"tensor '{name_or_index}' is missing from the file")
+        p, n = C.c_void_p(), C.c_uint64()
+        err = C.create_string_buffer(1024)
+        rc = lib().strata_cuda_gguf_tensor_data(self.h, i, C.byref(p), C.byref(n), err, len(err))
+        if rc != OK:
+            raise BackendError(rc, err.value.decode())
+        if n.value == 0:
+            return np.zeros(0, np.uint8)
+        a = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(n.value,))
+        a.flags.writeable = False
+        return a
+
+    def get(self, key: str):
+        """A metadata value of the first shard (GgufModel::get), or None."""
+        v = GgufValue()
+        if lib().strata_cuda_gguf_meta(self.h, key.encode(), C.byref(v)) != OK:
+            return None
+        s = C.string_at(v.str, v.str_len).decode() if v.str_len else ""
+        return MetaValue(v.type, v.i, v.u, v.f, s, v.elem, v.count)
 
 
 class MoeLayer:
@@ -249,6 +419,36 @@ class Context:
         self.check(lib().strata_cuda_upload(self.h, data.ctypes.data, data.nbytes, quant, n_expert, rows, cols,
                                             C.byref(h)))
         return Weight(self, h, quant, n_expert, rows, cols)
+
+    def upload_many(self, items: list) -> list:
+        """strata_cuda_upload_many: items are (data, quant, rows, cols, n_expert) tuples."""
+        arrs = [np.ascontiguousarray(d, dtype=np.uint8) for d, *_ in items]
+        descs = (UploadItem * max(1, len(items)))()
+        for k, (a, (_, quant, rows, cols, n_expert)) in enumerate(zip(arrs, items)):
+            descs[k] = UploadItem(a.ctypes.data, a.nbytes, quant, n_expert, rows, cols)
+        hs = (C.c_void_p * max(1, len(items)))()
+        self.check(lib().strata_cuda_upload_many(self.h, descs, len(items), hs))
+        return [Weight(self, C.c_void_p(hs[k]), q, ne, r, c) for k, (_, q, r, c, ne) in enumerate(items)]
+
+    def ingest(self, model: GgufModel, names: list) -> dict:
+        """strata_cuda_gguf_ingest: the named tensors of an opened model, as WeightStore views them."""
+        idx = []
+        for nm in names:
+            i = model.index_of(nm)
+            if i < 0:
+                raise BackendError(ERR_TENSOR_NOT_FOUND, f"tensor '{nm}' is missing from the file")
+            idx.append(i)
+        ix = (C.c_int64 * max(1, len(idx)))(*idx)
+        hs = (C.c_void_p * max(1, len(idx)))()
+        self.check(lib().strata_cuda_gguf_ingest(self.h, model.h, ix, len(idx), hs))
+        out = {}
+        for k, nm in enumerate(names):
+            t = model.tensor(idx[k])
+            d = t.shape + [1] * (3 - len(t.shape))
+            n_expert = d[2] if len(t.shape) == 3 else 0
+            rows = 1 if len(t.shape) == 1 else d[1]
+            out[nm] = Weight(self, C.c_void_p(hs[k]), t.ty, n_expert, rows, d[0])
+        return out
 
     def dequant(self, w: Weight, row0: int = 0, nrows: int | None = None, expert: int = 0) -> np.ndarray:
         nrows = w.rows - row0 if nrows is None else nrows

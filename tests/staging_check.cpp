@@ -1,0 +1,79 @@
+// Host check of the upload staging plan (strata-rs_b200/csrc/staging.h):
+// random lists of byte ranges (empty ones, ranges smaller and larger than a
+// chunk, ranges that end exactly on a chunk boundary) are pushed through
+// stage_plan / stage_fill with a small chunk and split among 8 "threads" the
+// way the upload splits a chunk; every destination must come out equal to its
+// source, every piece must stay inside its segment and its chunk, and the
+// chunks must be full except the last. Prints "ok" and exits 0, or names the
+// first failure and exits 1.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <random>
+#include <vector>
+
+#include "staging.h"
+
+using namespace strata;
+
+static int check(std::mt19937_64& g, size_t cap, int nseg_max) {
+    std::uniform_int_distribution<int> nseg_d(0, nseg_max);
+    const int nseg = nseg_d(g);
+    std::vector<std::vector<uint8_t>> src(nseg), dst(nseg);
+    std::vector<StageSeg> segs(nseg);
+    size_t total = 0;
+    for (int i = 0; i < nseg; ++i) {
+        size_t n;
+        switch (g() % 5) {
+            case 0: n = 0; break;
+            case 1: n = cap; break;
+            case 2: n = 1 + g() % (cap / 3 + 1); break;
+            case 3: n = cap * (1 + g() % 3) - g() % 2; break;
+            default: n = 1 + g() % (4 * cap); break;
+        }
+        src[i].resize(n);
+        for (auto& b : src[i]) b = (uint8_t)g();
+        dst[i].assign(n, 0xEE);
+        segs[i] = {dst[i].data(), src[i].data(), n};
+        total += n;
+    }
+    std::vector<uint8_t> stage(cap);
+    std::vector<StagePiece> pieces;
+    StageCursor cur;
+    size_t streamed = 0;
+    for (int chunk = 0;; ++chunk) {
+        const size_t len = stage_plan(segs.data(), nseg, cur, cap, pieces);
+        if (!len) break;
+        if (len > cap) return printf("chunk %d holds %zu > %zu bytes\n", chunk, len, cap), 1;
+        if (len < cap && streamed + len != total) return printf("short chunk %d before the end\n", chunk), 1;
+        size_t covered = 0;
+        for (const StagePiece& p : pieces) {
+            if (p.n == 0 || p.off != covered || p.off + p.n > len || p.seg_off + p.n > segs[p.seg].n)
+                return printf("bad piece in chunk %d\n", chunk), 1;
+            covered += p.n;
+        }
+        if (covered != len) return printf("chunk %d pieces cover %zu of %zu\n", chunk, covered, len), 1;
+        std::fill(stage.begin(), stage.end(), 0xCD);
+        const int T = 8;
+        const size_t part = (len + T - 1) / T;
+        for (int t = 0; t < T; ++t) {
+            const size_t a = t * part, b = a + part < len ? a + part : len;
+            if (a < b) stage_fill(pieces, segs.data(), stage.data(), a, b);
+        }
+        for (const StagePiece& p : pieces) memcpy(segs[p.seg].dst + p.seg_off, stage.data() + p.off, p.n);
+        streamed += len;
+    }
+    if (streamed != total) return printf("streamed %zu of %zu bytes\n", streamed, total), 1;
+    for (int i = 0; i < nseg; ++i)
+        if (src[i] != dst[i]) return printf("segment %d differs\n", i), 1;
+    return 0;
+}
+
+int main() {
+    std::mt19937_64 g(20261202);
+    for (size_t cap : {size_t(1), size_t(7), size_t(64), size_t(1000), size_t(4096)})
+        for (int it = 0; it < 300; ++it)
+            if (check(g, cap, it % 3 == 0 ? 3 : 40)) return printf("cap %zu case %d\n", cap, it), 1;
+    printf("ok\n");
+    return 0;
+}
