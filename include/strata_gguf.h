@@ -119,6 +119,14 @@ typedef struct {
 /* STRATA_OK, or STRATA_ERR_INVALID when the key is absent. */
 int strata_cuda_gguf_meta(const strata_gguf *g, const char *key, strata_gguf_value *out);
 
+/* The upload item (strata_cuda.h) for rows [first, first + count) of a 1-D or
+ * 2-D tensor (1-D: one row) or experts [first, first + count) of a 3-D one;
+ * count < 0 means to the end. `bytes` points into the mapping, so a rank of a
+ * row-sharded projection or of an expert-parallel MoE reads only its own
+ * slice of the file; pass the items to strata_cuda_upload_many. */
+int strata_cuda_gguf_view(const strata_gguf *g, int64_t index, int64_t first, int64_t count, strata_upload *out,
+                          char *err, size_t err_len);
+
 /* Uploads n of the model's tensors (by index) to HBM in one staged pass, as
  * strata_cuda_upload_many: all or nothing, errors on the context. A tensor
  * of 4 dims is refused (no WeightStore view has 4). */

@@ -41,7 +41,7 @@ constexpr int kMaxDepth = 2;                           // array nesting the read
 
 // A failure: a status code of strata_gguf.h and strata_gguf::Error's text.
 struct GgufError {
-    int code;
+    int code = STRATA_OK;
     std::string msg;
 };
 
@@ -440,6 +440,54 @@ bool tensor_payload(const Shard& sh, const TensorInfo& t, const uint8_t** data, 
     return true;
 }
 
+// The upload item for rows [first, first + count) of a 1-D / 2-D tensor or
+// experts [first, first + count) of a 3-D one, viewed as WeightStore views it
+// (weights.rs:122-152): 1-D one row of dims[0]; 2-D [cols, rows]; 3-D
+// [cols, rows, n_expert]. count < 0 means to the end.
+bool tensor_view(const strata_gguf& g, int64_t index, int64_t first, int64_t count, strata_upload* u,
+                 GgufError* e) {
+    const Shard& sh = *g.shards[g.order[index].first];
+    const TensorInfo& t = g.tensor(index);
+    const uint8_t* data;
+    uint64_t nbytes;
+    if (!tensor_payload(sh, t, &data, &nbytes, e)) return false;
+    for (uint64_t d : t.shape)
+        if (d > (uint64_t)INT64_MAX) {
+            *e = make_error(STRATA_ERR_INVALID, "tensor '%s' has a dimension beyond int64", t.name.c_str());
+            return false;
+        }
+    const int nd = (int)t.shape.size();
+    if (nd > 3) {
+        *e = make_error(STRATA_ERR_INVALID, "tensor '%s' has %d dimensions; a weight view has 1 to 3", t.name.c_str(),
+                        nd);
+        return false;
+    }
+    const int64_t cols = (int64_t)t.shape[0];
+    const int64_t rows = nd == 1 ? 1 : (int64_t)t.shape[1];
+    const int64_t outer = nd == 3 ? (int64_t)t.shape[2] : rows;  // what [first, first + count) counts
+    if (count < 0) count = outer - first;
+    if (first < 0 || first > outer || count < 0 || count > outer - first) {
+        *e = make_error(STRATA_ERR_INVALID, "range [%lld, %lld) is outside tensor '%s' (%lld %s)", (long long)first,
+                        (long long)(first + count), t.name.c_str(), (long long)outer, nd == 3 ? "experts" : "rows");
+        return false;
+    }
+    uint64_t bs = 1, ts = 0;
+    type_geometry(t.ty, &bs, &ts);  // known: the payload was found
+    const uint64_t row_bytes = ((uint64_t)cols + bs - 1) / bs * ts;
+    const uint64_t unit = nd == 3 ? row_bytes * (uint64_t)rows : row_bytes;  // bytes per counted item
+    if (unit && (uint64_t)outer > nbytes / unit) {
+        *e = truncated(unit * (uint64_t)outer, nbytes);  // rows that are not whole blocks
+        return false;
+    }
+    u->bytes = data ? data + unit * (uint64_t)first : nullptr;
+    u->len = (size_t)(unit * (uint64_t)count);
+    u->quant = t.ty;
+    u->cols = cols;
+    u->n_expert = nd == 3 ? count : 0;
+    u->rows = nd == 3 ? rows : count;
+    return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -563,41 +611,33 @@ int strata_cuda_gguf_meta(const strata_gguf* g, const char* key, strata_gguf_val
     return STRATA_OK;
 }
 
+int strata_cuda_gguf_view(const strata_gguf* g, int64_t index, int64_t first, int64_t count, strata_upload* out,
+                          char* err, size_t err_len) {
+    if (!g || !out || index < 0 || index >= (int64_t)g->order.size()) return STRATA_ERR_INVALID;
+    GgufError e;
+    if (!tensor_view(*g, index, first, count, out, &e)) {
+        put_error(e, err, err_len);
+        return e.code;
+    }
+    return STRATA_OK;
+}
+
 int strata_cuda_gguf_ingest(strata_ctx* ctx, const strata_gguf* g, const int64_t* tensors, int64_t n,
                             strata_weight** out) {
     if (!ctx || !g || n < 0 || (n > 0 && (!tensors || !out))) return STRATA_ERR_INVALID;
-    auto refuse = [&](int code, const std::string& msg) {
-        for (int64_t i = 0; i < n; ++i) out[i] = nullptr;
-        return strata::report(ctx, code, msg.c_str());
-    };
     std::vector<strata_upload> items((size_t)n);
     for (int64_t i = 0; i < n; ++i) {
         const int64_t ix = tensors[i];
-        if (ix < 0 || ix >= (int64_t)g->order.size())
-            return refuse(STRATA_ERR_INVALID, "tensor index " + std::to_string(ix) + " is out of range");
-        const TensorInfo& t = g->tensor(ix);
-        const uint8_t* data;
-        uint64_t nbytes;
         GgufError e;
-        if (!tensor_payload(*g->shards[g->order[ix].first], t, &data, &nbytes, &e)) return refuse(e.code, e.msg);
-        for (uint64_t d : t.shape)
-            if (d > (uint64_t)INT64_MAX)
-                return refuse(STRATA_ERR_INVALID, "tensor '" + t.name + "' has a dimension beyond int64");
-        if (!strata::quant_on_device(t.ty))
-            return refuse(STRATA_ERR_UNSUPPORTED_QUANT,
-                          "tensor '" + t.name + "': quant type id " + std::to_string(t.ty) + " is not on the CUDA path");
-        strata_upload& u = items[(size_t)i];
-        u.bytes = data;
-        u.len = (size_t)nbytes;
-        u.quant = t.ty;
-        u.cols = (int64_t)t.shape[0];
-        switch (t.shape.size()) {
-            case 1: u.n_expert = 0; u.rows = 1; break;
-            case 2: u.n_expert = 0; u.rows = (int64_t)t.shape[1]; break;
-            case 3: u.n_expert = (int64_t)t.shape[2]; u.rows = (int64_t)t.shape[1]; break;
-            default:
-                return refuse(STRATA_ERR_INVALID, "tensor '" + t.name + "' has 4 dimensions; a weight view has 1 to 3");
-        }
+        if (ix < 0 || ix >= (int64_t)g->order.size())
+            e = make_error(STRATA_ERR_INVALID, "tensor index %lld is out of range", (long long)ix);
+        else if (tensor_view(*g, ix, 0, -1, &items[(size_t)i], &e) && !strata::quant_on_device(items[(size_t)i].quant))
+            e = make_error(STRATA_ERR_UNSUPPORTED_QUANT, "tensor '%s': quant type id %u is not on the CUDA path",
+                           g->tensor(ix).name.c_str(), items[(size_t)i].quant);
+        else if (e.code == STRATA_OK)
+            continue;
+        for (int64_t k = 0; k < n; ++k) out[k] = nullptr;
+        return strata::report(ctx, e.code, e.msg.c_str());
     }
     return strata_cuda_upload_many(ctx, items.data(), n, out);
 }

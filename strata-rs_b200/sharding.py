@@ -41,3 +41,17 @@ def expert_shard(data: np.ndarray, n_expert: int, world: int, rank: int) -> np.n
     e0, e1 = expert_range(n_expert, world, rank)
     per = data.size // n_expert
     return np.ascontiguousarray(data[e0 * per:e1 * per])
+
+
+def row_shard_view(model, name: str, world: int, rank: int):
+    """This rank's rows of a dense tensor of an opened GGUF model, as an upload
+    item pointing into the mapping (only those bytes are read from the file)."""
+    rows = model.find(name).shape[1]
+    r0, r1 = row_range(rows, world, rank)
+    return model.view(name, r0, r1 - r0)
+
+
+def expert_shard_view(model, name: str, world: int, rank: int):
+    """This rank's experts of an [n_expert][rows][cols] tensor of an opened GGUF model."""
+    e0, e1 = expert_range(model.find(name).shape[2], world, rank)
+    return model.view(name, e0, e1 - e0)

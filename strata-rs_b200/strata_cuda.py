@@ -90,6 +90,7 @@ def lib() -> C.CDLL:
             "strata_cuda_gguf_tensor_data": (i32, [vp, i64, C.POINTER(vp), C.POINTER(u64), C.c_char_p, sz]),
             "strata_cuda_gguf_meta": (i32, [vp, C.c_char_p, C.POINTER(GgufValue)]),
             "strata_cuda_gguf_ingest": (i32, [vp, vp, C.POINTER(i64), i64, C.POINTER(vp)]),
+            "strata_cuda_gguf_view": (i32, [vp, i64, i64, i64, C.POINTER(UploadItem), C.c_char_p, sz]),
             "strata_cuda_free_weight": (i32, [vp]),
             "strata_cuda_dequant": (i32, [vp, vp, i64, i64, i64, fp]),
             "strata_cuda_gemv": (i32, [vp, vp, fp, fp, i32]),
@@ -341,6 +342,19 @@ class GgufModel:
         a.flags.writeable = False
         return a
 
+    def view(self, name_or_index, first: int = 0, count: int = -1) -> UploadItem:
+        """strata_cuda_gguf_view: the upload item for rows (1-D / 2-D) or experts (3-D)
+        [first, first + count) of a tensor, pointing into the mapping."""
+        i = self.index_of(name_or_index) if isinstance(name_or_index, str) else name_or_index
+        if i < 0:
+            raise BackendError(ERR_TENSOR_NOT_FOUND, f"tensor '{name_or_index}' is missing from the file")
+        u = UploadItem()
+        err = C.create_string_buffer(1024)
+        rc = lib().strata_cuda_gguf_view(self.h, i, first, count, C.byref(u), err, len(err))
+        if rc != OK:
+            raise BackendError(rc, err.value.decode())
+        return u
+
     def get(self, key: str):
         """A metadata value of the first shard (GgufModel::get), or None."""
         v = GgufValue()
@@ -429,6 +443,13 @@ class Context:
         hs = (C.c_void_p * max(1, len(items)))()
         self.check(lib().strata_cuda_upload_many(self.h, descs, len(items), hs))
         return [Weight(self, C.c_void_p(hs[k]), q, ne, r, c) for k, (_, q, r, c, ne) in enumerate(items)]
+
+    def upload_views(self, views: list) -> list:
+        """strata_cuda_upload_many over UploadItems (GgufModel.view): the bytes stay in the mapping."""
+        items = (UploadItem * max(1, len(views)))(*views)
+        hs = (C.c_void_p * max(1, len(views)))()
+        self.check(lib().strata_cuda_upload_many(self.h, items, len(views), hs))
+        return [Weight(self, C.c_void_p(hs[k]), v.quant, v.n_expert, v.rows, v.cols) for k, v in enumerate(views)]
 
     def ingest(self, model: GgufModel, names: list) -> dict:
         """strata_cuda_gguf_ingest: the named tensors of an opened model, as WeightStore views them."""

@@ -409,3 +409,62 @@ def test_null_arguments_are_refused():
     assert L.strata_cuda_gguf_ingest(None, None, None, 0, None) == sc.ERR_INVALID
     assert L.strata_cuda_upload_many(None, None, 0, None) == sc.ERR_INVALID
     L.strata_cuda_gguf_close(None)
+
+
+# ---------------------------------------------------------------- views: what one rank reads
+
+def view_bytes(v) -> bytes:
+    import ctypes
+    return ctypes.string_at(v.bytes, v.len) if v.len else b""
+
+
+def test_views_of_rows_and_experts(tmp_path):
+    """strata_cuda_gguf_view: WeightStore's geometry (1-D one row, 2-D [cols, rows],
+    3-D [cols, rows, n_expert]) and the byte slice of a row or expert range."""
+    g = rng(808)
+    dense = g.integers(0, 256, 12 * 2 * 144, dtype=np.uint8).tobytes()    # Q4_K [512, 12]
+    experts = g.integers(0, 256, 5 * 4 * 34, dtype=np.uint8).tobytes()    # Q8_0 [32, 4, 5]
+    norm = g.integers(0, 256, 64 * 4, dtype=np.uint8).tobytes()           # F32 [64]
+    data, _, _ = build([], [("dense", [512, 12], Q4_K, dense), ("exps", [32, 4, 5], Q8_0, experts),
+                            ("norm", [64], F32_T, norm), ("four", [32, 1, 1, 2], Q8_0, bytes(68)),
+                            ("ragged", [33, 2], Q8_0, bytes(68))])
+    with sc.GgufModel(write(tmp_path, "views.gguf", data)) as m:
+        v = m.view("dense")
+        assert (v.quant, v.n_expert, v.rows, v.cols, v.len) == (Q4_K, 0, 12, 512, len(dense))
+        assert view_bytes(v) == dense
+        v = m.view("dense", 3, 4)
+        assert (v.rows, v.cols, v.n_expert) == (4, 512, 0) and view_bytes(v) == dense[3 * 288:7 * 288]
+        v = m.view("dense", 12, 0)
+        assert v.len == 0 and v.rows == 0
+        v = m.view("exps")
+        assert (v.quant, v.n_expert, v.rows, v.cols) == (Q8_0, 5, 4, 32) and view_bytes(v) == experts
+        v = m.view("exps", 2, -1)
+        assert (v.n_expert, v.rows) == (3, 4) and view_bytes(v) == experts[2 * 136:]
+        v = m.view("norm")
+        assert (v.quant, v.n_expert, v.rows, v.cols) == (F32_T, 0, 1, 64) and view_bytes(v) == norm
+        for name, first, count in [("dense", 0, 13), ("dense", 13, 0), ("dense", -1, 2), ("exps", 4, 2),
+                                   ("norm", 1, 1), ("four", 0, -1)]:
+            with pytest.raises(sc.BackendError) as ei:
+                m.view(name, first, count)
+            assert ei.value.code == sc.ERR_INVALID, (name, first, count)
+        with pytest.raises(sc.BackendError) as ei:  # rows that are not whole blocks
+            m.view("ragged")
+        assert ei.value.code == sc.ERR_TRUNCATED
+
+
+def test_shard_views_cover_the_tensor_once(tmp_path):
+    """Each rank's row or expert range (strata-rs_b200/sharding.py): the ranks'
+    slices are disjoint, in order, and together the whole payload."""
+    import sharding
+    g = rng(909)
+    dense = g.integers(0, 256, 64 * 8 * 144, dtype=np.uint8).tobytes()    # Q4_K [2048, 64]
+    experts = g.integers(0, 256, 16 * 8 * 288, dtype=np.uint8).tobytes()  # Q4_K [512, 8, 16]
+    data, _, _ = build([], [("proj", [2048, 64], Q4_K, dense), ("exps", [512, 8, 16], Q4_K, experts)])
+    with sc.GgufModel(write(tmp_path, "shards.gguf", data)) as m:
+        for world in (1, 2, 4, 8):
+            rows = [sharding.row_shard_view(m, "proj", world, r) for r in range(world)]
+            assert b"".join(view_bytes(v) for v in rows) == dense
+            assert all(v.rows == 64 // world and v.n_expert == 0 for v in rows)
+            exps = [sharding.expert_shard_view(m, "exps", world, r) for r in range(world)]
+            assert b"".join(view_bytes(v) for v in exps) == experts
+            assert all(v.n_expert == 16 // world and v.rows == 8 and v.cols == 512 for v in exps)

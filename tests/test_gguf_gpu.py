@@ -133,3 +133,33 @@ def test_upload_many_small_ranges_across_chunks(ctx):
         ctx.upload_many(bad)
     assert ei.value.code == sc.ERR_TRUNCATED and "upload 5 of 9" in str(ei.value)
     assert ctx.resident_bytes() == before
+
+
+def test_rank_slices_upload_only_their_bytes(ctx, model):
+    """A rank of a row-sharded projection or of the expert-parallel MoE uploads
+    its own slice straight from the mapping (strata_cuda_gguf_view +
+    strata_cuda_upload_many); the slice dequantizes as the matching rows or
+    experts of the whole tensor."""
+    import sharding
+    m, blobs = model
+    world, rank = 4, 1
+    before = ctx.resident_bytes()
+    views = [sharding.row_shard_view(m, "blk.0.attn_q.weight", world, rank),
+             sharding.expert_shard_view(m, "blk.0.ffn_gate_exps.weight", world, rank)]
+    dense, exps = ctx.upload_views(views)
+    assert ctx.resident_bytes() - before == views[0].len + views[1].len
+    q = np.frombuffer(blobs["blk.0.attn_q.weight"], np.uint8)
+    rb = sc.byte_size(sc.Q4_K, 2048)
+    r0, r1 = sharding.row_range(512, world, rank)
+    want = oracle.dequantize(sc.Q4_K, q[r0 * rb:r1 * rb], r1 - r0, 2048)
+    assert np.array_equal(ctx.dequant(dense).view(np.uint32), want.view(np.uint32))
+    ge = np.frombuffer(blobs["blk.0.ffn_gate_exps.weight"], np.uint8)
+    e0, e1 = sharding.expert_range(128, world, rank)
+    per = 2048 * sc.byte_size(sc.Q4_K, 512)
+    for k in (0, e1 - e0 - 1):
+        got = ctx.dequant(exps, expert=k)
+        want = oracle.dequantize(sc.Q4_K, ge[(e0 + k) * per:(e0 + k + 1) * per], 2048, 512)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), k
+    dense.free()
+    exps.free()
+    assert ctx.resident_bytes() == before

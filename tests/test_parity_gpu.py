@@ -36,6 +36,23 @@ def _special_scales(blocks, quant):
     return blocks
 
 
+@pytest.mark.parametrize("quant", [F16, BF16])
+def test_every_16_bit_pattern(ctx, quant):
+    """All 65,536 F16 / BF16 bit patterns through the device's conversion
+    against the oracle's restatement of the `half` crate (the f16 -> f32 of
+    crates/strata-gguf/src/dequant.rs:28-36): bit-exact for every finite value
+    and both infinities; NaNs stay NaN (their payload bits are not pinned)."""
+    data = np.arange(65536, dtype=np.uint16).view(np.uint8)
+    w = ctx.upload(data, quant, 64, 1024)
+    got = ctx.dequant(w).reshape(-1)
+    want = oracle.dequantize(quant, data, 64, 1024).reshape(-1)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+    assert nan.sum() == (2046 if quant == F16 else 254)
+    w.free()
+
+
 @pytest.mark.parametrize("quant", [Q8_0, Q4_K, Q5_K, Q6_K, F32, F16, BF16])
 def test_dequant_bit_exact(ctx, quant):
     rows, cols = 24, 1024
