@@ -75,6 +75,10 @@ const char *strata_cuda_name(void);
 
 /* Creates a context on `device` (its own non-blocking stream, pinned staging). */
 int strata_cuda_create(int device, strata_ctx **out);
+/* Waits (bounded) for the context's work, then frees everything it owns:
+ * buffers, streams, the communicator, and any weight not yet released with
+ * strata_cuda_free_weight (those handles become invalid). MoE layers built
+ * on its weights must not be used afterwards. */
 int strata_cuda_destroy(strata_ctx *ctx);
 
 /* Message of the last failure on ctx ("" if none). Valid until the next call. */

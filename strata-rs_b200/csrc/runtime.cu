@@ -166,6 +166,9 @@ int strata_cuda_create(int device, strata_ctx** out) {
         cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess ||
         cudaHostAlloc((void**)&ctx->err_host, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer((void**)&ctx->err_dev, ctx->err_host, 0) != cudaSuccess) {
+        if (ctx->err_host) cudaFreeHost(ctx->err_host);
+        if (ctx->done) cudaEventDestroy(ctx->done);
+        if (ctx->stream) cudaStreamDestroy(ctx->stream);
         delete ctx;
         return STRATA_ERR_CUDA;
     }
@@ -179,6 +182,12 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     cudaSetDevice(ctx->device);
     int rc = wait_stream(ctx, ctx->stream);
     comm_release(ctx);
+    for (strata_weight* w : ctx->weights) {  // weights the caller did not free
+        if (w->dev) cudaFree(w->dev);
+        w->magic = 0;
+        delete w;
+    }
+    ctx->weights.clear();
     for (DevBuf* b : {&ctx->x_dev, &ctx->y_dev, &ctx->work, &ctx->xfrag, &ctx->gemm_work, &ctx->x_bf16, &ctx->moe_work})
         if (b->ptr) cudaFree(b->ptr);
     for (PinnedBuf* b : {&ctx->x_host, &ctx->y_host, &ctx->stage[0], &ctx->stage[1]})
@@ -207,6 +216,7 @@ int strata_cuda_set_weight_budget(strata_ctx* ctx, uint64_t bytes) {
 
 int strata_cuda_resident_bytes(const strata_ctx* ctx, uint64_t* out) {
     if (!ctx || !out) return STRATA_ERR_INVALID;
+    std::lock_guard<std::mutex> g(const_cast<strata_ctx*>(ctx)->mu);
     *out = ctx->resident_bytes;
     return STRATA_OK;
 }
@@ -397,6 +407,7 @@ int upload_locked(strata_ctx* ctx, const strata_upload* items, int64_t n, strata
         if (w->n_expert == 0 && w->bytes > 0)
             w->has_tmap = encode_gemv_tmap(w->quant, w->dev, w->rows, w->row_bytes, w->tmap);
         out[i] = w;
+        ctx->weights.insert(w);
     }
     ctx->resident_bytes += total;
     return STRATA_OK;
@@ -426,6 +437,7 @@ int strata_cuda_free_weight(strata_weight* w) {
     int rc = wait_stream(ctx, ctx->stream);
     if (w->dev) cudaFree(w->dev);
     ctx->resident_bytes -= (uint64_t)w->bytes;
+    ctx->weights.erase(w);
     w->magic = 0;
     delete w;
     return rc;

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <mutex>
 #include <string>
+#include <unordered_set>
 
 #include "../../include/strata_cuda.h"
 #include "kernels.cuh"
@@ -52,6 +53,8 @@ struct strata_ctx {
     // other one is copied to the device (large tensors), with their events
     strata::PinnedBuf stage[2];
     cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+    // every weight uploaded and not yet freed (released by strata_cuda_destroy)
+    std::unordered_set<strata_weight*> weights;
     strata::CommState* comm = nullptr;
     int* err_host = nullptr;  // host-mapped word kernels set when a bounded wait expires
     int* err_dev = nullptr;

@@ -207,9 +207,9 @@ class Weight:
         self.n_expert, self.rows, self.cols = n_expert, rows, cols
 
     def free(self):
-        if self.handle:
+        if self.handle and self.ctx.h:  # a closed context has released its weights already
             lib().strata_cuda_free_weight(self.handle)
-            self.handle = None
+        self.handle = None
 
 
 def comm_unique_id() -> bytes:

@@ -39,3 +39,24 @@ def test_large_upload_round_trips():
             want = oracle.dequantize(Q4_K, data[r0 * rb:(r0 + got.shape[0]) * rb], got.shape[0], cols)
             assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), r0
         w.free()
+
+
+def test_destroy_releases_weights_left_resident():
+    """strata_cuda_destroy frees weights the caller did not free (a backend
+    dropped with its cache full must not leak HBM)."""
+    import torch
+    torch.cuda.init()
+    free0, _ = torch.cuda.mem_get_info(0)
+    data = np.zeros(512 << 20, np.uint8)  # 512 MiB of Q8_0 blocks (zero scales)
+    cols = 4096
+    rows = data.nbytes // (cols // 32 * 34)
+    ctx = sc.Context(0)
+    kept = ctx.upload(data[:rows * (cols // 32 * 34)], sc.Q8_0, rows, cols)
+    gone = ctx.upload(data[:1 << 20], sc.Q8_0, (1 << 20) // (cols // 32 * 34), cols)
+    gone.free()
+    free1, _ = torch.cuda.mem_get_info(0)
+    assert free0 - free1 > 400 << 20
+    ctx.close()
+    kept.free()  # a no-op once the context is gone
+    free2, _ = torch.cuda.mem_get_info(0)
+    assert free0 - free2 < 100 << 20, (free0 - free2) >> 20
