@@ -21,6 +21,15 @@ def dequant_case(case: dict) -> np.ndarray:
     return b
 
 
+def q2_0_invariant_block() -> np.ndarray:
+    """dequant_tests.rs:43-60 (q2_0_structural_invariant): d = 0.5 and bytes
+    (37 i + 11) mod 256; every output must be one of -d, 0, +d, +2d."""
+    b = np.zeros(18, np.uint8)
+    b[0:2] = f16_bytes(0.5)
+    b[2:] = [(i * 37 + 11) & 0xFF for i in range(16)]
+    return b
+
+
 def lcg_block(quant: int, nbytes: int, spec: dict) -> np.ndarray:
     """dequant_tests.rs:219-237: LCG bytes, then a finite scale: the E8M0 /
     UE4M3 scale bytes of MXFP4 / NVFP4, an fp16 0.125 in the first two bytes

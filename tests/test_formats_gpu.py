@@ -100,3 +100,12 @@ def test_expert_gemv(ctx, quant):
             want = oracle.expert_gemv(quant, data, E, IN, OUT, e, x[b]).reshape(-1)
             assert rel_err(got[b], want) < 1e-3, (sc.NAMES[quant], e, b)
     w.free()
+
+
+def test_q2_0_structural_invariant_on_gpu(ctx):
+    """dequant_tests.rs:43-60 through the device: every value is -d, 0, +d or +2d."""
+    w = ctx.upload(rc.q2_0_invariant_block(), synth.Q2_0, 1, 64)
+    out = ctx.dequant(w).reshape(-1)
+    d = 0.5
+    assert all(min(abs(v + d), abs(v), abs(v - d), abs(v - 2 * d)) < 1e-6 for v in out)
+    w.free()

@@ -199,6 +199,19 @@ def test_softmax_sums_to_one():
     assert got[2] > got[1] > got[0] > got[3]
 
 
+def test_silu_and_sigmoid_known_values():
+    """ops_tests.rs:137-143 (silu and sigmoid; softplus is not on this path)."""
+    assert abs(oracle.lib().orc_silu(0.0)) < 1e-7
+    assert abs(oracle.lib().orc_sigmoid(0.0) - 0.5) < 1e-7
+
+
+def test_q2_0_structural_invariant():
+    """Every Q2_0 output is one of -d, 0, +d, +2d."""
+    out = oracle.dequantize_row(synth.Q2_0, rc.q2_0_invariant_block(), 64)
+    d = 0.5
+    assert all(min(abs(v + d), abs(v), abs(v - d), abs(v - 2 * d)) < 1e-6 for v in out)
+
+
 def test_elementwise_ops_match_numpy_f64():
     """The same arithmetic restated in numpy (f64 where ops.rs uses f64)."""
     g = rng(77)

@@ -53,6 +53,17 @@ def test_every_16_bit_pattern(ctx, quant):
     w.free()
 
 
+@pytest.mark.parametrize("case", [c for c in rc.KATS["dequant"] if c["quant"] in BS], ids=lambda c: c["name"])
+def test_reference_dequant_known_answers_on_gpu(ctx, case):
+    """The reference's dequant known answers for the benchmark and float types
+    (dequant_tests.rs:70-79, :123-140, :160-169) through the device."""
+    w = ctx.upload(rc.dequant_case(case), case["quant"], 1, case["n"])
+    out = ctx.dequant(w).reshape(-1)
+    for j, v in case["expect"]:
+        assert out[j] == np.float32(v), (case["name"], j, out[j], v)
+    w.free()
+
+
 @pytest.mark.parametrize("quant", [Q8_0, Q4_K, Q5_K, Q6_K, F32, F16, BF16])
 def test_dequant_bit_exact(ctx, quant):
     rows, cols = 24, 1024
