@@ -617,6 +617,7 @@ int strata_cuda_comm_unique_id(uint8_t* id_out) {
 
 int strata_cuda_comm_init(strata_ctx* ctx, int rank, int world, const uint8_t* id_in) {
     if (!ctx || !id_in || world < 1 || rank < 0 || rank >= world) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     if (ctx->comm) return fail(ctx, STRATA_ERR_INVALID, "communicator already initialised");
     if (!nccl().ok) return fail(ctx, STRATA_ERR_NCCL, "NCCL unavailable: %s", nccl().why.c_str());
@@ -700,6 +701,7 @@ int strata_cuda_comm_group_end(strata_ctx* ctx) {
 int strata_cuda_gemv_sharded_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                                  void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_weight(ctx, w, false);
     if (rc || (rc = need_comm(ctx))) return rc;
@@ -722,6 +724,7 @@ int strata_cuda_gemv_sharded_dev(strata_ctx* ctx, const strata_weight* w, const 
 int strata_cuda_gemm_sharded_dev(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev,
                                  int64_t m, void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_weight(ctx, w, false);
     if (rc || (rc = need_comm(ctx))) return rc;
@@ -744,6 +747,7 @@ int strata_cuda_gemm_sharded_dev(strata_ctx* ctx, const strata_weight* w, const 
 int strata_cuda_moe_ffn_ep_dev(strata_ctx* ctx, const strata_moe* layer, const float* x_dev,
                                const float* logits_dev, int64_t tokens, float* out_dev, void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = need_comm(ctx);
     if (rc) return rc;

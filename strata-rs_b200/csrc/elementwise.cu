@@ -164,6 +164,7 @@ extern "C" {
 int strata_cuda_rms_norm_dev(strata_ctx* ctx, float* x_dev, const float* w_dev, int64_t n, int64_t rows, double eps,
                              void* stream) {
     if (!ctx || !x_dev || !w_dev) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, rows);
     if (rc) return rc;
@@ -175,6 +176,7 @@ int strata_cuda_rms_norm_dev(strata_ctx* ctx, float* x_dev, const float* w_dev, 
 int strata_cuda_l2_norm_dev(strata_ctx* ctx, float* x_dev, int64_t head_dim, int64_t heads, double eps,
                             void* stream) {
     if (!ctx || !x_dev) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, head_dim, heads);
     if (rc) return rc;
@@ -185,6 +187,7 @@ int strata_cuda_l2_norm_dev(strata_ctx* ctx, float* x_dev, int64_t head_dim, int
 
 int strata_cuda_softmax_dev(strata_ctx* ctx, float* x_dev, int64_t n, int64_t rows, void* stream) {
     if (!ctx || !x_dev) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, rows);
     if (rc) return rc;
@@ -196,6 +199,7 @@ int strata_cuda_softmax_dev(strata_ctx* ctx, float* x_dev, int64_t n, int64_t ro
 int strata_cuda_rope_neox_dev(strata_ctx* ctx, float* x_dev, int64_t head_dim, int64_t heads, int64_t n_rot,
                               int64_t pos, double freq_base, void* stream) {
     if (!ctx || !x_dev || pos < 0 || n_rot < 0) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, head_dim, heads);
     if (rc) return rc;
@@ -209,6 +213,7 @@ int strata_cuda_rope_neox_dev(strata_ctx* ctx, float* x_dev, int64_t head_dim, i
 
 int strata_cuda_add_dev(strata_ctx* ctx, float* a_dev, const float* b_dev, int64_t n, void* stream) {
     if (!ctx || !a_dev || !b_dev) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, 1);
     if (rc) return rc;
@@ -221,6 +226,7 @@ int strata_cuda_add_dev(strata_ctx* ctx, float* a_dev, const float* b_dev, int64
 
 int strata_cuda_rms_norm(strata_ctx* ctx, float* x, const float* w, int64_t n, double eps) {
     if (!ctx || !x || !w) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, 1);
     if (rc) return rc;
@@ -232,6 +238,7 @@ int strata_cuda_rms_norm(strata_ctx* ctx, float* x, const float* w, int64_t n, d
 
 int strata_cuda_l2_norm(strata_ctx* ctx, float* head, int64_t n, double eps) {
     if (!ctx || !head) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, 1);
     if (rc) return rc;
@@ -243,6 +250,7 @@ int strata_cuda_l2_norm(strata_ctx* ctx, float* head, int64_t n, double eps) {
 
 int strata_cuda_softmax(strata_ctx* ctx, float* xs, int64_t n) {
     if (!ctx || !xs) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, 1);
     if (rc) return rc;
@@ -255,6 +263,7 @@ int strata_cuda_softmax(strata_ctx* ctx, float* xs, int64_t n) {
 int strata_cuda_rope_neox(strata_ctx* ctx, float* head, int64_t len, int64_t pos, int64_t n_rot, int64_t head_dim,
                           double freq_base) {
     if (!ctx || !head || pos < 0 || n_rot < 0) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, len, 1);
     if (rc) return rc;
@@ -268,6 +277,7 @@ int strata_cuda_rope_neox(strata_ctx* ctx, float* head, int64_t len, int64_t pos
 
 int strata_cuda_add(strata_ctx* ctx, float* a, const float* b, int64_t n) {
     if (!ctx || !a || !b) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = ew_checked(ctx, n, 1);
     if (rc) return rc;

@@ -625,6 +625,7 @@ int strata_cuda_gguf_view(const strata_gguf* g, int64_t index, int64_t first, in
 int strata_cuda_gguf_ingest(strata_ctx* ctx, const strata_gguf* g, const int64_t* tensors, int64_t n,
                             strata_weight** out) {
     if (!ctx || !g || n < 0 || (n > 0 && (!tensors || !out))) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::vector<strata_upload> items((size_t)n);
     for (int64_t i = 0; i < n; ++i) {
         const int64_t ix = tensors[i];

@@ -197,6 +197,7 @@ int strata_cuda_moe_destroy(strata_moe* L) {
 int strata_cuda_moe_ffn_dev(strata_ctx* ctx, const strata_moe* L, const float* x, const float* logits, int64_t T,
                             float* out, int32_t* ids, float* wts, void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_moe(ctx, L);
     if (rc) return rc;
@@ -208,6 +209,7 @@ int strata_cuda_moe_ffn_dev(strata_ctx* ctx, const strata_moe* L, const float* x
 int strata_cuda_moe_ffn(strata_ctx* ctx, const strata_moe* L, const float* x, const float* logits, int64_t T,
                         float* out, int32_t* ids, float* wts) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_moe(ctx, L);
     if (rc) return rc;

@@ -65,6 +65,7 @@ extern "C" int strata_cuda_gemv_noalloc(const uint8_t* w_dev, uint32_t quant, in
                                         const float* x_dev, float* y_dev, int batch, void* stream) {
     if (quant != kQ4_K && quant != kQ5_K) return STRATA_ERR_UNSUPPORTED_QUANT;
     if (!w_dev || !x_dev || !y_dev || rows <= 0 || cols <= 0 || batch < 1 || batch > 8) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     if (cols % 256 != 0) return STRATA_ERR_TRUNCATED;
     if (cols * batch > kNoallocMaxColsTimesBatch) return STRATA_ERR_SCRATCH_LIMIT;
     if (((uintptr_t)w_dev & 15) || ((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3)) return STRATA_ERR_INVALID;

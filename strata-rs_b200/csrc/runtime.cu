@@ -418,6 +418,7 @@ int upload_locked(strata_ctx* ctx, const strata_upload* items, int64_t n, strata
 int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32_t quant, int64_t n_expert,
                        int64_t rows, int64_t cols, strata_weight** out) {
     if (!ctx || !out) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     const strata_upload u{bytes, len, quant, n_expert, rows, cols};
     return upload_locked(ctx, &u, 1, out);
@@ -425,6 +426,7 @@ int strata_cuda_upload(strata_ctx* ctx, const uint8_t* bytes, size_t len, uint32
 
 int strata_cuda_upload_many(strata_ctx* ctx, const strata_upload* items, int64_t n, strata_weight** out) {
     if (!ctx || n < 0 || (n > 0 && (!items || !out))) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     return upload_locked(ctx, items, n, out);
 }
@@ -446,6 +448,7 @@ int strata_cuda_free_weight(strata_weight* w) {
 int strata_cuda_dequant(strata_ctx* ctx, const strata_weight* w, int64_t expert, int64_t row0, int64_t nrows,
                         float* out_host) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     if (!w || w->magic != kWeightMagic || w->ctx != ctx) return fail(ctx, STRATA_ERR_INVALID, "invalid weight handle");
     int64_t mats = w->n_expert > 0 ? w->n_expert : 1;
@@ -519,6 +522,7 @@ extern "C" {
 int strata_cuda_gemv_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                          void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_weight(ctx, w, false);
     if (rc) return rc;
@@ -528,6 +532,7 @@ int strata_cuda_gemv_dev(strata_ctx* ctx, const strata_weight* w, const float* x
 
 int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int batch) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_weight(ctx, w, false);
     if (rc) return rc;
@@ -596,6 +601,7 @@ static int gemm_check(strata_ctx* ctx, const strata_weight* w, const void* x, co
 int strata_cuda_gemm_bf16_dev(strata_ctx* ctx, const strata_weight* w, const uint16_t* x_dev, float* y_dev,
                               int64_t m, void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = gemm_check(ctx, w, x_dev, y_dev);
     if (rc) return rc;
@@ -606,6 +612,7 @@ int strata_cuda_gemm_bf16_dev(strata_ctx* ctx, const strata_weight* w, const uin
 int strata_cuda_gemm_f32_dev(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int64_t m,
                              void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = gemm_check(ctx, w, x_dev, y_dev);
     if (rc) return rc;
@@ -656,10 +663,12 @@ static int gemm_host(strata_ctx* ctx, const strata_weight* w, const void* x, siz
 }
 
 int strata_cuda_gemm_bf16(strata_ctx* ctx, const strata_weight* w, const uint16_t* x, float* y, int64_t m) {
+    STRATA_CALL_RANGE();
     return gemm_host(ctx, w, x, 2, y, m);
 }
 
 int strata_cuda_gemm_f32(strata_ctx* ctx, const strata_weight* w, const float* x, float* y, int64_t m) {
+    STRATA_CALL_RANGE();
     return gemm_host(ctx, w, x, 4, y, m);
 }
 
@@ -682,6 +691,7 @@ static int expert_enqueue(strata_ctx* ctx, const strata_weight* w, int64_t e, co
 int strata_cuda_expert_gemv_dev(strata_ctx* ctx, const strata_weight* w, int64_t e, const float* x_dev,
                                 float* y_dev, int batch, void* stream) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_weight(ctx, w, true);
     if (rc) return rc;
@@ -692,6 +702,7 @@ int strata_cuda_expert_gemv_dev(strata_ctx* ctx, const strata_weight* w, int64_t
 int strata_cuda_expert_gemv(strata_ctx* ctx, const strata_weight* w, int64_t e, const float* x, float* y,
                             int batch) {
     if (!ctx) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
     std::lock_guard<std::mutex> g(ctx->mu);
     int rc = check_weight(ctx, w, true);
     if (rc) return rc;

@@ -8,6 +8,7 @@
 #include <unordered_set>
 
 #include "../../include/strata_cuda.h"
+#include "host.h"
 #include "kernels.cuh"
 #include "quant.cuh"
 
