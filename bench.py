@@ -194,6 +194,13 @@ class CpuSweep:
         return nbytes / dt / 1e9, desc, dt
 
 
+def serial_baseline(shapes, batches) -> dict:
+    """The same sweep on one thread, as the reference runs ops::gemv (it is
+    single-threaded): a bounded 3 s sample beside the all-cores figure."""
+    v, desc, _ = CpuSweep(shapes, batches, 1).run(3.0)
+    return {"value": round(v, 3), "unit": UNIT, "cores": 1, "sample": desc}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -218,7 +225,7 @@ def run_reference(args):
         "config": {"workload": "Q4_K decode GEMV sweep (K->N 4096->4096, 4096->12288, 12288->4096, 2048->151936; "
                                "batch 1,2,4,8)", "path": "reference CPU path (oracle port of ops::gemv)"},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": desc},
+                         "sample": desc, "single_thread": serial_baseline(shapes, batches)},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -716,7 +723,8 @@ def run_gpu(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         v, desc, dt = CpuSweep(shapes, batches, threads).run(10.0)
-        cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc,
+               "single_thread": serial_baseline(shapes, batches)}
 
     if rank == 0:
         line = {
