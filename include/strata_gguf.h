@@ -78,7 +78,8 @@ int strata_cuda_gguf_n_shards(const strata_gguf *g);
 int strata_cuda_gguf_shard(const strata_gguf *g, int shard, strata_gguf_shard *out);
 
 typedef struct {
-    const char *name;
+    const char *name;  /* NUL-terminated; a name may itself hold NUL bytes (valid UTF-8), so: */
+    uint64_t name_len; /* its length in bytes */
     uint32_t type;     /* Strata ggml type id as stored (not validated until the payload is asked for) */
     int32_t n_dims;    /* 1..4 */
     uint64_t dims[4];  /* GGUF order: dims[0] varies fastest; unused entries are 0 */
@@ -89,7 +90,8 @@ typedef struct {
 /* Tensors across all shards, in shard order then directory order. */
 int64_t strata_cuda_gguf_tensor_count(const strata_gguf *g);
 int strata_cuda_gguf_tensor(const strata_gguf *g, int64_t index, strata_gguf_tensor *out);
-/* STRATA_OK with *index set, or STRATA_ERR_TENSOR_NOT_FOUND with *index = -1. */
+/* STRATA_OK with *index set, or STRATA_ERR_TENSOR_NOT_FOUND with *index = -1.
+ * The name is taken up to its first NUL byte. */
 int strata_cuda_gguf_find(const strata_gguf *g, const char *name, int64_t *index);
 
 /* The tensor's payload in the mapping: exactly the bytes its shape and type
@@ -116,7 +118,8 @@ typedef struct {
     uint32_t elem;
     uint64_t count;
 } strata_gguf_value;
-/* STRATA_OK, or STRATA_ERR_INVALID when the key is absent. */
+/* STRATA_OK, or STRATA_ERR_INVALID when the key is absent (the key is taken
+ * up to its first NUL byte). */
 int strata_cuda_gguf_meta(const strata_gguf *g, const char *key, strata_gguf_value *out);
 
 /* The upload item (strata_cuda.h) for rows [first, first + count) of a 1-D or

@@ -465,10 +465,16 @@ bool tensor_view(const strata_gguf& g, int64_t index, int64_t first, int64_t cou
     const int64_t cols = (int64_t)t.shape[0];
     const int64_t rows = nd == 1 ? 1 : (int64_t)t.shape[1];
     const int64_t outer = nd == 3 ? (int64_t)t.shape[2] : rows;  // what [first, first + count) counts
+    const char* what = nd == 3 ? "experts" : "rows";
+    if (first < 0 || first > outer) {
+        *e = make_error(STRATA_ERR_INVALID, "first %s %lld is outside tensor '%s' (%lld %s)", what, (long long)first,
+                        t.name.c_str(), (long long)outer, what);
+        return false;
+    }
     if (count < 0) count = outer - first;
-    if (first < 0 || first > outer || count < 0 || count > outer - first) {
-        *e = make_error(STRATA_ERR_INVALID, "range [%lld, %lld) is outside tensor '%s' (%lld %s)", (long long)first,
-                        (long long)(first + count), t.name.c_str(), (long long)outer, nd == 3 ? "experts" : "rows");
+    if (count > outer - first) {
+        *e = make_error(STRATA_ERR_INVALID, "%lld %s from %lld run past the end of tensor '%s' (%lld %s)",
+                        (long long)count, what, (long long)first, t.name.c_str(), (long long)outer, what);
         return false;
     }
     uint64_t bs = 1, ts = 0;
@@ -566,6 +572,7 @@ int strata_cuda_gguf_tensor(const strata_gguf* g, int64_t index, strata_gguf_ten
     if (!g || !out || index < 0 || index >= (int64_t)g->order.size()) return STRATA_ERR_INVALID;
     const TensorInfo& t = g->tensor(index);
     out->name = t.name.c_str();
+    out->name_len = t.name.size();
     out->type = t.ty;
     out->n_dims = (int32_t)t.shape.size();
     for (int d = 0; d < 4; ++d) out->dims[d] = d < (int)t.shape.size() ? t.shape[d] : 0;

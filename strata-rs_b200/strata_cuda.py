@@ -161,8 +161,8 @@ class GgufShardInfo(C.Structure):
 
 class GgufTensorInfo(C.Structure):
     """strata_gguf_tensor (strata_gguf.h)."""
-    _fields_ = [("name", C.c_char_p), ("type", C.c_uint32), ("n_dims", C.c_int32), ("dims", C.c_uint64 * 4),
-                ("offset", C.c_uint64), ("shard", C.c_int32)]
+    _fields_ = [("name", C.c_void_p), ("name_len", C.c_uint64), ("type", C.c_uint32), ("n_dims", C.c_int32),
+                ("dims", C.c_uint64 * 4), ("offset", C.c_uint64), ("shard", C.c_int32)]
 
 
 class GgufValue(C.Structure):
@@ -311,7 +311,8 @@ class GgufModel:
         rc = lib().strata_cuda_gguf_tensor(self.h, index, C.byref(t))
         if rc != OK:
             raise BackendError(rc, f"no tensor {index}")
-        return GgufTensor(t.name.decode(), list(t.dims[:t.n_dims]), t.type, t.offset, t.shard)
+        name = C.string_at(t.name, t.name_len).decode()
+        return GgufTensor(name, list(t.dims[:t.n_dims]), t.type, t.offset, t.shard)
 
     def tensors(self) -> list:
         return [self.tensor(i) for i in range(self.tensor_count())]
