@@ -344,6 +344,8 @@ int check_upload(strata_ctx* ctx, const strata_upload& u, int64_t* need, int64_t
     if (u.cols % be != 0)
         return fail(ctx, STRATA_ERR_TRUNCATED, "cols=%lld is not a whole number of %d-element blocks",
                     (long long)u.cols, be);
+    if (u.cols / be > INT64_MAX / block_bytes(u.quant))
+        return fail(ctx, STRATA_ERR_INVALID, "cols=%lld is too large", (long long)u.cols);
     *rb = quant_row_bytes(u.quant, u.cols);
     const int64_t mats = u.n_expert > 0 ? u.n_expert : 1;
     if (u.rows > 0 && (mats > INT64_MAX / u.rows || mats * u.rows > INT64_MAX / *rb))
