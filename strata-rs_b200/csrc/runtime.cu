@@ -469,7 +469,7 @@ int strata_cuda_dequant(strata_ctx* ctx, const strata_weight* w, int64_t expert,
     cudaError_t e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, nbytes, cudaMemcpyDeviceToHost, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
     if ((rc = wait_stream(ctx, ctx->stream))) return rc;
-    memcpy(out_host, ctx->y_host.ptr, nbytes);
+    copy_host(out_host, ctx->y_host.ptr, nbytes);
     return STRATA_OK;
 }
 
@@ -547,7 +547,7 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     if ((rc = ensure_device(ctx, ctx->y_dev, yb, "cudaMalloc(y)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
-    memcpy(ctx->x_host.ptr, x, xb);
+    copy_host(ctx->x_host.ptr, x, xb);
     cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
     if ((rc = gemv_enqueue(ctx, w, (const float*)ctx->x_dev.ptr, (float*)ctx->y_dev.ptr, batch, ctx->stream)))
@@ -555,7 +555,7 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
     if ((rc = wait_stream(ctx, ctx->stream))) return rc;
-    memcpy(y, ctx->y_host.ptr, yb);
+    copy_host(y, ctx->y_host.ptr, yb);
     return STRATA_OK;
 }
 
@@ -648,7 +648,7 @@ static int gemm_host(strata_ctx* ctx, const strata_weight* w, const void* x, siz
         if ((rc = ensure_device(ctx, ctx->x_bf16, nb, "cudaMalloc(x bf16)"))) return rc;
         xg = (const uint16_t*)ctx->x_bf16.ptr;
     }
-    memcpy(ctx->x_host.ptr, x, xb);
+    copy_host(ctx->x_host.ptr, x, xb);
     cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
     if (x_elem == 4) {
@@ -660,7 +660,7 @@ static int gemm_host(strata_ctx* ctx, const strata_weight* w, const void* x, siz
     e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
     if ((rc = wait_stream(ctx, ctx->stream))) return rc;
-    memcpy(y, ctx->y_host.ptr, yb);
+    copy_host(y, ctx->y_host.ptr, yb);
     return STRATA_OK;
 }
 
@@ -717,7 +717,7 @@ int strata_cuda_expert_gemv(strata_ctx* ctx, const strata_weight* w, int64_t e, 
     if ((rc = ensure_device(ctx, ctx->y_dev, yb, "cudaMalloc(y)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
-    memcpy(ctx->x_host.ptr, x, xb);
+    copy_host(ctx->x_host.ptr, x, xb);
     cudaError_t err = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
     if (err != cudaSuccess) return cuda_fail(ctx, err, "cudaMemcpyAsync(H2D)");
     if ((rc = expert_enqueue(ctx, w, e, (const float*)ctx->x_dev.ptr, (float*)ctx->y_dev.ptr, batch, ctx->stream)))
@@ -725,7 +725,7 @@ int strata_cuda_expert_gemv(strata_ctx* ctx, const strata_weight* w, int64_t e, 
     err = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
     if (err != cudaSuccess) return cuda_fail(ctx, err, "cudaMemcpyAsync(D2H)");
     if ((rc = wait_stream(ctx, ctx->stream))) return rc;
-    memcpy(y, ctx->y_host.ptr, yb);
+    copy_host(y, ctx->y_host.ptr, yb);
     return STRATA_OK;
 }
 

@@ -10,6 +10,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 namespace strata {
@@ -62,6 +63,39 @@ inline void stage_fill(const std::vector<StagePiece>& pieces, const StageSeg* se
         const size_t hi = p.off + p.n < b ? p.off + p.n : b;
         if (lo < hi) memcpy(stage + lo, segs[p.seg].src + p.seg_off + (lo - p.off), hi - lo);
     }
+}
+
+// Copies n bytes between host buffers (the pinned staging and a caller's
+// slice). One host thread copies at roughly 10 GB/s, so a synchronous call
+// returning a few MB would spend most of its time here: copies of 2 MiB and
+// more are split over up to 8 threads, at least 1 MiB each, in 64-byte-aligned
+// parts; the calling thread copies the first part. If a thread cannot be
+// started, its part is copied here instead.
+inline void copy_host(void* dst, const void* src, size_t n) {
+    constexpr size_t kMin = size_t(2) << 20, kPerThread = size_t(1) << 20;
+    constexpr int kMaxThreads = 8;
+    if (n < kMin) {
+        if (n) memcpy(dst, src, n);
+        return;
+    }
+    const size_t T = n / kPerThread < (size_t)kMaxThreads ? n / kPerThread : (size_t)kMaxThreads;  // >= 2
+    const size_t part = ((n + T - 1) / T + 63) & ~size_t(63);  // T parts cover n
+    char* d = static_cast<char*>(dst);
+    const char* s = static_cast<const char*>(src);
+    std::thread th[kMaxThreads];
+    for (size_t t = 1; t < T; ++t) {
+        const size_t a = t * part;
+        if (a >= n) break;
+        const size_t len = a + part < n ? part : n - a;
+        try {
+            th[t] = std::thread([d, s, a, len] { memcpy(d + a, s + a, len); });
+        } catch (...) {
+            memcpy(d + a, s + a, len);
+        }
+    }
+    memcpy(d, s, part);
+    for (auto& x : th)
+        if (x.joinable()) x.join();
 }
 
 }  // namespace strata

@@ -4,8 +4,9 @@
 // stage_plan / stage_fill with a small chunk and split among 8 "threads" the
 // way the upload splits a chunk; every destination must come out equal to its
 // source, every piece must stay inside its segment and its chunk, and the
-// chunks must be full except the last. Prints "ok" and exits 0, or names the
-// first failure and exits 1.
+// chunks must be full except the last. copy_host (the threaded host copy of
+// large results) is checked on sizes around its thresholds with unaligned
+// ends. Prints "ok" and exits 0, or names the first failure and exits 1.
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
@@ -69,8 +70,29 @@ static int check(std::mt19937_64& g, size_t cap, int nseg_max) {
     return 0;
 }
 
+// copy_host over sizes on both sides of its thresholds and unaligned ends.
+static int check_copy(std::mt19937_64& g) {
+    const size_t sizes[] = {0, 1, 63, 4096, (size_t(2) << 20) - 1, size_t(2) << 20, (size_t(2) << 20) + 1,
+                            (size_t(3) << 20) + 77, (size_t(9) << 20) + 5, (size_t(17) << 20) - 3};
+    std::vector<size_t> all(sizes, sizes + sizeof(sizes) / sizeof(sizes[0]));
+    for (int i = 0; i < 24; ++i) all.push_back((size_t(2) << 20) + g() % (size_t(15) << 20));
+    for (size_t n : all) {
+        const size_t so = g() % 64, dof = g() % 64;
+        std::vector<uint8_t> src(n + so), dst(n + dof + 64, 0xAB);
+        for (auto& b : src) b = (uint8_t)g();
+        copy_host(dst.data() + dof, src.data() + so, n);
+        if (n && memcmp(dst.data() + dof, src.data() + so, n) != 0) return printf("copy_host(%zu) differs\n", n), 1;
+        for (size_t i = 0; i < dof; ++i)
+            if (dst[i] != 0xAB) return printf("copy_host(%zu) wrote before dst\n", n), 1;
+        for (size_t i = dof + n; i < dst.size(); ++i)
+            if (dst[i] != 0xAB) return printf("copy_host(%zu) wrote past dst\n", n), 1;
+    }
+    return 0;
+}
+
 int main() {
     std::mt19937_64 g(20261202);
+    if (check_copy(g)) return 1;
     for (size_t cap : {size_t(1), size_t(7), size_t(64), size_t(1000), size_t(4096)})
         for (int it = 0; it < 300; ++it)
             if (check(g, cap, it % 3 == 0 ? 3 : 40)) return printf("cap %zu case %d\n", cap, it), 1;
