@@ -311,7 +311,12 @@ int copy_in(strata_ctx* ctx, const StageSeg* segs, int64_t nseg) {
         const size_t part = (len + kStageThreads - 1) / kStageThreads;
         for (int t = 0; t < kStageThreads; ++t) {
             const size_t a = t * part, b = a + part < len ? a + part : len;
-            if (a < b) th[t] = std::thread([&pieces, segs, stage, a, b] { stage_fill(pieces, segs, stage, a, b); });
+            if (a >= b) continue;
+            try {
+                th[t] = std::thread([&pieces, segs, stage, a, b] { stage_fill(pieces, segs, stage, a, b); });
+            } catch (...) {  // no thread to be had: fill this part here
+                stage_fill(pieces, segs, stage, a, b);
+            }
         }
         for (auto& t : th)
             if (t.joinable()) t.join();
