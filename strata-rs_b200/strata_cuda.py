@@ -565,6 +565,8 @@ class Context:
     def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
         x = np.array(x, dtype=np.float32, copy=True).reshape(-1)
         w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+        if w.size < x.size:  # ops::rms_norm indexes w[i] for every i of x (a panic there)
+            raise BackendError(ERR_INVALID, f"rms_norm: {w.size} weights for {x.size} values")
         self.check(lib().strata_cuda_rms_norm(self.h, _fptr(x), _fptr(w), x.size, eps))
         return x
 
@@ -584,9 +586,12 @@ class Context:
         return x
 
     def add(self, a: np.ndarray, b: np.ndarray) -> np.ndarray:
+        """a + b over the common length, a's tail unchanged (ops::add_into zips the two)."""
         x = np.array(a, dtype=np.float32, copy=True).reshape(-1)
         bb = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
-        self.check(lib().strata_cuda_add(self.h, _fptr(x), _fptr(bb), x.size))
+        n = min(x.size, bb.size)
+        if n:
+            self.check(lib().strata_cuda_add(self.h, _fptr(x), _fptr(bb), n))
         return x
 
     # ---- the same on device pointers, many vectors per call
@@ -649,6 +654,15 @@ class Context:
         self.check(lib().strata_cuda_expert_gemv_dev(self.h, w.handle, e, x_ptr, y_ptr, batch, stream or None))
 
 
+@dataclass
+class RopeCfg:
+    """strata_core::backend::RopeCfg (crates/strata-core/src/backend.rs:158-167)."""
+    pos: int
+    n_rot: int
+    head_dim: int
+    freq_base: float
+
+
 class CudaBackend:
     """strata-core's ComputeBackend over the CUDA path (name() == "cuda").
 
@@ -682,6 +696,22 @@ class CudaBackend:
             raise BackendError(ERR_INVALID, f"expert_gemv {w.name}: x/y do not match {w.rows}x{w.cols}")
         dw = self._resident(w.data, w.quant, w.rows, w.cols, w.n_expert)
         y[...] = self.ctx.expert_gemv(dw, e, x)
+
+    # the elementwise trait methods (backend.rs:37-50), in place on the caller's slices
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> None:
+        x[...] = self.ctx.rms_norm(x, w, eps).reshape(x.shape)
+
+    def rope_neox(self, head: np.ndarray, cfg: RopeCfg) -> None:
+        head[...] = self.ctx.rope_neox(head, cfg.pos, cfg.n_rot, cfg.head_dim, cfg.freq_base).reshape(head.shape)
+
+    def softmax(self, xs: np.ndarray) -> None:
+        xs[...] = self.ctx.softmax(xs).reshape(xs.shape)
+
+    def l2_norm(self, head: np.ndarray, eps: float) -> None:
+        head[...] = self.ctx.l2_norm(head, eps).reshape(head.shape)
+
+    def add(self, a: np.ndarray, b: np.ndarray) -> None:
+        a[...] = self.ctx.add(a, b).reshape(a.shape)
 
     def close(self):
         for w in self._cache.values():

@@ -1,0 +1,75 @@
+"""The Python mirror of ComputeBackend's elementwise methods
+(crates/strata-core/src/backend.rs:37-50) without a GPU: CudaBackend's
+in-place wrappers are driven through a stand-in context that computes with
+the oracle, so the argument order, the RopeCfg fields and the in-place
+writes are checked here; the device itself is checked in
+tests/test_elementwise_gpu.py. Also the host-side length rules the reference
+has: rms_norm needs a weight per value (ops::rms_norm indexes w[i]), add
+works over the common length (ops::add_into zips)."""
+import numpy as np
+import pytest
+
+import oracle
+import strata_cuda as sc
+from synth import rng
+
+
+class OracleCtx:
+    """Context's host-slice elementwise methods, computed by the oracle."""
+
+    def rms_norm(self, x, w, eps):
+        return oracle.rms_norm(np.asarray(x, np.float32).reshape(-1), np.asarray(w, np.float32).reshape(-1), eps)
+
+    def l2_norm(self, head, eps):
+        h = np.asarray(head, np.float32).reshape(-1)
+        return oracle.l2_norm(h, h.size, eps)
+
+    def softmax(self, xs):
+        v = np.asarray(xs, np.float32).reshape(-1)
+        return oracle.softmax(v, v.size)
+
+    def rope_neox(self, head, pos, n_rot, head_dim, freq_base):
+        return oracle.rope_neox(np.asarray(head, np.float32).reshape(-1), head_dim, pos, n_rot, freq_base)
+
+    def add(self, a, b):
+        a = np.asarray(a, np.float32).reshape(-1).copy()
+        n = min(a.size, np.asarray(b).size)
+        a[:n] = oracle.add(a[:n], np.asarray(b, np.float32).reshape(-1)[:n])
+        return a
+
+
+def backend():
+    be = object.__new__(sc.CudaBackend)
+    be.ctx, be._cache = OracleCtx(), {}
+    return be
+
+
+def test_elementwise_trait_methods_write_in_place():
+    be, g = backend(), rng(77)
+    x = g.standard_normal(64).astype(np.float32)
+    w = g.standard_normal(64).astype(np.float32)
+    y = x.copy()
+    be.rms_norm(y, w, 1e-6)
+    assert np.array_equal(y, oracle.rms_norm(x, w, 1e-6))
+    h = x.copy()
+    be.l2_norm(h, 0.0)
+    assert np.array_equal(h, oracle.l2_norm(x, 64, 0.0))
+    s = x.copy()
+    be.softmax(s)
+    assert np.array_equal(s, oracle.softmax(x, 64))
+    r = x.copy()
+    be.rope_neox(r, sc.RopeCfg(pos=17, n_rot=32, head_dim=64, freq_base=1e6))
+    assert np.array_equal(r, oracle.rope_neox(x, 64, 17, 32, 1e6))
+    a = x.copy()
+    be.add(a, w[:40])
+    assert np.array_equal(a[:40], x[:40] + w[:40]) and np.array_equal(a[40:], x[40:])
+
+
+def test_length_rules_are_checked_before_the_device():
+    ctx = object.__new__(sc.Context)
+    ctx.h = None
+    with pytest.raises(sc.BackendError) as ei:
+        ctx.rms_norm(np.ones(8, np.float32), np.ones(7, np.float32), 0.0)
+    assert ei.value.code == sc.ERR_INVALID
+    a = np.arange(4, dtype=np.float32)
+    assert np.array_equal(ctx.add(a, np.zeros(0, np.float32)), a)  # nothing in common: a unchanged

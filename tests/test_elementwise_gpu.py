@@ -132,3 +132,28 @@ def test_device_forms_many_rows(ctx):
 def test_rejects_bad_shapes(ctx):
     with pytest.raises(sc.BackendError):
         ctx.softmax(np.zeros(0, np.float32))
+
+
+def test_backend_trait_methods_in_place():
+    """CudaBackend's rms_norm / rope_neox / softmax / l2_norm / add write the
+    caller's slices in place, as the trait's &mut [f32] arguments do."""
+    be = sc.CudaBackend(0)
+    g = rng(600)
+    x = g.standard_normal(256).astype(np.float32)
+    w = g.standard_normal(256).astype(np.float32)
+    y = x.copy()
+    be.rms_norm(y, w, 1e-6)
+    assert_close(y, oracle.rms_norm(x, w, 1e-6), "trait rms_norm")
+    r = x[:128].copy()
+    be.rope_neox(r, sc.RopeCfg(pos=99, n_rot=64, head_dim=128, freq_base=1e6))
+    assert_close(r, oracle.rope_neox(x[:128], 128, 99, 64, 1e6), "trait rope_neox")
+    s = x.copy()
+    be.softmax(s)
+    assert_close(s, oracle.softmax(x, 256), "trait softmax", max_ulps=2)
+    h = x[:128].copy()
+    be.l2_norm(h, 0.0)
+    assert_close(h, oracle.l2_norm(x[:128], 128, 0.0), "trait l2_norm")
+    a = x.copy()
+    be.add(a, w[:100])
+    assert np.array_equal(a[:100], oracle.add(x[:100], w[:100])) and np.array_equal(a[100:], x[100:])
+    be.close()
