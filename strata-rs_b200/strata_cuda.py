@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+from collections import OrderedDict
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -663,26 +664,48 @@ class RopeCfg:
     freq_base: float
 
 
+DEFAULT_WEIGHT_BUDGET = 4 << 30  # WgpuBackend::probe's default (crates/strata-backend-wgpu/src/gpu.rs:227-229)
+
+
 class CudaBackend:
     """strata-core's ComputeBackend over the CUDA path (name() == "cuda").
 
-    Weights are uploaded on first use and cached by (data address, length),
-    like the wgpu backend's name-keyed cache (crates/strata-backend-wgpu/src/gpu.rs:271,287).
+    Weights are uploaded on first use and cached by (data address, length,
+    n_expert), like the wgpu backend's cache (crates/strata-backend-wgpu/src/gpu.rs:271,287);
+    as its WeightCache (gpu.rs:61-112), the cache holds at most `budget_bytes`
+    of resident weights and evicts the least recently used first when a new
+    weight would not fit (an entry larger than the budget is still uploaded).
+    The CLI's --gpu-weights-mib (crates/strata-cli/src/main.rs:116-118) maps here.
     """
 
-    def __init__(self, device: int = 0):
+    def __init__(self, device: int = 0, budget_bytes: int = DEFAULT_WEIGHT_BUDGET):
         self.ctx = Context(device)
-        self._cache: dict[tuple[int, int, int], Weight] = {}
+        self.budget = budget_bytes
+        self._cache: OrderedDict[tuple[int, int, int], Weight] = OrderedDict()
+        self._bytes = 0
 
     def name(self) -> str:
         return lib().strata_cuda_name().decode()
 
+    def resident_bytes(self) -> int:
+        """Bytes of weights the cache holds (WgpuBackend::resident_bytes)."""
+        return self._bytes
+
     def _resident(self, data: np.ndarray, quant: int, rows: int, cols: int, n_expert: int) -> Weight:
         key = (data.ctypes.data, data.nbytes, n_expert)
         w = self._cache.get(key)
-        if w is None:
-            w = self.ctx.upload(data, quant, rows, cols, n_expert)
-            self._cache[key] = w
+        if w is not None:
+            self._cache.move_to_end(key)  # most recently used
+            return w
+        need = byte_size(quant, cols) * rows * max(1, n_expert) if quant in BLOCK else data.nbytes
+        while self._cache and self._bytes + need > self.budget:
+            _, victim = self._cache.popitem(last=False)
+            self._bytes -= victim.cached_bytes
+            victim.free()
+        w = self.ctx.upload(data, quant, rows, cols, n_expert)
+        w.cached_bytes = need
+        self._cache[key] = w
+        self._bytes += need
         return w
 
     def gemv(self, w: QuantTensor, x: np.ndarray, y: np.ndarray, scratch=None) -> None:
@@ -717,4 +740,5 @@ class CudaBackend:
         for w in self._cache.values():
             w.free()
         self._cache.clear()
+        self._bytes = 0
         self.ctx.close()

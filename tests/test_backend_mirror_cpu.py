@@ -73,3 +73,39 @@ def test_length_rules_are_checked_before_the_device():
     assert ei.value.code == sc.ERR_INVALID
     a = np.arange(4, dtype=np.float32)
     assert np.array_equal(ctx.add(a, np.zeros(0, np.float32)), a)  # nothing in common: a unchanged
+
+
+class CountingCtx:
+    """A stand-in context that records uploads and frees (no device)."""
+
+    def __init__(self):
+        self.live = set()
+
+    def upload(self, data, quant, rows, cols, n_expert=0):
+        w = sc.Weight(self, object(), quant, n_expert, rows, cols)
+        w.free = lambda w=w: self.live.discard(id(w))
+        self.live.add(id(w))
+        return w
+
+    def gemv(self, w, x):
+        return np.zeros(w.rows, np.float32)
+
+
+def test_weight_cache_evicts_least_recently_used_over_budget():
+    """gpu.rs:577-599 (a 24 MiB budget and three 10 MiB matrices: the first
+    must go), with the LRU order of WeightCache (gpu.rs:61-112)."""
+    be = object.__new__(sc.CudaBackend)
+    be.ctx, be.budget, be._cache, be._bytes = CountingCtx(), 24 << 20, sc.OrderedDict(), 0
+    cols = 4096
+    rows = (10 << 20) // sc.byte_size(sc.Q8_0, cols)
+    mats = [np.zeros(rows * sc.byte_size(sc.Q8_0, cols), np.uint8) for _ in range(3)]
+    ts = [sc.QuantTensor(f"big{i}", sc.Q8_0, rows, cols, m) for i, m in enumerate(mats)]
+    x, y = np.ones(cols, np.float32), np.empty(rows, np.float32)
+    for t in ts:
+        be.gemv(t, x, y)
+    assert be.resident_bytes() <= 2 * mats[0].nbytes and len(be.ctx.live) == 2
+    assert [k[0] for k in be._cache] == [mats[1].ctypes.data, mats[2].ctypes.data]  # big0 went first
+    be.gemv(ts[1], x, y)       # big1 becomes the most recent
+    be.gemv(ts[0], x, y)       # big0 comes back: big2, now the least recent, goes
+    assert [k[0] for k in be._cache] == [mats[1].ctypes.data, mats[0].ctypes.data]
+    assert be.resident_bytes() == 2 * mats[0].nbytes and len(be.ctx.live) == 2
