@@ -189,6 +189,24 @@ def test_backend_trait_mirror(ctx):
     be.close()
 
 
+def test_backend_weight_cache_evicts_over_budget():
+    """crates/strata-backend-wgpu/src/gpu.rs:577-599 on the device: a 24 MiB budget and three
+    10 MiB matrices (Q8_0 here; F32 [n x 1] there): the first must go, and what stays
+    resident is what the context holds."""
+    be = sc.CudaBackend(0, budget_bytes=24 << 20)
+    cols = 4096
+    rows = (10 << 20) // sc.byte_size(Q8_0, cols)
+    x = activations(1402, 1, cols)[0]
+    y = np.empty(rows, np.float32)
+    mats = [quant_matrix(1403 + i, Q8_0, rows, cols) for i in range(3)]
+    for i, m in enumerate(mats):
+        be.gemv(sc.QuantTensor(f"big{i}", Q8_0, rows, cols, m), x, y, None)
+    assert be.resident_bytes() <= 2 * mats[0].nbytes
+    assert be.ctx.resident_bytes() == be.resident_bytes()
+    assert rel_err(y, oracle.gemv(Q8_0, mats[2], rows, cols, x, threads=4)) < TOL
+    be.close()
+
+
 # ---- error behaviour (host-side checks; nothing here faults the device)
 
 def test_errors(ctx):
