@@ -136,6 +136,23 @@ int strata_cuda_gguf_view(const strata_gguf *g, int64_t index, int64_t first, in
 int strata_cuda_gguf_ingest(strata_ctx *ctx, const strata_gguf *g, const int64_t *tensors, int64_t n,
                             strata_weight **out);
 
+/* One MoE layer of a GGUF model on the device, as strata-core's load_layer
+ * (crates/strata-core/src/moe.rs:147-188) finds it: blk.<layer>.ffn_gate_inp.weight
+ * (the router), ffn_gate_exps / ffn_up_exps / ffn_down_exps.weight and, when
+ * with_shared, ffn_gate_shexp / ffn_up_shexp / ffn_down_shexp.weight and
+ * ffn_gate_inp_shexp.weight. Only experts [expert_begin, expert_end) of the
+ * expert tensors are read and uploaded (expert_end <= 0: to the last one;
+ * n_expert is the expert tensors' count), together with the other tensors
+ * in one staged pass (strata_cuda_upload_many); then the layer is created
+ * (strata_cuda_moe_create) with n_ff = gate_exps' columns. weights_out (8
+ * entries, in strata_moe_desc's order) receives the handles the layer uses
+ * (NULL for the shared expert's when not loaded): free them after
+ * strata_cuda_moe_destroy. A missing tensor is STRATA_ERR_TENSOR_NOT_FOUND
+ * naming it (MissingTensor there); nothing stays resident on an error. */
+int strata_cuda_gguf_moe_layer(strata_ctx *ctx, const strata_gguf *g, int64_t layer, int64_t top_k,
+                               int64_t expert_begin, int64_t expert_end, int with_shared, strata_moe **out,
+                               strata_weight **weights_out);
+
 #ifdef __cplusplus
 }
 #endif

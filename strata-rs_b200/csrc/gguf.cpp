@@ -650,4 +650,80 @@ int strata_cuda_gguf_ingest(strata_ctx* ctx, const strata_gguf* g, const int64_t
     return strata_cuda_upload_many(ctx, items.data(), n, out);
 }
 
+int strata_cuda_gguf_moe_layer(strata_ctx* ctx, const strata_gguf* g, int64_t layer, int64_t top_k,
+                               int64_t expert_begin, int64_t expert_end, int with_shared, strata_moe** out,
+                               strata_weight** weights_out) {
+    if (!ctx || !g || !out || !weights_out || layer < 0) return STRATA_ERR_INVALID;
+    STRATA_CALL_RANGE();
+    *out = nullptr;
+    for (int i = 0; i < 8; ++i) weights_out[i] = nullptr;
+    // strata_moe_desc's order: router, gate/up/down experts, gate/up/down shared, shared gate input
+    static const char* const kNames[8] = {"ffn_gate_inp",   "ffn_gate_exps",  "ffn_up_exps",
+                                          "ffn_down_exps",  "ffn_gate_shexp", "ffn_up_shexp",
+                                          "ffn_down_shexp", "ffn_gate_inp_shexp"};
+    const int n_tensors = with_shared ? 8 : 4;
+    const std::string prefix = "blk." + std::to_string(layer) + ".";
+    int64_t index[8];
+    for (int i = 0; i < n_tensors; ++i) {
+        const std::string name = prefix + kNames[i] + ".weight";
+        auto it = g->index.find(name);
+        if (it == g->index.end())
+            return strata::report(ctx, STRATA_ERR_TENSOR_NOT_FOUND,
+                                  ("tensor '" + name + "' is missing from the model").c_str());
+        index[i] = it->second;
+    }
+    // the expert count and range from gate_exps ([n_ff, n_embd, n_expert])
+    const TensorInfo& ge = g->tensor(index[1]);
+    if (ge.shape.size() != 3 || ge.shape[2] > (uint64_t)INT64_MAX)
+        return strata::report(ctx, STRATA_ERR_WRONG_TENSOR_DIMS,
+                              ("tensor '" + ge.name + "' is not a 3-D expert tensor").c_str());
+    const int64_t n_expert = (int64_t)ge.shape[2];
+    if (expert_end <= 0) expert_end = n_expert;
+    if (expert_begin < 0 || expert_begin >= expert_end || expert_end > n_expert)
+        return strata::report(ctx, STRATA_ERR_INVALID,
+                              ("expert range [" + std::to_string(expert_begin) + ", " + std::to_string(expert_end) +
+                               ") outside the " + std::to_string(n_expert) + " experts of '" + ge.name + "'")
+                                  .c_str());
+    strata_upload items[8];
+    for (int i = 0; i < n_tensors; ++i) {
+        const bool experts = i >= 1 && i <= 3;
+        GgufError e;
+        if (!tensor_view(*g, index[i], experts ? expert_begin : 0, experts ? expert_end - expert_begin : -1,
+                         &items[i], &e))
+            return strata::report(ctx, e.code, e.msg.c_str());
+        if (experts != (items[i].n_expert > 0))
+            return strata::report(ctx, STRATA_ERR_WRONG_TENSOR_DIMS,
+                                  ("tensor '" + g->tensor(index[i]).name + "' has " +
+                                   std::to_string(g->tensor(index[i]).shape.size()) + " dimensions")
+                                      .c_str());
+    }
+    strata_weight* ws[8] = {};
+    int rc = strata_cuda_upload_many(ctx, items, n_tensors, ws);
+    if (rc) return rc;
+    strata_moe_desc d{};
+    d.router = ws[0];
+    d.gate_exps = ws[1];
+    d.up_exps = ws[2];
+    d.down_exps = ws[3];
+    d.gate_shexp = with_shared ? ws[4] : nullptr;
+    d.up_shexp = with_shared ? ws[5] : nullptr;
+    d.down_shexp = with_shared ? ws[6] : nullptr;
+    d.gate_inp_shexp = with_shared ? ws[7] : nullptr;
+    d.n_embd = items[0].cols;   // the router is [n_expert rows][n_embd]
+    d.n_expert = n_expert;
+    d.top_k = top_k;
+    d.n_ff = items[1].cols;     // gate_exps' columns, as load_layer takes n_ff
+    d.n_ff_shexp = with_shared ? items[4].rows : 0;
+    d.expert_begin = expert_begin;
+    d.expert_end = expert_end;
+    d.with_shared = with_shared ? 1 : 0;
+    rc = strata_cuda_moe_create(ctx, &d, out);
+    if (rc) {
+        for (int i = 0; i < n_tensors; ++i) strata_cuda_free_weight(ws[i]);
+        return rc;
+    }
+    for (int i = 0; i < n_tensors; ++i) weights_out[i] = ws[i];
+    return STRATA_OK;
+}
+
 }  // extern "C"

@@ -92,6 +92,7 @@ def lib() -> C.CDLL:
             "strata_cuda_gguf_meta": (i32, [vp, C.c_char_p, C.POINTER(GgufValue)]),
             "strata_cuda_gguf_ingest": (i32, [vp, vp, C.POINTER(i64), i64, C.POINTER(vp)]),
             "strata_cuda_gguf_view": (i32, [vp, i64, i64, i64, C.POINTER(UploadItem), C.c_char_p, sz]),
+            "strata_cuda_gguf_moe_layer": (i32, [vp, vp, i64, i64, i64, i64, i32, C.POINTER(vp), C.POINTER(vp)]),
             "strata_cuda_free_weight": (i32, [vp]),
             "strata_cuda_dequant": (i32, [vp, vp, i64, i64, i64, fp]),
             "strata_cuda_gemv": (i32, [vp, vp, fp, fp, i32]),
@@ -525,6 +526,19 @@ class Context:
         h = C.c_void_p()
         self.check(lib().strata_cuda_moe_create(self.h, C.byref(d), C.byref(h)))
         return MoeLayer(self, h, n_embd, n_expert, top_k)
+
+    def gguf_moe_layer(self, model: "GgufModel", layer: int, top_k: int, expert_begin: int = 0,
+                       expert_end: int = 0, with_shared: bool = True):
+        """strata_cuda_gguf_moe_layer (load_layer, crates/strata-core/src/moe.rs:147-188):
+        returns the MoeLayer and its uploaded weights (free them after the layer)."""
+        h = C.c_void_p()
+        ws = (C.c_void_p * 8)()
+        self.check(lib().strata_cuda_gguf_moe_layer(self.h, model.h, layer, top_k, expert_begin, expert_end,
+                                                    1 if with_shared else 0, C.byref(h), ws))
+        router = model.find(f"blk.{layer}.ffn_gate_inp.weight")
+        exps = model.find(f"blk.{layer}.ffn_gate_exps.weight")
+        weights = [Weight(self, C.c_void_p(p), 0, 0, 0, 0) for p in ws if p]
+        return MoeLayer(self, h, router.shape[0], exps.shape[2], top_k), weights
 
     def moe_ffn(self, layer: "MoeLayer", x: np.ndarray, logits: np.ndarray | None = None):
         """MoE layer for each row of x (tokens x n_embd) -> (out, ids, weights)."""

@@ -18,8 +18,10 @@
 
 #include "../include/strata_gguf.h"
 
-// The ingest entry point links against the upload; the fuzzer never reaches it.
+// The ingest and layer entry points link against these; the fuzzer never reaches them.
 extern "C" int strata_cuda_upload_many(strata_ctx*, const strata_upload*, int64_t, strata_weight**) { return 1; }
+extern "C" int strata_cuda_moe_create(strata_ctx*, const strata_moe_desc*, strata_moe**) { return 1; }
+extern "C" int strata_cuda_free_weight(strata_weight*) { return 1; }
 namespace strata {
 int report(strata_ctx*, int code, const char*) { return code; }
 bool quant_on_device(uint32_t) { return true; }

@@ -163,3 +163,40 @@ def test_rank_slices_upload_only_their_bytes(ctx, model):
     dense.free()
     exps.free()
     assert ctx.resident_bytes() == before
+
+
+def test_moe_layer_from_a_gguf_file(ctx, tmp_path):
+    """strata_cuda_gguf_moe_layer: a layer's tensors found by name in a GGUF
+    file (load_layer, crates/strata-core/src/moe.rs:147-188), uploaded in one
+    pass, run on the device against the oracle's layer on the same bytes."""
+    n_embd, E, k, n_ff, n_ffs = 256, 8, 2, 256, 256
+    t = {"router": (sc.Q4_K, quant_matrix(7001, sc.Q4_K, E, n_embd)),
+         "gate_exps": (sc.Q4_K, quant_matrix(7002, sc.Q4_K, n_embd, n_ff, E)),
+         "up_exps": (sc.Q4_K, quant_matrix(7003, sc.Q4_K, n_embd, n_ff, E)),
+         "down_exps": (sc.Q4_K, quant_matrix(7004, sc.Q4_K, n_ff, n_embd, E)),
+         "gate_shexp": (sc.Q4_K, quant_matrix(7005, sc.Q4_K, n_ffs, n_embd)),
+         "up_shexp": (sc.Q4_K, quant_matrix(7006, sc.Q4_K, n_ffs, n_embd)),
+         "down_shexp": (sc.Q4_K, quant_matrix(7007, sc.Q4_K, n_embd, n_ffs)),
+         "gate_inp_shexp": (sc.Q4_K, quant_matrix(7008, sc.Q4_K, 1, n_embd))}
+    gguf = {"router": ("ffn_gate_inp", [n_embd, E]), "gate_exps": ("ffn_gate_exps", [n_ff, n_embd, E]),
+            "up_exps": ("ffn_up_exps", [n_ff, n_embd, E]), "down_exps": ("ffn_down_exps", [n_embd, n_ff, E]),
+            "gate_shexp": ("ffn_gate_shexp", [n_embd, n_ffs]), "up_shexp": ("ffn_up_shexp", [n_embd, n_ffs]),
+            "down_shexp": ("ffn_down_shexp", [n_ffs, n_embd]), "gate_inp_shexp": ("ffn_gate_inp_shexp", [n_embd])}
+    tensors = [(f"blk.0.{gguf[nm][0]}.weight", gguf[nm][1], q, arr.tobytes()) for nm, (q, arr) in t.items()]
+    data, _, _ = build([("general.architecture", STRING, "qwen35moe")], tensors)
+    (tmp_path / "layer.gguf").write_bytes(data)
+    before = ctx.resident_bytes()
+    with sc.GgufModel(tmp_path / "layer.gguf") as m:
+        layer, ws = ctx.gguf_moe_layer(m, 0, k)
+    assert len(ws) == 8
+    x = activations(7009, 3, n_embd)
+    logits = rng(7010).standard_normal((3, E)).astype(np.float32)
+    out, ids, w = ctx.moe_ffn(layer, x, logits)
+    want, want_ids, _ = oracle.moe_layer(t, n_embd, E, k, n_ff, n_ffs, x, logits)
+    assert np.array_equal(ids, want_ids.astype(np.int32))
+    for i in range(3):
+        assert rel_err(out[i], want[i]) < 1e-3, i
+    layer.free()
+    for wt in ws:
+        wt.free()
+    assert ctx.resident_bytes() == before
