@@ -3,7 +3,9 @@
 Each rank runs ops::gemv (the oracle) on its row shard of a Q4_K matrix and
 the shards are all-gathered: the result must equal the full product bit for
 bit, which pins the byte ranges sharding.row_shard hands to each rank. The
-expert split is checked the same way on expert_gemv.
+expert split is checked the same way on expert_gemv, and the expert-parallel
+MoE layer end to end: each rank's weighted partial sum over its experts (the
+shared expert on rank 0), all-reduced, equals the oracle's whole layer.
 """
 import multiprocessing as mp
 import os
@@ -87,3 +89,80 @@ def test_ranges_cover_without_overlap():
         pass
     else:
         raise AssertionError("uneven split accepted")
+
+
+def _ep_worker(rank, world, port, q):
+    """Expert parallelism on gloo ranks: each rank sums its experts' weighted
+    outputs (the shared expert on rank 0 only), the partial sums are
+    all-reduced, and the total must match the oracle's whole layer."""
+    try:
+        sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "strata-rs_b200"),
+                        os.path.join(os.path.dirname(HERE), "oracle")]
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        import oracle
+        import sharding
+        from synth import Q4_K, activations, quant_matrix
+        from test_moe_restatement_cpu import route, silu, sigmoid
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        n_embd, E, k, n_ff, n_ffs = 256, 8, 3, 256, 256
+        t = {"router": (Q4_K, quant_matrix(6001, Q4_K, E, n_embd)),
+             "gate_exps": (Q4_K, quant_matrix(6002, Q4_K, n_embd, n_ff, E)),
+             "up_exps": (Q4_K, quant_matrix(6003, Q4_K, n_embd, n_ff, E)),
+             "down_exps": (Q4_K, quant_matrix(6004, Q4_K, n_ff, n_embd, E)),
+             "gate_shexp": (Q4_K, quant_matrix(6005, Q4_K, n_ffs, n_embd)),
+             "up_shexp": (Q4_K, quant_matrix(6006, Q4_K, n_ffs, n_embd)),
+             "down_shexp": (Q4_K, quant_matrix(6007, Q4_K, n_embd, n_ffs)),
+             "gate_inp_shexp": (Q4_K, quant_matrix(6008, Q4_K, 1, n_embd))}
+        x = activations(6009, 2, n_embd)
+        logits = np.random.default_rng(6010).standard_normal((2, E)).astype(np.float32)
+        e0, e1 = sharding.expert_range(E, world, rank)
+        per = {nm: t[nm][1].size // E for nm in ("gate_exps", "up_exps", "down_exps")}
+        mine = {nm: t[nm][1][e0 * per[nm]:e1 * per[nm]] for nm in per}  # this rank's bytes only
+        part = np.zeros((2, n_embd), np.float32)
+        for tok in range(2):
+            ids, w = route(logits[tok], k)
+            for e, we in zip(ids, w):
+                if not e0 <= e < e1 or we == 0.0:
+                    continue
+                g = oracle.expert_gemv(Q4_K, mine["gate_exps"], e1 - e0, n_embd, n_ff, int(e) - e0, x[tok])
+                u = oracle.expert_gemv(Q4_K, mine["up_exps"], e1 - e0, n_embd, n_ff, int(e) - e0, x[tok])
+                h = (silu(g.reshape(-1)) * u.reshape(-1)).astype(np.float32)
+                d = oracle.expert_gemv(Q4_K, mine["down_exps"], e1 - e0, n_ff, n_embd, int(e) - e0, h).reshape(-1)
+                part[tok] = (part[tok] + np.float32(we) * d).astype(np.float32)
+            if rank == 0:
+                g = oracle.gemv(Q4_K, t["gate_shexp"][1], n_ffs, n_embd, x[tok]).reshape(-1)
+                u = oracle.gemv(Q4_K, t["up_shexp"][1], n_ffs, n_embd, x[tok]).reshape(-1)
+                h = (silu(g) * u).astype(np.float32)
+                d = oracle.gemv(Q4_K, t["down_shexp"][1], n_embd, n_ffs, h).reshape(-1)
+                sg = sigmoid(oracle.gemv(Q4_K, t["gate_inp_shexp"][1], 1, n_embd, x[tok]).reshape(-1))[0]
+                part[tok] = (part[tok] + sg * d).astype(np.float32)
+        total = torch.from_numpy(part.copy())
+        dist.all_reduce(total)
+        want, _, _ = oracle.moe_layer(t, n_embd, E, k, n_ff, n_ffs, x, logits)
+        from conftest import rel_err
+        for tok in range(2):
+            assert rel_err(total.numpy()[tok], want[tok]) < 1e-5, (rank, tok)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def test_expert_parallel_partial_sums_gloo_world2():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert all(m == "ok" for m in res.values()), res
