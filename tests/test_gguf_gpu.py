@@ -14,7 +14,7 @@ import oracle
 import strata_cuda as sc
 from conftest import rel_err
 from gguf_writer import STRING, U32, build
-from synth import activations, quant_blocks, rng
+from synth import activations, quant_blocks, quant_matrix, rng
 
 pytestmark = pytest.mark.gpu
 IQ2_XXS = 16  # read by the GGUF reader, not on the device path
