@@ -772,14 +772,29 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def parse_profile_case(spec: str):
+    """K,N,B[,TYPE] -> (k, n, b, quant id); TYPE is a ggml type name (default Q4_K)."""
+    import strata_cuda as sc
+    parts = spec.split(",")
+    if len(parts) not in (3, 4):
+        raise SystemExit(f"--profile-case wants K,N,B[,TYPE], got {spec!r}")
+    k, n, b = (int(v) for v in parts[:3])
+    by_name = {name: q for q, name in sc.NAMES.items()}
+    name = parts[3].strip().upper() if len(parts) == 4 else "Q4_K"
+    if name not in by_name:
+        raise SystemExit(f"--profile-case: unknown type {name!r} (one of {', '.join(sorted(by_name))})")
+    return k, n, b, by_name[name]
+
+
 def run_profile_case(args):
-    """One GEMV case (K,N,B) launched warmup + steps times on one weight copy:
-    the small, single-kernel workload the ncu captures under profiles/ use."""
+    """One GEMV case (K,N,B[,TYPE]) launched warmup + steps times on one weight
+    copy: the small, single-kernel workload the ncu captures under profiles/
+    use, and a quick look at the other block formats' GEMV."""
     import torch
     import strata_cuda as sc
-    k, n, b = (int(v) for v in args.profile_case.split(","))
+    k, n, b, quant = parse_profile_case(args.profile_case)
     ctx = sc.Context(0)
-    w = ctx.upload(quant_matrix(k + n, Q4_K, n, k), Q4_K, n, k)
+    w = ctx.upload(quant_matrix(k + n, quant, n, k), quant, n, k)
     x = torch.from_numpy(activations(900 + b, b, k)).cuda()
     y = torch.empty(b, n, device="cuda")
     s = torch.cuda.current_stream()
@@ -792,8 +807,11 @@ def run_profile_case(args):
     e1.record(s)
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / max(1, args.steps)
-    print(json.dumps({"profile_case": [k, n, b], "us_per_gemv": round(us, 2),
-                      "note": "same weights every launch (L2-warm): a profiling workload, not a bench value"}))
+    nbytes = sc.byte_size(quant, k) * n + b * k * 4 + b * n * 4
+    print(json.dumps({"profile_case": [k, n, b, sc.NAMES[quant]], "us_per_gemv": round(us, 2),
+                      "gb_per_s": round(nbytes / (us * 1e-6) / 1e9, 1),
+                      "note": "same weights every launch (L2-resident below ~126 MB): a profiling workload, "
+                              "not a bench value"}))
     w.free()
     ctx.close()
 
@@ -863,8 +881,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the per-case table")
     ap.add_argument("--skip-sections", action="store_true", help="only the GEMV sweep (no gemm / moe / sharded lines)")
-    ap.add_argument("--profile-case", default=None, metavar="K,N,B",
-                    help="launch one Q4_K GEMV case repeatedly (for ncu captures) instead of the bench")
+    ap.add_argument("--profile-case", default=None, metavar="K,N,B[,TYPE]",
+                    help="launch one GEMV case (Q4_K unless TYPE names another ggml type) repeatedly "
+                         "(for ncu captures) instead of the bench")
     ap.add_argument("--profile-gemm", default=None, metavar="QUANT,K,N,M",
                     help="launch one prefill GEMM case repeatedly (for ncu captures) instead of the bench")
     ap.add_argument("--profile-moe", default=None, metavar="T",
