@@ -249,7 +249,8 @@ struct Shard {
 // GgufFile::open + parse (reader.rs:231-352).
 bool open_shard(const std::string& path, Shard* sh, GgufError* e) {
     sh->path = path;
-    const int fd = open(path.c_str(), O_RDONLY | O_CLOEXEC);
+    // non-blocking open: a FIFO or device node is refused below instead of blocking here
+    const int fd = open(path.c_str(), O_RDONLY | O_CLOEXEC | O_NONBLOCK);
     if (fd < 0) {
         *e = io_error(path, os_error(errno));
         return false;
@@ -259,6 +260,11 @@ bool open_shard(const std::string& path, Shard* sh, GgufError* e) {
         const int err = errno;
         close(fd);
         *e = io_error(path, os_error(err));
+        return false;
+    }
+    if (!S_ISREG(st.st_mode)) {
+        close(fd);
+        *e = io_error(path, S_ISDIR(st.st_mode) ? "is a directory" : "not a regular file");
         return false;
     }
     sh->size = (uint64_t)st.st_size;

@@ -289,6 +289,12 @@ class GgufModel:
             lib().strata_cuda_gguf_close(self.h)
             self.h = None
 
+    def __del__(self):  # unmaps the shards of a model nobody closed
+        try:
+            self.close()
+        except Exception:
+            pass
+
     def __enter__(self):
         return self
 

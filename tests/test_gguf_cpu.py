@@ -163,7 +163,11 @@ def test_empty_and_missing_files(tmp_path):
     e = open_err(tmp_path / "nope.gguf")
     assert e.code == sc.ERR_IO and "No such file or directory (os error 2)" in str(e)
     e = open_err(tmp_path)
-    assert e.code == sc.ERR_IO
+    assert e.code == sc.ERR_IO and "is a directory" in str(e)
+    import os
+    os.mkfifo(tmp_path / "fifo.gguf")  # refused at once, not waited on for a writer
+    e = open_err(tmp_path / "fifo.gguf")
+    assert e.code == sc.ERR_IO and "not a regular file" in str(e)
 
 
 @pytest.mark.parametrize("version", [1, 2, 4])
