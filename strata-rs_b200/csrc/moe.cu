@@ -85,16 +85,24 @@ __device__ void route_token(const float* __restrict__ lg, int E, int k, float* s
     __syncwarp();
     // the k first experts of the order (probability desc, index asc): k rounds
     // of a warp arg-max over the experts not yet taken (lane-owned bit masks:
-    // expert i belongs to lane i % 32, bit i / 32)
+    // expert i belongs to lane i % 32, bit i / 32). `before` is the reference's
+    // comparator (partial_cmp, unwrap_or(Equal), then the index): two values of
+    // which one is NaN compare equal and fall back to the index. A NaN or +Inf
+    // logit makes the f64 sum, and so every probability, NaN; the order is then
+    // the index order and the ids are 0..k-1, as in the reference. The order is
+    // total either way, so every round takes an expert that exists.
+    auto before = [](float v, int i, float w, int j) {
+        return (v != v || w != w) ? i < j : (v > w || (v == w && i < j));
+    };
     const int kk = k < E ? k : E;
     uint32_t taken = 0;
-    int sel = 0x7FFFFFFF;  // lane j < kk ends holding the j-th chosen id
+    int sel = 0;  // lane j < kk ends holding the j-th chosen id
     for (int r = 0; r < kk; ++r) {
         float bp = -1.0f;
         int bi = 0x7FFFFFFF;
         for (int i = lane, m = 0; i < E; i += 32, ++m) {
             const float v = sp[i];
-            if (!((taken >> m) & 1u) && (v > bp || (v == bp && i < bi))) {
+            if (!((taken >> m) & 1u) && before(v, i, bp, bi)) {
                 bp = v;
                 bi = i;
             }
@@ -103,13 +111,14 @@ __device__ void route_token(const float* __restrict__ lg, int E, int k, float* s
         for (int o = 16; o > 0; o >>= 1) {
             const float op = __shfl_xor_sync(0xFFFFFFFFu, bp, o);
             const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-            if (op > bp || (op == bp && oi < bi)) {
+            if (before(op, oi, bp, bi)) {
                 bp = op;
                 bi = oi;
             }
         }
+        bi = bi < E ? bi : E - 1;  // never taken: an untaken expert always exists (kk <= E)
         if (lane == r) sel = bi;
-        if (lane == (bi & 31)) taken |= 1u << (bi >> 5);
+        if (lane == (bi & 31)) taken |= 1u << ((bi >> 5) & 31);
     }
     // ids ascending: lane q receives the chosen id of rank q
     const float psel = lane < kk ? sp[sel] : 0.0f;

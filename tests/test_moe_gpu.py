@@ -91,6 +91,35 @@ def test_moe_small_from_logits(ctx, T, qe, threads):
     free_all(ws, layer)
 
 
+def test_moe_routing_with_nan_and_inf_logits(ctx, threads):
+    """A NaN or +Inf router logit makes every probability NaN (the f64 sum is
+    NaN): the reference then picks experts 0..k-1 in index order with NaN
+    weights. The device must pick the same ids and stay inside the expert
+    array; tokens with ordinary logits route as usual."""
+    dims = dict(n_embd=512, E=64, k=8, n_ff=256, n_ff_s=256)
+    t = make_layer(1500, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"])
+    ws = upload(ctx, t, dims)
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    T = 4
+    x = activations(1501, T, dims["n_embd"])
+    logits = rng(1502).standard_normal((T, dims["E"])).astype(np.float32)
+    logits[0, 33] = np.nan
+    logits[1, 2] = np.inf
+    logits[2, :] = np.nan
+    logits[3, 7] = -np.inf
+    out, ids, w = ctx.moe_ffn(layer, x, logits)
+    want, want_ids, want_w = oracle.moe_layer(t, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                                              x, logits, threads=threads)
+    assert np.array_equal(ids.astype(np.int64), want_ids)
+    for tok in (0, 1, 2):
+        assert np.array_equal(want_ids[tok], np.arange(dims["k"]))
+        assert np.all(np.isnan(w[tok])) and np.all(np.isnan(want_w[tok]))
+        assert np.array_equal(np.isnan(out[tok]), np.isnan(want[tok]))
+    check_routing(ids[3:], w[3:], want_ids[3:], want_w[3:])
+    assert rel_err(out[3], want[3]) < TOL
+    free_all(ws, layer)
+
+
 def test_moe_router_gemv_path(ctx, threads):
     dims = dict(n_embd=512, E=32, k=4, n_ff=256, n_ff_s=256)
     t = make_layer(1100, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"])

@@ -244,3 +244,25 @@ def test_other_formats_match_independent_numpy_restatement(quant):
     got = oracle.dequantize_row(quant, blocks.reshape(-1), blocks.shape[0] * bs)
     want = numpy_dequant.DEQUANT[quant](blocks)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("bad", [np.nan, np.inf])
+def test_route_with_a_nan_or_inf_logit_falls_back_to_index_order(bad):
+    """MoeLayer::route (moe.rs:57-91) on a NaN or +Inf logit: the max-shifted
+    exp of that logit is NaN (inf - inf), so the f64 sum, the f32 reciprocal and
+    every probability are NaN; the comparator's partial_cmp then yields Equal
+    for every pair and the index decides: ids 0..k-1. Their weights are NaN
+    (NaN / max(NaN, 2^-14) = NaN / 2^-14). A -Inf logit is an ordinary zero."""
+    E, k = 64, 8
+    lg = rng(91).standard_normal((3, E)).astype(np.float32)
+    lg[0, 17] = bad
+    lg[1, :] = bad
+    lg[2, 5] = -np.inf
+    ids, w = oracle.route_logits(lg, k)
+    for t in (0, 1):
+        assert np.array_equal(ids[t], np.arange(k))
+        assert np.all(np.isnan(w[t]))
+    assert 5 not in ids[2]
+    p = np.exp((lg[2] - lg[2].max()).astype(np.float64))
+    want = np.sort(np.argsort(-p, kind="stable")[:k])
+    assert np.array_equal(ids[2], want)
