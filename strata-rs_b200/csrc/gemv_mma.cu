@@ -89,8 +89,12 @@ __device__ __forceinline__ void mma16816_z(float d[4], uint32_t a0, uint32_t a1,
 // and 2t+1, limb (n & 1) of batch (n >> 1) -- the B operand of the min MMA.
 __global__ void prep_x_limbs_kernel(const float* __restrict__ X, int64_t K, int batch, uint2* __restrict__ XF,
                                     float* __restrict__ XS, __half* __restrict__ XQ, int64_t chunk_bytes) {
-    // XF is addressed here in uint2 halves of the uint4 entries
+    // XF is addressed here in uint2 halves of the uint4 entries.
+    // Launched as a programmatic dependent of the previous kernel in the
+    // stream: x may be that kernel's output, and the workspace written below
+    // may still be read by it (a preceding GEMV), so wait for it first.
     asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // token chunk blockIdx.y: its own activation rows and workspace slice
     X += (int64_t)blockIdx.y * batch * K;
     XF = reinterpret_cast<uint2*>(reinterpret_cast<char*>(XF) + blockIdx.y * chunk_bytes);
@@ -472,6 +476,10 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
                    float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap,
                    int64_t chunk_bytes, int64_t ldy, const __grid_constant__ PeerOut po) {
+    // The next kernel in the stream may launch now: its pre-wait part only
+    // reads constant weights (a following GEMV's producer) or nothing at all,
+    // so its CTAs can fill the SMs this grid's CTAs leave while it drains.
+    asm volatile("griddepcontrol.launch_dependents;");
     // token chunk blockIdx.y (batches above 8): its limbs and its NB output rows
     XF = reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(XF) + blockIdx.y * chunk_bytes);
     XS = reinterpret_cast<const float*>(reinterpret_cast<const char*>(XS) + blockIdx.y * chunk_bytes);
@@ -802,9 +810,18 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     const int64_t xs_bytes = ((int64_t)nb * nblk * 4 + 255) / 256 * 256;
     __half* xq = reinterpret_cast<__half*>(base + xf_bytes + xs_bytes);
     const int64_t warps = (int64_t)nblk * nb;
-    if (prep)
-        prep_x_limbs_kernel<<<dim3((unsigned)((warps + 7) / 8), chunks), 256, 0, s>>>(a.X, a.K, nb, xf, xs, xq,
-                                                                                    chunk_bytes);
+    if (prep) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)((warps + 7) / 8), chunks);
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, prep_x_limbs_kernel, a.X, a.K, nb, xf, xs, xq, chunk_bytes);
+    }
     GemvArgs c = a;
     c.batch = nb;
     const bool tm = a.tmap != nullptr;
