@@ -342,9 +342,19 @@ int strata_cuda_moe_ffn_ep_dev(strata_ctx *ctx, const strata_moe *layer, const f
  * Every call shares the one array: calls that can overlap on the GPU (other
  * streams, other threads) race on it and must be serialised by the caller.
  * The scratch keeps the last call's contents; each call rewrites all of it
- * that it reads. Returns without synchronising. */
+ * that it reads. Returns without synchronising; a kernel whose bounded wait
+ * expired is reported by strata_cuda_gemv_noalloc_status. An error already
+ * pending from earlier work makes the call return STRATA_ERR_CUDA unlaunched. */
 int strata_cuda_gemv_noalloc(const uint8_t *w_dev, uint32_t quant, int64_t rows, int64_t cols,
                              const float *x_dev, float *y_dev, int batch, void *stream);
+
+/* No counterpart in the reference: the status of strata_cuda_gemv_noalloc on
+ * the current device after the work queued on `stream` (it waits for that
+ * stream). STRATA_ERR_TIMEOUT if any of its kernels since the last clear gave
+ * up a bounded wait (that call's y is incomplete), else STRATA_OK. With
+ * `clear` non-zero the recorded timeout is reset. Allocates nothing (one word
+ * is copied to the host and, when clearing, back). */
+int strata_cuda_gemv_noalloc_status(void *stream, int clear);
 
 #ifdef __cplusplus
 }

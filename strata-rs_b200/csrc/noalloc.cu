@@ -81,6 +81,32 @@ extern "C" int strata_cuda_gemv_noalloc(const uint8_t* w_dev, uint32_t quant, in
     // the tensor map is a 128-byte host struct filled in place (no allocation)
     alignas(64) unsigned char tmap[128];
     if (encode_gemv_tmap(quant, w_dev, rows, row_bytes, tmap)) a.tmap = tmap;
+    // an error left by earlier work is not this call's: report it without launching
+    if (cudaPeekAtLastError() != cudaSuccess) return STRATA_ERR_CUDA;
     launch_gemv_mma(quant, a, slot->scratch, slot->err, reinterpret_cast<cudaStream_t>(stream));
     return cudaGetLastError() == cudaSuccess ? STRATA_OK : STRATA_ERR_CUDA;
+}
+
+// The kernels of strata_cuda_gemv_noalloc set g_noalloc_err when one of their
+// bounded waits expires (their output is then incomplete). This reads it after
+// the work queued on `stream`, without allocating: a device-to-host copy of
+// one word into a local, then a wait for the stream.
+extern "C" int strata_cuda_gemv_noalloc_status(void* stream, int clear) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return STRATA_ERR_CUDA;
+    DeviceSlot* slot = nullptr;
+    int rc = setup_device(dev, &slot);
+    if (rc) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int word = 0;
+    if (cudaMemcpyAsync(&word, slot->err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return STRATA_ERR_CUDA;
+    if (clear && word) {
+        static const int zero = 0;
+        if (cudaMemcpyAsync(slot->err, &zero, sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess)
+            return STRATA_ERR_CUDA;
+    }
+    return word ? STRATA_ERR_TIMEOUT : STRATA_OK;
 }

@@ -100,6 +100,7 @@ def lib() -> C.CDLL:
             "strata_cuda_expert_gemv": (i32, [vp, vp, i64, fp, fp, i32]),
             "strata_cuda_expert_gemv_dev": (i32, [vp, vp, i64, vp, vp, i32, vp]),
             "strata_cuda_gemv_noalloc": (i32, [vp, u32, i64, i64, vp, vp, i32, vp]),
+            "strata_cuda_gemv_noalloc_status": (i32, [vp, i32]),
             "strata_cuda_gemm_bf16": (i32, [vp, vp, vp, fp, i64]),
             "strata_cuda_gemm_bf16_dev": (i32, [vp, vp, vp, vp, i64, vp]),
             "strata_cuda_gemm_f32": (i32, [vp, vp, fp, fp, i64]),

@@ -21,8 +21,15 @@ def _noalloc(w_dev, quant, rows, cols, x, y, batch, stream):
     return sc.lib().strata_cuda_gemv_noalloc(w_dev, quant, rows, cols, x, y, batch, stream)
 
 
+def _status(stream, clear):
+    return sc.lib().strata_cuda_gemv_noalloc_status(stream, clear)
+
+
+# K = 2304 and 1280 are not whole 2048-weight chunks: those rows are staged by
+# per-row bulk copies instead of the tensor map
 @pytest.mark.parametrize("quant,rows,cols,batch", [(Q4_K, 4096, 4096, 1), (Q5_K, 1000, 2048, 3),
-                                                   (Q4_K, 777, 8192, 8)])
+                                                   (Q4_K, 777, 8192, 8), (Q4_K, 300, 2304, 1),
+                                                   (Q5_K, 64, 1280, 5)])
 def test_noalloc_matches_context_entry_point(quant, rows, cols, batch):
     import torch
     data = quant_matrix(3000 + cols + batch, quant, rows, cols)
@@ -39,6 +46,9 @@ def test_noalloc_matches_context_entry_point(quant, rows, cols, batch):
             assert rc == sc.OK
             torch.cuda.synchronize()
             assert rel_err(y.cpu().numpy(), y_ref.cpu().numpy()) < TOL, (quant, call)
+        # no kernel of these calls gave up a wait; reading the status clears nothing else
+        assert _status(s.cuda_stream, 1) == sc.OK
+        assert _status(s.cuda_stream, 0) == sc.OK
         w.free()
 
 
