@@ -23,12 +23,16 @@ def pytest_configure(config):
 
 def rel_err(y: np.ndarray, ref: np.ndarray) -> float:
     """max_i |y - ref| / max(|ref_i|, 1e-3 * ||ref||_inf): the parity metric for
-    GEMV/GEMM outputs (near-zero outputs are judged against the vector's scale)."""
+    GEMV/GEMM outputs (near-zero outputs are judged against the vector's scale).
+    The floor is taken per output vector: along the last axis, so each row of a
+    batched output (one token's projection) is judged against its own norm."""
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
     if ref.size == 0:
         return 0.0
-    floor = 1e-3 * max(float(np.max(np.abs(ref))), 1e-30)
+    if ref.ndim == 0:
+        ref, y = ref.reshape(1), y.reshape(1)
+    floor = 1e-3 * np.maximum(np.max(np.abs(ref), axis=-1, keepdims=True), 1e-30)
     return float(np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor)))
 
 
