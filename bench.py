@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: Q4_K decode GEMV sweep on B200 (the reference's headline path).
 
-Workload (the BASELINE config "Q4_K decode GEMV sweep"): Q4_K weights of shapes
+Workload (the "Q4_K decode GEMV sweep" configuration): Q4_K weights of shapes
 (K -> N) 4096->4096, 4096->12288, 12288->4096 and 2048->151936, activations
 f32 N(0,1) at batch 1, 2, 4 and 8. One step = one pass over all 16
 (shape, batch) GEMVs, batch-major, so no matrix is re-read before the ~241 MB
@@ -54,12 +54,26 @@ ROOT = Path(__file__).resolve().parent
 PKG = ROOT / "strata-rs_b200"
 sys.path.insert(0, str(PKG))
 
-from synth import (Q4K_SWEEP, SWEEP_BATCHES, Q4_K, Q5_K, Q6_K, activations, bf16_bits,  # noqa: E402
+from synth import (Q4K_SWEEP, SWEEP_BATCHES, Q4_K, Q5_K, Q6_K, Q8_0, activations, bf16_bits,  # noqa: E402
                    quant_matrix, rng)
 import sharding  # noqa: E402
 
 METRIC = "Q4_K GEMV GB/s (% of HBM peak); MoE layer tokens/s at 1/2/4/8 B200"
 UNIT = "GB/s"
+
+
+DTYPE = ("f32 activations (split into two fp16 limbs, 22 significant bits, with a power-of-two scale per "
+         "256-block), Q4_K weights, fp32 accumulate")
+
+
+def sweep_config(world: int) -> dict:
+    """The workload keys both arms print (the reference arm and this one)."""
+    return {"workload": "Q4_K decode GEMV sweep: K->N 4096->4096, 4096->12288, 12288->4096, 2048->151936 at "
+                        "batch 1,2,4,8 (16 GEMVs per step, batch-major)",
+            "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 per "
+                  "matrix), no matrix re-read within 241 MB of traffic",
+            "parallelism": "single GPU" if world == 1 else f"row-sharded x{world}: output rows split across "
+                                                           f"ranks, gathered after every GEMV"}
 
 
 def gemv_bytes(k: int, n: int, b: int) -> int:
@@ -222,8 +236,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / (value * 1e9) * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32 (f64 accumulate)", "data": "synthetic",
-        "config": {"workload": "Q4_K decode GEMV sweep (K->N 4096->4096, 4096->12288, 12288->4096, 2048->151936; "
-                               "batch 1,2,4,8)", "path": "reference CPU path (oracle port of ops::gemv)"},
+        "config": sweep_config(args.gpus), "path": "reference CPU path (oracle port of ops::gemv)",
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": desc, "single_thread": serial_baseline(shapes, batches)},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -406,6 +419,49 @@ def bench_moe(ctx, torch, stream, world: int, rank: int, dist, with_e2e: bool) -
 
 
 SHARDED_SHAPES = [(8192, 28672), (28672, 8192)]  # (K, N), Q4_K
+
+
+def bench_q8_0(ctx, torch, stream, with_cpu: bool) -> dict:
+    """The Q8_0 configuration: one 4096x4096 Q8_0 matrix (fp16 d ~ U(0.002, 0.02),
+    int8 quants in [-127, 127]), f32 activation, batch 1, on rotated copies so
+    every launch reads HBM; the CPU port of ops::gemv on the same matrix beside it."""
+    k = n = 4096
+    data = quant_matrix(8080, Q8_0, n, k)
+    ws = [ctx.upload(data, Q8_0, n, k) for _ in range(max(1, -(-4 * 126 * 2**20 // data.nbytes)))]
+    x = torch.from_numpy(activations(8081, 1, k)).cuda()
+    y = torch.empty((1, n), dtype=torch.float32, device="cuda")
+    it = [0]
+
+    def fn():
+        w = ws[it[0] % len(ws)]
+        it[0] += 1
+        ctx.gemv_dev(w, x.data_ptr(), y.data_ptr(), 1, stream.cuda_stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(len(ws)):
+            fn()
+    ms = timed(torch, stream, g.replay, 20) / len(ws)
+    nbytes = data.nbytes + k * 4 + n * 4
+    hbm, peak_kind = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    out = {"k": k, "n": n, "batch": 1, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
+           "algorithmic_bytes": nbytes, "kernel": "gemv_q8_0_kernel (CUDA cores)"}
+    if with_cpu:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle
+        xv = activations(8081, 1, k)[0]
+        for threads in (1, os.cpu_count() or 1):
+            oracle.gemv_rows(Q8_0, data, n, k, xv, 0, 64, threads)
+            reps, t = 0, time.perf_counter()
+            while time.perf_counter() - t < 2.0:
+                oracle.gemv_rows(Q8_0, data, n, k, xv, 0, n, threads)
+                reps += 1
+            dt = (time.perf_counter() - t) / reps
+            out["cpu_threads_%d" % threads] = {"gbs": round(nbytes / dt / 1e9, 3), "cores": threads,
+                                               "sample": "the whole matrix, ops::gemv port (oracle)"}
+    for w in ws:
+        w.free()
+    return out
 
 
 def bench_sharded(ctx, torch, stream, world: int, rank: int, dist) -> dict:
@@ -713,7 +769,9 @@ def run_gpu(args):
                "timer": "CUDA events around pinned H2D + strata_cuda_gemv_sharded_dev + D2H, max over ranks"}
 
     # the other rows of the path (every rank takes part: their collectives run in the same order)
-    gemm = moe = sharded_proj = None
+    gemm = moe = sharded_proj = q8 = None
+    if not args.skip_sections and world == 1:
+        q8 = bench_q8_0(ctx, torch, stream, with_cpu=not args.no_cpu)
     if not args.skip_sections:
         gemm = bench_gemm(ctx, torch, stream, l2, world, rank, dist)
         moe = bench_moe(ctx, torch, stream, world, rank, dist, with_e2e=not args.no_e2e)
@@ -730,20 +788,16 @@ def run_gpu(args):
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (Q4_K weights, fp32 accumulate)",
-            "data": "synthetic (seeded PCG64; BASELINE config distributions)",
-            "config": {"workload": "Q4_K decode GEMV sweep: K->N 4096->4096, 4096->12288, 12288->4096, "
-                                   "2048->151936 at batch 1,2,4,8 (16 GEMVs per step, batch-major)",
-                       "l2": "inputs larger than L2: per step 964 MB of weights, rotated weight copies (>= 4x L2 "
-                             "per matrix), no matrix re-read within 241 MB of traffic",
-                       "parallelism": ((f"row-sharded x{world}: each GEMV writes its columns into this rank's "
-                                        f"exchange buffer; one peer all-gather kernel per step (16-byte pushes "
-                                        f"over NVLink, one signal per rank) inside the library's collective "
-                                        f"group" if peer else
-                                        f"row-sharded x{world}: local GEMV into its columns of y + in-place "
-                                        f"NCCL all-gathers inside strata_cuda_gemv_sharded_dev, the step's "
-                                        f"16 in one NCCL group") if world > 1 else "single GPU"),
-                       "launch": "CUDA graph per step" if graphs else "direct launches"},
+            "scaling": "strong", "vs_baseline": None, "dtype": DTYPE,
+            "data": "synthetic (seeded PCG64: fp16 d, dmin ~ U(0.001, 0.01), uniform random scale and quant "
+                    "bits, N(0,1) activations)",
+            "config": sweep_config(world),
+            "collective": ((f"each GEMV writes its columns into this rank's exchange buffer; one peer all-gather "
+                            f"kernel per step (16-byte pushes over NVLink, one signal per rank) inside the "
+                            f"library's collective group" if peer else
+                            f"local GEMV into its columns of y + in-place NCCL all-gathers inside "
+                            f"strata_cuda_gemv_sharded_dev, the step's 16 in one NCCL group") if world > 1 else None),
+            "launch": "CUDA graph per step" if graphs else "direct launches",
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(value / hbm, 3), "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": total // (len(batches) * len(shapes)),
@@ -759,6 +813,7 @@ def run_gpu(args):
             "gemm": gemm,
             "moe": moe,
             "sharded_projection": sharded_proj,
+            "q8_0": q8,
         }
         print(json.dumps(line), flush=True)
 

@@ -744,6 +744,475 @@ void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __h
     }
 }
 
+
+// ============================================================ tall matrices, batch 1
+//
+// A second decode kernel for batch 1 on matrices with many rows (at least four
+// 64-row items per SM, e.g. the 151936-row output projection): one CTA of 16
+// consumer warps and a producer per SM streams 64-row x 8-block stages through
+// a 3-deep ring (216 KB for Q4_K), each warp computing two m16 tiles of one
+// block per stage, so the per-stage work outside the math is paid once per two
+// tiles; the producer also adds the warps' partial sums, so no consumer ever
+// waits for another. The general kernel above serves every other case.
+namespace tall {
+
+constexpr int kGroups = 2;               // row groups of 16 per 32-row half of a stage
+constexpr int kWarps = 8 * kGroups;      // consumer warps: warp w computes block w % 8 of row group w / 8
+constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kHalfRows = 16 * kGroups;  // 32
+constexpr int kT = 2;                    // m16 tiles per warp and stage
+constexpr int kItemRows = kT * kHalfRows;  // 64 rows per stage
+constexpr int kPitch = kItemRows + 8;    // floats per block row of a reduction slot
+constexpr int kRedSlots = 4;
+__host__ __device__ constexpr int stage_bytes(uint32_t q) { return kItemRows * kChunk * block_bytes(q); }
+constexpr int kRedBytes = kRedSlots * 8 * kPitch * 4;
+__host__ __device__ constexpr int stages_for(uint32_t q) {
+    return (220 * 1024 - kRedBytes - 1024) / stage_bytes(q) > 4 ? 4 : (220 * 1024 - kRedBytes - 1024) / stage_bytes(q);
+}
+__host__ __device__ constexpr int smem_for(uint32_t q) { return stages_for(q) * stage_bytes(q) + kRedBytes + 1024; }
+
+// Per-lane selectors for the 6-bit (scale, min) pairs of sub-blocks 2t and
+// 2t + 1 (get_scale_min_k4, dequant.rs:237-245). With the 12 scale bytes as
+// words y = bytes 0-3, z = 4-7, w = 8-11 and p = t & 1:
+//   t < 2 : sc = y[2p..2p+1] & 63,                      m = z[2p..2p+1] & 63
+//   t >= 2: sc = (w & 15) | (y >> 6) << 4 (same bytes),  m = (w >> 4) | (z >> 6) << 4
+// Both pairs come out as two 16-bit integers (one per half), no branch.
+struct LaneScale {
+    uint32_t sel_lo;  // byte_perm selector: t < 2 bytes 2p, 2p+1 of the first word, else of w
+    uint32_t sel_hi;  // byte_perm selector: t < 2 zero, else bytes 2p, 2p+1 of the first word
+    uint32_t mlo;     // low-part mask: 6 bits (t < 2) or 4 bits
+    uint32_t shm;     // shift of the min's low part: 0 (t < 2) or 4
+};
+__device__ __forceinline__ LaneScale lane_scale(int t) {
+    const uint32_t p = 2u * (uint32_t)(t & 1);
+    LaneScale s;
+    if (t < 2) {
+        s.sel_lo = p | (p << 4) | ((p + 1) << 8) | ((p + 1) << 12);
+        s.sel_hi = 0x4444u;
+        s.mlo = 0x003F003Fu;
+        s.shm = 0;
+    } else {
+        s.sel_lo = (p + 4) | ((p + 4) << 4) | ((p + 5) << 8) | ((p + 5) << 12);
+        s.sel_hi = p | (4u << 4) | ((p + 1) << 8) | (4u << 12);
+        s.mlo = 0x000F000Fu;
+        s.shm = 4;
+    }
+    return s;
+}
+// (sc, m) of this lane's two sub-blocks from a block header hd (hd.y/z/w =
+// scale bytes 0-3 / 4-7 / 8-11).
+__device__ __forceinline__ void sc_m_pair(const uint4& hd, const LaneScale& ls, uint32_t& SC, uint32_t& M) {
+    const uint32_t p1 = __byte_perm(hd.y, hd.w, ls.sel_lo);
+    const uint32_t p2 = __byte_perm(hd.y, 0u, ls.sel_hi);
+    const uint32_t p3 = __byte_perm(hd.z, hd.w, ls.sel_lo);
+    const uint32_t p4 = __byte_perm(hd.z, 0u, ls.sel_hi);
+    SC = (p1 & ls.mlo) | ((p2 >> 2) & 0x00300030u);
+    M = ((p3 >> ls.shm) & ls.mlo) | ((p4 >> 2) & 0x00300030u);
+}
+// the 16-bit integer in the low / high half of v as an exact float (2^23 + v - 2^23)
+__device__ __forceinline__ float u16_lo_f(uint32_t v) {
+    return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7610)) - 8388608.0f;
+}
+__device__ __forceinline__ float u16_hi_f(uint32_t v) {
+    return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7632)) - 8388608.0f;
+}
+// two small integers (one per 16-bit half, < 1024) as an exact half2
+__device__ __forceinline__ uint32_t u16x2_h2(uint32_t v) {
+    return h2u(__hsub2(u2h(v | 0x64006400u), __float2half2_rn(1024.0f)));
+}
+
+// Shared-memory offsets of one lane's fields of one block in a stage: row r0
+// of the stage, block position `w`. Row r0 + 8 follows at 8 * ROWB, a multiple
+// of 1024 bytes (8 rows are 72 or 88 whole 128-byte lines), so the 128-byte
+// swizzle of that row is the same and its offsets are a compile-time
+// displacement from these.
+struct LaneOff {
+    uint32_t hd, qa, qb, ha, hb;
+};
+template <uint32_t Q, bool SW>
+__device__ __forceinline__ LaneOff lane_offsets(int r0, int t, int w) {
+    constexpr int BB = block_bytes(Q);
+    constexpr int ROWB = SW ? kChunk * BB : kChunk * BB + 16;
+    constexpr int QOFF = (Q == kQ4_K) ? 16 : 48;
+    auto swz = [](uint32_t o) { return SW ? (o ^ ((o >> 3) & 0x70u)) : o; };
+    const uint32_t base = (uint32_t)(r0 * ROWB + w * BB);
+    LaneOff o;
+    o.hd = swz(base);
+    o.qa = swz(base + QOFF + 32 * t);
+    o.qb = swz(base + QOFF + 32 * t + 16);
+    o.ha = swz(base + 16);
+    o.hb = swz(base + 32);
+    return o;
+}
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Batch 1, one m16 tile (the lane's rows r0 and r0 + 8) of one block: A holds
+// the raw quants as fp16 subnormals (a nibble ANDed into the low mantissa bits
+// is q * 2^-24, a high nibble 16 q * 2^-24; exact) and B is block-diagonal in
+// the sub-blocks, so D column (t, limb) is lane t's own sub-block partial sum
+// and the scales are applied in fp32 once per block. The min term
+// sum_j m_j * (sum of x over sub-block j) is one more MMA whose K slots are the
+// 8 sub-blocks: A the rows' mins, B the per-sub-block activation sums (two fp16
+// limbs; only columns 0 and 1 are non-zero).
+// acc[r] collects lane t's share of row r0 (r = 0) or r0 + 8 (r = 1).
+template <uint32_t Q, bool SW>
+__device__ __forceinline__ void unit_diag(const uint8_t* st, const LaneOff& lo, const uint4 (&bf)[8], uint32_t bq,
+                                          float xs24, float xs20, float xs, const LaneScale& ls, int t,
+                                          float (&acc)[2]) {
+    constexpr int BB = block_bytes(Q);
+    constexpr int R8 = 8 * (SW ? kChunk * BB : kChunk * BB + 16);  // 8 rows of the stage
+    (void)t;
+    uint4 qa[2], qb[2], ha[2], hb[2];
+    float fs0[2], fs1[2], fm[2];
+    uint32_t ma[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint8_t* sr = st + r * R8;
+        const uint4 hd = lds128(sr + lo.hd);
+        qa[r] = lds128(sr + lo.qa);
+        qb[r] = lds128(sr + lo.qb);
+        if constexpr (Q == kQ5_K) {
+            ha[r] = lds128(sr + lo.ha);
+            hb[r] = lds128(sr + lo.hb);
+        }
+        uint32_t SC, M;
+        sc_m_pair(hd, ls, SC, M);
+        const float d = __low2float(u2h(hd.x)), dmin = __high2float(u2h(hd.x));
+        fs0[r] = u16_lo_f(SC) * (d * xs24);
+        fs1[r] = u16_hi_f(SC) * (d * xs20);
+        fm[r] = dmin * xs;
+        ma[r] = u16x2_h2(M);
+    }
+    float dm[4], dlo[4], dhi[4];
+    mma16816_z(dm, ma[0], ma[1], 0u, 0u, bq, 0u);
+    const uint32_t kLoMask = 0x000F000Fu, kHiMask = 0x00F000F0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t a_lo0[2], a_lo1[2], a_hi0[2], a_hi1[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint32_t w = word_of(qa[r], qb[r], i);
+            const uint32_t w8 = w >> 8;
+            uint32_t lo0 = w & kLoMask, lo1 = w8 & kLoMask, hi0 = w & kHiMask, hi1 = w8 & kHiMask;
+            if constexpr (Q == kQ5_K) {
+                // qh byte l holds the 5th bit of element l of every sub-block:
+                // bit 2t for this lane's low sub-block, bit 2t+1 for the high one.
+                const uint32_t h = word_of(ha[r], hb[r], i) >> (2 * t);
+                lo0 = and_or(h << 4, 0x00100010u, lo0);
+                lo1 = and_or(h >> 4, 0x00100010u, lo1);
+                hi0 = and_or(h << 7, 0x01000100u, hi0);
+                hi1 = and_or(h >> 1, 0x01000100u, hi1);
+            }
+            a_lo0[r] = lo0;
+            a_lo1[r] = lo1;
+            a_hi0[r] = hi0;
+            a_hi1[r] = hi1;
+        }
+        if (i == 0) {
+            mma16816_z(dlo, a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[i].x, bf[i].y);
+            mma16816_z(dhi, a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[i].z, bf[i].w);
+        } else {
+            mma16816(dlo, a_lo0[0], a_lo0[1], a_lo1[0], a_lo1[1], bf[i].x, bf[i].y);
+            mma16816(dhi, a_hi0[0], a_hi0[1], a_hi1[0], a_hi1[1], bf[i].z, bf[i].w);
+        }
+    }
+    // D columns 2t (limb 0) and 2t + 1 (limb 1); rows r0 (c = 0, 1), r0 + 8 (c = 2, 3)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const float vlo = fmaf(dlo[2 * r + 1], 1.0f / 2048.0f, dlo[2 * r]);
+        const float vhi = fmaf(dhi[2 * r + 1], 1.0f / 2048.0f, dhi[2 * r]);
+        const float vm = fmaf(dm[2 * r + 1], 1.0f / 2048.0f, dm[2 * r]);
+        acc[r] = fmaf(fs0[r], vlo, fmaf(fs1[r], vhi, fmaf(-fm[r], vm, acc[r])));
+    }
+}
+
+// Bounded wait with a fast path: one try_wait (which itself may suspend the
+// thread in hardware for a while), then, only if the phase is still open, a
+// loop that sleeps between polls (suspend-time hint), gives up early once the
+// CTA has aborted and records a timeout after about a second.
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err, const volatile int* abort) {
+    const uint64_t t0 = global_ns();
+    for (long long i = 0; i < kSpinLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity), "r"(1000000u)
+            : "memory");
+        if (done) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > 1000000000ull) break;
+    }
+    if (err) atomicExch(err, 1);
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, int* err, const volatile int* abort) {
+    return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, err, abort);
+}
+
+// Persistent, warp-specialised: CTA c takes 64-row items c, c + grid, ...; an
+// item's K range is cut into stages of kChunk blocks. The producer (warp 16)
+// copies each stage with four 16-row tensor-map boxes into the ring; consumer
+// warp w computes block w % 8 of the stage for rows 16 (w / 8) + 32 u .. + 15,
+// u = 0, 1, and releases the slot. At the end of an item every consumer writes
+// its partial sums to a reduction slot; the producer, between copies, adds
+// each row's eight blocks in order and stores the rows. Every wait is bounded;
+// a timeout sets *err and the CTA stops.
+template <uint32_t Q>
+__global__ void __launch_bounds__(kThreads, 1)
+gemv_b1_tall_kernel(int N, int nblk, const uint2* __restrict__ XF, const float* __restrict__ XS,
+                    const __half* __restrict__ XQ, float* __restrict__ Y, int* __restrict__ err,
+                    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ PeerOut po) {
+    // the next kernel in the stream may launch now (its pre-wait part reads only constant weights)
+    asm volatile("griddepcontrol.launch_dependents;");
+    constexpr int NC = 2;  // (limb 0, limb 1) of the one token
+    constexpr int BB = block_bytes(Q);
+    constexpr int ROWB = kChunk * BB;  // dense, 128-byte swizzled rows
+    constexpr int HALF = kHalfRows * ROWB;
+    constexpr int STAGE = kT * HALF;
+    constexpr int kStages = stages_for(Q);
+    static_assert(kStages >= 2, "the ring needs two stages");
+    constexpr int LINES = kChunk * BB / 128;
+    constexpr int RED = 8 * kPitch;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* red = reinterpret_cast<float*>(ring + kStages * STAGE);  // [kRedSlots][8 blocks][kPitch]
+    __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages], rfull_bar[kRedSlots],
+        rempty_bar[kRedSlots];
+    __shared__ int abort_flag;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nchunks = (nblk + kChunk - 1) / kChunk;
+    const int nitems = (N + kItemRows - 1) / kItemRows;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(smem_u32(&full_bar[i]), 1);
+            mbar_init(smem_u32(&empty_bar[i]), kWarps);
+        }
+        for (int i = 0; i < kRedSlots; ++i) {
+            mbar_init(smem_u32(&rfull_bar[i]), kWarps);
+            mbar_init(smem_u32(&rempty_bar[i]), 1);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const volatile int* abortp = &abort_flag;
+
+    if (warp == kWarps) {
+        // ---------------- producer: streams the stages and reduces finished items
+        bool waited = false;  // griddepcontrol.wait done (before the first store)
+        int64_t peer_off = 0;
+        auto reduce = [&](int it, int q) -> bool {
+            if (!waited) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                const unsigned half = po.G ? (*po.epoch & 1u) : 0u;
+                peer_off = (int64_t)half * po.half_floats + po.off;
+                waited = true;
+            }
+            const int rs = q & (kRedSlots - 1), use = q / kRedSlots;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_ab(smem_u32(&rfull_bar[rs]), use & 1, err, abortp)))
+                return false;
+            const float* rr = red + rs * RED;
+            float v[kT];
+#pragma unroll
+            for (int u = 0; u < kT; ++u) {
+                float sum = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) sum += rr[w * kPitch + kHalfRows * u + lane];
+                v[u] = sum;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&rempty_bar[rs]));
+#pragma unroll
+            for (int u = 0; u < kT; ++u) {
+                const int row = it * kItemRows + kHalfRows * u + lane;
+                if (row < N) {
+                    if (po.G) po.y[peer_off + row] = v[u];
+                    else Y[row] = v[u];
+                }
+            }
+            return true;
+        };
+        int j = 0, slot = 0, par = 0;  // stages issued; ring slot and round parity of stage j
+        int rit = blockIdx.x, rq = 0, rend = nchunks;  // next item to reduce, its ordinal, stage just past it
+        bool ok = true;
+        for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+            for (int c = 0; c < nchunks; ++c) {
+                if (j >= kStages &&
+                    !__all_sync(0xFFFFFFFFu, mbar_wait_ab(smem_u32(&empty_bar[slot]), par ^ 1, err, abortp))) {
+                    abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                const uint32_t fb = smem_u32(&full_bar[slot]);
+                if (lane == 0) {
+                    // four 16-row boxes (rows past N are zero-filled)
+                    mbar_expect_tx(fb, (uint32_t)STAGE);
+#pragma unroll
+                    for (int h = 0; h < kItemRows / 16; ++h)
+                        tma_load_3d(smem_u32(ring + slot * STAGE + h * 16 * ROWB), &tmap, 0, c * LINES,
+                                    it * kItemRows + 16 * h, fb);
+                }
+                __syncwarp();
+                ++j;
+                if (++slot == kStages) {
+                    slot = 0;
+                    par ^= 1;
+                }
+                // every consumer has released stage j - 1 - kStages: the items that
+                // ended before it have their partials in place
+                while (rit < nitems && rend <= j - 1 - kStages) {
+                    if (!reduce(rit, rq)) {
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    rit += gridDim.x;
+                    ++rq;
+                    rend += nchunks;
+                }
+                if (!ok) break;
+            }
+        }
+        for (; ok && rit < nitems; rit += gridDim.x, ++rq)
+            if (!reduce(rit, rq)) {
+                abort_flag = 1;
+                ok = false;
+            }
+        // drain after an abort: wait (bounded) for the copies issued that may still be in flight
+        if (!ok)
+            for (int i = max(0, j - kStages); i < j; ++i)
+                mbar_wait(smem_u32(&full_bar[i % kStages]), (i / kStages) & 1, nullptr);
+        return;
+    }
+
+    // ---------------- consumers
+    const int g = lane >> 2, t = lane & 3;
+    const int grp = warp >> 3, wb = warp & 7;  // row group, block position in the stage
+    const LaneScale ls = lane_scale(t);
+    const LaneOff lo = lane_offsets<Q, true>(g + 16 * grp, t, wb);
+    // diagonal B: lane (g, t) holds column (g / 2, g & 1), nonzero when g / 2 == t
+    const bool active = (g >> 1) == t;
+    const uint4* xfd = reinterpret_cast<const uint4*>(XF) + (g & 1) * 4 + t;
+    const uint32_t* xq32 = reinterpret_cast<const uint32_t*>(XQ);
+    float acc[kT][2];
+#pragma unroll
+    for (int u = 0; u < kT; ++u) acc[u][0] = acc[u][1] = 0.0f;
+    // the B fragments of the warp's current block (with one chunk per row they are loaded once)
+    uint4 bf[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bf[i] = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t bq = 0u;
+    float xs = 0.0f;
+    int cur_kb = -1;
+
+    // the activation limbs come from the preceding kernel in the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    int slot = 0, par = 0;
+    int q = 0;
+    bool live = true;
+    for (int it = blockIdx.x; it < nitems && live; it += gridDim.x, ++q) {
+        for (int c = 0; c < nchunks; ++c) {
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_ab(smem_u32(&full_bar[slot]), par, err, abortp))) {
+                abort_flag = 1;
+                live = false;
+                break;
+            }
+            const int kb = c * kChunk + wb;
+            if (kb < nblk) {
+                if (kb != cur_kb) {
+                    cur_kb = kb;
+                    if (active) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) bf[i] = __ldg(xfd + (kb * 8 + i) * NC * 4);
+                    }
+                    bq = g < 2 ? __ldg(xq32 + (kb * 4 + t) * NC + g) : 0u;
+                    xs = __ldg(XS + kb);
+                }
+                const uint8_t* st = ring + slot * STAGE;
+#pragma unroll
+                for (int u = 0; u < kT; ++u)
+                    unit_diag<Q, true>(st + u * HALF, lo, bf, bq, xs * 16777216.0f, xs * 1048576.0f, xs, ls, t,
+                                       acc[u]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
+            if (++slot == kStages) {
+                slot = 0;
+                par ^= 1;
+            }
+        }
+        if (!live) break;
+        // ---- item done: this warp's partial sums into reduction slot q % kRedSlots
+        const int rs = q & (kRedSlots - 1), use = q / kRedSlots;
+        if (use >= 1 &&
+            !__all_sync(0xFFFFFFFFu, mbar_wait_ab(smem_u32(&rempty_bar[rs]), (use - 1) & 1, err, abortp))) {
+            abort_flag = 1;
+            break;
+        }
+        float* rw = red + rs * RED + wb * kPitch + 16 * grp;
+        const bool hr = (t & 1) != 0;
+#pragma unroll
+        for (int u = 0; u < kT; ++u) {
+            // sum over the four t lanes of each row: lanes t = 0, 1 end with rows g and g + 8
+            float k = hr ? acc[u][1] : acc[u][0];
+            k += __shfl_xor_sync(0xFFFFFFFFu, hr ? acc[u][0] : acc[u][1], 1);
+            k += __shfl_xor_sync(0xFFFFFFFFu, k, 2);
+            if (t < 2) rw[kHalfRows * u + 8 * t + g] = k;
+            acc[u][0] = acc[u][1] = 0.0f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&rfull_bar[rs]));
+    }
+}
+
+// Whether the tall kernel takes this batch-1 GEMV: Q4_K / Q5_K with its
+// tensor map and at least four 64-row items per SM.
+inline bool takes(uint32_t quant, const GemvArgs& a) {
+    return (quant == kQ4_K || quant == kQ5_K) && a.batch == 1 && a.tmap &&
+           (a.N + kItemRows - 1) / kItemRows >= 4ll * a.sm_count;
+}
+
+template <uint32_t Q>
+void launch(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s) {
+    constexpr int smem = smem_for(Q);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(gemv_b1_tall_kernel<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        attr_set = true;
+    }
+    const int64_t items = (a.N + kItemRows - 1) / kItemRows;
+    const int64_t grid = items < a.sm_count ? items : a.sm_count;
+    const CUtensorMap map = *reinterpret_cast<const CUtensorMap*>(a.tmap);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PeerOut po{};
+    if (a.peers) po = *a.peers;
+    cudaLaunchKernelEx(&cfg, gemv_b1_tall_kernel<Q>, (int)a.N, (int)(a.K / 256), xf, xs, xq, a.Y, err, map, po);
+}
+
+}  // namespace tall
+
 }  // namespace
 
 // The 3-D view of a Q4_K / Q5_K matrix the tensor-core GEMV copies from:
@@ -825,6 +1294,11 @@ int launch_gemv_mma(uint32_t quant, const GemvArgs& a, void* work, int* err, cud
     GemvArgs c = a;
     c.batch = nb;
     const bool tm = a.tmap != nullptr;
+    if (!full && tall::takes(quant, c)) {
+        if (quant == kQ4_K) tall::launch<kQ4_K>(c, xf, xs, xq, err, s);
+        else tall::launch<kQ5_K>(c, xf, xs, xq, err, s);
+        return 0;
+    }
     if (quant == kQ4_K) tm ? dispatch_mma<kQ4_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
                            : dispatch_mma<kQ4_K, false>(c, xf, xs, xq, err, s, chunks, chunk_bytes);
     else tm ? dispatch_mma<kQ5_K, true>(c, xf, xs, xq, err, s, chunks, chunk_bytes)
