@@ -194,6 +194,8 @@ int strata_cuda_destroy(strata_ctx* ctx) {
         if (b->ptr) cudaFreeHost(b->ptr);
     for (cudaEvent_t& e : ctx->stage_ev)
         if (e) cudaEventDestroy(e);
+    for (cudaEvent_t& e : ctx->piece_ev)
+        if (e) cudaEventDestroy(e);
     cudaEventDestroy(ctx->done);
     if (ctx->fork) cudaEventDestroy(ctx->fork);
     if (ctx->join) cudaEventDestroy(ctx->join);
@@ -484,6 +486,57 @@ int strata_cuda_dequant(strata_ctx* ctx, const strata_weight* w, int64_t expert,
 
 namespace strata {
 
+// Waits (bounded, like wait_stream) for an event already recorded.
+static int wait_event(strata_ctx* ctx, cudaEvent_t ev) {
+    auto t0 = std::chrono::steady_clock::now();
+    int spins = 0;
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return STRATA_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "device work");
+        auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if ((uint64_t)ms > ctx->wait_timeout_ms)
+            return fail(ctx, STRATA_ERR_TIMEOUT, "device work did not finish within %u ms", ctx->wait_timeout_ms);
+        if (++spins > 64) std::this_thread::yield();
+    }
+}
+
+// The result of the work queued on the context stream, `bytes` at `src_dev`,
+// into the caller's buffer: in pieces of at least 512 KiB (up to kPieces),
+// each copied device -> pinned staging -> caller, the host copy of piece k
+// overlapping the transfer of piece k + 1; returns once every byte is out.
+int copy_out(strata_ctx* ctx, void* dst, const void* src_dev, size_t bytes) {
+    constexpr size_t kMinPiece = size_t(512) << 10;
+    size_t np = (bytes + kMinPiece - 1) / kMinPiece;
+    np = np < 1 ? 1 : (np > (size_t)strata_ctx::kPieces ? (size_t)strata_ctx::kPieces : np);
+    const size_t piece = ((bytes + np - 1) / np + 255) & ~size_t(255);
+    for (size_t k = 0; k < np; ++k)
+        if (!ctx->piece_ev[k]) {
+            cudaError_t e = cudaEventCreateWithFlags(&ctx->piece_ev[k], cudaEventDisableTiming);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventCreate(result pieces)");
+        }
+    char* h = static_cast<char*>(ctx->y_host.ptr);
+    const char* d = static_cast<const char*>(src_dev);
+    size_t issued = 0;
+    for (size_t k = 0; k < np && issued < bytes; ++k) {
+        const size_t len = issued + piece < bytes ? piece : bytes - issued;
+        cudaError_t e = cudaMemcpyAsync(h + issued, d + issued, len, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(ctx->piece_ev[k], ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
+        issued += len;
+    }
+    size_t done = 0;
+    for (size_t k = 0; k < np && done < bytes; ++k) {
+        const size_t len = done + piece < bytes ? piece : bytes - done;
+        int rc = wait_event(ctx, ctx->piece_ev[k]);
+        if (rc) return rc;
+        if (k == 0 && (rc = check_device_error(ctx))) return rc;
+        ctx->copy_pool.copy(static_cast<char*>(dst) + done, h + done, len);
+        done += len;
+    }
+    return check_device_error(ctx);
+}
+
 int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                  cudaStream_t s) {
     return gemv_enqueue_strided(ctx, w, x_dev, y_dev, batch, 0, s);
@@ -552,16 +605,12 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     if ((rc = ensure_device(ctx, ctx->y_dev, yb, "cudaMalloc(y)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
-    copy_host(ctx->x_host.ptr, x, xb);
+    ctx->copy_pool.copy(ctx->x_host.ptr, x, xb);
     cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
     if ((rc = gemv_enqueue(ctx, w, (const float*)ctx->x_dev.ptr, (float*)ctx->y_dev.ptr, batch, ctx->stream)))
         return rc;
-    e = cudaMemcpyAsync(ctx->y_host.ptr, ctx->y_dev.ptr, yb, cudaMemcpyDeviceToHost, ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
-    if ((rc = wait_stream(ctx, ctx->stream))) return rc;
-    copy_host(y, ctx->y_host.ptr, yb);
-    return STRATA_OK;
+    return copy_out(ctx, y, ctx->y_dev.ptr, yb);
 }
 
 // ---- prefill GEMM

@@ -1,5 +1,6 @@
 // runtime.cuh — the host-side state behind the opaque handles of strata_cuda.h.
 #pragma once
+#include "staging.h"
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -50,6 +51,11 @@ struct strata_ctx {
     cudaStream_t aux = nullptr, aux_lo = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
     strata::PinnedBuf x_host, y_host;
+    // host-buffer calls: the result comes back in pieces, each copied out to
+    // the caller (by the pool's threads) while the next is still in transfer
+    static constexpr int kPieces = 8;
+    cudaEvent_t piece_ev[kPieces] = {};
+    strata::CopyPool copy_pool;
     // upload staging: two pinned chunks filled by host threads while the
     // other one is copied to the device (large tensors), with their events
     strata::PinnedBuf stage[2];

@@ -7,9 +7,11 @@
 // each piece then goes to its own device destination in one copy. Plain host
 // code with no CUDA types, so the arithmetic is checked on the CPU as well.
 #pragma once
+#include <condition_variable>
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -97,5 +99,96 @@ inline void copy_host(void* dst, const void* src, size_t n) {
     for (auto& x : th)
         if (x.joinable()) x.join();
 }
+
+// A host copy split over persistent worker threads: started on first use
+// and kept until the pool is destroyed, so a synchronous call that returns a
+// few MB pays no thread start-up. copy() blocks until every part is written;
+// one copy at a time (the owner serialises its calls). Copies under `kMin`
+// bytes, or when no worker can be started, are one memcpy on the caller.
+class CopyPool {
+  public:
+    static constexpr size_t kMin = size_t(256) << 10;
+    static constexpr int kWorkers = 7;
+
+    CopyPool() = default;
+    CopyPool(const CopyPool&) = delete;
+    CopyPool& operator=(const CopyPool&) = delete;
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> g(m_);
+            stop_ = true;
+        }
+        go_.notify_all();
+        for (auto& t : th_) t.join();
+    }
+
+    void copy(void* dst, const void* src, size_t n) {
+        if (n < kMin || !start()) {
+            if (n) memcpy(dst, src, n);
+            return;
+        }
+        const size_t parts = (size_t)th_.size() + 1;
+        size_t part = ((n + parts - 1) / parts + 63) & ~size_t(63);
+        {
+            std::lock_guard<std::mutex> g(m_);
+            d_ = static_cast<char*>(dst);
+            s_ = static_cast<const char*>(src);
+            n_ = n;
+            part_ = part;
+            pending_ = (int)th_.size();
+            ++gen_;
+        }
+        go_.notify_all();
+        memcpy(d_, s_, part < n ? part : n);  // the caller's part: the first
+        std::unique_lock<std::mutex> g(m_);
+        done_.wait(g, [this] { return pending_ == 0; });
+    }
+
+  private:
+    bool start() {
+        if (started_) return !th_.empty();
+        started_ = true;
+        for (int w = 0; w < kWorkers; ++w) {
+            try {
+                th_.emplace_back([this, w] { run(w + 1); });
+            } catch (...) {
+                break;
+            }
+        }
+        return !th_.empty();
+    }
+    void run(size_t idx) {
+        uint64_t seen = 0;
+        for (;;) {
+            char* d;
+            const char* s;
+            size_t n, part;
+            {
+                std::unique_lock<std::mutex> g(m_);
+                go_.wait(g, [&] { return stop_ || gen_ != seen; });
+                if (stop_) return;
+                seen = gen_;
+                d = d_;
+                s = s_;
+                n = n_;
+                part = part_;
+            }
+            const size_t a = idx * part;
+            if (a < n) memcpy(d + a, s + a, a + part < n ? part : n - a);
+            std::lock_guard<std::mutex> g(m_);
+            if (--pending_ == 0) done_.notify_one();
+        }
+    }
+
+    std::mutex m_;
+    std::condition_variable go_, done_;
+    std::vector<std::thread> th_;
+    bool started_ = false, stop_ = false;
+    uint64_t gen_ = 0;
+    int pending_ = 0;
+    char* d_ = nullptr;
+    const char* s_ = nullptr;
+    size_t n_ = 0, part_ = 0;
+};
 
 }  // namespace strata

@@ -90,9 +90,29 @@ static int check_copy(std::mt19937_64& g) {
     return 0;
 }
 
+// CopyPool: the same property over consecutive copies through one pool (the
+// workers persist between calls), including sizes under its threshold.
+static int check_pool(std::mt19937_64& g) {
+    CopyPool pool;
+    for (int i = 0; i < 40; ++i) {
+        const size_t n = i % 4 == 0 ? g() % (CopyPool::kMin + 1) : CopyPool::kMin + g() % (size_t(12) << 20);
+        const size_t so = g() % 64, dof = g() % 64;
+        std::vector<uint8_t> src(n + so), dst(n + dof + 64, 0xAB);
+        for (auto& b : src) b = (uint8_t)g();
+        pool.copy(dst.data() + dof, src.data() + so, n);
+        if (n && memcmp(dst.data() + dof, src.data() + so, n) != 0) return printf("pool.copy(%zu) differs\n", n), 1;
+        for (size_t k = 0; k < dof; ++k)
+            if (dst[k] != 0xAB) return printf("pool.copy(%zu) wrote before dst\n", n), 1;
+        for (size_t k = dof + n; k < dst.size(); ++k)
+            if (dst[k] != 0xAB) return printf("pool.copy(%zu) wrote past dst\n", n), 1;
+    }
+    return 0;
+}
+
 int main() {
     std::mt19937_64 g(20261202);
     if (check_copy(g)) return 1;
+    if (check_pool(g)) return 1;
     for (size_t cap : {size_t(1), size_t(7), size_t(64), size_t(1000), size_t(4096)})
         for (int it = 0; it < 300; ++it)
             if (check(g, cap, it % 3 == 0 ? 3 : 40)) return printf("cap %zu case %d\n", cap, it), 1;
