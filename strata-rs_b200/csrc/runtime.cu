@@ -502,11 +502,13 @@ static int wait_event(strata_ctx* ctx, cudaEvent_t ev) {
 }
 
 // The result of the work queued on the context stream, `bytes` at `src_dev`,
-// into the caller's buffer: in pieces of at least 512 KiB (up to kPieces),
+// into the caller's buffer: in pieces of at least 2 MiB (up to kPieces),
 // each copied device -> pinned staging -> caller, the host copy of piece k
 // overlapping the transfer of piece k + 1; returns once every byte is out.
+// (Each transfer has ~10-15 us of fixed latency, which smaller pieces would
+// add up to more than the overlap saves.)
 int copy_out(strata_ctx* ctx, void* dst, const void* src_dev, size_t bytes) {
-    constexpr size_t kMinPiece = size_t(512) << 10;
+    constexpr size_t kMinPiece = size_t(2) << 20;
     size_t np = (bytes + kMinPiece - 1) / kMinPiece;
     np = np < 1 ? 1 : (np > (size_t)strata_ctx::kPieces ? (size_t)strata_ctx::kPieces : np);
     const size_t piece = ((bytes + np - 1) / np + 255) & ~size_t(255);
@@ -517,6 +519,7 @@ int copy_out(strata_ctx* ctx, void* dst, const void* src_dev, size_t bytes) {
         }
     char* h = static_cast<char*>(ctx->y_host.ptr);
     const char* d = static_cast<const char*>(src_dev);
+    if (bytes >= CopyPool::kMin) ctx->copy_pool.prime();  // threads ready when the first piece lands
     size_t issued = 0;
     for (size_t k = 0; k < np && issued < bytes; ++k) {
         const size_t len = issued + piece < bytes ? piece : bytes - issued;

@@ -53,7 +53,7 @@ struct strata_ctx {
     strata::PinnedBuf x_host, y_host;
     // host-buffer calls: the result comes back in pieces, each copied out to
     // the caller (by the pool's threads) while the next is still in transfer
-    static constexpr int kPieces = 8;
+    static constexpr int kPieces = 4;
     cudaEvent_t piece_ev[kPieces] = {};
     strata::CopyPool copy_pool;
     // upload staging: two pinned chunks filled by host threads while the

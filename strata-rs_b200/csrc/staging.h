@@ -7,6 +7,7 @@
 // each piece then goes to its own device destination in one copy. Plain host
 // code with no CUDA types, so the arithmetic is checked on the CPU as well.
 #pragma once
+#include <atomic>
 #include <condition_variable>
 #include <cstddef>
 #include <cstdint>
@@ -102,13 +103,18 @@ inline void copy_host(void* dst, const void* src, size_t n) {
 
 // A host copy split over persistent worker threads: started on first use
 // and kept until the pool is destroyed, so a synchronous call that returns a
-// few MB pays no thread start-up. copy() blocks until every part is written;
-// one copy at a time (the owner serialises its calls). Copies under `kMin`
-// bytes, or when no worker can be started, are one memcpy on the caller.
+// few MB pays no thread start-up. Between copies a worker spins on the job
+// counter for a while (about 100 us) and then sleeps on a condition variable;
+// prime() wakes sleeping workers into that spin ahead of a copy whose data is
+// still in flight, so the copy does not wait for threads to wake. copy() blocks until
+// every part is written; one copy at a time (the owner serialises its calls).
+// Copies under `kMin` bytes, or when no worker can be started, are one memcpy
+// on the caller.
 class CopyPool {
   public:
     static constexpr size_t kMin = size_t(256) << 10;
     static constexpr int kWorkers = 7;
+    static constexpr int kSpin = 1 << 17;  // polls before a worker sleeps
 
     CopyPool() = default;
     CopyPool(const CopyPool&) = delete;
@@ -116,10 +122,21 @@ class CopyPool {
     ~CopyPool() {
         {
             std::lock_guard<std::mutex> g(m_);
-            stop_ = true;
+            stop_.store(true);
         }
         go_.notify_all();
         for (auto& t : th_) t.join();
+    }
+
+    // Wakes the workers (starting them on first use) so they spin, ready for
+    // a copy of at least kMin bytes that is about to come.
+    void prime() {
+        if (!start()) return;
+        {
+            std::lock_guard<std::mutex> g(m_);
+            wake_.fetch_add(1);
+        }
+        go_.notify_all();
     }
 
     void copy(void* dst, const void* src, size_t n) {
@@ -128,20 +145,19 @@ class CopyPool {
             return;
         }
         const size_t parts = (size_t)th_.size() + 1;
-        size_t part = ((n + parts - 1) / parts + 63) & ~size_t(63);
+        const size_t part = ((n + parts - 1) / parts + 63) & ~size_t(63);
         {
             std::lock_guard<std::mutex> g(m_);
             d_ = static_cast<char*>(dst);
             s_ = static_cast<const char*>(src);
             n_ = n;
             part_ = part;
-            pending_ = (int)th_.size();
-            ++gen_;
+            pending_.store((int)th_.size());
+            gen_.fetch_add(1);
         }
         go_.notify_all();
         memcpy(d_, s_, part < n ? part : n);  // the caller's part: the first
-        std::unique_lock<std::mutex> g(m_);
-        done_.wait(g, [this] { return pending_ == 0; });
+        while (pending_.load() != 0) std::this_thread::yield();
     }
 
   private:
@@ -158,16 +174,20 @@ class CopyPool {
         return !th_.empty();
     }
     void run(size_t idx) {
-        uint64_t seen = 0;
+        uint64_t seen = 0, woken = 0;
         for (;;) {
+            int spin = 0;
+            while (gen_.load() == seen && !stop_.load() && spin < kSpin) ++spin;
             char* d;
             const char* s;
             size_t n, part;
             {
                 std::unique_lock<std::mutex> g(m_);
-                go_.wait(g, [&] { return stop_ || gen_ != seen; });
-                if (stop_) return;
-                seen = gen_;
+                go_.wait(g, [&] { return stop_.load() || gen_.load() != seen || wake_.load() != woken; });
+                if (stop_.load()) return;
+                woken = wake_.load();
+                if (gen_.load() == seen) continue;  // primed: spin for the coming copy
+                seen = gen_.load();
                 d = d_;
                 s = s_;
                 n = n_;
@@ -175,17 +195,17 @@ class CopyPool {
             }
             const size_t a = idx * part;
             if (a < n) memcpy(d + a, s + a, a + part < n ? part : n - a);
-            std::lock_guard<std::mutex> g(m_);
-            if (--pending_ == 0) done_.notify_one();
+            pending_.fetch_sub(1);
         }
     }
 
     std::mutex m_;
-    std::condition_variable go_, done_;
+    std::condition_variable go_;
     std::vector<std::thread> th_;
-    bool started_ = false, stop_ = false;
-    uint64_t gen_ = 0;
-    int pending_ = 0;
+    bool started_ = false;
+    std::atomic<bool> stop_{false};
+    std::atomic<uint64_t> gen_{0}, wake_{0};
+    std::atomic<int> pending_{0};
     char* d_ = nullptr;
     const char* s_ = nullptr;
     size_t n_ = 0, part_ = 0;

@@ -99,6 +99,7 @@ static int check_pool(std::mt19937_64& g) {
         const size_t so = g() % 64, dof = g() % 64;
         std::vector<uint8_t> src(n + so), dst(n + dof + 64, 0xAB);
         for (auto& b : src) b = (uint8_t)g();
+        if (i % 3 == 0) pool.prime();
         pool.copy(dst.data() + dof, src.data() + so, n);
         if (n && memcmp(dst.data() + dof, src.data() + so, n) != 0) return printf("pool.copy(%zu) differs\n", n), 1;
         for (size_t k = 0; k < dof; ++k)
