@@ -200,6 +200,35 @@ def test_moe_expert_parallel_partials_sum(ctx, G):
     free_all(ws, full)
 
 
+@pytest.mark.parametrize("q", [Q4_K, Q5_K])
+@pytest.mark.parametrize("G", [1, 2, 4])
+def test_moe_one_token_layer(ctx, q, G, threads):
+    """One token (the decode chain: routing with assignment, the few-token
+    gate/up and down passes, the combine) with every expert and shared tensor
+    Q4_K or every one Q5_K, 64 experts, top-8: the output against the oracle's
+    layer and, over expert slices (G > 1, the shared expert in the first), the
+    partial outputs summing to it; routing identical on every slice, on two
+    calls in a row."""
+    dims = dict(n_embd=1024, E=64, k=8, n_ff=512, n_ff_s=256)
+    t = make_layer(1700 + q, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"], qe=q, qs=q, router=False)
+    x = activations(1701, 1, dims["n_embd"])
+    logits = rng(1702 + G).standard_normal((1, dims["E"])).astype(np.float32)
+    want, want_ids, want_w = oracle.moe_layer(t, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                                              x, logits, threads=threads)
+    total = np.zeros_like(want)
+    per = dims["E"] // G
+    for r in range(G):
+        ws = upload(ctx, t, dims, e0=r * per, e1=(r + 1) * per)
+        layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"],
+                               expert_begin=r * per, expert_end=(r + 1) * per, with_shared=(r == 0))
+        for call in range(2):
+            part, ids, w = ctx.moe_ffn(layer, x, logits)
+            check_routing(ids, w, want_ids, want_w)
+        total += part
+        free_all(ws, layer)
+    assert rel_err(total[0], want[0]) < TOL, rel_err(total[0], want[0])
+
+
 def test_moe_dev_entry_on_torch_stream(ctx):
     torch = pytest.importorskip("torch")
     dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
