@@ -223,11 +223,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 
 constexpr int kStages = 2;  // smem ring depth
 constexpr int kChunk = 8;   // K blocks per stage (whole 128-byte lines for the tensor map)
-// Consumer warps per CTA by batch: four warps of two blocks per stage up to
-// batch 4 (three CTAs per SM), eight warps of one block from batch 5 (two CTAs
-// per SM, the registers of the larger accumulators).
-__host__ __device__ constexpr int consumers_for(int nb) { return nb >= 5 ? 8 : 4; }
-__host__ __device__ constexpr int min_ctas_for(int nb) { return nb >= 5 ? 2 : 3; }
+// Consumer warps per CTA: four warps of two blocks per stage (three CTAs per
+// SM) or eight warps of one block (two CTAs per SM). From batch 5 always eight
+// (the registers of the larger accumulators); up to batch 4 eight when that
+// takes no more rounds of tiles over the resident CTAs than four: a CTA then
+// spends half the time on each stage, which is what bounds matrices of few
+// tiles (their time does not change when the weights are L2-resident).
+__host__ __device__ constexpr int min_ctas_for_consumers(int c) { return c == 8 ? 2 : 3; }
 constexpr int kTileRows = 16;
 
 // One (16-row tile, K block) work item of a consumer warp: rows g and g+8 of
@@ -470,8 +472,8 @@ __device__ __forceinline__ void mma_blocks_diag(const uint8_t* stage, const uint
 // kBpw - 1 of each stage and releases the slot through its `empty` mbarrier. Consumers keep their
 // partial sums across a tile's stages and combine them in shared memory when
 // the tile ends. Every wait is bounded; a timeout sets *err and the CTA stops.
-template <uint32_t Q, int NB, bool TM>
-__global__ void __launch_bounds__((consumers_for(NB) + 1) * 32, min_ctas_for(NB))
+template <uint32_t Q, int NB, bool TM, int NCONS>
+__global__ void __launch_bounds__((NCONS + 1) * 32, min_ctas_for_consumers(NCONS))
 gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
                    const uint2* __restrict__ XF, const float* __restrict__ XS, const __half* __restrict__ XQ,
                    float* __restrict__ Y, int* __restrict__ err, const __grid_constant__ CUtensorMap tmap,
@@ -487,7 +489,8 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     Y += (int64_t)blockIdx.y * NB * ldy;
     constexpr int NC = 2 * NB, NT = (NC + 7) / 8;
     constexpr int BB = block_bytes(Q);
-    constexpr int kConsumers = consumers_for(NB), kBpw = kChunk / kConsumers;
+    constexpr int kConsumers = NCONS, kBpw = kChunk / kConsumers;
+    static_assert(NCONS == 8 || (NCONS == 4 && NB <= 4), "four consumer warps serve batches up to 4");
     // smem stride of one row of a stage. TM (one tensor-map copy per stage):
     // the rows are dense and 128-byte swizzled, which puts consecutive rows'
     // units on different banks. Otherwise (one bulk copy per row): each row is
@@ -521,6 +524,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     if (warp == kConsumers) {
         // ---------------- producer: the weights do not depend on the prologue
         // (abort decisions are made warp-uniform: the loop has __syncwarp)
+        int issued = 0;  // stages whose copies were issued
         for (int j = 0; j < nstages; ++j) {
             const int slot = j % kStages;
             bool ok = true;
@@ -552,9 +556,11 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                     bulk_g2s(smem_u32(ring + slot * STAGE + lane * ROWB), src, bytes, fb);
                 }
             }
+            issued = j + 1;
         }
-        // drain: wait (bounded) for the copies still in flight before exiting
-        for (int j = max(0, nstages - kStages); j < nstages; ++j)
+        // drain: wait (bounded) for the copies of the last stages issued, which
+        // may still be in flight (after an abort, stages never issued are not waited on)
+        for (int j = max(0, issued - kStages); j < issued; ++j)
             mbar_wait(smem_u32(&full_bar[j % kStages]), (j / kStages) & 1, nullptr);
         return;
     }
@@ -695,27 +701,39 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
 }
 
 template <uint32_t Q, int NB, bool TM>
+constexpr int tma_smem_bytes() {
+    return kStages * kTileRows * (kChunk * block_bytes(Q) + (TM ? 0 : 16)) + 1024;
+}
+
+// Resident CTAs per SM of one instantiation (computed once).
+template <uint32_t Q, int NB, bool TM, int NCONS>
+int tma_ctas_per_sm() {
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        constexpr int smem = tma_smem_bytes<Q, NB, TM>();
+        cudaFuncSetAttribute(gemv_kq_tma_kernel<Q, NB, TM, NCONS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kq_tma_kernel<Q, NB, TM, NCONS>, (NCONS + 1) * 32,
+                                                      smem);
+        per_sm = n < 1 ? 1 : n;
+    }
+    return per_sm;
+}
+
+template <uint32_t Q, int NB, bool TM, int NCONS>
 void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
-                   unsigned chunks = 1, int64_t chunk_bytes = 0) {
+                unsigned chunks, int64_t chunk_bytes) {
     const int nblk = (int)(a.K / 256);
     const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
-    const int smem = kStages * kTileRows * (kChunk * block_bytes(Q) + (TM ? 0 : 16)) + 1024;
-    static int per_sm = 0;  // resident CTAs per SM, per instantiation
-    if (per_sm == 0) {
-        cudaFuncSetAttribute(gemv_kq_tma_kernel<Q, NB, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_tma_kernel<Q, NB, TM>, (consumers_for(NB) + 1) * 32,
-                                                      smem);
-        if (per_sm < 1) per_sm = 1;
-    }
     CUtensorMap map;
     if (TM) map = *reinterpret_cast<const CUtensorMap*>(a.tmap);
     else memset(&map, 0, sizeof(map));
-    int64_t grid = (int64_t)a.sm_count * per_sm;
+    int64_t grid = (int64_t)a.sm_count * tma_ctas_per_sm<Q, NB, TM, NCONS>();
     if (grid > ntiles) grid = ntiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid, chunks);
-    cfg.blockDim = dim3((consumers_for(NB) + 1) * 32);
-    cfg.dynamicSmemBytes = smem;
+    cfg.blockDim = dim3((NCONS + 1) * 32);
+    cfg.dynamicSmemBytes = tma_smem_bytes<Q, NB, TM>();
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -724,23 +742,40 @@ void launch_tma(const GemvArgs& a, const uint2* xf, const float* xs, const __hal
     cfg.numAttrs = 1;
     PeerOut po{};
     if (a.peers) po = *a.peers;
-    cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y, err,
-                       map, chunk_bytes, ldy_of(a), po);
+    cudaLaunchKernelEx(&cfg, gemv_kq_tma_kernel<Q, NB, TM, NCONS>, a.W, a.row_bytes, (int)a.N, nblk, xf, xs, xq, a.Y,
+                       err, map, chunk_bytes, ldy_of(a), po);
+}
+
+// Four or eight consumer warps (see min_ctas_for_consumers).
+template <uint32_t Q, int NB, bool TM>
+void launch_general(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
+                    unsigned chunks = 1, int64_t chunk_bytes = 0) {
+    if constexpr (NB >= 5) {
+        launch_tma<Q, NB, TM, 8>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
+    } else {
+        const int64_t ntiles = (a.N + kTileRows - 1) / kTileRows;
+        const int64_t cap4 = (int64_t)a.sm_count * tma_ctas_per_sm<Q, NB, TM, 4>();
+        const int64_t cap8 = (int64_t)a.sm_count * tma_ctas_per_sm<Q, NB, TM, 8>();
+        if ((ntiles + cap8 - 1) / cap8 <= (ntiles + cap4 - 1) / cap4)
+            launch_tma<Q, NB, TM, 8>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
+        else
+            launch_tma<Q, NB, TM, 4>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
+    }
 }
 
 template <uint32_t Q, bool TM>
 void dispatch_mma(const GemvArgs& a, const uint2* xf, const float* xs, const __half* xq, int* err, cudaStream_t s,
                   unsigned chunks = 1, int64_t chunk_bytes = 0) {
-    if (chunks > 1) return launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
+    if (chunks > 1) return launch_general<Q, 8, TM>(a, xf, xs, xq, err, s, chunks, chunk_bytes);
     switch (a.batch) {
-    case 1: return launch_tma<Q, 1, TM>(a, xf, xs, xq, err, s);
-    case 2: return launch_tma<Q, 2, TM>(a, xf, xs, xq, err, s);
-    case 3: return launch_tma<Q, 3, TM>(a, xf, xs, xq, err, s);
-    case 4: return launch_tma<Q, 4, TM>(a, xf, xs, xq, err, s);
-    case 5: return launch_tma<Q, 5, TM>(a, xf, xs, xq, err, s);
-    case 6: return launch_tma<Q, 6, TM>(a, xf, xs, xq, err, s);
-    case 7: return launch_tma<Q, 7, TM>(a, xf, xs, xq, err, s);
-    default: return launch_tma<Q, 8, TM>(a, xf, xs, xq, err, s);
+    case 1: return launch_general<Q, 1, TM>(a, xf, xs, xq, err, s);
+    case 2: return launch_general<Q, 2, TM>(a, xf, xs, xq, err, s);
+    case 3: return launch_general<Q, 3, TM>(a, xf, xs, xq, err, s);
+    case 4: return launch_general<Q, 4, TM>(a, xf, xs, xq, err, s);
+    case 5: return launch_general<Q, 5, TM>(a, xf, xs, xq, err, s);
+    case 6: return launch_general<Q, 6, TM>(a, xf, xs, xq, err, s);
+    case 7: return launch_general<Q, 7, TM>(a, xf, xs, xq, err, s);
+    default: return launch_general<Q, 8, TM>(a, xf, xs, xq, err, s);
     }
 }
 
