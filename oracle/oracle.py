@@ -58,6 +58,8 @@ def lib() -> C.CDLL:
             "orc_softmax": (None, [fp, i64]),
             "orc_rope_neox": (None, [fp, i64, i64, i64, i64, C.c_double]),
             "orc_add": (None, [fp, fp, i64]),
+            "orc_expf_misrounded": (i64, [C.c_float, C.c_float, fp, i64]),
+            "orc_expf_tie_pairs": (i64, [C.c_float, C.c_float, fp, i64]),
         }
         for name, (res, args) in sigs.items():
             f = getattr(L, name)
@@ -172,6 +174,22 @@ def add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     bb = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
     lib().orc_add(_fp(out), _fp(bb), out.size)
     return out.reshape(np.shape(a))
+
+
+def expf_misrounded(lo: float, hi: float, cap: int) -> np.ndarray:
+    """Inputs in [lo, hi] where the C library's expf (the reference's f32::exp)
+    is not the correctly rounded exp (test support)."""
+    out = np.empty(cap, np.float32)
+    n = lib().orc_expf_misrounded(lo, hi, _fp(out), cap)
+    return out[:n].copy()
+
+
+def expf_tie_pairs(lo: float, hi: float, cap: int) -> np.ndarray:
+    """[n, 2] pairs x1 < x2 a few floats apart where expf ties and the
+    correctly rounded exp does not (test support)."""
+    out = np.empty((cap, 2), np.float32)
+    n = lib().orc_expf_tie_pairs(lo, hi, _fp(out), cap)
+    return out[:n].copy()
 
 
 def route_logits(logits: np.ndarray, top_k: int) -> tuple[np.ndarray, np.ndarray]:

@@ -760,3 +760,60 @@ void orc_rope_neox(float *head, int64_t len, int64_t pos, int64_t n_rot, int64_t
 void orc_add(float *out, const float *a, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] += a[i];
 }
+
+/* ---- test support (not a restatement): where the C library's expf, which
+ * the reference's f32::exp is, is not correctly rounded. The correctly
+ * rounded value is the x87 long double expl (64-bit significand) rounded to
+ * f32. Inputs are scanned upward from lo to hi (both finite, lo <= hi, same
+ * sign). */
+static uint32_t orc_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static float orc_float(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static float orc_expf_cr(float x) { return (float)expl((long double)x); }
+static float orc_next_up(float x) {
+    const uint32_t u = orc_bits(x);
+    if (x == 0.0f) return orc_float(1u);
+    return orc_float(x > 0.0f ? u + 1u : u - 1u);
+}
+
+/* Inputs x in [lo, hi] where expf(x) differs from the correctly rounded value;
+ * at most cap of them into out. Returns the number written. */
+int64_t orc_expf_misrounded(float lo, float hi, float *out, int64_t cap) {
+    int64_t n = 0;
+    for (float x = lo; x <= hi && n < cap; x = orc_next_up(x))
+        if (orc_bits(expf(x)) != orc_bits(orc_expf_cr(x))) out[n++] = x;
+    return n;
+}
+
+/* Pairs x1 < x2 in [lo, hi], at most 4 floats apart, where expf(x1) ==
+ * expf(x2) but the correctly rounded values differ (so an ordering by the
+ * correctly rounded exp separates what expf ties); at most cap pairs into
+ * out[2 i], out[2 i + 1]. Returns the number of pairs written. */
+int64_t orc_expf_tie_pairs(float lo, float hi, float *out, int64_t cap) {
+    int64_t n = 0;
+    for (float x = lo; x <= hi && n < cap; x = orc_next_up(x)) {
+        if (orc_bits(expf(x)) == orc_bits(orc_expf_cr(x))) continue;  /* one of the pair is misrounded */
+        /* neighbours on both sides */
+        float y = x;
+        for (int s = 1; s <= 4; ++s) {
+            y = orc_next_up(y);
+            if (orc_bits(expf(y)) == orc_bits(expf(x)) && orc_bits(orc_expf_cr(y)) != orc_bits(orc_expf_cr(x))) {
+                out[2 * n] = x;
+                out[2 * n + 1] = y;
+                if (++n >= cap) return n;
+                break;
+            }
+        }
+        float w = x;
+        for (int s = 1; s <= 4 && n < cap; ++s) {
+            const uint32_t u = orc_bits(w);
+            w = orc_float(x > 0.0f ? u - 1u : u + 1u);  /* next down */
+            if (orc_bits(expf(w)) == orc_bits(expf(x)) && orc_bits(orc_expf_cr(w)) != orc_bits(orc_expf_cr(x))) {
+                out[2 * n] = w;
+                out[2 * n + 1] = x;
+                ++n;
+                break;
+            }
+        }
+    }
+    return n;
+}

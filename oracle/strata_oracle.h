@@ -82,6 +82,10 @@ void orc_softmax(float *xs, int64_t n);
 void orc_rope_neox(float *head, int64_t len, int64_t pos, int64_t n_rot, int64_t head_dim, double freq_base);
 void orc_add(float *out, const float *a, int64_t n);
 
+/* test support: inputs where the C library's expf is not correctly rounded */
+int64_t orc_expf_misrounded(float lo, float hi, float *out, int64_t cap);
+int64_t orc_expf_tie_pairs(float lo, float hi, float *out, int64_t cap);
+
 /* MoeLayer::route from the router logits on (crates/strata-core/src/moe.rs:57-91):
  * softmax (max-shift, f64 sum, f32 inv), stable top-k, ids ascending,
  * renormalised with a 2^-14 floor. logits is overwritten with the probs. */

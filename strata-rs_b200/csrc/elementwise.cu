@@ -18,6 +18,7 @@
 #include <cmath>
 #include <cstring>
 
+#include "expf_libm.cuh"
 #include "runtime.cuh"
 
 namespace strata {
@@ -81,7 +82,7 @@ __global__ void __launch_bounds__(kEwThreads) softmax_kernel(float* __restrict__
     mx = block_max(mx, shf);
     double sum = 0.0;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const float e = (float)exp((double)(row[i] - mx));
+        const float e = expf_libm(row[i] - mx);  // f32::exp, as the C library rounds it
         row[i] = e;
         sum += (double)e;
     }

@@ -22,6 +22,7 @@
 
 #include <cmath>
 
+#include "expf_libm.cuh"
 #include "kernels.cuh"
 #include "moe.cuh"
 #include "quant.cuh"
@@ -32,7 +33,9 @@ namespace {
 constexpr int kMoeThreads = 256;
 
 // f32 exp rounded from a double exp (correctly rounded except within about
-// 2^-29 ulp of a rounding boundary), standing in for Rust's f32::exp.
+// 2^-29 ulp of a rounding boundary), standing in for Rust's f32::exp in silu
+// and sigmoid (whose results the 1e-3 output bound covers); the router's
+// softmax uses expf_libm, the C library's expf bit for bit.
 __device__ __forceinline__ float exp_f32(float x) { return (float)exp((double)x); }
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + exp_f32(-x)); }      // ops.rs:85-87
 __device__ __forceinline__ float sigmoid_f32(float x) { return 1.0f / (1.0f + exp_f32(-x)); }  // ops.rs:90-92
@@ -74,7 +77,7 @@ __device__ void route_token(const float* __restrict__ lg, int E, int k, float* s
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
     double sum = 0.0;
     for (int i = lane; i < E; i += 32) {
-        const float e = exp_f32(lg[i] - mx);
+        const float e = expf_libm(lg[i] - mx);
         sp[i] = e;
         sum += (double)e;
     }

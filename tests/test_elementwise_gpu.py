@@ -6,9 +6,11 @@ ComputeBackend::rms_norm / l2_norm / softmax / rope_neox / add
 keep the reference's f64 arithmetic, so the f32 results are expected to be
 the same bits, except where a CTA-order f64 sum or a libm-vs-CUDA f64
 function lands within 1e-16 of an f32 rounding boundary: at most one ulp,
-and rare. softmax's f32 exp is the f64 exp rounded to f32 on the device and
-glibc's expf in the oracle (as in the reference), which differ by an ulp now
-and then; with the division that makes at most two. `add` is exact.
+and rare. softmax's f32 exp is the C library's expf bit for bit on the max-shifted
+domain (expf_libm, checked on every float of it at build time), so softmax
+differs only where the device's CTA-order f64 sum does: at most two ulps with
+the division; rows whose sum is exact in any order are the same bits. `add`
+is exact.
 """
 import numpy as np
 import pytest
@@ -71,6 +73,22 @@ def test_rms_norm_and_l2_norm(ctx, n):
 def test_softmax(ctx, n):
     x = (rng(200 + n).standard_normal(n) * 4).astype(np.float32)
     assert_close(ctx.softmax(x), oracle.softmax(x, n), ("softmax", n), max_ulps=2)
+
+
+def test_softmax_exp_is_the_c_librarys_expf(ctx):
+    """f32::exp is the C library's expf, which is not correctly rounded: the
+    device matches it bit for bit (expf_libm). Rows of one 0 (the maximum, so
+    the exp arguments are the values themselves) and 255 inputs where expf
+    differs from the correctly rounded exp, all in [-8, 0]: every exp is then
+    above 3.4e-4, so the f64 sum of the row is exact in any order and the
+    outputs must be the same bits."""
+    m = oracle.expf_misrounded(-8.0, -0.25, 8 * 255)
+    assert m.size == 8 * 255
+    x = np.zeros((8, 256), np.float32)
+    x[:, 1:] = rng(250).permutation(m).reshape(8, 255)
+    got = np.stack([ctx.softmax(r) for r in x])
+    want = oracle.softmax(x, 256)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), int(ulps(got, want).max())
 
 
 @pytest.mark.parametrize("head_dim,n_rot,pos,base", [(128, 128, 1234, 1e6), (128, 64, 7, 1e4), (64, 64, 0, 1e7),

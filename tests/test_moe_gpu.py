@@ -5,6 +5,8 @@ routing from given logits is compared exactly (ids) and to the bit or one
 ulp (weights); the layer output within rel_err 1e-3 (fp32 accumulation
 against the reference's f32/f64 mix).
 """
+import math
+
 import numpy as np
 import pytest
 
@@ -117,6 +119,49 @@ def test_moe_routing_with_nan_and_inf_logits(ctx, threads):
         assert np.array_equal(np.isnan(out[tok]), np.isnan(want[tok]))
     check_routing(ids[3:], w[3:], want_ids[3:], want_w[3:])
     assert rel_err(out[3], want[3]) < TOL
+    free_all(ws, layer)
+
+
+def test_moe_routing_exp_is_the_c_librarys_expf(ctx, threads):
+    """The router's f32::exp is the C library's expf, not the correctly
+    rounded exp (they differ on about 1 in 11,500 inputs of the max-shifted
+    domain). (a) Logit rows of one 0 and 63 inputs where expf is misrounded,
+    all in [-8, 0] so the f64 sums are exact in any order: ids and weights are
+    the oracle's bits. (b) The top-k boundary: experts 3 and 9 get two logits
+    a few floats apart on which expf ties but the correctly rounded exp does
+    not; the reference's tie goes to the lower index (expert 3), a correctly
+    rounded exp would take expert 9. The device must take expert 3."""
+    dims = dict(n_embd=512, E=64, k=8, n_ff=256, n_ff_s=256)
+    t = make_layer(1600, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"])
+    ws = upload(ctx, t, dims)
+    layer = ctx.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    T = 16
+    m = oracle.expf_misrounded(-8.0, -0.25, T * 63)
+    assert m.size == T * 63
+    logits = np.zeros((T, dims["E"]), np.float32)
+    logits[:, 1:] = rng(1601).permutation(m).reshape(T, 63)
+    x = activations(1602, T, dims["n_embd"])
+    _, ids, w = ctx.moe_ffn(layer, x, logits)
+    want_ids, want_w = oracle.route_logits(logits, dims["k"])
+    assert np.array_equal(ids.astype(np.int64), want_ids)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+
+    pairs = oracle.expf_tie_pairs(-2.0, -0.25, T)
+    assert len(pairs) == T
+    k = 4
+    logits = np.full((T, dims["E"]), -3.0, np.float32)
+    logits[:, 0], logits[:, 1], logits[:, 2] = 0.0, -0.01, -0.02   # the first three picks
+    logits[:, 3], logits[:, 9] = pairs[:, 0], pairs[:, 1]           # x1 < x2: expf(x1) == expf(x2)
+    layer4 = ctx.moe_create(ws, dims["n_embd"], dims["E"], k, dims["n_ff"], dims["n_ff_s"])
+    _, ids, w = ctx.moe_ffn(layer4, x, logits)
+    want_ids, want_w = oracle.route_logits(logits, k)
+    assert np.array_equal(want_ids, np.tile([0, 1, 2, 3], (T, 1)))  # the tie to the lower index
+    # a correctly rounded exp separates the pair: expert 9 would come fourth
+    cr = np.float32([[math.exp(float(v)) for v in row] for row in logits])
+    assert np.all(cr[:, 9] > cr[:, 3])
+    assert np.array_equal(ids.astype(np.int64), want_ids)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+    layer4.free()
     free_all(ws, layer)
 
 

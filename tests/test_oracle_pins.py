@@ -266,3 +266,28 @@ def test_route_with_a_nan_or_inf_logit_falls_back_to_index_order(bad):
     p = np.exp((lg[2] - lg[2].max()).astype(np.float64))
     want = np.sort(np.argsort(-p, kind="stable")[:k])
     assert np.array_equal(ids[2], want)
+
+
+def test_expf_helpers_find_where_the_c_library_is_not_correctly_rounded():
+    """The reference's f32::exp is the C library's expf, which misrounds a few
+    inputs (its error bound is 0.502 ulp). The test-support scans return
+    inputs where expf differs from the correctly rounded exp (the double exp
+    rounded to f32: the two agree on every float of [-104, 0]), and pairs a few
+    floats apart that expf ties and the correctly rounded exp separates."""
+    import ctypes
+    import math
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.restype, libm.expf.argtypes = ctypes.c_float, [ctypes.c_float]
+
+    def expf(v):
+        return np.float32(libm.expf(float(v)))
+
+    m = oracle.expf_misrounded(-1.0, -0.5, 10**6)
+    assert 100 < m.size < 10**5
+    for v in m[:: max(1, m.size // 200)]:
+        assert expf(v) != np.float32(math.exp(float(v))), v
+    pairs = oracle.expf_tie_pairs(-1.0, -0.5, 32)
+    assert len(pairs) == 32
+    for a, b in pairs:
+        assert a < b and expf(a) == expf(b)
+        assert np.float32(math.exp(float(a))) < np.float32(math.exp(float(b)))
