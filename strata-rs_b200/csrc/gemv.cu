@@ -299,97 +299,6 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, in
     }
 }
 
-// Q8_0 GEMV for rows whose byte pitch is a multiple of 16 (K a multiple of
-// 256): lane l takes blocks 2 l and 2 l + 1 of each 64-block step of its
-// warp's R rows, i.e. the 17 4-byte-aligned words at byte 68 l of the step
-// (2176 bytes), loaded together with its 64 activations so each step waits
-// for memory once. The first block's quants start 2 bytes into its words and
-// are realigned with one byte_perm per word; each byte becomes an exact float
-// through the mantissa of 2^23 (two at a time with packed fp32 adds), and the
-// products accumulate in fp32 pairs per block before the block's scale d.
-constexpr int kQ8Step = 64;  // blocks per step
-template <int NB, int R, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32)
-gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
-                        const float* __restrict__ X, float* __restrict__ Y, int64_t ldy) {
-    X += (int64_t)blockIdx.y * NB * K;
-    Y += (int64_t)blockIdx.y * NB * ldy;
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int64_t nblk = K / 32;
-    const int64_t tiles = (N + R - 1) / R;
-    const float2 kNegOff = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    for (int64_t tile = (int64_t)blockIdx.x * WARPS + warp; tile < tiles; tile += (int64_t)gridDim.x * WARPS) {
-        const int64_t row0 = tile * R;
-        float sum[R][NB];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int b = 0; b < NB; ++b) sum[r][b] = 0.0f;
-        for (int64_t b0 = 2 * lane; b0 < nblk; b0 += kQ8Step) {  // this lane's blocks b0, b0 + 1
-            uint32_t w[R][17];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int64_t row = row0 + r < N ? row0 + r : N - 1;
-                const uint32_t* src = reinterpret_cast<const uint32_t*>(W + row * row_bytes + b0 * 34);
-#pragma unroll
-                for (int i = 0; i < 17; ++i) w[r][i] = __ldg(src + i);
-            }
-            float2 xa[NB][16], xb[NB][16];
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                const float4* xp = reinterpret_cast<const float4*>(X + b * K + b0 * 32);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float4 va = __ldg(xp + i), vb = __ldg(xp + 8 + i);
-                    xa[b][2 * i] = make_float2(va.x, va.y);
-                    xa[b][2 * i + 1] = make_float2(va.z, va.w);
-                    xb[b][2 * i] = make_float2(vb.x, vb.y);
-                    xb[b][2 * i + 1] = make_float2(vb.z, vb.w);
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const float da = f16_bits_to_f32(w[r][0] & 0xFFFFu), db = f16_bits_to_f32(w[r][8] >> 16);
-                float2 aa[NB], ab[NB];
-#pragma unroll
-                for (int b = 0; b < NB; ++b) aa[b] = ab[b] = make_float2(0.0f, 0.0f);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    // four quants of each block, offset by 128 (unsigned bytes)
-                    const uint32_t qa = __byte_perm(w[r][i], w[r][i + 1], 0x5432) ^ 0x80808080u;
-                    const uint32_t qb = w[r][9 + i] ^ 0x80808080u;
-                    const float2 fa0 = __fadd2_rn(make_float2(as_f(__byte_perm(qa, 0x4B000000u, 0x7440u)),
-                                                              as_f(__byte_perm(qa, 0x4B000000u, 0x7441u))), kNegOff);
-                    const float2 fa1 = __fadd2_rn(make_float2(as_f(__byte_perm(qa, 0x4B000000u, 0x7442u)),
-                                                              as_f(__byte_perm(qa, 0x4B000000u, 0x7443u))), kNegOff);
-                    const float2 fb0 = __fadd2_rn(make_float2(as_f(__byte_perm(qb, 0x4B000000u, 0x7440u)),
-                                                              as_f(__byte_perm(qb, 0x4B000000u, 0x7441u))), kNegOff);
-                    const float2 fb1 = __fadd2_rn(make_float2(as_f(__byte_perm(qb, 0x4B000000u, 0x7442u)),
-                                                              as_f(__byte_perm(qb, 0x4B000000u, 0x7443u))), kNegOff);
-#pragma unroll
-                    for (int b = 0; b < NB; ++b) {
-                        aa[b] = __ffma2_rn(fa0, xa[b][2 * i], aa[b]);
-                        aa[b] = __ffma2_rn(fa1, xa[b][2 * i + 1], aa[b]);
-                        ab[b] = __ffma2_rn(fb0, xb[b][2 * i], ab[b]);
-                        ab[b] = __ffma2_rn(fb1, xb[b][2 * i + 1], ab[b]);
-                    }
-                }
-#pragma unroll
-                for (int b = 0; b < NB; ++b)
-                    sum[r][b] = fmaf(db, ab[b].x + ab[b].y, fmaf(da, aa[b].x + aa[b].y, sum[r][b]));
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                float v = warp_sum(sum[r][b]);
-                if (lane == 0 && row0 + r < N) Y[b * ldy + row0 + r] = v;
-            }
-    }
-}
-
 // Plain float weights (F32 / F16 / BF16): one warp per row, lanes stride over K.
 template <uint32_t Q, int NB>
 __global__ void gemv_float_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int64_t N, int64_t K,
@@ -490,17 +399,6 @@ void launch_kq(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
 template <int NB, int R>
 void launch_q8(const GemvArgs& a, cudaStream_t s, unsigned chunks = 1) {
     constexpr int WARPS = 4;
-    if (a.row_bytes % 16 == 0 && ((uintptr_t)a.W % 16) == 0 && ((uintptr_t)a.X % 16) == 0 && a.K % 256 == 0) {
-        // the streamed form: one row per warp (more warps, each lane's loads of a step issued together)
-        constexpr int RS = 1;
-        int64_t tiles = (a.N + RS - 1) / RS;
-        int64_t grid = (tiles + WARPS - 1) / WARPS;
-        int64_t cap = (int64_t)a.sm_count * 8;
-        if (grid > cap) grid = cap;
-        gemv_q8_0_stream_kernel<NB, RS, WARPS><<<dim3((unsigned)grid, chunks), WARPS * 32, 0, s>>>(
-            a.W, a.row_bytes, a.N, a.K, a.X, a.Y, ldy_of(a));
-        return;
-    }
     int64_t tiles = (a.N + R - 1) / R;
     int64_t grid = (tiles + WARPS - 1) / WARPS;
     int64_t cap = (int64_t)a.sm_count * 8;

@@ -9,14 +9,19 @@
  * on 97,052 inputs, each within 1/256 ulp of a rounding midpoint (its error is
  * below 0.502 ulp). The device computes y = exp((double)x) and rounds it to
  * f32, which is correctly rounded unless y lies within a few double ulps of a
- * midpoint. So the device rule (expf_libm.cuh) is: if y is at least 2^-7 ulp
+ * midpoint. So the device rule (expf_libm.cuh) is: if y is at least 2^-9 ulp
  * from the midpoint on its side, return the rounded y (there the C library
- * rounds correctly too); otherwise look x up here and return the entry when
- * there is one. The table holds every input of the domain where expf differs
+ * rounds correctly too: its misrounded inputs all lie within 2^-9.25 ulp of
+ * one); otherwise look x up here and return the entry when there is one. The table holds every input of the domain where expf differs
  * from the correctly rounded value (found with the x87 long double expl), and
  * every input whose exact value lies within 16 double ulps of a midpoint
  * (where the device's own double exp may round either way), each with expf's
  * result.
+ *
+ * The entries are kept in an open-addressing hash table of 2^18 (key, value)
+ * slots (key = |x|'s bits, value = expf's bits; Fibonacci hashing, linear
+ * probing), so a lookup reads about one cache line; the longest probe any key
+ * can take is recorded with it.
  *
  * The program then replays the device rule on every input of the domain, with
  * this host's double exp standing in for the device's, and fails unless all
@@ -33,8 +38,10 @@
 
 #define LO 0x80000000u /* -0.0 */
 #define HI 0xC2D00000u /* -104.0 */
-#define NBUCKET (((HI & 0x7FFFFFFFu) >> 16) + 1)
 #define NTHREAD 8
+#define SLOT_BITS 18
+#define NSLOT (1u << SLOT_BITS)
+#define EMPTY 0xFFFFFFFFu /* no key: |x| <= 0x42D00000 */
 
 static float f_of(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 static uint32_t u_of(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -76,11 +83,14 @@ static void* collect(void* arg) {
     return NULL;
 }
 
-/* the table, merged */
+/* the table, merged, and its hash slots */
 static uint32_t* T_in;
 static uint32_t* T_out;
 static size_t T_n;
-static uint32_t idx[NBUCKET + 1];
+static uint32_t slot_key[NSLOT], slot_val[NSLOT];
+static uint32_t max_probe; /* longest probe sequence of any key, hit or miss */
+
+static uint32_t hash_of(uint32_t v) { return (v * 0x9E3779B1u) >> (32 - SLOT_BITS); }
 
 /* the device rule of expf_libm.cuh, with the host's double exp */
 static uint32_t device_rule(float x) {
@@ -91,12 +101,13 @@ static uint32_t device_rule(float x) {
     const double e = y - (double)r;
     const float nb = f_of(e >= 0.0 ? ur + 1u : ur - 1u);
     const double half = 0.5 * fabs((double)nb - (double)r);
-    if (fabs(fabs(e) - half) >= half * (1.0 / 64.0)) return ur;
-    const uint32_t v = u_of(x) & 0x7FFFFFFFu, b = v >> 16, key = v & 0xFFFFu;
-    for (uint32_t i = idx[b]; i < idx[b + 1]; ++i) {
-        const uint32_t k = T_in[i] & 0xFFFFu;
-        if (k == key) return T_out[i];
-        if (k > key) break;
+    if (fabs(fabs(e) - half) >= half * (1.0 / 256.0)) return ur;
+    const uint32_t v = u_of(x) & 0x7FFFFFFFu;
+    uint32_t h = hash_of(v);
+    for (uint32_t p = 0; p < max_probe; ++p) {
+        if (slot_key[h] == v) return slot_val[h];
+        if (slot_key[h] == EMPTY) return ur;
+        h = (h + 1) & (NSLOT - 1);
     }
     return ur;
 }
@@ -135,9 +146,18 @@ int main(int argc, char** argv) {
         memcpy(T_out + k, parts[t].out, parts[t].n * 4);
         k += parts[t].n;
     }
-    for (size_t i = 0, b = 0; b <= NBUCKET; ++b) {  /* idx[b] = first entry of bucket b */
-        while (i < T_n && (T_in[i] >> 16) < b) ++i;
-        idx[b] = (uint32_t)i;
+    for (uint32_t h = 0; h < NSLOT; ++h) slot_key[h] = EMPTY;
+    for (size_t i = 0; i < T_n; ++i) {
+        uint32_t h = hash_of(T_in[i]);
+        while (slot_key[h] != EMPTY) h = (h + 1) & (NSLOT - 1);
+        slot_key[h] = T_in[i];
+        slot_val[h] = T_out[i];
+    }
+    /* a probe from any slot ends at the first empty one: the longest run of
+     * occupied slots (cyclically) plus that empty slot */
+    for (uint32_t h = 0, run = 0, seen = 0; seen < 2 * NSLOT; ++seen, h = (h + 1) & (NSLOT - 1)) {
+        run = slot_key[h] == EMPTY ? 0 : run + 1;
+        if (run + 1 > max_probe) max_probe = run + 1;
     }
 
     check cs[NTHREAD];
@@ -158,14 +178,13 @@ int main(int argc, char** argv) {
     fprintf(f, "// generated by gen_expf_fix.c from this host's expf: %zu entries, checked on every\n"
                "// float in [-104, 0] (the device rule with the host double exp equals expf on all).\n", T_n);
     fprintf(f, "#define STRATA_EXPF_FIX_ENTRIES %zu\n", T_n);
-    fprintf(f, "static __device__ const uint32_t kExpfFixIdx[%u] = {", NBUCKET + 1);
-    for (uint32_t b = 0; b <= NBUCKET; ++b) fprintf(f, "%s%u,", b % 16 ? "" : "\n", idx[b]);
-    fprintf(f, "\n};\nstatic __device__ const uint16_t kExpfFixKey[%zu] = {", T_n);
-    for (size_t i = 0; i < T_n; ++i) fprintf(f, "%s%u,", i % 20 ? "" : "\n", T_in[i] & 0xFFFFu);
-    fprintf(f, "\n};\nstatic __device__ const uint32_t kExpfFixVal[%zu] = {", T_n);
-    for (size_t i = 0; i < T_n; ++i) fprintf(f, "%s0x%08xu,", i % 10 ? "" : "\n", T_out[i]);
+    fprintf(f, "constexpr int kExpfFixBits = %d;\nconstexpr uint32_t kExpfFixMaxProbe = %u;\n", SLOT_BITS, max_probe);
+    fprintf(f, "static __device__ const uint2 kExpfFix[%u] = {", NSLOT);
+    for (uint32_t h = 0; h < NSLOT; ++h)
+        fprintf(f, "%s{0x%08xu,0x%08xu},", h % 6 ? "" : "\n", slot_key[h], slot_val[h]);
     fprintf(f, "\n};\n");
     if (fclose(f)) { perror(argv[1]); return 1; }
-    printf("gen_expf_fix: %zu entries, all %u inputs match expf\n", T_n, HI + 1u - LO);
+    printf("gen_expf_fix: %zu entries in %u slots (longest probe %u), all %u inputs match expf\n", T_n, NSLOT,
+           max_probe, HI + 1u - LO);
     return 0;
 }

@@ -71,16 +71,39 @@ void launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
 // (k each) and, when given, the ids to ids_s too.
 __device__ void route_token(const float* __restrict__ lg, int E, int k, float* sp, int lane, int* __restrict__ ids,
                             float* __restrict__ wts, int* ids_s) {
+    // the logits into sp (each lane its own entries i = lane mod 32) and their maximum
     float mx = -INFINITY;
-    for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lg[i]);
+    for (int i = lane; i < E; i += 32) {
+        const float v = lg[i];
+        sp[i] = v;
+        mx = fmaxf(mx, v);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-    double sum = 0.0;
-    for (int i = lane; i < E; i += 32) {
-        const float e = expf_libm(lg[i] - mx);
-        sp[i] = e;
-        sum += (double)e;
+    // exp as the C library rounds it (expf_libm): the rounded double exp in a
+    // loop without calls, the few inputs near a rounding midpoint (bit j of
+    // `near`: entry lane + 32 j of the 1024-entry chunk) settled afterwards
+    for (int i0 = 0; i0 < E; i0 += 1024) {
+        uint32_t near = 0;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            const int i = i0 + 32 * j + lane;
+            if (i < E) {
+                bool exact;
+                const float r = expf_libm_try(sp[i] - mx, exact);
+                if (exact) sp[i] = r;
+                else near |= 1u << j;
+            }
+        }
+        while (near) {
+            const int j = __ffs((int)near) - 1;
+            near &= near - 1;
+            const int i = i0 + 32 * j + lane;
+            sp[i] = expf_libm_near(sp[i] - mx);
+        }
     }
+    double sum = 0.0;
+    for (int i = lane; i < E; i += 32) sum += (double)sp[i];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
     const float inv = (float)(1.0 / sum);
