@@ -104,11 +104,13 @@ def _rel_err_rows(y, ref):
     return np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor), axis=1)
 
 
-@pytest.mark.parametrize("quant,K,N", [(Q5_K, 4096, 12288), (Q6_K, 4096, 12288), (Q5_K, 12288, 4096),
-                                       (Q6_K, 12288, 4096)])
-@pytest.mark.parametrize("m", [64, 512, 2048])
+@pytest.mark.parametrize("quant,K,N,m", [(q, K, N, m) for (q, K, N) in [(Q5_K, 4096, 12288), (Q6_K, 4096, 12288),
+                                                                        (Q5_K, 12288, 4096), (Q6_K, 12288, 4096)]
+                                          for m in (64, 512, 2048)]
+                         + [(Q4_K, 8192, 28672, 1024), (Q4_K, 28672, 8192, 1024)])
 def test_gemm_config_shapes(ctx, quant, K, N, m, threads):
-    """The mixed K-quant prefill configuration at full size. Every output is
+    """The mixed K-quant prefill configuration at full size, and the
+    row-sharded projection configuration's two matrices. Every output is
     checked against an f64 product of the oracle's bit-exact dequantized
     weights with the bf16 activations (computed on the GPU in float64, where
     the sequential f64 sum of ops::gemv would take the CPU minutes), and
