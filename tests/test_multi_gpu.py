@@ -205,6 +205,103 @@ def _worker(rank, world, uid, q):
         q.put((rank, traceback.format_exc()))
 
 
+def _config_worker(rank, world, uid, q):
+    """The configuration shapes: row-sharded Q4_K 8192 -> 28672 and 28672 ->
+    8192 GEMVs at batch 1 and 8 (bitwise the one-GPU GEMV, through the peer
+    gather), their M = 1024 GEMMs (within fp32 reassociation of the one-GPU
+    GEMM), and the 256-expert layer (hidden 2048, expert width 512, top 8,
+    shared expert 512) expert-parallel at T = 1 and 64 (within 1e-3 of the
+    one-GPU layer)."""
+    try:
+        sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "strata-rs_b200"),
+                        os.path.join(os.path.dirname(HERE), "oracle")]
+        import torch
+        import strata_cuda as sc
+        import sharding
+        from conftest import rel_err
+        from synth import Q4_K, activations, bf16_bits, quant_matrix, rng
+        torch.cuda.set_device(rank)
+        ctx = sc.Context(rank)
+        ctx.set_wait_timeout_ms(60000)
+        ctx.comm_init(rank, world, uid)
+        ctx.set_wait_timeout_ms(10000)
+        st = torch.cuda.Stream()
+        dev = f"cuda:{rank}"
+        for (K, N) in ((8192, 28672), (28672, 8192)):
+            data = quant_matrix(2100 + K, Q4_K, N, K)
+            full = ctx.upload(data, Q4_K, N, K)
+            shard = ctx.upload(sharding.row_shard(data, Q4_K, N, K, world, rank), Q4_K, N // world, K)
+            for B in (1, 8):
+                x = torch.from_numpy(activations(2101 + B, B, K)).to(dev)
+                y = torch.empty((B, N), dtype=torch.float32, device=dev)
+                st.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(st):
+                    ctx.gemv_sharded_dev(shard, x.data_ptr(), y.data_ptr(), B, st.cuda_stream)
+                st.synchronize()
+                want = ctx.gemv(full, x.cpu().numpy())
+                assert np.array_equal(y.cpu().numpy().view(np.uint32), want.reshape(B, N).view(np.uint32)), \
+                    ("config gemv", K, N, B)
+            M = 1024
+            bits = bf16_bits(activations(2102, M, K))
+            xb = torch.from_numpy(bits.view(np.int16)).to(dev)
+            yg = torch.empty((M, N), dtype=torch.float32, device=dev)
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                ctx.gemm_sharded_dev(shard, xb.data_ptr(), yg.data_ptr(), M, st.cuda_stream)
+            st.synchronize()
+            # sampled tokens against the f64 product of the oracle's bit-exact
+            # dequantized weights with the bf16 activations (the GEMM's 1e-2 bound;
+            # the shard and the full matrix take other split-K factors, so the
+            # sharded result is not the one-GPU GEMM's bits)
+            import oracle
+            got = yg.cpu().numpy()
+            toks = list(range(0, M, 37))
+            Wd = torch.from_numpy(oracle.dequantize(Q4_K, data, N, K)).to(dev).double()
+            xr = (bits[toks].astype(np.uint32) << 16).view(np.float32)
+            ref = (torch.from_numpy(xr).to(dev).double() @ Wd.T).cpu().numpy()
+            del Wd
+            worst = max(rel_err(got[t], ref[i]) for i, t in enumerate(toks))
+            assert worst < 1e-2, ("config gemm", K, N, worst)
+            full.free()
+            shard.free()
+
+        n_embd, E, k, n_ff, n_ff_s = 2048, 256, 8, 512, 512
+        ge = quant_matrix(2120, Q4_K, n_embd, n_ff, E)
+        ue = quant_matrix(2121, Q4_K, n_embd, n_ff, E)
+        de = quant_matrix(2122, Q4_K, n_ff, n_embd, E)
+        sh = {nm: ctx.upload(quant_matrix(2123 + i, Q4_K, r, c), Q4_K, r, c)
+              for i, (nm, r, c) in enumerate([("gate_shexp", n_ff_s, n_embd), ("up_shexp", n_ff_s, n_embd),
+                                              ("down_shexp", n_embd, n_ff_s), ("gate_inp_shexp", 1, n_embd)])}
+        wf = dict(sh, gate_exps=ctx.upload(ge, Q4_K, n_embd, n_ff, n_expert=E),
+                  up_exps=ctx.upload(ue, Q4_K, n_embd, n_ff, n_expert=E),
+                  down_exps=ctx.upload(de, Q4_K, n_ff, n_embd, n_expert=E))
+        lf = ctx.moe_create(wf, n_embd, E, k, n_ff, n_ff_s)
+        e0, e1 = sharding.expert_range(E, world, rank)
+        wr = dict(sh, gate_exps=ctx.upload(sharding.expert_shard(ge, E, world, rank), Q4_K, n_embd, n_ff,
+                                           n_expert=e1 - e0),
+                  up_exps=ctx.upload(sharding.expert_shard(ue, E, world, rank), Q4_K, n_embd, n_ff, n_expert=e1 - e0),
+                  down_exps=ctx.upload(sharding.expert_shard(de, E, world, rank), Q4_K, n_ff, n_embd,
+                                       n_expert=e1 - e0))
+        lr = ctx.moe_create(wr, n_embd, E, k, n_ff, n_ff_s, expert_begin=e0, expert_end=e1, with_shared=(rank == 0))
+        for T in (1, 64):
+            x = activations(2130 + T, T, n_embd)
+            lg = rng(2131 + T).standard_normal((T, E)).astype(np.float32)
+            want_m, _, _ = ctx.moe_ffn(lf, x, lg)
+            xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
+            od = torch.empty((T, n_embd), dtype=torch.float32, device=dev)
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                ctx.moe_ffn_ep_dev(lr, xd.data_ptr(), ld.data_ptr(), T, od.data_ptr(), st.cuda_stream)
+            st.synchronize()
+            got_m = od.cpu().numpy()
+            for t in range(T):
+                assert rel_err(got_m[t], want_m[t]) < 1e-3, ("config moe", T, t)
+        ctx.close()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
 def _peer_timeout_worker(rank, world, uid, q, bar):
     """Rank 1 skips a sharded GEMV: rank 0's wait for its arrivals expires
     (bounded), the call reports STRATA_ERR_TIMEOUT and the context stays
@@ -248,12 +345,12 @@ def _peer_timeout_worker(rank, world, uid, q, bar):
         q.put((rank, traceback.format_exc()))
 
 
-def _run_world(world, target=None):
+def _run_world(world, target=None, worker=None):
     uid = sc.comm_unique_id()
     ctxm = mp.get_context("spawn")
     q = ctxm.Queue()
     if target is None:
-        procs = [ctxm.Process(target=_worker, args=(r, world, uid, q)) for r in range(world)]
+        procs = [ctxm.Process(target=worker or _worker, args=(r, world, uid, q)) for r in range(world)]
     else:
         bar = ctxm.Barrier(world)
         procs = [ctxm.Process(target=target, args=(r, world, uid, q, bar)) for r in range(world)]
@@ -285,6 +382,20 @@ def test_peer_gather_times_out_when_a_rank_skips_the_call():
 @pytest.mark.skipif(_ngpu() < 4, reason="needs 4 GPUs")
 def test_sharded_paths_world4():
     res = _run_world(4)
+    assert all(m == "ok" for m in res.values()), res
+
+
+@pytest.mark.skipif(_ngpu() < 8, reason="needs 8 GPUs")
+def test_sharded_paths_world8():
+    res = _run_world(8)
+    assert all(m == "ok" for m in res.values()), res
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_config_shapes_sharded(world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run_world(world, worker=_config_worker)
     assert all(m == "ok" for m in res.values()), res
 
 
