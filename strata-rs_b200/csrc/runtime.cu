@@ -77,6 +77,7 @@ int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what)
         if (rc) return rc;
         cudaFreeHost(b.ptr);
         b.ptr = nullptr;
+        b.dev = nullptr;
         b.bytes = 0;
     }
     size_t want = bytes < 4096 ? 4096 : bytes;
@@ -84,6 +85,12 @@ int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what)
     if (e != cudaSuccess) {
         b.ptr = nullptr;
         return cuda_fail(ctx, e, what);
+    }
+    // page-locked memory is mapped into the device's address space (unified
+    // addressing); kernels may read and write it in place
+    if (cudaHostGetDevicePointer(&b.dev, b.ptr, 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        b.dev = nullptr;
     }
     b.bytes = want;
     return STRATA_OK;
@@ -609,11 +616,32 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     if ((rc = ensure_pinned(ctx, ctx->x_host, xb, "cudaMallocHost(x)"))) return rc;
     if ((rc = ensure_pinned(ctx, ctx->y_host, yb, "cudaMallocHost(y)"))) return rc;
     ctx->copy_pool.copy(ctx->x_host.ptr, x, xb);
-    cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
-    if ((rc = gemv_enqueue(ctx, w, (const float*)ctx->x_dev.ptr, (float*)ctx->y_dev.ptr, batch, ctx->stream)))
-        return rc;
-    return copy_out(ctx, y, ctx->y_dev.ptr, yb);
+    // On the tensor-core path x is read once, by the activation prologue: it
+    // reads the pinned staging in place (no copy of its own). The CUDA-core
+    // kernels re-read x per row, so they get a device copy.
+    const float* xd = static_cast<const float*>(ctx->x_host.dev);
+    if (!xd || !gemv_peer_capable(ctx, w, xd, batch)) {
+        cudaError_t e = cudaMemcpyAsync(ctx->x_dev.ptr, ctx->x_host.ptr, xb, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
+        xd = static_cast<const float*>(ctx->x_dev.ptr);
+    }
+    // A result of up to 1 MiB is stored by the GEMV straight into the pinned
+    // staging (each value written once; no transfer to wait for), larger ones
+    // go through device memory and the pieced copy-out.
+    constexpr size_t kInPlaceOut = size_t(1) << 20;
+    float* yd = yb <= kInPlaceOut ? static_cast<float*>(ctx->y_host.dev) : nullptr;
+    if ((rc = gemv_enqueue(ctx, w, xd, yd ? yd : (float*)ctx->y_dev.ptr, batch, ctx->stream))) return rc;
+    if (!yd) return copy_out(ctx, y, ctx->y_dev.ptr, yb);
+    if (!ctx->piece_ev[0]) {
+        cudaError_t e = cudaEventCreateWithFlags(&ctx->piece_ev[0], cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventCreate(result pieces)");
+    }
+    cudaError_t e = cudaEventRecord(ctx->piece_ev[0], ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventRecord(result)");
+    if ((rc = wait_event(ctx, ctx->piece_ev[0]))) return rc;
+    if ((rc = check_device_error(ctx))) return rc;
+    ctx->copy_pool.copy(y, ctx->y_host.ptr, yb);
+    return STRATA_OK;
 }
 
 // ---- prefill GEMM

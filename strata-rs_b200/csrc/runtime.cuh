@@ -22,6 +22,7 @@ struct DevBuf {
 struct PinnedBuf {
     void* ptr = nullptr;
     size_t bytes = 0;
+    void* dev = nullptr;  // the same memory's device address (unified addressing: usually ptr itself)
 };
 
 struct CommState;  // comm.cu
