@@ -491,6 +491,10 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     constexpr int BB = block_bytes(Q);
     constexpr int kConsumers = NCONS, kBpw = kChunk / kConsumers;
     static_assert(NCONS == 8 || (NCONS == 4 && NB <= 4), "four consumer warps serve batches up to 4");
+    // Stage j's tile and chunk: running counters, or (batches from 5, whose
+    // accumulators leave no registers to spare) recomputed from j each stage,
+    // which measured faster there.
+    constexpr bool kDivide = NB >= 5;
     // smem stride of one row of a stage. TM (one tensor-map copy per stage):
     // the rows are dense and 128-byte swizzled, which puts consecutive rows'
     // units on different banks. Otherwise (one bulk copy per row): each row is
@@ -525,8 +529,11 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
         // ---------------- producer: the weights do not depend on the prologue
         // (abort decisions are made warp-uniform: the loop has __syncwarp)
         int issued = 0;  // stages whose copies were issued
+        int tile_c = blockIdx.x, c0_c = 0;  // tile and first K block of stage j (counters)
         for (int j = 0; j < nstages; ++j) {
             const int slot = j % kStages;
+            const int tile = kDivide ? blockIdx.x + (j / nchunks) * gridDim.x : tile_c;
+            const int c0 = kDivide ? (j % nchunks) * kChunk : c0_c;
             bool ok = true;
             if (j >= kStages) ok = mbar_wait(smem_u32(&empty_bar[slot]), ((j / kStages) - 1) & 1, err);
             ok = __all_sync(0xFFFFFFFFu, ok) && __shfl_sync(0xFFFFFFFFu, *(volatile int*)&abort_flag, 0) == 0;
@@ -534,8 +541,6 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                 abort_flag = 1;
                 break;
             }
-            const int tile = blockIdx.x + (j / nchunks) * gridDim.x;
-            const int c0 = (j % nchunks) * kChunk;
             const int nb = min(kChunk, nblk - c0);
             const uint32_t bytes = (uint32_t)(nb * BB);
             const uint32_t fb = smem_u32(&full_bar[slot]);
@@ -557,6 +562,13 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                 }
             }
             issued = j + 1;
+            if constexpr (!kDivide) {
+                c0_c += kChunk;
+                if (c0_c >= nblk) {
+                    c0_c = 0;
+                    tile_c += gridDim.x;
+                }
+            }
         }
         // drain: wait (bounded) for the copies of the last stages issued, which
         // may still be in flight (after an abort, stages never issued are not waited on)
@@ -603,6 +615,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
     // walking the same stages, so every consumer still reaches every
     // tile-end barrier (nothing can be left waiting there).
     bool live = true;
+    int tile_c = blockIdx.x, chunk_c = 0, set_c = 0;  // stage j's tile, its chunk, the tile's scratch set
     for (int j = 0; j < nstages; ++j) {
         const int slot = j % kStages;
         if (live) {
@@ -610,8 +623,8 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
             live = __all_sync(0xFFFFFFFFu, ok) && __shfl_sync(0xFFFFFFFFu, *(volatile int*)&abort_flag, 0) == 0;
             if (!live) abort_flag = 1;
         }
-        const int tile = blockIdx.x + (j / nchunks) * gridDim.x;
-        const int chunk = j % nchunks;
+        const int tile = kDivide ? blockIdx.x + (j / nchunks) * gridDim.x : tile_c;
+        const int chunk = kDivide ? j % nchunks : chunk_c;
         const int kb0 = chunk * kChunk + warp * kBpw;
         if (live && kb0 + kBpw <= nblk) {
             // the warp's kBpw blocks, interleaved for instruction-level parallelism
@@ -649,7 +662,7 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
             // each n8 tile. The scratch alternates between two sets, so the
             // next tile's writes cannot race this tile's reads and one barrier
             // per tile suffices.
-            const int set = (j / nchunks) & 1;
+            const int set = kDivide ? (j / nchunks) & 1 : set_c;
             if constexpr (kDiag) {
                 // sum the four t lanes of each row, then the warps: red[set][w] as [b][16 rows]
                 float* rw = &red[set][warp][0][0][0];
@@ -695,6 +708,13 @@ gemv_kq_tma_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int 
                         else Y[b * ldy + row] = v;
                     }
                 }
+            }
+        }
+        if constexpr (!kDivide) {
+            if (++chunk_c == nchunks) {
+                chunk_c = 0;
+                tile_c += gridDim.x;
+                set_c ^= 1;
             }
         }
     }

@@ -5,6 +5,7 @@
 // and the weights uploaded byte-for-byte. Kernels live in the other .cu files.
 #include "runtime.cuh"
 
+#include <algorithm>
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
@@ -203,6 +204,9 @@ int strata_cuda_destroy(strata_ctx* ctx) {
         if (e) cudaEventDestroy(e);
     for (cudaEvent_t& e : ctx->piece_ev)
         if (e) cudaEventDestroy(e);
+    for (cudaEvent_t& e : ctx->slice_ev)
+        if (e) cudaEventDestroy(e);
+    if (ctx->copy) cudaStreamDestroy(ctx->copy);
     cudaEventDestroy(ctx->done);
     if (ctx->fork) cudaEventDestroy(ctx->fork);
     if (ctx->join) cudaEventDestroy(ctx->join);
@@ -547,6 +551,70 @@ int copy_out(strata_ctx* ctx, void* dst, const void* src_dev, size_t bytes) {
     return check_device_error(ctx);
 }
 
+// A host-buffer GEMV whose result is too large to store in place: the rows
+// are cut into up to kPieces slices (whole rounds of 16-row tiles over the
+// SMs at two or three CTAs each; a short last slice), computed one after
+// another on the context stream (the activation prologue once, the slices
+// reusing its limbs). Each slice's rows of every token are copied device ->
+// pinned on the copy stream as soon as that slice is done, overlapping the
+// next slices' compute, and pinned -> caller by the pool's threads while the
+// next slice transfers. Returns once every byte is out.
+static int gemv_sliced_out(strata_ctx* ctx, const strata_weight* w, const float* xd, float* y, int batch) {
+    const int64_t N = w->rows;
+    const size_t yb = (size_t)batch * (size_t)N * sizeof(float);
+    constexpr size_t kMinSlice = size_t(512) << 10;
+    int S = (int)(yb / kMinSlice);
+    S = S < 1 ? 1 : (S > strata_ctx::kPieces ? strata_ctx::kPieces : S);
+    const int64_t unit = (int64_t)16 * ctx->sm_count * 6;
+    int64_t rs = (N + S - 1) / S;
+    rs = (rs + unit - 1) / unit * unit;
+    if (!ctx->copy) {
+        cudaError_t e = cudaStreamCreateWithFlags(&ctx->copy, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamCreate(result copies)");
+    }
+    for (int k = 0; k < strata_ctx::kPieces; ++k)
+        for (cudaEvent_t* ev : {&ctx->slice_ev[k], &ctx->piece_ev[k]})
+            if (!*ev) {
+                cudaError_t e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+                if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventCreate(result slices)");
+            }
+    int rc = ensure_device(ctx, ctx->xfrag, (size_t)std::max<int64_t>(gemv_mma_work_bytes(w->cols, batch), 4 << 20),
+                           "cudaMalloc(x limbs)");
+    if (rc) return rc;
+    char* h = static_cast<char*>(ctx->y_host.ptr);
+    char* d = static_cast<char*>(ctx->y_dev.ptr);
+    const size_t pitch = (size_t)N * sizeof(float);
+    int issued = 0;
+    for (int64_t r0 = 0; r0 < N; r0 += rs, ++issued) {
+        const int64_t r1 = std::min(N, r0 + rs);
+        alignas(64) unsigned char tm[128];
+        const uint8_t* base = w->dev + r0 * w->row_bytes;
+        const bool has_tm = w->has_tmap && encode_gemv_tmap(w->quant, base, r1 - r0, w->row_bytes, tm);
+        GemvArgs a{base, w->row_bytes, r1 - r0, w->cols, xd, reinterpret_cast<float*>(d) + r0, batch, ctx->sm_count,
+                   has_tm ? tm : nullptr, N, nullptr};
+        launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, ctx->stream, issued == 0);
+        if ((rc = check_launch(ctx, "tensor-core gemv kernel (slice)"))) return rc;
+        const size_t off = (size_t)r0 * sizeof(float), width = (size_t)(r1 - r0) * sizeof(float);
+        cudaError_t e = cudaEventRecord(ctx->slice_ev[issued], ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->copy, ctx->slice_ev[issued], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(h + off, pitch, d + off, pitch, width, (size_t)batch, cudaMemcpyDeviceToHost,
+                                  ctx->copy);
+        if (e == cudaSuccess) e = cudaEventRecord(ctx->piece_ev[issued], ctx->copy);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "result slice copy");
+    }
+    ctx->copy_pool.prime();  // threads ready when the first slice lands
+    for (int k = 0; k < issued; ++k) {
+        const int64_t r0 = k * rs, r1 = std::min(N, r0 + rs);
+        if ((rc = wait_event(ctx, ctx->piece_ev[k]))) return rc;
+        if ((rc = check_device_error(ctx))) return rc;
+        const size_t off = (size_t)r0 * sizeof(float);
+        ctx->copy_pool.copy2d(reinterpret_cast<char*>(y) + off, pitch, h + off, pitch,
+                              (size_t)(r1 - r0) * sizeof(float), (size_t)batch);
+    }
+    return STRATA_OK;
+}
+
 int gemv_enqueue(strata_ctx* ctx, const strata_weight* w, const float* x_dev, float* y_dev, int batch,
                  cudaStream_t s) {
     return gemv_enqueue_strided(ctx, w, x_dev, y_dev, batch, 0, s);
@@ -629,6 +697,7 @@ int strata_cuda_gemv(strata_ctx* ctx, const strata_weight* w, const float* x, fl
     // staging (each value written once; no transfer to wait for), larger ones
     // go through device memory and the pieced copy-out.
     constexpr size_t kInPlaceOut = size_t(1) << 20;
+    if (yb > kInPlaceOut && xd == ctx->x_host.dev) return gemv_sliced_out(ctx, w, xd, y, batch);
     float* yd = yb <= kInPlaceOut ? static_cast<float*>(ctx->y_host.dev) : nullptr;
     if ((rc = gemv_enqueue(ctx, w, xd, yd ? yd : (float*)ctx->y_dev.ptr, batch, ctx->stream))) return rc;
     if (!yd) return copy_out(ctx, y, ctx->y_dev.ptr, yb);

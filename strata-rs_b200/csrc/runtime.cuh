@@ -56,6 +56,10 @@ struct strata_ctx {
     // the caller (by the pool's threads) while the next is still in transfer
     static constexpr int kPieces = 4;
     cudaEvent_t piece_ev[kPieces] = {};
+    // a large GEMV result computed as row slices: slice k's rows leave on
+    // `copy` (created with the first such call) once slice_ev[k] says they are done
+    cudaStream_t copy = nullptr;
+    cudaEvent_t slice_ev[kPieces] = {};
     strata::CopyPool copy_pool;
     // upload staging: two pinned chunks filled by host threads while the
     // other one is copied to the device (large tensors), with their events

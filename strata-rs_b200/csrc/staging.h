@@ -109,7 +109,8 @@ inline void copy_host(void* dst, const void* src, size_t n) {
 // still in flight, so the copy does not wait for threads to wake. copy() blocks until
 // every part is written; one copy at a time (the owner serialises its calls).
 // Copies under `kMin` bytes, or when no worker can be started, are one memcpy
-// on the caller.
+// on the caller. copy2d() copies `height` rows of `width` bytes between
+// pitched buffers, the rows' bytes split evenly over the threads.
 class CopyPool {
   public:
     static constexpr size_t kMin = size_t(256) << 10;
@@ -139,9 +140,13 @@ class CopyPool {
         go_.notify_all();
     }
 
-    void copy(void* dst, const void* src, size_t n) {
+    void copy(void* dst, const void* src, size_t n) { copy2d(dst, n, src, n, n, 1); }
+
+    void copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height) {
+        const size_t n = width * height;
         if (n < kMin || !start()) {
-            if (n) memcpy(dst, src, n);
+            for (size_t r = 0; r < height && width; ++r)
+                memcpy(static_cast<char*>(dst) + r * dpitch, static_cast<const char*>(src) + r * spitch, width);
             return;
         }
         const size_t parts = (size_t)th_.size() + 1;
@@ -150,17 +155,28 @@ class CopyPool {
             std::lock_guard<std::mutex> g(m_);
             d_ = static_cast<char*>(dst);
             s_ = static_cast<const char*>(src);
+            dp_ = dpitch;
+            sp_ = spitch;
+            w_ = width;
             n_ = n;
             part_ = part;
             pending_.store((int)th_.size());
             gen_.fetch_add(1);
         }
         go_.notify_all();
-        memcpy(d_, s_, part < n ? part : n);  // the caller's part: the first
+        span(d_, dp_, s_, sp_, w_, 0, part < n ? part : n);  // the caller's part: the first
         while (pending_.load() != 0) std::this_thread::yield();
     }
 
   private:
+    // bytes [a, b) of the rows laid end to end
+    static void span(char* d, size_t dp, const char* s, size_t sp, size_t w, size_t a, size_t b) {
+        while (a < b) {
+            const size_t r = a / w, c = a % w, len = b - a < w - c ? b - a : w - c;
+            memcpy(d + r * dp + c, s + r * sp + c, len);
+            a += len;
+        }
+    }
     bool start() {
         if (started_) return !th_.empty();
         started_ = true;
@@ -180,7 +196,7 @@ class CopyPool {
             while (gen_.load() == seen && !stop_.load() && spin < kSpin) ++spin;
             char* d;
             const char* s;
-            size_t n, part;
+            size_t n, part, dp, sp, w;
             {
                 std::unique_lock<std::mutex> g(m_);
                 go_.wait(g, [&] { return stop_.load() || gen_.load() != seen || wake_.load() != woken; });
@@ -190,11 +206,14 @@ class CopyPool {
                 seen = gen_.load();
                 d = d_;
                 s = s_;
+                dp = dp_;
+                sp = sp_;
+                w = w_;
                 n = n_;
                 part = part_;
             }
             const size_t a = idx * part;
-            if (a < n) memcpy(d + a, s + a, a + part < n ? part : n - a);
+            if (a < n) span(d, dp, s, sp, w, a, a + part < n ? a + part : n);
             pending_.fetch_sub(1);
         }
     }
@@ -208,7 +227,7 @@ class CopyPool {
     std::atomic<int> pending_{0};
     char* d_ = nullptr;
     const char* s_ = nullptr;
-    size_t n_ = 0, part_ = 0;
+    size_t n_ = 0, part_ = 0, dp_ = 0, sp_ = 0, w_ = 0;
 };
 
 }  // namespace strata

@@ -110,10 +110,37 @@ static int check_pool(std::mt19937_64& g) {
     return 0;
 }
 
+// CopyPool::copy2d: `height` rows of `width` bytes between pitched buffers
+// land exactly, and nothing between or past the rows is written (row
+// lengths over and under the threshold, one row to a few, parts that start
+// and end inside rows).
+static int check_pool_2d(std::mt19937_64& g) {
+    CopyPool pool;
+    for (int i = 0; i < 40; ++i) {
+        const size_t h = 1 + g() % 9;
+        const size_t w = i % 4 == 0 ? g() % 4096 : (CopyPool::kMin / h) + g() % (size_t(2) << 20);
+        const size_t sp = w + g() % 200, dp = w + g() % 200;
+        std::vector<uint8_t> src(sp * h + 64), dst(dp * h + 64, 0xAB);
+        for (auto& b : src) b = (uint8_t)g();
+        const size_t so = g() % 64;
+        if (i % 3 == 0) pool.prime();
+        pool.copy2d(dst.data(), dp, src.data() + so, sp, w, h);
+        for (size_t r = 0; r < h; ++r) {
+            if (w && memcmp(dst.data() + r * dp, src.data() + so + r * sp, w) != 0)
+                return printf("pool.copy2d(%zu x %zu) row %zu differs\n", h, w, r), 1;
+            const size_t end = r + 1 < h ? (r + 1) * dp : dst.size();
+            for (size_t k = r * dp + w; k < end; ++k)
+                if (dst[k] != 0xAB) return printf("pool.copy2d(%zu x %zu) wrote past row %zu\n", h, w, r), 1;
+        }
+    }
+    return 0;
+}
+
 int main() {
     std::mt19937_64 g(20261202);
     if (check_copy(g)) return 1;
     if (check_pool(g)) return 1;
+    if (check_pool_2d(g)) return 1;
     for (size_t cap : {size_t(1), size_t(7), size_t(64), size_t(1000), size_t(4096)})
         for (int it = 0; it < 300; ++it)
             if (check(g, cap, it % 3 == 0 ? 3 : 40)) return printf("cap %zu case %d\n", cap, it), 1;

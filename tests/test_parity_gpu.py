@@ -121,6 +121,29 @@ def test_q4_k_sweep_shapes(ctx, k, n, batch, threads):
     w.free()
 
 
+@pytest.mark.parametrize("k,n,batch", [(2048, 151936, 2), (2048, 151936, 4), (2304, 40000, 8)])
+def test_gemv_large_result_in_slices(ctx, k, n, batch, threads):
+    """A host-buffer result above 1 MiB is computed in row slices, each copied
+    out while the next computes (K = 2304 has no tensor map: the bulk-copy
+    form): every row against ops::gemv, and against the device-buffer entry
+    point's result of the same product."""
+    torch = pytest.importorskip("torch")
+    data = quant_matrix(1050 + k + batch, Q4_K, n, k)
+    x = activations(1051 + batch, batch, k)
+    w = ctx.upload(data, Q4_K, n, k)
+    got = ctx.gemv(w, x)
+    want = oracle.gemv(Q4_K, data, n, k, x, threads=threads)
+    assert rel_err(got, want) < TOL
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((batch, n), dtype=torch.float32, device="cuda")
+    ctx.gemv_dev(w, xd.data_ptr(), yd.data_ptr(), batch)
+    torch.cuda.synchronize()
+    assert rel_err(got, yd.cpu().numpy()) < 1e-6
+    again = ctx.gemv(w, x)
+    assert np.array_equal(again.view(np.uint32), got.view(np.uint32))
+    w.free()
+
+
 def test_q8_0_config_shape(ctx, threads):
     data = quant_matrix(1100, Q8_0, 4096, 4096)
     x = activations(1101, 1, 4096)
