@@ -12,10 +12,24 @@
 
 using namespace strata;
 
+// A host-buffer call of the layer captured as one CUDA graph (the input
+// copy, the layer's launches on both streams, the output copy) for a token
+// count, valid while the context's buffers are those of generation `gen`.
+struct MoeGraph {
+    int64_t T = 0;
+    bool logits = false;
+    uint64_t gen = 0;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t used = 0;
+};
+
 struct strata_moe {
     uint32_t magic = 0x454F4D53u;  // "SMOE"
     strata_ctx* ctx = nullptr;
     strata_moe_desc d{};
+    static constexpr int kGraphs = 4;  // token counts kept (least recently used replaced)
+    mutable MoeGraph graphs[kGraphs];
+    mutable uint64_t tick = 0;
 };
 
 namespace {
@@ -110,6 +124,47 @@ int moe_enqueue(strata_ctx* ctx, const strata_moe* L, const float* x, const floa
     return check_launch(ctx, "moe layer kernels");
 }
 
+// Captures `enqueue` (the whole host-buffer call on the context stream) into
+// a graph for token count T, replacing the least recently used entry. Best
+// effort: when the capture or the instantiation fails the call simply stays
+// uncached (the error is cleared; the direct path has already run).
+template <typename F>
+void capture_layer(strata_ctx* ctx, const strata_moe* L, int64_t T, bool logits, F&& enqueue) {
+    MoeGraph* slot = &L->graphs[0];
+    for (MoeGraph& m : L->graphs)
+        if (!m.exec || m.used < slot->used) slot = &m;
+    if (slot->exec) cudaGraphExecDestroy(slot->exec);
+    *slot = MoeGraph{};
+    const uint64_t gen = ctx->buf_gen;
+    if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return;
+    }
+    const std::string saved = ctx->last_error;
+    const int rc = enqueue();
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (rc == STRATA_OK && e == cudaSuccess && g && ctx->buf_gen == gen &&
+        cudaGraphInstantiate(&exec, g, 0) == cudaSuccess) {
+        slot->T = T;
+        slot->logits = logits;
+        slot->gen = gen;
+        slot->exec = exec;
+        slot->used = ++L->tick;
+    }
+    if (g) cudaGraphDestroy(g);
+    (void)cudaGetLastError();
+    ctx->last_error = saved;
+}
+
+void release_graphs(const strata_moe* L) {
+    for (MoeGraph& m : L->graphs) {
+        if (m.exec) cudaGraphExecDestroy(m.exec);
+        m = MoeGraph{};
+    }
+}
+
 int check_moe(strata_ctx* ctx, const strata_moe* L) {
     if (!L || L->magic != kMoeMagic) return fail(ctx, STRATA_ERR_INVALID, "invalid moe layer handle");
     if (L->ctx != ctx) return fail(ctx, STRATA_ERR_INVALID, "moe layer belongs to another context");
@@ -119,6 +174,14 @@ int check_moe(strata_ctx* ctx, const strata_moe* L) {
 }  // namespace
 
 namespace strata {
+
+void moe_release_all(strata_ctx* ctx) {
+    for (strata_moe* L : ctx->moes) {
+        release_graphs(L);
+        L->ctx = nullptr;
+    }
+    ctx->moes.clear();
+}
 
 int moe_enqueue_checked(strata_ctx* ctx, const strata_moe* L, const float* x, const float* logits, int64_t T,
                         float* out, int32_t* ids, float* wts, cudaStream_t s) {
@@ -183,6 +246,7 @@ int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe
     strata_moe* L = new strata_moe();
     L->ctx = ctx;
     L->d = *d;
+    ctx->moes.insert(L);
     *out = L;
     return STRATA_OK;
 }
@@ -190,6 +254,12 @@ int strata_cuda_moe_create(strata_ctx* ctx, const strata_moe_desc* d, strata_moe
 int strata_cuda_moe_destroy(strata_moe* L) {
     if (!L || L->magic != kMoeMagic) return STRATA_ERR_INVALID;
     L->magic = 0;
+    if (L->ctx) {  // null once its context was destroyed (the graphs went with it)
+        std::lock_guard<std::mutex> g(L->ctx->mu);
+        cudaSetDevice(L->ctx->device);
+        release_graphs(L);
+        L->ctx->moes.erase(L);
+    }
     delete L;
     return STRATA_OK;
 }
@@ -227,21 +297,41 @@ int strata_cuda_moe_ffn(strata_ctx* ctx, const strata_moe* L, const float* x, co
     if ((rc = ensure_pinned(ctx, ctx->y_host, out_bytes + 512, "cudaMallocHost(out)"))) return rc;
     uint8_t* hx = static_cast<uint8_t*>(ctx->x_host.ptr);
     uint8_t* dx = static_cast<uint8_t*>(ctx->x_dev.ptr);
+    uint8_t* dy = static_cast<uint8_t*>(ctx->y_dev.ptr);
+    uint8_t* hy = static_cast<uint8_t*>(ctx->y_host.ptr);
     const size_t lo = (xb + 255) & ~size_t(255);
+    const size_t io = (xb + 255) & ~size_t(255), wo = io + ((rb + 255) & ~size_t(255));
     memcpy(hx, x, xb);
     if (logits) memcpy(hx + lo, logits, lb);
-    cudaError_t e = cudaMemcpyAsync(dx, hx, lo + lb, cudaMemcpyHostToDevice, ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
-    uint8_t* dy = static_cast<uint8_t*>(ctx->y_dev.ptr);
-    const size_t io = (xb + 255) & ~size_t(255), wo = io + ((rb + 255) & ~size_t(255));
-    rc = moe_enqueue(ctx, L, reinterpret_cast<const float*>(dx), logits ? reinterpret_cast<const float*>(dx + lo) : nullptr,
-                     T, reinterpret_cast<float*>(dy), reinterpret_cast<int32_t*>(dy + io),
-                     reinterpret_cast<float*>(dy + wo), ctx->stream);
-    if (rc) return rc;
-    uint8_t* hy = static_cast<uint8_t*>(ctx->y_host.ptr);
-    e = cudaMemcpyAsync(hy, dy, wo + rb, cudaMemcpyDeviceToHost, ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
+    // input copy, the layer, output copy: all on the context stream (the
+    // shared expert forks from it and joins back)
+    auto enqueue = [&]() -> int {
+        cudaError_t e = cudaMemcpyAsync(dx, hx, lo + lb, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(H2D)");
+        int r = moe_enqueue(ctx, L, reinterpret_cast<const float*>(dx),
+                            logits ? reinterpret_cast<const float*>(dx + lo) : nullptr, T, reinterpret_cast<float*>(dy),
+                            reinterpret_cast<int32_t*>(dy + io), reinterpret_cast<float*>(dy + wo), ctx->stream);
+        if (r) return r;
+        e = cudaMemcpyAsync(hy, dy, wo + rb, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpyAsync(D2H)");
+        return STRATA_OK;
+    };
+    // A token count seen before with the same buffers replays its graph: one
+    // launch instead of the chain's dozen, so the device never waits for the
+    // host between kernels. The first call of a count runs directly (it sizes
+    // the buffers) and then captures the graph for the next one.
+    MoeGraph* hit = nullptr;
+    for (MoeGraph& m : L->graphs)
+        if (m.exec && m.T == T && m.logits == (logits != nullptr) && m.gen == ctx->buf_gen) hit = &m;
+    if (hit) {
+        hit->used = ++L->tick;
+        cudaError_t e = cudaGraphLaunch(hit->exec, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGraphLaunch(moe layer)");
+    } else if ((rc = enqueue())) {
+        return rc;
+    }
     if ((rc = wait_stream(ctx, ctx->stream))) return rc;
+    if (!hit) capture_layer(ctx, L, T, logits != nullptr, enqueue);
     memcpy(out, hy, xb);
     if (ids) memcpy(ids, hy + io, rb);
     if (wts) memcpy(wts, hy + wo, rb);

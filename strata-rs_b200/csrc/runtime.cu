@@ -62,6 +62,7 @@ int ensure_device(strata_ctx* ctx, DevBuf& b, size_t bytes, const char* what) {
         b.bytes = 0;
     }
     size_t want = bytes < 4096 ? 4096 : bytes;
+    ++ctx->buf_gen;
     cudaError_t e = cudaMalloc(&b.ptr, want);
     if (e != cudaSuccess) {
         b.ptr = nullptr;
@@ -82,6 +83,7 @@ int ensure_pinned(strata_ctx* ctx, PinnedBuf& b, size_t bytes, const char* what)
         b.bytes = 0;
     }
     size_t want = bytes < 4096 ? 4096 : bytes;
+    ++ctx->buf_gen;
     cudaError_t e = cudaMallocHost(&b.ptr, want);
     if (e != cudaSuccess) {
         b.ptr = nullptr;
@@ -189,6 +191,7 @@ int strata_cuda_destroy(strata_ctx* ctx) {
     if (!ctx) return STRATA_ERR_INVALID;
     cudaSetDevice(ctx->device);
     int rc = wait_stream(ctx, ctx->stream);
+    moe_release_all(ctx);
     comm_release(ctx);
     for (strata_weight* w : ctx->weights) {  // weights the caller did not free
         if (w->dev) cudaFree(w->dev);

@@ -67,9 +67,16 @@ struct strata_ctx {
     cudaEvent_t stage_ev[2] = {nullptr, nullptr};
     // every weight uploaded and not yet freed (released by strata_cuda_destroy)
     std::unordered_set<strata_weight*> weights;
+    // every MoE layer created and not yet destroyed: strata_cuda_destroy
+    // releases their captured graphs and detaches them
+    std::unordered_set<strata_moe*> moes;
     strata::CommState* comm = nullptr;
     int* err_host = nullptr;  // host-mapped word kernels set when a bounded wait expires
     int* err_dev = nullptr;
+    // bumped whenever ensure_device / ensure_pinned (re)allocates a buffer:
+    // a captured graph that reads the context's buffers is valid only for
+    // the generation it was captured in
+    uint64_t buf_gen = 0;
 };
 
 constexpr uint32_t kWeightMagic = 0x57545253u;  // "SRTW"
@@ -122,5 +129,8 @@ int64_t moe_embd(const strata_moe* layer);
 
 // comm.cu
 void comm_release(strata_ctx* ctx);
+
+// moe_host.cu: the context's layers give up their graphs and their context
+void moe_release_all(strata_ctx* ctx);
 
 }  // namespace strata

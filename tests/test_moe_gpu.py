@@ -274,6 +274,51 @@ def test_moe_one_token_layer(ctx, q, G, threads):
     assert rel_err(total[0], want[0]) < TOL, rel_err(total[0], want[0])
 
 
+def test_moe_host_calls_replay_captured_graphs(threads):
+    """The host-buffer layer call captures its work (input copy, both streams'
+    launches, output copy) as a graph per token count and replays it on later
+    calls with that count. Over more token counts than the cache keeps, with
+    and without router logits, a replayed call on new inputs matches the
+    oracle, and a replayed call on the first inputs equals the direct first
+    call bit for bit. A context destroyed before its layer releases the
+    layer's graphs (the layer is freed afterwards)."""
+    dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
+    t = make_layer(1600, dims["n_embd"], dims["E"], dims["n_ff"], dims["n_ff_s"])
+    c = sc.Context(0)
+    ws = upload(c, t, dims)
+    layer = c.moe_create(ws, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    checked = 0
+    for n, T in enumerate([1, 2, 3, 5, 7, 1, 3]):
+        for with_logits in (True, False):
+            xa = activations(1601 + n, T, dims["n_embd"])
+            xb = activations(1651 + n, T, dims["n_embd"])
+            la = rng(1701 + n).standard_normal((T, dims["E"])).astype(np.float32) if with_logits else None
+            lb = rng(1751 + n).standard_normal((T, dims["E"])).astype(np.float32) if with_logits else None
+            first = c.moe_ffn(layer, xa, la)
+            other = c.moe_ffn(layer, xb, lb)
+            again = c.moe_ffn(layer, xa, la)
+            for u, v in zip(first, again):
+                assert np.array_equal(u.view(np.uint32), v.view(np.uint32)), (T, with_logits)
+            if with_logits and checked < 3:
+                want, want_ids, want_w = oracle.moe_layer(t, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"],
+                                                          dims["n_ff_s"], xb, lb, threads=threads)
+                check_routing(other[1], other[2], want_ids, want_w)
+                for i in range(T):
+                    assert rel_err(other[0][i], want[i]) < TOL, (T, i)
+                checked += 1
+    c2 = sc.Context(0)
+    ws2 = upload(c2, t, dims)
+    layer2 = c2.moe_create(ws2, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
+    x = activations(1800, 2, dims["n_embd"])
+    r1 = c2.moe_ffn(layer2, x)
+    r2 = c2.moe_ffn(layer2, x)
+    assert np.array_equal(r1[0].view(np.uint32), r2[0].view(np.uint32))
+    c2.close()
+    layer2.free()
+    free_all(ws, layer)
+    c.close()
+
+
 def test_moe_dev_entry_on_torch_stream(ctx):
     torch = pytest.importorskip("torch")
     dims = dict(n_embd=512, E=16, k=4, n_ff=256, n_ff_s=256)
