@@ -246,6 +246,7 @@ int strata_cuda_set_wait_timeout_ms(strata_ctx* ctx, uint32_t ms) {
 int strata_cuda_set_gemv_path(strata_ctx* ctx, int path) {
     if (!ctx || path < STRATA_GEMV_AUTO || path > STRATA_GEMV_TENSOR_CORES) return STRATA_ERR_INVALID;
     std::lock_guard<std::mutex> g(ctx->mu);
+    if (ctx->gemv_path != path) ++ctx->buf_gen;  // captured MoE graphs hold the old path's GEMV kernels
     ctx->gemv_path = path;
     return STRATA_OK;
 }

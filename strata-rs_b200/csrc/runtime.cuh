@@ -73,9 +73,9 @@ struct strata_ctx {
     strata::CommState* comm = nullptr;
     int* err_host = nullptr;  // host-mapped word kernels set when a bounded wait expires
     int* err_dev = nullptr;
-    // bumped whenever ensure_device / ensure_pinned (re)allocates a buffer:
-    // a captured graph that reads the context's buffers is valid only for
-    // the generation it was captured in
+    // bumped whenever ensure_device / ensure_pinned (re)allocates a buffer
+    // or the GEMV path changes: a captured graph that reads the context's
+    // buffers is valid only for the generation it was captured in
     uint64_t buf_gen = 0;
 };
 

@@ -306,6 +306,21 @@ def test_moe_host_calls_replay_captured_graphs(threads):
                 for i in range(T):
                     assert rel_err(other[0][i], want[i]) < TOL, (T, i)
                 checked += 1
+    # a change of GEMV path reaches the router and shared-expert GEMVs of a
+    # token count already cached: the host call then equals the (never
+    # cached) device-buffer call on the new path
+    torch = pytest.importorskip("torch")
+    x = activations(1850, 2, dims["n_embd"])
+    c.moe_ffn(layer, x)
+    c.moe_ffn(layer, x)
+    c.set_gemv_path(sc.Context.GEMV_CUDA_CORES)
+    host = c.moe_ffn(layer, x)[0]
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty((2, dims["n_embd"]), dtype=torch.float32, device="cuda")
+    c.moe_ffn_dev(layer, xd.data_ptr(), 0, 2, od.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(host.view(np.uint32), od.cpu().numpy().view(np.uint32))
+    c.set_gemv_path(sc.Context.GEMV_AUTO)
     c2 = sc.Context(0)
     ws2 = upload(c2, t, dims)
     layer2 = c2.moe_create(ws2, dims["n_embd"], dims["E"], dims["k"], dims["n_ff"], dims["n_ff_s"])
