@@ -589,6 +589,17 @@ static int gemv_sliced_out(strata_ctx* ctx, const strata_weight* w, const float*
     char* d = static_cast<char*>(ctx->y_dev.ptr);
     const size_t pitch = (size_t)N * sizeof(float);
     int issued = 0;
+    bool copying = false;  // a slice's copy is queued on the copy stream
+    // on an error after a slice's copy was queued, it may still be writing
+    // the pinned staging: wait (bounded) for it before returning
+    auto bail = [&](int code) {
+        if (copying) {
+            const std::string why = ctx->last_error;
+            (void)wait_stream(ctx, ctx->copy);
+            ctx->last_error = why;
+        }
+        return code;
+    };
     for (int64_t r0 = 0; r0 < N; r0 += rs, ++issued) {
         const int64_t r1 = std::min(N, r0 + rs);
         alignas(64) unsigned char tm[128];
@@ -597,21 +608,23 @@ static int gemv_sliced_out(strata_ctx* ctx, const strata_weight* w, const float*
         GemvArgs a{base, w->row_bytes, r1 - r0, w->cols, xd, reinterpret_cast<float*>(d) + r0, batch, ctx->sm_count,
                    has_tm ? tm : nullptr, N, nullptr};
         launch_gemv_mma(w->quant, a, ctx->xfrag.ptr, ctx->err_dev, ctx->stream, issued == 0);
-        if ((rc = check_launch(ctx, "tensor-core gemv kernel (slice)"))) return rc;
+        if ((rc = check_launch(ctx, "tensor-core gemv kernel (slice)"))) return bail(rc);
         const size_t off = (size_t)r0 * sizeof(float), width = (size_t)(r1 - r0) * sizeof(float);
         cudaError_t e = cudaEventRecord(ctx->slice_ev[issued], ctx->stream);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->copy, ctx->slice_ev[issued], 0);
-        if (e == cudaSuccess)
+        if (e == cudaSuccess) {
             e = cudaMemcpy2DAsync(h + off, pitch, d + off, pitch, width, (size_t)batch, cudaMemcpyDeviceToHost,
                                   ctx->copy);
+            copying = copying || e == cudaSuccess;
+        }
         if (e == cudaSuccess) e = cudaEventRecord(ctx->piece_ev[issued], ctx->copy);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "result slice copy");
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "result slice copy"));
     }
     ctx->copy_pool.prime();  // threads ready when the first slice lands
     for (int k = 0; k < issued; ++k) {
         const int64_t r0 = k * rs, r1 = std::min(N, r0 + rs);
-        if ((rc = wait_event(ctx, ctx->piece_ev[k]))) return rc;
-        if ((rc = check_device_error(ctx))) return rc;
+        if ((rc = wait_event(ctx, ctx->piece_ev[k]))) return bail(rc);
+        if ((rc = check_device_error(ctx))) return bail(rc);
         const size_t off = (size_t)r0 * sizeof(float);
         ctx->copy_pool.copy2d(reinterpret_cast<char*>(y) + off, pitch, h + off, pitch,
                               (size_t)(r1 - r0) * sizeof(float), (size_t)batch);
