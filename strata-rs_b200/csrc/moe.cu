@@ -919,27 +919,39 @@ moe_mma_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, i
 #pragma unroll
         for (int s = 0; s < kStages - 1; ++s) issue(s);
         for (int tile = 0; tile < ntiles; ++tile) {
-            issue(tile + kStages - 1);
-            cp_async_wait<kStages - 1>();
+            // one barrier per tile: after it this tile's copies (every thread's
+            // part) are visible, and every warp is done with the previous tile,
+            // whose stage the issue below rewrites
+            cp_async_wait<kStages - 2>();
             __syncthreads();
+            issue(tile + kStages - 1);
             const int i0 = r0 + tile * RS;
             const int rows = r1 - i0 < RS ? r1 - i0 : RS;
             const uint8_t* wt = wring + (int64_t)(tile % kStages) * tile_bytes;
             const float* xt = xring + (tile % kStages) * TP * RSX;
-            for (int q = tid; q < rows * G; q += kMoeThreads) {
-                const int rr = q / G, gg = q - rr * G;
-                const uint4 h = *reinterpret_cast<const uint4*>(wt + (int64_t)rr * RB + gg * block_bytes(Q));
-                uint32_t sc_lo, sc_hi, m_lo, m_hi;
-                scales_k4_packed(h.y, h.z, h.w, sc_lo, sc_hi, m_lo, m_hi);
-                const float d = h2f(h.x), dm = h2f(h.x >> 16);
-                float* tb = tab + rr * TPITCH + gg * 16;
+            // the scale table entries of this warp's own sub-blocks (d sc and dmin m
+            // per row): no other warp reads them, so a warp needs no barrier to use them
+            for (int rr = lane; rr < rows; rr += 32) {
+                int gcur = -1;
+                uint32_t sc_lo = 0, sc_hi = 0, m_lo = 0, m_hi = 0;
+                float d = 0.0f, dm = 0.0f;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int s2 = 0; s2 < SPW; ++s2) {
+                    const int sbg = sb0 + s2, gg = sbg >> 3, j = sbg & 7;
+                    if (gg >= G) break;
+                    if (gg != gcur) {
+                        const uint4 h = *reinterpret_cast<const uint4*>(wt + (int64_t)rr * RB + gg * block_bytes(Q));
+                        scales_k4_packed(h.y, h.z, h.w, sc_lo, sc_hi, m_lo, m_hi);
+                        d = h2f(h.x);
+                        dm = h2f(h.x >> 16);
+                        gcur = gg;
+                    }
+                    float* tb = tab + rr * TPITCH + gg * 16;
                     tb[j] = d * (float)(((j < 4 ? sc_lo : sc_hi) >> (8 * (j & 3))) & 0xFFu);
                     tb[8 + j] = dm * (float)(((j < 4 ? m_lo : m_hi) >> (8 * (j & 3))) & 0xFFu);
                 }
             }
-            __syncthreads();
+            __syncwarp();
             for (int k0 = 0; k0 + 16 <= rows; k0 += 16) {
                 // the k index of the MMA maps to rows of the tile as k = 2t4 -> t4,
                 // 2t4 + 1 -> t4 + 4, 2t4 + 8 -> t4 + 8, 2t4 + 9 -> t4 + 12 (A and B
@@ -1023,7 +1035,6 @@ moe_mma_kernel(const uint8_t* __restrict__ W0, const uint8_t* __restrict__ W1, i
                     }
                 }
             }
-            __syncthreads();  // the stage is rewritten by the next issue
         }
         cp_async_wait<0>();
         // min term of (sub-block, token): sum over the 4 lanes t4 (every lane of a
