@@ -465,7 +465,7 @@ def bench_q8_0(ctx, torch, stream, with_cpu: bool) -> dict:
     hbm, peak_kind = peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
     out = {"k": k, "n": n, "batch": 1, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
-           "algorithmic_bytes": nbytes, "kernel": "gemv_q8_0_kernel (CUDA cores)"}
+           "algorithmic_bytes": nbytes, "kernel": "q8::gemv_q8_0_bulk_kernel (CUDA cores, rows staged by bulk copies into a 4-stage shared-memory ring)"}
     if with_cpu:
         sys.path.insert(0, str(ROOT / "oracle"))
         import oracle

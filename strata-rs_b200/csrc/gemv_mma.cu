@@ -1268,7 +1268,217 @@ void launch(const GemvArgs& a, const uint2* xf, const float* xs, const __half* x
 
 }  // namespace tall
 
+// ============================================================ Q8_0, batch 1-2
+//
+// Q8_0 rows are 34-byte blocks, so per-lane global loads of a block are 2-byte
+// loads (17 per block). Here a producer warp copies each 16-row x 32-block
+// stage into a 4-deep shared-memory ring with one bulk copy per row (1088
+// bytes: a row's 32 blocks are contiguous and 16-byte aligned when K is a
+// multiple of 1024), and each consumer warp owns kRpw rows of the tile:
+// lane l takes block l of every row of the stage, reads its 34 bytes as 9
+// aligned words from shared memory and funnel-shifts the quants into place.
+// The arithmetic and its order are those of the CUDA-core Q8_0 kernel (per
+// block: 32 FMAs in index order, then d * acc into the lane's sum; lanes
+// summed by a butterfly at the end of the row), so the results are the same.
+namespace q8 {
+
+constexpr int kRows = 16;                  // rows per tile: 4 per consumer warp
+constexpr int kBlocks = 32;                // blocks per row and stage: one per lane
+constexpr int kRowBytes = kBlocks * 34;    // 1088
+constexpr int kStages = 4;
+constexpr int kConsumers = 4;
+constexpr int kRpw = kRows / kConsumers;   // rows per consumer warp
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kStage = kRows * kRowBytes;  // 17408 bytes
+// + 16: lane 31's ninth word of the last row of the last slot lies past the ring
+constexpr int kSmem = kStages * kStage + 16;
+
+template <int NB>
+__global__ void __launch_bounds__(kThreads, 3)
+gemv_q8_0_bulk_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, int nblk,
+                      const float* __restrict__ X, float* __restrict__ Y, int64_t ldy, int* __restrict__ err) {
+    // the next kernel may launch now: it reads this grid's outputs only after its own wait
+    asm volatile("griddepcontrol.launch_dependents;");
+    extern __shared__ __align__(16) uint8_t q8_ring[];
+    __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
+    __shared__ int abort_flag;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ntiles = (N + kRows - 1) / kRows;
+    const int nchunks = nblk / kBlocks;
+    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int nstages = my_tiles * nchunks;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(smem_u32(&full_bar[i]), 1);
+            mbar_init(smem_u32(&empty_bar[i]), kConsumers);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kConsumers) {
+        // ---------------- producer (the weights do not depend on the previous kernel)
+        int issued = 0, tile = blockIdx.x, chunk = 0;
+        for (int j = 0; j < nstages; ++j) {
+            const int slot = j % kStages;
+            bool ok = true;
+            if (j >= kStages) ok = mbar_wait(smem_u32(&empty_bar[slot]), ((j / kStages) - 1) & 1, err);
+            ok = __all_sync(0xFFFFFFFFu, ok) && __shfl_sync(0xFFFFFFFFu, *(volatile int*)&abort_flag, 0) == 0;
+            if (!ok) {
+                abort_flag = 1;
+                break;
+            }
+            const uint32_t fb = smem_u32(&full_bar[slot]);
+            if (lane == 0) mbar_expect_tx(fb, (uint32_t)kStage);
+            __syncwarp();
+            if (lane < kRows) {
+                int row = tile * kRows + lane;
+                row = row < N ? row : N - 1;  // rows past N repeat the last (never stored)
+                const uint8_t* src = W + (int64_t)row * row_bytes + (int64_t)chunk * kRowBytes;
+                bulk_g2s(smem_u32(q8_ring + slot * kStage + lane * kRowBytes), src, (uint32_t)kRowBytes, fb);
+            }
+            issued = j + 1;
+            if (++chunk == nchunks) {
+                chunk = 0;
+                tile += gridDim.x;
+            }
+        }
+        // drain: the copies of the last stages issued may still be in flight
+        for (int j = max(0, issued - kStages); j < issued; ++j)
+            mbar_wait(smem_u32(&full_bar[j % kStages]), (j / kStages) & 1, nullptr);
+        return;
+    }
+
+    // ---------------- consumers: x comes from the preceding kernel in the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int64_t K = (int64_t)nblk * 32;
+    // the quants of block `lane` start at byte 34 lane + 2 of a row: the aligned
+    // word below it and the shift that brings them into place (0 or 16 bits)
+    const uint32_t qoff = 34u * (uint32_t)lane + 2u;
+    const uint32_t qword = qoff & ~3u, qshift = (qoff & 3u) * 8u;
+    float sum[kRpw][NB];
+#pragma unroll
+    for (int r = 0; r < kRpw; ++r)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) sum[r][b] = 0.0f;
+    bool live = true;
+    int tile = blockIdx.x, chunk = 0;
+    for (int j = 0; j < nstages; ++j) {
+        const int slot = j % kStages;
+        if (live) {
+            const bool ok = mbar_wait(smem_u32(&full_bar[slot]), (j / kStages) & 1, err);
+            live = __all_sync(0xFFFFFFFFu, ok) && __shfl_sync(0xFFFFFFFFu, *(volatile int*)&abort_flag, 0) == 0;
+            if (!live) abort_flag = 1;
+        }
+        if (live) {
+            const uint8_t* st = q8_ring + slot * kStage + (kRpw * warp) * kRowBytes;
+            uint32_t q[kRpw][8];
+            float d[kRpw];
+#pragma unroll
+            for (int r = 0; r < kRpw; ++r) {
+                const uint8_t* row = st + r * kRowBytes;
+                d[r] = f16_bits_to_f32(*reinterpret_cast<const unsigned short*>(row + 34 * lane));
+                const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + qword);
+                uint32_t wv[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) wv[k] = wp[k];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) q[r][i] = __funnelshift_r(wv[i], wv[i + 1], qshift) ^ 0x80808080u;
+            }
+            float acc[kRpw][NB];
+#pragma unroll
+            for (int r = 0; r < kRpw; ++r)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
+            const float* xb = X + (int64_t)(chunk * kBlocks + lane) * 32;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float4 xv[NB];
+#pragma unroll
+                for (int b = 0; b < NB; ++b) xv[b] = __ldg(reinterpret_cast<const float4*>(xb + b * K + 4 * i));
+#pragma unroll
+                for (int r = 0; r < kRpw; ++r) {
+                    // 2^23 + (q + 128) - (2^23 + 128) = q, exactly
+                    const float f0 = __uint_as_float(__byte_perm(q[r][i], 0x4B000000u, 0x7440u)) - 8388736.0f;
+                    const float f1 = __uint_as_float(__byte_perm(q[r][i], 0x4B000000u, 0x7441u)) - 8388736.0f;
+                    const float f2 = __uint_as_float(__byte_perm(q[r][i], 0x4B000000u, 0x7442u)) - 8388736.0f;
+                    const float f3 = __uint_as_float(__byte_perm(q[r][i], 0x4B000000u, 0x7443u)) - 8388736.0f;
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) {
+                        acc[r][b] = fmaf(f0, xv[b].x, acc[r][b]);
+                        acc[r][b] = fmaf(f1, xv[b].y, acc[r][b]);
+                        acc[r][b] = fmaf(f2, xv[b].z, acc[r][b]);
+                        acc[r][b] = fmaf(f3, xv[b].w, acc[r][b]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRpw; ++r)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) sum[r][b] = fmaf(d[r], acc[r][b], sum[r][b]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
+        if (++chunk == nchunks) {
+            // the tile's rows are done: each warp sums its own rows over the lanes
+#pragma unroll
+            for (int r = 0; r < kRpw; ++r)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    float v = sum[r][b];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+                    const int row = tile * kRows + kRpw * warp + r;
+                    if (live && lane == 0 && row < N) Y[b * ldy + row] = v;
+                    sum[r][b] = 0.0f;
+                }
+            chunk = 0;
+            tile += gridDim.x;
+        }
+    }
+}
+
+template <int NB>
+void launch(const GemvArgs& a, int* err, cudaStream_t s) {
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        cudaFuncSetAttribute(gemv_q8_0_bulk_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q8_0_bulk_kernel<NB>, kThreads, kSmem);
+        per_sm = n < 1 ? 1 : n;
+    }
+    const int64_t ntiles = (a.N + kRows - 1) / kRows;
+    int64_t grid = (int64_t)a.sm_count * per_sm;
+    if (grid > ntiles) grid = ntiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gemv_q8_0_bulk_kernel<NB>, a.W, a.row_bytes, (int)a.N, (int)(a.K / 32), a.X, a.Y,
+                       ldy_of(a), err);
+}
+
+}  // namespace q8
+
 }  // namespace
+
+bool gemv_q8_0_bulk_supported(const GemvArgs& a) {
+    return a.batch >= 1 && a.batch <= 2 && a.K % 1024 == 0 && a.K > 0 && a.K < (1ll << 26) && a.N > 0 &&
+           a.N < (1ll << 31) && a.row_bytes == a.K / 32 * 34 && ((uintptr_t)a.W % 16) == 0 &&
+           ((uintptr_t)a.X % 16) == 0 && !a.peers;
+}
+
+void launch_gemv_q8_0_bulk(const GemvArgs& a, int* err, cudaStream_t s) {
+    if (a.batch == 1) q8::launch<1>(a, err, s);
+    else q8::launch<2>(a, err, s);
+}
 
 // The 3-D view of a Q4_K / Q5_K matrix the tensor-core GEMV copies from:
 // [8-byte units x 16][128-byte lines x row_bytes/128][rows], box

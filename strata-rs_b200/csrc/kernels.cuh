@@ -38,6 +38,10 @@ int launch_dequant(uint32_t quant, const uint8_t* w, int64_t row_bytes, int64_t 
                    float* out, cudaStream_t stream);
 // CUDA-core GEMV: every quant type, any batch (8-token chunks beyond 8)
 int launch_gemv(uint32_t quant, const GemvArgs& a, cudaStream_t s);
+// Q8_0 at batch 1-2 with K a multiple of 1024: rows staged by bulk copies
+// (gemv_mma.cu); the same arithmetic, in the same order, as launch_gemv's
+bool gemv_q8_0_bulk_supported(const GemvArgs& a);
+void launch_gemv_q8_0_bulk(const GemvArgs& a, int* err, cudaStream_t s);
 
 // Tensor-core GEMV (Q4_K / Q5_K): activation-limb prologue + GEMV kernel,
 // any batch (8-token chunks beyond 8); `work` holds gemv_mma_work_bytes.

@@ -665,6 +665,10 @@ int gemv_enqueue_strided(strata_ctx* ctx, const strata_weight* w, const float* x
     if (peers) return fail(ctx, STRATA_ERR_INVALID, "the peer-store epilogue needs the tensor-core gemv");
     if (ctx->gemv_path == STRATA_GEMV_TENSOR_CORES)
         return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no tensor-core gemv for quant %u", w->quant);
+    if (w->quant == kQ8_0 && gemv_q8_0_bulk_supported(a)) {
+        launch_gemv_q8_0_bulk(a, ctx->err_dev, s);
+        return check_launch(ctx, "q8_0 gemv kernel");
+    }
     if (launch_gemv(w->quant, a, s))
         return fail(ctx, STRATA_ERR_UNSUPPORTED_QUANT, "no gemv kernel for quant %u", w->quant);
     return check_launch(ctx, "gemv kernel");
