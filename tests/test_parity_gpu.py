@@ -343,3 +343,21 @@ def test_tensor_core_path_rejects_other_types():
     assert e.value.code == sc.ERR_UNSUPPORTED_QUANT
     w.free()
     c.close()
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (301, 2048), (77, 1024)])
+def test_q8_0_bulk_kernel_equals_the_cuda_core_kernel(ctx, rows, cols, threads):
+    """Q8_0 at batch 1-2 with K a multiple of 1024 runs the bulk-copy kernel;
+    batch 3 still runs the CUDA-core kernel. Both do the same arithmetic in the
+    same order, so each token's outputs agree bit for bit (and with ops::gemv
+    within tolerance)."""
+    data = quant_matrix(2500 + cols, Q8_0, rows, cols)
+    x = activations(2501 + rows, 3, cols)
+    w = ctx.upload(data, Q8_0, rows, cols)
+    y3 = ctx.gemv(w, x)
+    y1 = ctx.gemv(w, x[:1])
+    y2 = ctx.gemv(w, x[:2])
+    assert np.array_equal(y1[0].view(np.uint32), y3[0].view(np.uint32))
+    assert np.array_equal(y2.view(np.uint32), y3[:2].view(np.uint32))
+    assert rel_err(y1[0], oracle.gemv(Q8_0, data, rows, cols, x[:1], threads=threads)[0]) < TOL
+    w.free()
