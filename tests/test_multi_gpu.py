@@ -207,11 +207,18 @@ def _worker(rank, world, uid, q):
 
 def _config_worker(rank, world, uid, q):
     """The configuration shapes: row-sharded Q4_K 8192 -> 28672 and 28672 ->
-    8192 GEMVs at batch 1 and 8 (bitwise the one-GPU GEMV, through the peer
-    gather), their M = 1024 GEMMs (within fp32 reassociation of the one-GPU
-    GEMM), and the 256-expert layer (hidden 2048, expert width 512, top 8,
-    shared expert 512) expert-parallel at T = 1 and 64 (within 1e-3 of the
-    one-GPU layer)."""
+    8192 GEMVs at batch 1 and 8 through the peer gather, their M = 1024 GEMMs
+    (against the f64 product, the GEMM's 1e-2 bound), and the 256-expert layer
+    (hidden 2048, expert width 512, top 8, shared expert 512) expert-parallel
+    at T = 1 and 64 (within 1e-3 of the one-GPU layer).
+
+    A shard's GEMV equals the one-GPU GEMV bit for bit when the shard's row
+    count selects the same kernel shape; the consumer-warp count (four or
+    eight, from the number of 16-row tiles) and the tall batch-1 kernel follow
+    the row count, and a different shape adds the same per-block partial sums
+    in another grouping. So the shard is held to 1e-5 of the one-GPU result
+    (fp32 regrouping only; the parity bound is 1e-3) and to ops::gemv itself
+    on a row range, and to the bits when the shapes agree (world 2 here)."""
     try:
         sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "strata-rs_b200"),
                         os.path.join(os.path.dirname(HERE), "oracle")]
@@ -238,9 +245,15 @@ def _config_worker(rank, world, uid, q):
                 with torch.cuda.stream(st):
                     ctx.gemv_sharded_dev(shard, x.data_ptr(), y.data_ptr(), B, st.cuda_stream)
                 st.synchronize()
-                want = ctx.gemv(full, x.cpu().numpy())
-                assert np.array_equal(y.cpu().numpy().view(np.uint32), want.reshape(B, N).view(np.uint32)), \
-                    ("config gemv", K, N, B)
+                want = ctx.gemv(full, x.cpu().numpy()).reshape(B, N)
+                got = y.cpu().numpy()
+                assert rel_err(got, want) < 1e-5, ("config gemv", K, N, B, rel_err(got, want))
+                if world == 2:
+                    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), ("config gemv bits", K, N, B)
+                r0 = (N // world) * rank
+                import oracle
+                ref = oracle.gemv_rows(Q4_K, data, N, K, x[0].cpu().numpy(), r0, r0 + 256, threads=4)
+                assert rel_err(got[0, r0:r0 + 256], ref) < 1e-3, ("config gemv parity", K, N, B)
             M = 1024
             bits = bf16_bits(activations(2102, M, K))
             xb = torch.from_numpy(bits.view(np.int16)).to(dev)
