@@ -1291,7 +1291,10 @@ constexpr int kRpw = kRows / kConsumers;   // rows per consumer warp
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kStage = kRows * kRowBytes;  // 17408 bytes
 // + 16: lane 31's ninth word of the last row of the last slot lies past the ring
-constexpr int kSmem = kStages * kStage + 16;
+constexpr int kRing = kStages * kStage + 16;
+// the activations follow the ring: NB x K floats, at most this many bytes
+constexpr int kMaxXBytes = 48 * 1024;
+inline int smem_bytes(int nb, int64_t K) { return kRing + nb * (int)K * 4; }
 
 template <int NB>
 __global__ void __launch_bounds__(kThreads, 3)
@@ -1300,6 +1303,9 @@ gemv_q8_0_bulk_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, i
     // the next kernel may launch now: it reads this grid's outputs only after its own wait
     asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ __align__(16) uint8_t q8_ring[];
+    // activations, float4 (chunk, word i, lane) of token b at ((b * chunks + chunk) * 8 + i) * 32 + lane:
+    // the 32 lanes of one (chunk, i) read 512 contiguous bytes
+    float4* xs = reinterpret_cast<float4*>(q8_ring + kRing);
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ int abort_flag;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1350,9 +1356,20 @@ gemv_q8_0_bulk_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, i
         return;
     }
 
-    // ---------------- consumers: x comes from the preceding kernel in the stream
+    // ---------------- consumers: x comes from the preceding kernel in the stream;
+    // the CTA's 128 consumer threads stage all of it once (the weights of the
+    // first stages are in flight meanwhile)
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int64_t K = (int64_t)nblk * 32;
+    {
+        const int n4 = NB * nblk * 8;  // float4s of x
+        const float4* x4 = reinterpret_cast<const float4*>(X);
+        for (int g = threadIdx.x; g < n4; g += kConsumers * 32) {
+            const int b = g / (nblk * 8), r = g - b * (nblk * 8);
+            const int c = r >> 8, ln = (r >> 3) & 31, i = r & 7;  // global float4 (chunk c, lane ln, word i)
+            xs[((b * nchunks + c) * 8 + i) * 32 + ln] = __ldg(x4 + g);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+    }
     // the quants of block `lane` start at byte 34 lane + 2 of a row: the aligned
     // word below it and the shift that brings them into place (0 or 16 bits)
     const uint32_t qoff = 34u * (uint32_t)lane + 2u;
@@ -1391,12 +1408,11 @@ gemv_q8_0_bulk_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, i
             for (int r = 0; r < kRpw; ++r)
 #pragma unroll
                 for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
-            const float* xb = X + (int64_t)(chunk * kBlocks + lane) * 32;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 float4 xv[NB];
 #pragma unroll
-                for (int b = 0; b < NB; ++b) xv[b] = __ldg(reinterpret_cast<const float4*>(xb + b * K + 4 * i));
+                for (int b = 0; b < NB; ++b) xv[b] = xs[((b * nchunks + chunk) * 8 + i) * 32 + lane];
 #pragma unroll
                 for (int r = 0; r < kRpw; ++r) {
                     // 2^23 + (q + 128) - (2^23 + 128) = q, exactly
@@ -1441,12 +1457,19 @@ gemv_q8_0_bulk_kernel(const uint8_t* __restrict__ W, int64_t row_bytes, int N, i
 
 template <int NB>
 void launch(const GemvArgs& a, int* err, cudaStream_t s) {
-    static int per_sm = 0;
-    if (per_sm == 0) {
-        cudaFuncSetAttribute(gemv_q8_0_bulk_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(gemv_q8_0_bulk_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kRing + kMaxXBytes);
+        configured = true;
+    }
+    const int smem = smem_bytes(NB, a.K);
+    static int last_smem = -1, per_sm = 1;  // resident CTAs per SM at the last size asked
+    if (smem != last_smem) {
         int n = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q8_0_bulk_kernel<NB>, kThreads, kSmem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q8_0_bulk_kernel<NB>, kThreads, smem);
         per_sm = n < 1 ? 1 : n;
+        last_smem = smem;
     }
     const int64_t ntiles = (a.N + kRows - 1) / kRows;
     int64_t grid = (int64_t)a.sm_count * per_sm;
@@ -1454,7 +1477,7 @@ void launch(const GemvArgs& a, int* err, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1470,7 +1493,7 @@ void launch(const GemvArgs& a, int* err, cudaStream_t s) {
 }  // namespace
 
 bool gemv_q8_0_bulk_supported(const GemvArgs& a) {
-    return a.batch >= 1 && a.batch <= 2 && a.K % 1024 == 0 && a.K > 0 && a.K < (1ll << 26) && a.N > 0 &&
+    return a.batch >= 1 && a.batch <= 2 && a.K % 1024 == 0 && a.K > 0 && a.batch * a.K * 4 <= q8::kMaxXBytes && a.N > 0 &&
            a.N < (1ll << 31) && a.row_bytes == a.K / 32 * 34 && ((uintptr_t)a.W % 16) == 0 &&
            ((uintptr_t)a.X % 16) == 0 && !a.peers;
 }
